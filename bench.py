@@ -1,0 +1,347 @@
+"""Benchmark of the WarpGBM hot path on B200 (one JSON line on rank 0).
+
+Metric: train sec/100 trees @ 1M x 1K float32 regression
+(config 2: y = sum_{j<20} w_j x_j + sum_{j<10} 0.3 sin(x_{20+j}) + N(0, 0.5^2),
+num_bins=32, max_depth=5, 100 trees, lr=0.01), plus the histogram kernel's
+achieved HBM GB/s against the measured peak.
+
+A step is one complete ``WarpGBM.fit`` of the 100-tree ensemble (binning of
+the float matrix + every tree).  ``value``: inputs already resident in HBM
+(CUDA tensors).  ``e2e``: the same fit through the public numpy API, so the
+host->device copy of X and y and the device->host download of the forest are
+inside the timed region.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl reference]
+
+With N > 1 (torchrun), every rank holds its own 1M-row shard (weak scaling:
+the job trains on N x 1M rows); histograms are summed over ranks with NCCL.
+``--impl reference`` times the reference algorithm on the host cores (the
+CPU oracle port, all threads) on a bounded sample of the same workload.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import time
+
+import numpy as np
+import torch
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+CONFIG = dict(n=1_000_000, F=1000, num_bins=32, max_depth=5, n_estimators=100,
+              learning_rate=0.01)
+
+
+def parse():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=3)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--rows", type=int, default=CONFIG["n"])
+    ap.add_argument("--trees", type=int, default=CONFIG["n_estimators"])
+    ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--no-cpu", action="store_true", help="skip the cpu_baseline sample")
+    return ap.parse_args()
+
+
+def peaks():
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            p = json.load(f)
+        return float(p["hbm_gbs"]), "measured"
+    except Exception:
+        return 6650.0, "fallback"
+
+
+def make_data(rank: int, n: int, F: int, device):
+    """Config 2 synthetic regression, seeded per rank (rank r = shard r)."""
+    g = torch.Generator(device=device)
+    g.manual_seed(1234 + rank)
+    X = torch.randn((n, F), generator=g, device=device, dtype=torch.float32)
+    gw = torch.Generator(device=device)
+    gw.manual_seed(99)  # the same weights on every rank
+    w = torch.randn(20, generator=gw, device=device)
+    noise = torch.randn(n, generator=g, device=device) * 0.5
+    y = X[:, :20] @ w + 0.3 * torch.sin(X[:, 20:30]).sum(1) + noise
+    return X, y.contiguous()
+
+
+class Clocks:
+    """nvidia-smi sampling during the timed region."""
+
+    def __init__(self, index: int):
+        self.index = index
+        self.proc = None
+        self.path = os.path.join(ROOT, "gpurun_out", f"clocks_{os.getpid()}.csv")
+
+    def __enter__(self):
+        try:
+            os.makedirs(os.path.dirname(self.path), exist_ok=True)
+            self.f = open(self.path, "w")
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--id={self.index}",
+                 "--query-gpu=clocks.sm,clocks.max.sm,clocks_event_reasons.active,"
+                 "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+                 "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap",
+                 "--format=csv,noheader,nounits", "-lms", "200"],
+                stdout=self.f, stderr=subprocess.DEVNULL)
+        except Exception:
+            self.proc = None
+        return self
+
+    def __exit__(self, *a):
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except Exception:
+                self.proc.kill()
+            self.f.close()
+
+    def summary(self):
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        sm, mx, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for line in open(self.path):
+            parts = [p.strip() for p in line.split(",")]
+            if len(parts) < 7:
+                continue
+            try:
+                sm.append(float(parts[0]))
+                mx = float(parts[1])
+            except ValueError:
+                continue
+            for nm, v in zip(names, parts[3:7]):
+                if v.lower().startswith("active"):
+                    reasons.add(nm)
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": mx,
+                "reasons": sorted(reasons), "samples": len(sm)}
+
+
+def hist_algorithmic_bytes(model, n_total: int, k: int, E: int, B: int) -> float:
+    """Bytes the histogram builds must move (algorithmic, from the grown
+    trees): per built node n_rows * (k bins + 4 B q + 4 B row id [+4 B era])
+    + its E*k*B*(8+4) B histogram; built nodes = root + the smaller child of
+    every split above the last level."""
+    D = model.max_depth
+    per_row = k + 8 + (4 if E > 1 else 0)
+    per_node = E * k * B * 12
+
+    def count(nd):
+        return nd["samples"] if "leaf_value" in nd else count(nd["left"]) + count(nd["right"])
+
+    total = 0.0
+
+    def walk(nd, d):
+        nonlocal total
+        if "leaf_value" in nd or d + 1 >= D:
+            return
+        cl, cr = count(nd["left"]), count(nd["right"])
+        total += (cl if cl <= cr else cr) * per_row + per_node
+        walk(nd["left"], d + 1)
+        walk(nd["right"], d + 1)
+
+    for t in model._flat_trees():
+        total += n_total * per_row + per_node
+        walk(t, 0)
+    return total
+
+
+def cpu_sample(Xh: np.ndarray, yh: np.ndarray, bins_h: np.ndarray, edges_h: np.ndarray, trees: int):
+    """Reference algorithm on the host cores: quantile edges of 20 columns
+    (extrapolated to all features) + one full tree on the full 1M x 1K matrix
+    (fp32 histograms, reference mode), scaled to sec/100 trees."""
+    import oracle as O
+    threads = O.lib().orc_num_threads()
+    F = Xh.shape[1]
+    q = O.linspace_q(CONFIG["num_bins"])
+    t0 = time.perf_counter()
+    ncols = 20
+    for f in range(ncols):
+        O.quantile_edges(Xh[:, f], q)
+    bin_time = (time.perf_counter() - t0) * F / ncols
+    t0 = time.perf_counter()
+    O.bin_matrix(Xh, edges_h)
+    bin_time += time.perf_counter() - t0
+    m = O.OracleGBM(mode="reference", num_bins=CONFIG["num_bins"], max_depth=CONFIG["max_depth"],
+                    learning_rate=CONFIG["learning_rate"], n_estimators=1)
+    m.num_samples, m.num_features = bins_h.shape
+    m.bins, m.era, m.E = bins_h, np.zeros(bins_h.shape[0], np.int32), 1
+    m.imp = np.zeros((1, F), np.float32)
+    m.base_prediction = float(np.float32(yh.mean()))
+    m.pred = np.zeros((bins_h.shape[0], 1), np.float32) + np.float32(m.base_prediction)
+    t0 = time.perf_counter()
+    m._tree(yh - m.pred[:, 0], 0, np.arange(F, dtype=np.int32))
+    tree_time = time.perf_counter() - t0
+    total = bin_time + tree_time * trees
+    value = total * 100.0 / trees
+    return {"value": round(value, 3), "unit": "s/100 trees", "cores": threads, "kind": "port",
+            "sample": f"quantile edges of {ncols}/{F} columns (x{F // ncols}) + full binning + "
+                      f"1 tree of 1M x 1K, depth {CONFIG['max_depth']} (x{trees}); "
+                      f"measured {bin_time:.2f} s binning, {tree_time:.2f} s/tree"}
+
+
+def run_reference(args, rank):
+    """--impl reference: the reference algorithm (oracle port) on the host."""
+    if rank != 0:
+        return
+    rng = np.random.default_rng(0)
+    n, F = args.rows, CONFIG["F"]
+    Xh = rng.standard_normal((n, F), dtype=np.float32)
+    w = rng.standard_normal(20)
+    yh = (Xh[:, :20] @ w + 0.3 * np.sin(Xh[:, 20:30]).sum(1) + rng.normal(0, 0.5, n)).astype(np.float32)
+    import oracle as O
+    q = O.linspace_q(CONFIG["num_bins"])
+    edges = np.stack([O.quantile_edges(Xh[:, f], q) if f < 20 else
+                      np.quantile(Xh[:, f], q).astype(np.float32) for f in range(F)])
+    bins = O.bin_matrix(Xh, edges)
+    samples = []
+    for i in range(args.warmup + args.steps):
+        r = cpu_sample(Xh, yh, bins, edges, args.trees)
+        if i >= args.warmup:
+            samples.append(r)
+    v = statistics.median(s["value"] for s in samples)
+    last = samples[-1]
+    line = {"metric": "train sec/100 trees @1M×1K", "value": v, "unit": "s/100 trees",
+            "impl": "reference", "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": v * 1000.0, "higher_is_better": False, "scaling": "weak",
+            "vs_baseline": None, "dtype": "f32", "data": "synthetic (config 2 generator, numpy seed 0)",
+            "config": {"workload": "config2: 1M x 1000 f32 regression, B=32, depth 5, 100 trees, lr 0.01",
+                       "rows_per_rank": n},
+            "cpu_baseline": {**last, "value": v},
+            "e2e": {"value": v, "unit": "s/100 trees", "h2d_bytes_per_step": 0,
+                    "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+
+
+def main():
+    args = parse()
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if args.impl == "reference":
+        run_reference(args, rank)
+        return
+    import torch.distributed as dist
+    from datetime import timedelta
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        dist.init_process_group("nccl", timeout=timedelta(seconds=300), device_id=dev)
+    from warpgbm_b200 import WarpGBM, _lib
+    n, F = args.rows, CONFIG["F"]
+    X, y = make_data(rank, n, F, dev)
+    params = dict(num_bins=CONFIG["num_bins"], max_depth=CONFIG["max_depth"],
+                  n_estimators=args.trees, learning_rate=CONFIG["learning_rate"],
+                  distributed=world > 1)
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize()
+
+    import contextlib
+    import io
+    quiet = contextlib.redirect_stdout(io.StringIO())
+    with quiet:
+        for _ in range(args.warmup):
+            WarpGBM(**params).fit(X, y)
+    barrier()
+    model = None
+    times, hist_ms, hist_bytes = [], 0.0, 0.0
+    launches0 = _lib.LAUNCHES[0]
+    with Clocks(local) as clk:
+        barrier()
+        e0 = torch.cuda.Event(enable_timing=True)
+        e1 = torch.cuda.Event(enable_timing=True)
+        e0.record()
+        with contextlib.redirect_stdout(io.StringIO()):
+            for _ in range(args.steps):
+                model = WarpGBM(**params)
+                model._hist_events = []
+                model.fit(X, y)
+                hist_ms += sum(a.elapsed_time(b) for a, b in model._hist_events)
+                hist_bytes += hist_algorithmic_bytes(model, model._n_global // max(world, 1) if world > 1 else n,
+                                                     F, 1, CONFIG["num_bins"])
+        e1.record()
+        barrier()
+    launches = _lib.LAUNCHES[0] - launches0
+    t = e0.elapsed_time(e1) / args.steps
+    tt = torch.tensor([t], device=dev)
+    if world > 1:
+        dist.all_reduce(tt, op=dist.ReduceOp.MAX)
+    t = float(tt.item())
+    value = t / 1000.0 * 100.0 / args.trees
+    peak, peak_kind = peaks()
+    achieved = hist_bytes / (hist_ms / 1000.0) / 1e9 if hist_ms > 0 else None
+    nlaunch = len(model._hist_events) if model is not None else 0
+
+    e2e = None
+    if not args.no_e2e:
+        Xh = X.cpu().numpy()
+        yh = y.cpu().numpy()
+        barrier()
+        f0 = torch.cuda.Event(enable_timing=True)
+        f1 = torch.cuda.Event(enable_timing=True)
+        f0.record()
+        with contextlib.redirect_stdout(io.StringIO()):
+            for _ in range(args.steps):
+                WarpGBM(**params).fit(Xh, yh)
+        f1.record()
+        barrier()
+        te = f0.elapsed_time(f1) / args.steps
+        tt = torch.tensor([te], device=dev)
+        if world > 1:
+            dist.all_reduce(tt, op=dist.ReduceOp.MAX)
+        te = float(tt.item())
+        D = CONFIG["max_depth"]
+        d2h = args.trees * (((1 << (D + 1)) - 1) * 64 + ((1 << D) - 1) * 4 + F * 4)
+        e2e = {"value": round(te / 1000.0 * 100.0 / args.trees, 4), "unit": "s/100 trees",
+               "h2d_bytes_per_step": int(Xh.nbytes + yh.nbytes), "d2h_bytes_per_step": int(d2h)}
+
+    if rank == 0:
+        line = {
+            "metric": "train sec/100 trees @1M×1K", "value": round(value, 4), "unit": "s/100 trees",
+            "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": round(t, 3), "higher_is_better": False, "scaling": "weak",
+            "vs_baseline": None, "dtype": "f32 (int64 fixed-point histograms)",
+            "data": "synthetic (config 2 generator, torch seed 1234+rank)",
+            "config": {"workload": "config2: 1M x 1000 f32 regression, B=32, depth 5, 100 trees, lr 0.01",
+                       "rows_per_rank": n, "features": F, "trees": args.trees,
+                       "parallelism": f"row-shard dp{world}",
+                       "l2": "inputs > L2 (X 4 GB, bins 1 GB); no flush needed"},
+            "roofline": {"bound": "hbm", "kernel": "k_hist (wgb_level_hist)",
+                         "achieved": round(achieved, 1) if achieved else None, "peak": peak,
+                         "unit": "GB/s", "frac": round(achieved / peak, 4) if achieved else None,
+                         "peak_kind": peak_kind, "traffic": None,
+                         "launches_timed": nlaunch * args.steps,
+                         "avg_launch_ms": round(hist_ms / max(nlaunch * args.steps, 1), 4)},
+            "e2e": e2e,
+            "gpu_launches": launches,
+            "clocks": clk.summary(),
+        }
+        if world == 1 and not args.no_cpu:
+            # CPU leg on the same matrix; the bins it grows the sample tree on
+            # are the model's own (identical to the oracle's binning)
+            Xh = X.cpu().numpy()
+            yh = y.cpu().numpy()
+            with contextlib.redirect_stdout(io.StringIO()):
+                bd = model.bin_inference_data(X)
+            bins_h = bd[:, :F].cpu().numpy()
+            line["cpu_baseline"] = cpu_sample(Xh, yh, bins_h, model.bin_edges.cpu().numpy(), args.trees)
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

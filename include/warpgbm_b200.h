@@ -1,0 +1,222 @@
+/*
+ * warpgbm_b200.h -- C ABI of the B200-native WarpGBM tree-growing hot path.
+ *
+ * Library: warpgbm_b200/libwgb_b200.so (sm_100a).  All entry points are
+ * asynchronous on the CUDA stream they are given (cudaStream_t passed as
+ * void*; NULL = legacy default stream), take plain device pointers and
+ * sizes, and return 0 on success or a non-zero wgb status; wgb_last_error()
+ * returns the message of the last failure on the calling thread.
+ *
+ * Two groups of entry points:
+ *
+ * 1. Drop-in replacements for the reference's PyTorch extension
+ *    warpgbm.cuda.node_kernel (warpgbm/cuda/node_kernel.cpp:41-46).  Same
+ *    argument meaning and in-place semantics; they raise (return non-zero)
+ *    on bad sizes where the reference only printf's a launch error.
+ *
+ * 2. The level-wise tree engine that warpgbm_b200.core.WarpGBM drives: one
+ *    fused histogram build per tree level over all of that level's nodes,
+ *    one split search per level, an on-device stable partition, and no host
+ *    synchronisation inside a tree.  It replaces the depth-first recursion
+ *    of warpgbm/core.py:543-658 and 692-744.
+ */
+#ifndef WARPGBM_B200_H
+#define WARPGBM_B200_H
+
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* ---------------------------------------------------------------------- */
+/* status                                                                  */
+/* ---------------------------------------------------------------------- */
+#define WGB_OK 0
+#define WGB_ERR_ARG 1      /* invalid argument (size, pointer, range) */
+#define WGB_ERR_CUDA 2     /* a CUDA runtime call or kernel launch failed */
+#define WGB_ERR_ALLOC 3    /* device scratch allocation failed */
+
+const char *wgb_last_error(void);
+int wgb_version(void);
+/* sizeof(wgb_node), sizeof(wgb_ws): lets bindings check their struct layout */
+int32_t wgb_sizeof_node(void);
+int32_t wgb_sizeof_ws(void);
+
+/* ---------------------------------------------------------------------- */
+/* 1. reference-compatible operations                                       */
+/* ---------------------------------------------------------------------- */
+
+/* Replaces node_kernel.compute_histogram3 = launch_histogram_kernel_cuda_
+ * configurable (warpgbm/cuda/histogram_kernel.cu:63-104,
+ * node_kernel.cpp:16-26,42).  For every sample s in sample_indices[0..n) and
+ * feature position j < k with b = bin_indices[s*F_master +
+ * feature_indices[j]] in [0, num_bins):
+ *     grad_hist[era[s]][j][b] += residuals[s];  hess_hist[...] += 1.
+ * Accumulates into the caller's [num_eras][k][num_bins] fp32 buffers like
+ * the reference.  The sums are formed exactly (int64 fixed point on a
+ * power-of-two grid chosen from max|residual|), so the result is
+ * deterministic.  threads_per_block / rows_per_thread are validated
+ * (multiple of 32; 1..16) and otherwise ignored.  feature_indices must not
+ * repeat a feature.  Allocates its int64 scratch from the stream-ordered
+ * pool of the current device. */
+int wgb_compute_histogram3(const int8_t *bin_indices, int64_t num_rows,
+                           int64_t F_master, const float *residuals,
+                           const int32_t *sample_indices, int64_t n,
+                           const int32_t *feature_indices, int32_t k,
+                           const int32_t *era_indices, float *grad_hist,
+                           float *hess_hist, int32_t num_eras,
+                           int32_t num_bins, int32_t threads_per_block,
+                           int32_t rows_per_thread, void *stream);
+
+/* Replaces node_kernel.compute_split = launch_directional_split_kernel
+ * (warpgbm/cuda/best_split_kernel.cu:57-88, node_kernel.cpp:6-14,43).
+ * Per (era, feature): totals over all B bins, prefix over b < B-1;
+ * gain = GL^2/(HL+eps) + GR^2/(HR+eps) - GT^2/(HT+eps) and
+ * dir = (GL/(HL+eps) > GR/(HR+eps)) ? 1 : -1 where HL, HR >= min_child_samples,
+ * else 0 / 0 -- with one IEEE rounding per operation, bit-identical to the
+ * reference kernel.  Outputs [E][k][B-1].  min_split_gain is unused, as in the
+ * reference. */
+int wgb_compute_split(const float *G, const float *H, int32_t num_eras,
+                      int32_t k, int32_t num_bins, float min_split_gain,
+                      float min_child_samples, float eps, float *per_era_gain,
+                      float *per_era_direction, int32_t threads, void *stream);
+
+/* Replaces node_kernel.custom_cuda_binner = launch_bin_column_kernel
+ * (warpgbm/cuda/binner.cu:29-52, node_kernel.cpp:28-31,44):
+ * out[i] = number of leading edges with X[i] >= edge (NaN -> 0). */
+int wgb_custom_cuda_binner(const float *X, int64_t n, const float *bin_edges,
+                           int32_t num_edges, int8_t *bin_indices,
+                           void *stream);
+
+/* Replaces node_kernel.predict_forest = predict_with_forest
+ * (warpgbm/cuda/predict.cu:48-76, node_kernel.cpp:33-38,45).  tree_tensor is
+ * the flattened forest of warpgbm/core.py:1215-1252, [T][max_nodes][6] =
+ * (feature, split_bin, left_id, right_id, is_leaf, leaf_value).
+ * out[i] += learning_rate * leaf_t(i) for every tree t, summed in tree order
+ * (deterministic; the reference's atomics use any order). */
+int wgb_predict_forest(const int8_t *bin_indices, int64_t n, int64_t F,
+                       const float *tree_tensor, int32_t T, int32_t max_nodes,
+                       float learning_rate, float *out, void *stream);
+
+/* ---------------------------------------------------------------------- */
+/* 2. level-wise engine                                                    */
+/* ---------------------------------------------------------------------- */
+
+/* Binning of a row-major float32 matrix in one pass (replaces the per-column
+ * loop of warpgbm/core.py:527-538 and core.py:902-915).  X is [n][F] with
+ * row stride x_stride (elements); edges [F][num_bins-1]; out is int8
+ * [n][out_stride] (out_stride >= F; padding bytes are written as 0).
+ * Semantics of binner.cu:16-25 per element. */
+int wgb_bin_matrix(const float *X, int64_t n, int32_t F, int64_t x_stride,
+                   const float *edges, int32_t num_bins, int8_t *out,
+                   int64_t out_stride, void *stream);
+
+/* One node of one tree level (64 bytes).  Global quantities (summed over all
+ * ranks of a row-sharded job) and local ones (this rank's rows). */
+typedef struct wgb_node {
+    int64_t sumq;    /* global sum of quantised residuals of the node       */
+    int64_t count;   /* global row count                                    */
+    int64_t lsumq;   /* left-child sum (valid when fpos >= 0)               */
+    int64_t lcount;  /* left-child count                                    */
+    int32_t lstart;  /* local rows: positions [lstart, lstart+lcnt) of the  */
+    int32_t lcnt;    /*   level's row order                                 */
+    int32_t slot;    /* histogram slot                                      */
+    int32_t built;   /* 1: histogram built from rows; 0: parent - sibling   */
+    int32_t fpos;    /* chosen split: position in the tree's feature subset,
+                        -1 = leaf                                           */
+    int32_t bin;     /* chosen threshold bin (go left iff bin <= this)      */
+    int32_t child;   /* index of the left child at the next level (-1)      */
+    float leaf;      /* leaf value (mean residual) of the node              */
+} wgb_node;
+
+/* Device workspace of one fit on one rank.  The host allocates every buffer
+ * and fills the pointers; sizes in comments.  N = local rows, S = bins row
+ * stride, F = features, k = features per tree, E = eras, B = num_bins,
+ * D = max_depth, K = output columns (1, or classes).  Per-level node arrays
+ * are packed: level d occupies nodes[(1<<d)-1 .. (1<<(d+1))-2]. */
+typedef struct wgb_ws {
+    /* data (fixed for the fit) */
+    const int8_t *bins;      /* [N][S]                                       */
+    const int32_t *era;      /* [N] dense era id per row, or NULL if E == 1   */
+    const int32_t *root_order; /* [N] row ids sorted by era (stable)          */
+    const float *y;          /* [N] regression target (NULL: g given)        */
+    float *pred;             /* [N][K] running prediction                    */
+    float *g;                /* [N] residual of the current tree             */
+    int32_t *qg;             /* [N] quantised residual                        */
+    /* per tree */
+    const int32_t *feats;    /* [k] physical feature of each position         */
+    int32_t *kpos;           /* [F] position of each physical feature or -1   */
+    /* row order per level (ping-pong) */
+    int32_t *order[2];       /* [N]                                           */
+    int32_t *posnode[2];     /* [N] node index (within level) per position    */
+    uint8_t *flags;          /* [N]                                           */
+    int32_t *tile_cnt;       /* [ntiles]                                      */
+    int32_t *tile_off;       /* [ntiles]                                      */
+    int32_t *part;           /* [2^D][4] per-node partition scratch           */
+    /* histograms */
+    int64_t *hg;             /* [2^(D-1)][E][k][B+1] quantised grad sums      */
+    int32_t *hc;             /* [2^(D-1)][E][k][B+1] counts                   */
+    /* chunk work list of the histogram build */
+    int32_t *chunks;         /* [chunk_cap][4] = node, p0, p1, -              */
+    int32_t *nchunks;        /* [1]                                           */
+    /* split search */
+    int32_t *cand;           /* [2^(D-1)][ceil(k/128)][4] partial arg-max    */
+    float *era_gain;         /* [2^D - 1][E] per-era gain of chosen split     */
+    /* nodes and level sizes */
+    wgb_node *nodes;         /* [2^(D+1) - 1]                                 */
+    int32_t *nn;             /* [D+1] nodes per level                         */
+    int32_t *nact;           /* [D+1] local rows per level                    */
+    /* scalars of the current tree */
+    float *maxabs;           /* [1] max |g| (bit pattern compared as int)     */
+    int32_t *shift;          /* [1] s                                         */
+    int64_t *rootsum;        /* [1] sum of q over local rows                  */
+    /* sizes */
+    int64_t N, S;
+    int64_t N_global;
+    int32_t F, k, E, B, D, K;
+    int32_t cls;             /* output column updated by this tree            */
+    int32_t chunk_cap, ntiles, ncand_blk;
+    int32_t hist_ew;         /* eras per shared-memory window                 */
+    /* hyper-parameters (fp32 as the reference passes them) */
+    float mcw, eps, msg, lr, mean_factor;
+} wgb_ws;
+
+/* Tree start: g = y - pred[:, cls] (if y != NULL), max|g| into *maxabs
+ * (*maxabs must be 0 on entry; see wgb_tree_reset). */
+int wgb_tree_residual(const wgb_ws *ws, void *stream);
+/* Zero the per-tree scalars (maxabs, rootsum). */
+int wgb_tree_reset(const wgb_ws *ws, void *stream);
+/* Quantise g (shift from *maxabs, which must already be the global max),
+ * sum q over local rows into *rootsum. */
+int wgb_tree_quantize(const wgb_ws *ws, void *stream);
+/* Root record (needs the global *rootsum) and level counters. */
+int wgb_tree_root(const wgb_ws *ws, void *stream);
+/* Level d: chunk plan, zero of the built slots, histogram build of the
+ * built nodes from local rows.  Built slots of level d are the contiguous
+ * range returned by wgb_built_slots (an all-reduce over ranks goes there). */
+int wgb_level_hist(const wgb_ws *ws, int32_t d, void *stream);
+void wgb_built_slots(int32_t d, int32_t *first, int32_t *count);
+/* Level d: sibling = parent - built (in place), split search, per-era gains,
+ * child totals, next level's node records. */
+int wgb_level_split(const wgb_ws *ws, int32_t d, void *stream);
+/* Level d: stable partition of local rows into the next level's order; rows
+ * of nodes that became leaves get pred[:, cls] += lr * leaf. */
+int wgb_level_partition(const wgb_ws *ws, int32_t d, void *stream);
+/* Level D: every remaining row gets its leaf update. */
+int wgb_tree_finish(const wgb_ws *ws, void *stream);
+
+/* Forest prediction with trees packed by warpgbm_b200 (pre-order, 8 bytes per
+ * node: internal = {feature, bin | right_id << 8}, leaf = {-1, value bits}).
+ * out[i*K + class_of_tree(t)] += lr * leaf_t(i), trees in order t = 0..T-1,
+ * class_of_tree(t) = t % K.  tree_off[t] = first node of tree t. */
+int wgb_predict_packed(const int8_t *bins, int64_t n, int64_t S,
+                       const int32_t *nodes, const int32_t *tree_off,
+                       int32_t T, int32_t K, float lr, float *out,
+                       void *stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* WARPGBM_B200_H */

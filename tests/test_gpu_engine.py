@@ -1,0 +1,182 @@
+"""End-to-end parity of the level-wise engine (WarpGBM on the B200) against
+the CPU oracle in canonical mode (bit-exact: same quantised arithmetic) and
+against the reference's own outputs (tests/golden, within tolerance)."""
+import numpy as np
+import pytest
+import torch
+
+import oracle as O
+from conftest import load_golden
+from warpgbm_b200 import WarpGBM
+
+pytestmark = pytest.mark.gpu
+
+
+def _flat(model_or_forest, D, classification=False):
+    forest = model_or_forest.forest if hasattr(model_or_forest, "forest") else model_or_forest
+    trees = [t for r in forest if r for t in r] if classification else [t for t in forest if t]
+    return np.stack([O.flatten_tree(t, 2 ** (D + 1)) for t in trees])
+
+
+def _same(a, b):
+    return a.shape == b.shape and np.array_equal(np.nan_to_num(a, nan=-7.0), np.nan_to_num(b, nan=-7.0))
+
+
+def _oracle_for(model, params, X, y, era, k=None):
+    p = dict(params)
+    p.pop("random_state", None)
+    subs = None
+    if p.get("colsample_bytree", 1.0) < 1.0:
+        subs = model.feature_subsets_
+    hook = None
+    if p.get("objective", "regression") != "regression":
+        res = model._residuals
+        K = model.num_classes
+        hook = lambda i, c, r: res[i * K + c]  # noqa: E731
+    edges = None
+    if not np.issubdtype(X.dtype, np.integer):
+        edges = model.bin_edges.cpu().numpy()
+    return O.OracleGBM(mode="canonical", **p).fit(X, y, era_id=era, edges=edges,
+                                                   feature_subsets=subs, residual_hook=hook)
+
+
+@pytest.mark.parametrize("case", ["c1_regression", "era_des", "prebinned_colsample", "binning_edges"])
+def test_regression_bit_exact_vs_oracle_and_close_to_reference(cuda, case):
+    d, params = load_golden(case)
+    era = d["era"] if d["era"].size else None
+    m = WarpGBM(**params).fit(d["X"], d["y"], era_id=era)
+    o = _oracle_for(m, params, d["X"], d["y"], era)
+    D = params["max_depth"]
+    # bins and edges equal the reference's (same torch.quantile op + binner semantics)
+    assert np.array_equal(m.bin_edges.cpu().numpy(), d["edges"], equal_nan=True)
+    assert np.float32(m.base_prediction) == np.float32(o.base_prediction)
+    assert _same(_flat(m, D), o.flat_forest())
+    assert np.array_equal(m.per_era_feature_importance_, o.per_era_feature_importance_)
+    p = m.predict(d["X"])
+    assert np.array_equal(p, o.predict(d["X"]))
+    # against the reference run: same trees unless colsample drew other subsets
+    if params.get("colsample_bytree", 1.0) == 1.0:
+        assert _same(_flat(m, D)[..., :5], d["forest"][..., :5])
+        assert np.abs(p - d["pred"]).max() <= 1e-5 * np.abs(d["pred"]).max()
+
+
+@pytest.mark.parametrize("case", ["multiclass", "binary"])
+def test_classification_bit_exact_trees(cuda, case):
+    d, params = load_golden(case)
+    m = WarpGBM(**params)
+    m._record_residuals = True
+    m.fit(d["X"], d["y"])
+    o = _oracle_for(m, params, d["X"], d["y"], None)
+    D = params["max_depth"]
+    assert _same(_flat(m, D, True), o.flat_forest())
+    pg = m.predict_proba(d["X"])
+    assert np.abs(pg - o.predict_proba(d["X"])).max() < 1e-6
+    assert np.abs(pg.sum(axis=1) - 1).max() < 1e-5          # test_multiclass.py:76
+    # vs the reference (fp32-noise splits in pure nodes may differ, see oracle tests)
+    assert np.abs(pg - d["proba"]).max() < 2e-3
+    assert (m.predict(d["X"]) == d["labels"]).mean() > 0.99
+
+
+def test_eval_and_early_stopping_match_reference(cuda):
+    d, params = load_golden("eval_corr")
+    m = WarpGBM(**params)
+    m.fit(d["X"], d["y"], X_eval=d["X_pred"], y_eval=d["y_eval"], eval_every_n_trees=2,
+          early_stopping_rounds=3, eval_metric="corr")
+    assert len(m.eval_loss) == len(d["eval_loss"])
+    np.testing.assert_allclose(m.eval_loss, d["eval_loss"], rtol=0, atol=1e-5)
+    np.testing.assert_allclose(m.training_loss, d["training_loss"], rtol=1e-5)
+    assert np.abs(m.predict(d["X_pred"]) - d["pred"]).max() <= 1e-5 * np.abs(d["pred"]).max()
+
+
+def test_c4_like_era_des_prebinned_colsample(cuda):
+    """BASELINE config 3 in miniature: pre-binned {0..4}, many sorted eras,
+    colsample 0.5, DES on."""
+    rng = np.random.default_rng(3)
+    n, F, E = 60000, 100, 60
+    X = rng.integers(0, 5, (n, F)).astype(np.int8)
+    era = np.repeat(np.arange(E), n // E).astype(np.int32)
+    c = rng.standard_normal((E, 10))
+    c[:, :6] = np.abs(c[:, :6])
+    score = (X[:, :10] * c[era]).sum(1) + rng.standard_normal(n)
+    y = np.zeros(n, np.float32)
+    for e in range(E):
+        m_ = era == e
+        r = np.argsort(np.argsort(score[m_])) / (m_.sum() - 1)
+        y[m_] = np.round(r * 4) / 4
+    params = dict(num_bins=5, max_depth=6, n_estimators=6, learning_rate=0.01,
+                  colsample_bytree=0.5, random_state=0, min_child_weight=5)
+    m = WarpGBM(**params).fit(X, y, era_id=era)
+    o = _oracle_for(m, params, X, y, era)
+    assert _same(_flat(m, 6), o.flat_forest())
+    assert np.array_equal(m.per_era_feature_importance_, o.per_era_feature_importance_)
+    assert np.array_equal(m.predict(X), o.predict(X))
+
+
+def test_moderate_scale_bit_exact_and_deterministic(cuda):
+    rng = np.random.default_rng(9)
+    n, F = 200_000, 256
+    X = rng.standard_normal((n, F)).astype(np.float32)
+    w = rng.standard_normal(20)
+    y = (X[:, :20] @ w + 0.3 * np.sin(X[:, 20:30]).sum(1) + rng.normal(0, 0.5, n)).astype(np.float32)
+    params = dict(num_bins=32, max_depth=6, n_estimators=8, learning_rate=0.05)
+    m1 = WarpGBM(**params).fit(X, y)
+    m2 = WarpGBM(**params).fit(X, y)
+    assert _same(_flat(m1, 6), _flat(m2, 6))
+    p1 = m1.predict(X)
+    assert np.array_equal(p1, m2.predict(X))
+    o = _oracle_for(m1, params, X, y, None)
+    assert _same(_flat(m1, 6), o.flat_forest())
+    assert np.array_equal(p1, o.predict(X))
+
+
+@pytest.mark.parametrize("kind", ["depth1", "bins2", "bins127", "constant_y", "tiny", "negative_bins"])
+def test_edge_cases_bit_exact(cuda, kind):
+    rng = np.random.default_rng(1)
+    n, F = 3000, 9
+    X = rng.standard_normal((n, F)).astype(np.float32)
+    y = (X[:, 0] + 0.1 * rng.standard_normal(n)).astype(np.float32)
+    params = dict(num_bins=16, max_depth=3, n_estimators=3, learning_rate=0.5, min_child_weight=10)
+    if kind == "depth1":
+        params["max_depth"] = 1
+    elif kind == "bins2":
+        params["num_bins"] = 2
+    elif kind == "bins127":
+        params["num_bins"] = 127
+    elif kind == "constant_y":
+        y[:] = 2.5
+    elif kind == "tiny":
+        X, y = X[:15], y[:15]
+    elif kind == "negative_bins":
+        X = rng.integers(-3, 8, (n, F)).astype(np.int8)
+        params["num_bins"] = 8
+        y = (X[:, 0] * 0.5 + rng.standard_normal(n)).astype(np.float32)
+    m = WarpGBM(**params).fit(X, y)
+    o = _oracle_for(m, params, X, y, None)
+    assert _same(_flat(m, params["max_depth"]), o.flat_forest())
+    assert np.array_equal(m.predict(X), o.predict(X))
+
+
+def test_warm_start_and_save_load_are_exact(cuda, tmp_path):
+    rng = np.random.default_rng(4)
+    X = rng.standard_normal((5000, 12)).astype(np.float32)
+    y = (X[:, 0] * X[:, 1] + rng.standard_normal(5000) * 0.1).astype(np.float32)
+    full = WarpGBM(n_estimators=10, max_depth=4, num_bins=16).fit(X, y)
+    ws = WarpGBM(n_estimators=5, max_depth=4, num_bins=16, warm_start=True).fit(X, y)
+    ws.n_estimators = 10
+    ws.fit(X, y)
+    assert ws._trees_trained == 10
+    assert np.array_equal(full.predict(X), ws.predict(X))   # test_warm_start.py:55 asks 1e-3
+    path = tmp_path / "m.pkl"
+    full.save_model(str(path))
+    loaded = WarpGBM().load_model(str(path))
+    assert np.array_equal(loaded.predict(X), full.predict(X))
+
+
+def test_fit_from_device_tensors_equals_numpy(cuda):
+    rng = np.random.default_rng(8)
+    X = rng.standard_normal((20000, 40)).astype(np.float32)
+    y = (X[:, 3] - X[:, 7] + rng.standard_normal(20000)).astype(np.float32)
+    a = WarpGBM(n_estimators=4, max_depth=4, num_bins=32).fit(X, y)
+    b = WarpGBM(n_estimators=4, max_depth=4, num_bins=32).fit(torch.from_numpy(X).to(cuda),
+                                                               torch.from_numpy(y).to(cuda))
+    assert _same(_flat(a, 4), _flat(b, 4))

@@ -1,0 +1,161 @@
+"""Kernel-level parity: every C-ABI operation against the CPU oracle on the
+same seeded inputs.  Integer / index results bit-exact; fp32 results
+bit-exact where the arithmetic is the same, otherwise with the stated
+tolerance."""
+import numpy as np
+import pytest
+import torch
+
+import oracle as O
+from warpgbm_b200 import _lib, node_kernel
+from warpgbm_b200.core import bins_stride
+
+pytestmark = pytest.mark.gpu
+
+
+def _st():
+    return torch.cuda.current_stream().cuda_stream
+
+
+def _edges_for(X, B, dev):
+    Xd = torch.from_numpy(X).to(dev)
+    q = torch.linspace(0, 1, B + 1, device=dev, dtype=torch.float32)[1:-1]
+    return torch.quantile(Xd, q, dim=0).T.contiguous()
+
+
+@pytest.mark.parametrize("n,F,B", [(1000, 13, 32), (4097, 128, 7), (3000, 300, 127), (17, 1, 2)])
+def test_bin_matrix_matches_oracle(cuda, n, F, B):
+    rng = np.random.default_rng(n + F)
+    X = rng.standard_normal((n, F)).astype(np.float32)
+    X[rng.random((n, F)) < 0.01] = np.nan
+    if F > 2:
+        X[:, 1] = np.round(X[:, 1])          # ties
+        X[:, 2] = 3.0                        # constant
+    edges = _edges_for(X, B, cuda)
+    S = bins_stride(F)
+    out = torch.full((n, S), 99, dtype=torch.int8, device=cuda)
+    Xd = torch.from_numpy(X).to(cuda)
+    _lib.call("wgb_bin_matrix", Xd.data_ptr(), n, F, F, edges.data_ptr(), B, out.data_ptr(), S, _st())
+    got = out.cpu().numpy()
+    ref = O.bin_matrix(X, edges.cpu().numpy())
+    assert np.array_equal(got[:, :F], ref)
+    assert (got[:, F:] == 0).all()
+
+
+def test_torch_cuda_quantile_equals_oracle(cuda):
+    """Pins the oracle's quantile restatement (FMA lerp, linspace formula) to
+    torch.quantile on the B200 -- the op the reference calls at core.py:532."""
+    rng = np.random.default_rng(11)
+    for B in (2, 5, 10, 32, 127):
+        qd = torch.linspace(0, 1, B + 1, device=cuda, dtype=torch.float32)[1:-1]
+        assert np.array_equal(qd.cpu().numpy(), O.linspace_q(B))
+        for trial in range(20):
+            n = int(rng.integers(1, 20000))
+            col = rng.standard_normal(n).astype(np.float32) * float(rng.exponential(10))
+            if trial % 4 == 1:
+                col = np.round(col)
+            if trial % 4 == 2:
+                col[rng.random(n) < 0.05] = np.nan
+            ref = torch.quantile(torch.from_numpy(col).to(cuda), qd).cpu().numpy()
+            assert np.array_equal(O.quantile_edges(col, O.linspace_q(B)), ref, equal_nan=True)
+
+
+def test_custom_cuda_binner_matches_oracle(cuda):
+    rng = np.random.default_rng(5)
+    x = rng.standard_normal(10001).astype(np.float32)
+    x[::97] = np.nan
+    e = np.sort(rng.standard_normal(9)).astype(np.float32)
+    out = torch.empty(x.size, dtype=torch.int8, device=cuda)
+    node_kernel.custom_cuda_binner(torch.from_numpy(x).to(cuda), torch.from_numpy(e).to(cuda), out)
+    ref = O.bin_matrix(x[:, None], e[None, :])[:, 0]
+    assert np.array_equal(out.cpu().numpy(), ref)
+
+
+@pytest.mark.parametrize("E,k,B", [(1, 1000, 32), (4, 37, 5), (2, 9, 127), (3, 3, 2)])
+def test_compute_split_bit_exact(cuda, E, k, B):
+    rng = np.random.default_rng(E * k + B)
+    H = rng.integers(0, 80, (E, k, B)).astype(np.float32)
+    G = (rng.standard_normal((E, k, B)) * H * 0.37).astype(np.float32)
+    gain = torch.empty((E, k, B - 1), device=cuda)
+    d = torch.empty_like(gain)
+    node_kernel.compute_split(torch.from_numpy(G).to(cuda), torch.from_numpy(H).to(cuda), 0.0, 20,
+                              1e-6, gain, d)
+    rg, rd = O.split(G, H, 20, 1e-6)
+    assert np.array_equal(gain.cpu().numpy(), rg)
+    assert np.array_equal(d.cpu().numpy(), rd)
+
+
+@pytest.mark.parametrize("n,F,k,E,B,sorted_eras", [
+    (50000, 300, 200, 1, 32, True),
+    (20000, 61, 61, 3, 10, False),      # unaligned rows (F % 4 != 0), unsorted eras
+    (30000, 40, 20, 37, 5, True),
+    (777, 8, 8, 1, 2, True),
+    (0, 8, 8, 1, 4, True),
+])
+def test_compute_histogram3(cuda, n, F, k, E, B, sorted_eras):
+    rng = np.random.default_rng(n + F + E)
+    N = max(n, 1) + 5
+    bins = rng.integers(-1, B + 1, (N, F)).astype(np.int8)   # includes skipped bins
+    g = (rng.standard_normal(N) * 3).astype(np.float32)
+    era = rng.integers(0, E, N).astype(np.int32)
+    samples = rng.permutation(N)[:n].astype(np.int32)
+    if sorted_eras:
+        samples = samples[np.argsort(era[samples], kind="stable")]
+    feats = rng.permutation(F)[:k].astype(np.int32)
+    Gd = torch.zeros((E, k, B), device=cuda)
+    Hd = torch.zeros((E, k, B), device=cuda)
+    node_kernel.compute_histogram3(
+        torch.from_numpy(bins).to(cuda), torch.from_numpy(g).to(cuda),
+        torch.from_numpy(samples).to(cuda), torch.from_numpy(feats).to(cuda),
+        torch.from_numpy(era).to(cuda), Gd, Hd, B, 64, 4)
+    Gg, Hg = Gd.cpu().numpy(), Hd.cpu().numpy()
+    if n == 0:
+        assert not Gg.any() and not Hg.any()
+        return
+    # canonical: exact sums on the grid of max|g| over the sampled rows
+    s = O.quant_shift(float(np.abs(g[samples]).max()))
+    Gq, Cq = O.hist_q(bins, O.quantize(g, s), samples, feats, era, E, B)
+    Gf, Hf = O.dequant(Gq, Cq, s)
+    assert np.array_equal(Hg, Hf)
+    assert np.array_equal(Gg, Gf)
+    # reference semantics: fp32 sums, within 1e-5 of the bin's sum |g|
+    Gr, Hr = O.hist_ref(bins, g, samples, feats, era, E, B)
+    Ga, _ = O.hist_ref(bins, np.abs(g), samples, feats, era, E, B)
+    assert np.array_equal(Hg, Hr)
+    assert (np.abs(Gg - Gr) <= 1e-5 * Ga + 1e-30).all()
+
+
+def test_predict_forest_flat_matches_oracle(cuda):
+    rng = np.random.default_rng(2)
+    d = np.load("tests/golden/c1_regression.npz")
+    forest = d["forest"]
+    bins = d["bins"]
+    out = torch.full((bins.shape[0],), 0.25, device=cuda)
+    node_kernel.predict_forest(torch.from_numpy(bins).to(cuda), torch.from_numpy(forest).to(cuda), 0.1, out)
+    ref = np.full(bins.shape[0], 0.25, np.float32)
+    O.predict_flat(bins, forest, 0.1, ref)
+    assert np.array_equal(out.cpu().numpy(), ref)
+    assert rng is not None
+
+
+def test_root_histogram_full_width(cuda):
+    """A C2-shaped root histogram (1M rows x 1000 features, B=32) against the
+    oracle: exact integer sums, counts summing to the row count."""
+    rng = np.random.default_rng(42)
+    n, F, B = 1_000_000, 1000, 32
+    bins = rng.integers(0, B, (n, F), dtype=np.int8)
+    g = rng.standard_normal(n).astype(np.float32)
+    samples = np.arange(n, dtype=np.int32)
+    feats = np.arange(F, dtype=np.int32)
+    era = np.zeros(n, np.int32)
+    Gd = torch.zeros((1, F, B), device=cuda)
+    Hd = torch.zeros((1, F, B), device=cuda)
+    node_kernel.compute_histogram3(torch.from_numpy(bins).to(cuda), torch.from_numpy(g).to(cuda),
+                                   torch.from_numpy(samples).to(cuda), torch.from_numpy(feats).to(cuda),
+                                   torch.from_numpy(era).to(cuda), Gd, Hd, B)
+    s = O.quant_shift(float(np.abs(g).max()))
+    Gq, Cq = O.hist_q(bins, O.quantize(g, s), samples, feats, era, 1, B)
+    Gf, Hf = O.dequant(Gq, Cq, s)
+    assert np.array_equal(Hd.cpu().numpy(), Hf)
+    assert np.array_equal(Gd.cpu().numpy(), Gf)
+    assert (Hf.sum(axis=2) == n).all()

@@ -1,0 +1,985 @@
+"""``WarpGBM`` -- the reference's sklearn-style estimator on the B200 engine.
+
+Host mirror of quantverse/warpgbm v2.2.0 ``warpgbm/core.py``: same
+constructor, ``fit`` / ``predict`` / ``predict_proba`` / importance / save /
+load API and the same Directional Era Splitting semantics.  The compute runs
+in libwgb_b200.so (include/warpgbm_b200.h):
+
+* binning: one ``wgb_bin_matrix`` launch over the whole matrix (edges from
+  ``torch.quantile`` on the device, exactly the op core.py:529-534 calls);
+* trees: level-wise, without host synchronisation inside a tree --
+  histogram of every node of a level in one launch, split search, on-device
+  partition and leaf updates;
+* prediction: ``wgb_predict_packed``, all trees (and all classes) in one
+  launch, summed in tree order.
+
+Histograms are exact integer sums of residuals quantised per tree to a
+power-of-two grid (q = rint(g * 2^s), s = 29 - exponent(max|g|)), so every
+decision is independent of summation order, run to run and across GPU
+counts.  With ``distributed=True`` inside an initialised torch.distributed
+process group, every rank passes its own row shard to ``fit``; histograms
+and the few global scalars are summed over ranks (NCCL over NVLink), and all
+ranks grow identical trees.
+"""
+from __future__ import annotations
+
+import math
+import pickle
+from typing import List, Optional
+
+import numpy as np
+import torch
+from sklearn.base import BaseEstimator, RegressorMixin
+from sklearn.preprocessing import LabelEncoder
+
+from . import _lib
+from .metrics import accuracy_torch, log_loss_torch, rmsle_torch, softmax
+
+HIST_FT = 128          # features per histogram tile (csrc/wgb_common.cuh)
+HIST_R = 1024          # rows per histogram chunk
+PART_TILE = 2048       # positions per partition tile
+SPLIT_THREADS = 128
+
+
+def _round_up(x, m):
+    return (x + m - 1) // m * m
+
+
+def hist_ew_for(B: int) -> int:
+    """Eras per shared-memory window of the histogram kernel (<= 48 KB)."""
+    return max(1, min(8, (48 * 1024) // ((B + 1) * HIST_FT * 8)))
+
+
+def bins_stride(F: int) -> int:
+    """Row stride of the device bin matrix: features padded to 32 bytes."""
+    return _round_up(max(F, 1), 32)
+
+
+def cuda_mean_factor(E: int, k: int, nb: int) -> float:
+    """torch's CUDA mean = sum * float(outputs)/float(numel) (ATen mean kernel)."""
+    return float(np.float32(np.float32(k * nb) / np.float32(E * k * nb)))
+
+
+# ---------------------------------------------------------------------------
+# multi-GPU plumbing
+# ---------------------------------------------------------------------------
+
+class _Comm:
+    """torch.distributed collectives for the row-sharded fit (no-ops when
+    running on one rank)."""
+
+    def __init__(self, enabled: bool):
+        import torch.distributed as dist
+        self.dist = dist
+        self.on = bool(enabled) and dist.is_available() and dist.is_initialized() \
+            and dist.get_world_size() > 1
+        self.world = dist.get_world_size() if self.on else 1
+        self.rank = dist.get_rank() if self.on else 0
+
+    def max_(self, t):
+        if self.on:
+            self.dist.all_reduce(t, op=self.dist.ReduceOp.MAX)
+        return t
+
+    def sum_(self, t):
+        if self.on:
+            self.dist.all_reduce(t, op=self.dist.ReduceOp.SUM)
+        return t
+
+    def bcast_(self, t, src=0):
+        if self.on:
+            self.dist.broadcast(t, src)
+        return t
+
+    def gather_var(self, t: torch.Tensor) -> List[torch.Tensor]:
+        """all_gather of 1-D tensors of different lengths."""
+        if not self.on:
+            return [t]
+        n = torch.tensor([t.numel()], dtype=torch.int64, device=t.device)
+        ns = [torch.zeros_like(n) for _ in range(self.world)]
+        self.dist.all_gather(ns, n)
+        ns = [int(x.item()) for x in ns]
+        m = max(ns)
+        pad = torch.zeros(m, dtype=t.dtype, device=t.device)
+        pad[: t.numel()] = t
+        outs = [torch.empty_like(pad) for _ in range(self.world)]
+        self.dist.all_gather(outs, pad)
+        return [o[:c] for o, c in zip(outs, ns)]
+
+
+def global_unique_eras(era: torch.Tensor, comm: _Comm):
+    """torch.unique(era, return_inverse=True) over the union of all ranks'
+    eras (core.py:540): sorted unique ids and the dense id of each local row."""
+    local = torch.unique(era)
+    uniq = torch.unique(torch.cat(comm.gather_var(local)))
+    inv = torch.searchsorted(uniq, era).to(torch.int32)
+    return uniq, inv
+
+
+def exact_mean(y: torch.Tensor, comm: _Comm) -> float:
+    """Base prediction: mean of y from an exact fixed-point sum, identical at
+    every GPU count.  t = 62 - L - e (n < 2^L, max|y| < 2^e);
+    mean = float32(float64(sum rint(y * 2^t)) * 2^-t / n)."""
+    n = torch.tensor([y.numel()], dtype=torch.int64, device=y.device)
+    comm.sum_(n)
+    n = int(n.item())
+    m = torch.zeros(1, dtype=torch.float32, device=y.device)
+    if y.numel():
+        m[0] = y.abs().max()
+    comm.max_(m)
+    m = float(m.item())
+    if n == 0:
+        raise ValueError("cannot fit on zero rows")
+    if not math.isfinite(m):
+        raise ValueError("y contains NaN or infinite values")
+    if m == 0.0:
+        return 0.0
+    L = n.bit_length()
+    e = math.frexp(m)[1]
+    t = 62 - L - e
+    q = torch.round(y.double() * math.ldexp(1.0, t)).to(torch.int64).sum().reshape(1)
+    comm.sum_(q)
+    return float(np.float32(math.ldexp(float(int(q.item())), -t) / float(n)))
+
+
+def sharded_quantile_edges(Xd: torch.Tensor, q: torch.Tensor, comm: _Comm) -> torch.Tensor:
+    """Quantile edges [F, B-1] of every column of the row-sharded float
+    matrix, bit-identical to torch.quantile over the full column
+    (core.py:529-534): columns are exchanged so each rank holds complete
+    columns of a feature slice, then the edges are all-gathered."""
+    F = Xd.shape[1]
+    if not comm.on:
+        return _quantile_columns(Xd, q)
+    W = comm.world
+    per = (F + W - 1) // W
+    Fp = per * W
+    Xp = torch.zeros((Xd.shape[0], Fp), dtype=Xd.dtype, device=Xd.device)
+    Xp[:, :F] = Xd
+    # send block w = my rows of columns [w*per, (w+1)*per)
+    send = Xp.reshape(Xd.shape[0], W, per).permute(1, 0, 2).contiguous()
+    ns = comm.gather_var(torch.tensor([Xd.shape[0]], dtype=torch.int64, device=Xd.device))
+    counts = [int(c.item()) for c in ns]
+    recv = torch.empty((sum(counts), per), dtype=Xd.dtype, device=Xd.device)
+    comm.dist.all_to_all_single(recv, send.reshape(-1, per),
+                                output_split_sizes=counts,
+                                input_split_sizes=[Xd.shape[0]] * W)
+    mine = _quantile_columns(recv, q)                      # [per, B-1]
+    outs = [torch.empty_like(mine) for _ in range(W)]
+    comm.dist.all_gather(outs, mine)
+    return torch.cat(outs, 0)[:F].contiguous()
+
+
+def _quantile_columns(Xd: torch.Tensor, q: torch.Tensor, chunk_elems: int = 1 << 27):
+    """torch.quantile(X[:, f], q) for every column, in column chunks."""
+    n, F = Xd.shape
+    if n > (1 << 24):
+        raise ValueError("quantile() input tensor is too large")  # torch's own limit
+    out = torch.empty((F, q.numel()), dtype=torch.float32, device=Xd.device)
+    step = max(1, chunk_elems // max(n, 1))
+    for c0 in range(0, F, step):
+        c1 = min(F, c0 + step)
+        out[c0:c1] = torch.quantile(Xd[:, c0:c1], q, dim=0).T
+    return out
+
+
+def _to_dev(a, dev, dtype=None):
+    """numpy array or tensor -> contiguous tensor on dev (pinned staging for
+    large host arrays so the copy runs at full PCIe bandwidth)."""
+    if torch.is_tensor(a):
+        t = a
+    else:
+        t = torch.from_numpy(np.ascontiguousarray(a))
+    if dtype is not None and t.dtype != dtype and t.device.type == "cpu" and t.element_size() != \
+            torch.empty((), dtype=dtype).element_size():
+        t = t.to(dtype)
+    t = t.to(dev, non_blocking=False)
+    if dtype is not None and t.dtype != dtype:
+        t = t.to(dtype)
+    return t.contiguous()
+
+
+# ---------------------------------------------------------------------------
+# forest packing
+# ---------------------------------------------------------------------------
+
+def pack_trees(trees) -> (np.ndarray, np.ndarray):
+    """Pre-order packing for wgb_predict_packed: internal node
+    (feature, bin | right_id << 8), leaf (-1, float bits)."""
+    nodes, offs = [], [0]
+    for tree in trees:
+        buf = []
+
+        def walk(nd):
+            i = len(buf)
+            buf.append(None)
+            if "leaf_value" in nd:
+                bits = np.array([nd["leaf_value"]], np.float32).view(np.int32)[0]
+                buf[i] = (-1, int(bits))
+            else:
+                walk(nd["left"])
+                right = len(buf)
+                walk(nd["right"])
+                buf[i] = (int(nd["feature"]), (int(nd["bin"]) & 0xFF) | (right << 8))
+        walk(tree)
+        nodes.extend(buf)
+        offs.append(len(nodes))
+    arr = np.array(nodes, np.int32).reshape(-1, 2) if nodes else np.zeros((0, 2), np.int32)
+    return arr, np.array(offs, np.int32)
+
+
+class WarpGBM(BaseEstimator, RegressorMixin):
+    def __init__(
+        self,
+        objective="regression",
+        num_bins=10,
+        max_depth=3,
+        learning_rate=0.1,
+        n_estimators=100,
+        min_child_weight=20,
+        min_split_gain=0.0,
+        threads_per_block=64,
+        rows_per_thread=4,
+        L2_reg=1e-6,
+        device="cuda",
+        colsample_bytree=1.0,
+        random_state=None,
+        warm_start=False,
+        distributed=False,
+    ):
+        self._validate_hyperparams(
+            objective=objective, num_bins=num_bins, max_depth=max_depth,
+            learning_rate=learning_rate, n_estimators=n_estimators,
+            min_child_weight=min_child_weight, min_split_gain=min_split_gain,
+            threads_per_block=threads_per_block, rows_per_thread=rows_per_thread,
+            L2_reg=L2_reg, colsample_bytree=colsample_bytree,
+        )
+        self.objective = objective
+        self.num_bins = num_bins
+        self.max_depth = max_depth
+        self.learning_rate = learning_rate
+        self.n_estimators = n_estimators
+        self.min_child_weight = min_child_weight
+        self.min_split_gain = min_split_gain
+        self.threads_per_block = threads_per_block
+        self.rows_per_thread = rows_per_thread
+        self.L2_reg = L2_reg
+        self.device = device
+        self.colsample_bytree = colsample_bytree
+        self.random_state = random_state
+        self.warm_start = warm_start
+        self.distributed = distributed
+        self.forest = [{} for _ in range(self.n_estimators)]
+        self.bin_edges = None
+        self.base_prediction = None
+        self.unique_eras = None
+        self.num_classes = None
+        self.classes_ = None
+        self.num_features = None
+        self.num_samples = None
+        self.label_encoder = None
+        self.feature_importance_ = None
+        self.per_era_feature_importance_ = None
+        self.training_loss = []
+        self.eval_loss = []
+        self._is_fitted = False
+        self._trees_trained = 0
+        self._packed = None
+
+    # ------------------------------------------------------------------
+    # validation (core.py:83-143, 216-291)
+    # ------------------------------------------------------------------
+    def _validate_hyperparams(self, **kw):
+        if kw["objective"] not in ["regression", "multiclass", "binary"]:
+            raise ValueError(
+                f"objective must be 'regression', 'binary', or 'multiclass', got {kw['objective']}.")
+        for p in ["num_bins", "max_depth", "n_estimators", "min_child_weight",
+                  "threads_per_block", "rows_per_thread"]:
+            if not isinstance(kw[p], int):
+                raise TypeError(f"{p} must be an integer, got {type(kw[p])}.")
+        for p in ["learning_rate", "min_split_gain", "L2_reg", "colsample_bytree"]:
+            if not isinstance(kw[p], (float, int)):
+                raise TypeError(f"{p} must be a float, got {type(kw[p])}.")
+        if not (2 <= kw["num_bins"] <= 127):
+            raise ValueError("num_bins must be between 2 and 127 inclusive.")
+        if kw["max_depth"] < 1:
+            raise ValueError("max_depth must be at least 1.")
+        if not (0.0 < kw["learning_rate"] <= 1.0):
+            raise ValueError("learning_rate must be in (0.0, 1.0].")
+        if kw["n_estimators"] <= 0:
+            raise ValueError("n_estimators must be positive.")
+        if kw["min_child_weight"] < 1:
+            raise ValueError("min_child_weight must be a positive integer.")
+        if kw["min_split_gain"] < 0:
+            raise ValueError("min_split_gain must be non-negative.")
+        if kw["threads_per_block"] <= 0 or kw["threads_per_block"] % 32 != 0:
+            raise ValueError("threads_per_block should be a positive multiple of 32 (warp size).")
+        if not (1 <= kw["rows_per_thread"] <= 16):
+            raise ValueError("rows_per_thread must be positive between 1 and 16 inclusive.")
+        if kw["L2_reg"] < 0:
+            raise ValueError("L2_reg must be non-negative.")
+        if kw["colsample_bytree"] <= 0 or kw["colsample_bytree"] > 1:
+            raise ValueError(
+                f"Invalid colsample_bytree: {kw['colsample_bytree']}. Must be a float value > 0 and <= 1.")
+
+    def validate_fit_params(self, X, y, era_id, X_eval, y_eval, eval_every_n_trees,
+                            early_stopping_rounds, eval_metric):
+        # numpy arrays as in the reference; CUDA tensors are also accepted
+        # (data already resident on the device skips the host->device copy)
+        arr = (np.ndarray, torch.Tensor)
+        if not isinstance(X, arr) or not isinstance(y, arr):
+            raise TypeError("X and y must be numpy arrays.")
+        if X.ndim != 2:
+            raise ValueError(f"X must be 2-dimensional, got shape {X.shape}")
+        if y.ndim != 1:
+            raise ValueError(f"y must be 1-dimensional, got shape {y.shape}")
+        if X.shape[0] != y.shape[0]:
+            raise ValueError(
+                f"X and y must have the same number of rows. Got {X.shape[0]} and {y.shape[0]}.")
+        if era_id is not None:
+            if not isinstance(era_id, arr):
+                raise TypeError("era_id must be a numpy array.")
+            if era_id.ndim != 1:
+                raise ValueError(f"era_id must be 1-dimensional, got shape {era_id.shape}")
+            if len(era_id) != len(y):
+                raise ValueError(
+                    f"era_id must have same length as y. Got {len(era_id)} and {len(y)}.")
+        if any(a is not None for a in (X_eval, y_eval, eval_every_n_trees)):
+            if X_eval is None or y_eval is None or eval_every_n_trees is None:
+                raise ValueError(
+                    "If using eval set, X_eval, y_eval, and eval_every_n_trees must all be defined.")
+            if not isinstance(X_eval, arr) or not isinstance(y_eval, arr):
+                raise TypeError("X_eval and y_eval must be numpy arrays.")
+            if X_eval.ndim != 2:
+                raise ValueError(f"X_eval must be 2-dimensional, got shape {X_eval.shape}")
+            if y_eval.ndim != 1:
+                raise ValueError(f"y_eval must be 1-dimensional, got shape {y_eval.shape}")
+            if X_eval.shape[0] != y_eval.shape[0]:
+                raise ValueError(
+                    f"X_eval and y_eval must have same number of rows. Got {X_eval.shape[0]} and {y_eval.shape[0]}.")
+            if not isinstance(eval_every_n_trees, int) or eval_every_n_trees <= 0:
+                raise ValueError(
+                    f"eval_every_n_trees must be a positive integer, got {eval_every_n_trees}.")
+            if early_stopping_rounds is not None:
+                if not isinstance(early_stopping_rounds, int) or early_stopping_rounds <= 0:
+                    raise ValueError(
+                        f"early_stopping_rounds must be a positive integer, got {early_stopping_rounds}.")
+            else:
+                early_stopping_rounds = self.n_estimators + 1
+            valid = ["mse", "corr", "rmsle", "logloss", "accuracy"]
+            if eval_metric not in valid:
+                raise ValueError(f"Invalid eval_metric: {eval_metric}. Choose from {valid}.")
+        return early_stopping_rounds
+
+    # ------------------------------------------------------------------
+    # fit (core.py:293-485)
+    # ------------------------------------------------------------------
+    def fit(self, X, y, era_id=None, X_eval=None, y_eval=None, eval_every_n_trees=None,
+            early_stopping_rounds=None, eval_metric="mse"):
+        early_stopping_rounds = self.validate_fit_params(
+            X, y, era_id, X_eval, y_eval, eval_every_n_trees, early_stopping_rounds, eval_metric)
+        self._comm = _Comm(self.distributed)
+        if self.random_state is not None:
+            torch.manual_seed(self.random_state)
+            np.random.seed(self.random_state)
+            if torch.cuda.is_available():
+                torch.cuda.manual_seed(self.random_state)
+                torch.cuda.manual_seed_all(self.random_state)
+        if not self.warm_start or not self._is_fitted:
+            self._is_fitted = False
+            self._trees_trained = 0
+            self.forest = [{} for _ in range(self.n_estimators)] if self.objective == "regression" else []
+            self.training_loss = []
+            self.eval_loss = []
+            self._packed = None
+        else:
+            if X.shape[1] != self.num_features:
+                raise ValueError(
+                    f"X has {X.shape[1]} features, but model was trained with {self.num_features} features.")
+            if self._trees_trained >= self.n_estimators:
+                print(f"Model already has {self._trees_trained} trees (n_estimators={self.n_estimators}). "
+                      "No additional training needed.")
+                return self
+        if era_id is None:
+            era_id = np.ones(X.shape[0], dtype="int32")
+        if self.objective in ("multiclass", "binary") and torch.is_tensor(y):
+            y = y.cpu().numpy()
+        self._dev = torch.device(self.device if str(self.device).startswith("cuda") else "cuda")
+        if self._dev.index is None:
+            self._dev = torch.device("cuda", torch.cuda.current_device())
+        _lib.lib()  # fail loudly before any work if the CUDA library is missing
+        with torch.cuda.device(self._dev):
+            if self.objective in ("multiclass", "binary"):
+                if not self.warm_start or not self._is_fitted:
+                    self.label_encoder = LabelEncoder()
+                    y_enc = self.label_encoder.fit_transform(y)
+                    self.classes_ = self.label_encoder.classes_
+                    self.num_classes = len(self.classes_)
+                else:
+                    y_enc = self.label_encoder.transform(y)
+                if self.objective == "binary" and self.num_classes != 2:
+                    raise ValueError(f"binary objective requires exactly 2 classes, got {self.num_classes}")
+                if self.objective == "multiclass" and self.num_classes < 2:
+                    raise ValueError(f"multiclass objective requires at least 2 classes, got {self.num_classes}")
+                return self._fit(X, y_enc, era_id, X_eval, y_eval, eval_every_n_trees,
+                                 early_stopping_rounds, eval_metric, classification=True)
+            return self._fit(X, y, era_id, X_eval, y_eval, eval_every_n_trees,
+                             early_stopping_rounds, eval_metric, classification=False)
+
+    # ------------------------------------------------------------------
+    def _upload_bins(self, X_np, fit: bool):
+        """core.py:487-541 / 934-955: pre-binned integer input is copied,
+        float input is binned with quantile edges (computed at fit)."""
+        dev = self._dev
+        B = self.num_bins
+        n, F = X_np.shape
+        S = bins_stride(F)
+        if torch.is_tensor(X_np):
+            is_int = not X_np.is_floating_point()
+        else:
+            is_int = np.issubdtype(X_np.dtype, np.integer)
+        if is_int and (fit or F == self.num_features):
+            Xi = _to_dev(X_np, dev)
+            mx = torch.full((F,), -(2 ** 62), dtype=torch.int64, device=dev)
+            if n:
+                mx = Xi.amax(dim=0).to(torch.int64)
+            if fit:
+                self._comm.max_(mx)
+            if bool((mx < B).all().item()):
+                print("Detected pre-binned integer input — skipping quantile binning." if fit
+                      else "Detected pre-binned input at predict-time — skipping binning.")
+                bins = torch.zeros((n, S), dtype=torch.int8, device=dev)
+                bins[:, :F] = Xi.to(torch.int8)
+                if fit:
+                    self.bin_edges = torch.arange(1, B, dtype=torch.float32, device=dev).repeat(F, 1)
+                return bins, True
+            Xd = Xi.to(torch.float32)
+        else:
+            Xd = _to_dev(X_np, dev, torch.float32)
+        if fit:
+            print("quantile binning.")
+            q = torch.linspace(0, 1, B + 1, device=dev, dtype=torch.float32)[1:-1]
+            self.bin_edges = sharded_quantile_edges(Xd, q, self._comm)
+        bins = torch.empty((n, S), dtype=torch.int8, device=dev)
+        _lib.call("wgb_bin_matrix", Xd.data_ptr(), n, F, F, self.bin_edges.data_ptr(), B,
+                  bins.data_ptr(), S, torch.cuda.current_stream().cuda_stream)
+        return bins, False
+
+    def _alloc_ws(self, N, F, k, E, K):
+        dev = self._dev
+        B, D = self.num_bins, self.max_depth
+        S = bins_stride(F)
+        nslots = 1 << (D - 1)
+        se = E * k * (B + 1)
+        hist_bytes = nslots * se * 12
+        free, _ = torch.cuda.mem_get_info(dev)
+        if hist_bytes > 0.6 * free:
+            raise MemoryError(
+                f"level-wise histograms need {hist_bytes / 2**30:.1f} GiB "
+                f"({nslots} slots x {E} eras x {k} features x {B + 1} bins); "
+                f"only {free / 2**30:.1f} GiB free -- reduce max_depth or features")
+        i32 = dict(dtype=torch.int32, device=dev)
+        t = {}
+        t["order0"] = torch.empty(max(N, 1), **i32)
+        t["order1"] = torch.empty(max(N, 1), **i32)
+        t["posnode0"] = torch.empty(max(N, 1), **i32)
+        t["posnode1"] = torch.empty(max(N, 1), **i32)
+        t["flags"] = torch.empty(max(N, 1), dtype=torch.uint8, device=dev)
+        ntiles = max(1, (N + PART_TILE - 1) // PART_TILE)
+        t["tile_cnt"] = torch.empty(ntiles, **i32)
+        t["tile_off"] = torch.empty(ntiles + 1, **i32)
+        t["part"] = torch.empty((max(nslots, 1), 4), **i32)
+        t["hg"] = torch.empty(nslots * se, dtype=torch.int64, device=dev)
+        t["hc"] = torch.empty(nslots * se, **i32)
+        chunk_cap = (N + HIST_R - 1) // HIST_R + nslots
+        t["chunks"] = torch.empty((max(chunk_cap, 1), 4), **i32)
+        ncand = (k + SPLIT_THREADS - 1) // SPLIT_THREADS
+        t["cand"] = torch.empty((nslots, ncand, 4), **i32)
+        t["era_gain"] = torch.zeros(((1 << D) - 1) * E, dtype=torch.float32, device=dev)
+        t["nodes"] = torch.zeros(((1 << (D + 1)) - 1) * 64, dtype=torch.uint8, device=dev)
+        t["nn"] = torch.zeros(D + 1, **i32)
+        t["nact"] = torch.zeros(D + 1, **i32)
+        t["nchunks"] = torch.zeros(1, **i32)
+        t["shift"] = torch.zeros(1, **i32)
+        t["maxabs"] = torch.zeros(1, dtype=torch.float32, device=dev)
+        t["rootsum"] = torch.zeros(1, dtype=torch.int64, device=dev)
+        t["g"] = torch.empty(max(N, 1), dtype=torch.float32, device=dev)
+        t["qg"] = torch.empty(max(N, 1), **i32)
+        t["feats"] = torch.empty(k, **i32)
+        t["kpos"] = torch.empty(F, **i32)
+        self._t = t
+        ws = _lib.WgbWs()
+        ws.order[0], ws.order[1] = t["order0"].data_ptr(), t["order1"].data_ptr()
+        ws.posnode[0], ws.posnode[1] = t["posnode0"].data_ptr(), t["posnode1"].data_ptr()
+        for name in ("flags", "tile_cnt", "tile_off", "part", "hg", "hc", "chunks", "cand",
+                     "era_gain", "nodes", "rootsum", "g", "qg", "feats", "kpos", "nn", "nact",
+                     "nchunks", "shift", "maxabs"):
+            setattr(ws, name, t[name].data_ptr())
+        ws.N, ws.S, ws.F, ws.k, ws.E, ws.B, ws.D, ws.K = N, S, F, k, E, B, D, K
+        ws.chunk_cap, ws.ntiles, ws.ncand_blk = max(chunk_cap, 1), ntiles, ncand
+        ws.hist_ew = hist_ew_for(B)
+        ws.mcw = float(np.float32(self.min_child_weight))
+        ws.eps = float(np.float32(self.L2_reg))
+        ws.msg = float(np.float32(self.min_split_gain))
+        ws.lr = float(np.float32(self.learning_rate))
+        ws.mean_factor = cuda_mean_factor(E, k, B - 1)
+        self._ws = ws
+        return ws
+
+    def _fit(self, X, y, era_id, X_eval, y_eval, every, esr, eval_metric, classification):
+        comm, dev = self._comm, self._dev
+        st = lambda: torch.cuda.current_stream().cuda_stream  # noqa: E731
+        with torch.no_grad():
+            self.num_samples, self.num_features = X.shape
+            N, F = X.shape
+            bins, _ = self._upload_bins(X, fit=True)
+            era_d = _to_dev(era_id, dev)
+            self.unique_eras, era_dense = global_unique_eras(era_d, comm)
+            self.num_eras = E = int(self.unique_eras.numel())
+            K = self.num_classes if classification else 1
+            k = max(1, int(self.colsample_bytree * F)) if self.colsample_bytree < 1.0 else F
+            nglob = torch.tensor([N], dtype=torch.int64, device=dev)
+            comm.sum_(nglob)
+            self._n_global = int(nglob.item())
+            if E > 1:
+                root_order = torch.sort(era_dense, stable=True).indices.to(torch.int32)
+            else:
+                root_order = torch.arange(N, dtype=torch.int32, device=dev)
+            ws = self._alloc_ws(N, F, k, E, K)
+            ws.bins, ws.root_order = bins.data_ptr(), root_order.data_ptr()
+            ws.era = era_dense.data_ptr() if E > 1 else None
+            ws.N_global = self._n_global
+            keep = [bins, root_order, era_dense]
+
+            resume = self.warm_start and self._is_fitted and self._trees_trained > 0
+            if classification:
+                Yl = _to_dev(y, dev, torch.int32)
+                pred = torch.zeros((N, K), dtype=torch.float32, device=dev)
+                # core.py:449-456: prior_k = mean(Y == k) as torch's CUDA mean
+                # (count * float(1/n)), from global counts, then log on device
+                cnts = torch.stack([(Yl == c).sum() for c in range(K)]).to(torch.int64)
+                comm.sum_(cnts)
+                inv_n = np.float32(np.float32(1.0) / np.float32(self._n_global))
+                for c, cnt in enumerate(cnts.tolist()):
+                    prior = np.float32(np.float32(cnt) * inv_n)
+                    if prior > 0:
+                        pred[:, c] = torch.log(torch.tensor(prior, dtype=torch.float32, device=dev) + 1e-10)
+                ws.y = None
+                self.Y_gpu = Yl
+            else:
+                Yf = _to_dev(y, dev, torch.float32)
+                if not resume:
+                    self.base_prediction = exact_mean(Yf, comm)
+                pred = torch.zeros((N, 1), dtype=torch.float32, device=dev) + np.float32(self.base_prediction)
+                ws.y = Yf.data_ptr()
+                self.Y_gpu = Yf
+                keep.append(Yf)
+            if resume:
+                self._ensure_packed()
+                self._predict_into(bins, pred, 0, self._trees_trained)
+            ws.pred = pred.data_ptr()
+            self._pred = pred
+            keep.append(pred)
+            self._keep = keep
+
+            if X_eval is not None:
+                self._eval_bins, _ = self._upload_bins(X_eval, fit=False)
+                if classification:
+                    ye = y_eval.cpu().numpy() if torch.is_tensor(y_eval) else y_eval
+                    self._Y_eval = _to_dev(self.label_encoder.transform(ye), dev, torch.int32)
+                    self.eval_metric = eval_metric if eval_metric != "mse" else "logloss"
+                    self._eval_pred = self._init_proba_logits(self._eval_bins.shape[0])
+                else:
+                    self._Y_eval = _to_dev(y_eval, dev, torch.float32)
+                    self.eval_metric = eval_metric
+                    self._eval_pred = torch.zeros(self._eval_bins.shape[0], 1, dtype=torch.float32,
+                                                  device=dev) + np.float32(self.base_prediction)
+                self._eval_upto = 0
+                self.eval_every_n_trees, self.early_stopping_rounds = every, esr
+            else:
+                self._eval_bins = None
+                self.eval_every_n_trees = self.early_stopping_rounds = None
+
+            if not self._is_fitted or not self.warm_start:
+                self.per_era_feature_importance_ = np.zeros((E, F), dtype=np.float32)
+                self.training_loss, self.eval_loss = [], []
+            self.stop = False
+            start = self._trees_trained if resume else 0
+            if self.objective == "regression" and len(self.forest) < self.n_estimators:
+                self.forest.extend([{} for _ in range(self.n_estimators - len(self.forest))])
+            D = self.max_depth
+            rec_nodes = ((1 << (D + 1)) - 1) * 64
+            rec_gain = ((1 << D) - 1) * E
+            T_new = (self.n_estimators - start) * K
+            self._rec_nodes = torch.empty((T_new, rec_nodes), dtype=torch.uint8, pin_memory=True)
+            self._rec_gain = torch.empty((T_new, max(rec_gain, 1)), dtype=torch.float32, pin_memory=True)
+            self._rec_feats = torch.empty((T_new, k), dtype=torch.int32, pin_memory=True)
+            self._rec_done = 0
+            self._rec_decoded = 0
+            self._rec_meta = []
+            self._residuals = []
+            if not resume:
+                self.feature_subsets_ = []
+            feats_all = torch.arange(F, dtype=torch.int32, device=dev)
+            for i in range(start, self.n_estimators):
+                if self.colsample_bytree < 1.0:
+                    feats = torch.randperm(F, device=dev, dtype=torch.int32)[:k]
+                    comm.bcast_(feats)
+                else:
+                    feats = feats_all
+                self._t["feats"].copy_(feats)
+                self._t["kpos"].fill_(-1)
+                self._t["kpos"][feats.long()] = torch.arange(k, dtype=torch.int32, device=dev)
+                if classification:
+                    grads = softmax(pred, dim=1)
+                    grads[torch.arange(N, device=dev), Yl.long()] -= 1.0
+                    for c in range(K):
+                        self._t["g"].copy_(-grads[:, c])
+                        self._grow_tree(ws, c, st, i, c)
+                    self._trees_trained = i + 1
+                    self._eval_classification(i)
+                else:
+                    self._grow_tree(ws, 0, st, i, 0)
+                    self._trees_trained = i + 1
+                    self._eval_regression(i)
+                if self.stop:
+                    break
+            self._finalize_records(classification)
+            self.feature_importance_ = self.per_era_feature_importance_.sum(axis=0)
+            self._is_fitted = True
+            if classification:
+                print(f"Finished training multiclass forest. Total rounds: {self._trees_trained} "
+                      f"({self._trees_trained * self.num_classes} trees)")
+            else:
+                print(f"Finished training forest. Total trees: {self._trees_trained}")
+            self._release()
+        return self
+
+    def _grow_tree(self, ws, cls, st, i, c):
+        comm = self._comm
+        ws.cls = cls
+        p = ctypes_ptr(ws)
+        _lib.call("wgb_tree_reset", p, st())
+        _lib.call("wgb_tree_residual", p, st())
+        if comm.on:
+            comm.max_(self._t["maxabs"])
+        _lib.call("wgb_tree_quantize", p, st())
+        if comm.on:
+            comm.sum_(self._t["rootsum"])
+        _lib.call("wgb_tree_root", p, st())
+        se = ws.E * ws.k * (ws.B + 1)
+        timer = getattr(self, "_hist_events", None)
+        for d in range(self.max_depth):
+            if timer is not None:
+                ev0 = torch.cuda.Event(enable_timing=True)
+                ev1 = torch.cuda.Event(enable_timing=True)
+                ev0.record()
+            _lib.call("wgb_level_hist", p, d, st())
+            if timer is not None:
+                ev1.record()
+                timer.append((ev0, ev1))
+            if comm.on:
+                first, count = _lib.built_slots(d)
+                comm.sum_(self._t["hg"][first * se:(first + count) * se])
+                comm.sum_(self._t["hc"][first * se:(first + count) * se])
+            _lib.call("wgb_level_split", p, d, st())
+            _lib.call("wgb_level_partition", p, d, st())
+        _lib.call("wgb_tree_finish", p, st())
+        if getattr(self, "_record_residuals", False):  # test hook: residual of every tree
+            self._residuals.append(self._t["g"][: ws.N].cpu().numpy().copy())
+        j = self._rec_done
+        self._rec_nodes[j].copy_(self._t["nodes"], non_blocking=True)
+        self._rec_gain[j, : self._t["era_gain"].numel()].copy_(self._t["era_gain"], non_blocking=True)
+        self._rec_feats[j].copy_(self._t["feats"], non_blocking=True)
+        self._rec_meta.append((i, c))
+        self._rec_done += 1
+
+    # ------------------------------------------------------------------
+    # tree records -> reference dict trees, importance (core.py:623-658)
+    # ------------------------------------------------------------------
+    def _decode_tree(self, j):
+        D, E = self.max_depth, self.num_eras
+        nodes = self._rec_nodes[j].numpy().view(_lib.NODE_DTYPE)
+        gains = self._rec_gain[j].numpy()
+        feats = self._rec_feats[j].numpy()
+        imp = self.per_era_feature_importance_
+
+        def rec(d, n):
+            nd = nodes[(1 << d) - 1 + n]
+            if d < D and nd["fpos"] >= 0:
+                gfi = int(feats[nd["fpos"]])
+                g0 = ((1 << d) - 1 + n) * E
+                imp[:, gfi] += gains[g0:g0 + E]
+                return {"feature": gfi, "bin": int(nd["bin"]),
+                        "left": rec(d + 1, int(nd["child"])),
+                        "right": rec(d + 1, int(nd["child"]) + 1)}
+            return {"leaf_value": float(nd["leaf"]), "samples": int(nd["count"])}
+        return rec(0, 0)
+
+    def _finalize_records(self, classification):
+        torch.cuda.current_stream().synchronize()
+        for j in range(getattr(self, "_rec_decoded", 0), self._rec_done):
+            self._store_tree(j, classification)
+        self._rec_decoded = self._rec_done
+
+    def _store_tree(self, j, classification):
+        i, c = self._rec_meta[j]
+        tree = self._decode_tree(j)
+        if not hasattr(self, "feature_subsets_"):
+            self.feature_subsets_ = []
+        if c == 0:
+            while len(self.feature_subsets_) <= i:
+                self.feature_subsets_.append(None)
+            self.feature_subsets_[i] = self._rec_feats[j].numpy().copy()
+        if classification:
+            while len(self.forest) <= i:
+                self.forest.append([None] * self.num_classes)
+            self.forest[i][c] = tree
+        else:
+            self.forest[i] = tree
+        self._packed = None
+
+    def _sync_records(self, classification):
+        if self._rec_done > getattr(self, "_rec_decoded", 0):
+            torch.cuda.current_stream().synchronize()
+            for j in range(self._rec_decoded, self._rec_done):
+                self._store_tree(j, classification)
+            self._rec_decoded = self._rec_done
+
+    def _release(self):
+        for name in ("_t", "_ws", "_keep", "_pred", "Y_gpu", "_eval_bins", "_eval_pred", "_Y_eval"):
+            if hasattr(self, name):
+                delattr(self, name)
+        for name in ("_rec_nodes", "_rec_gain", "_rec_feats", "_rec_meta"):
+            if hasattr(self, name):
+                delattr(self, name)
+        self._rec_decoded = 0
+
+    # ------------------------------------------------------------------
+    # eval / early stopping (core.py:660-690, 820-853)
+    # ------------------------------------------------------------------
+    def _gather_cat(self, t):
+        return torch.cat(self._comm.gather_var(t.reshape(-1))) if self._comm.on else t.reshape(-1)
+
+    def get_eval_metric(self, y_true, y_pred):
+        if self.eval_metric == "mse":
+            return ((y_true - y_pred) ** 2).mean().item()
+        elif self.eval_metric == "corr":
+            return 1 - torch.corrcoef(torch.vstack([y_true, y_pred]))[0, 1].item()
+        elif self.eval_metric == "rmsle":
+            return rmsle_torch(y_true, y_pred).item()
+        raise ValueError(f"Invalid eval_metric: {self.eval_metric}.")
+
+    def _eval_regression(self, i):
+        if self.eval_every_n_trees is None:
+            return
+        r = (self.Y_gpu - self._pred[:, 0])
+        s = torch.stack([(r * r).sum().double(), torch.tensor(float(r.numel()), dtype=torch.float64, device=r.device)])
+        self._comm.sum_(s)
+        train_loss = float((s[0] / s[1]).item()) if self._comm.on else ((r) ** 2).mean().item()
+        self.training_loss.append(train_loss)
+        if i % self.eval_every_n_trees == 0:
+            self._sync_records(False)
+            self._advance_eval(i + 1)
+            yt = self._gather_cat(self._Y_eval)
+            yp = self._gather_cat(self._eval_pred[:, 0])
+            eval_loss = self.get_eval_metric(yt, yp)
+            self.eval_loss.append(eval_loss)
+            if len(self.eval_loss) > self.early_stopping_rounds:
+                if self.eval_loss[-(self.early_stopping_rounds + 1)] < self.eval_loss[-1]:
+                    self.stop = True
+            print(f"🌲 Tree {i+1}/{self.n_estimators} | Train MSE: {train_loss:.6f} | "
+                  f"Eval {self.eval_metric}: {eval_loss:.6f}")
+
+    def _eval_classification(self, i):
+        if self.eval_every_n_trees is None:
+            return
+        probs = softmax(self._pred, dim=1)
+        if self._comm.on:
+            p = probs[torch.arange(probs.shape[0], device=probs.device), self.Y_gpu.long()]
+            p = torch.clamp(p, 1e-15, 1 - 1e-15)
+            s = torch.stack([-torch.log(p).sum().double(),
+                             torch.tensor(float(p.numel()), dtype=torch.float64, device=p.device)])
+            self._comm.sum_(s)
+            train_loss = float((s[0] / s[1]).item())
+        else:
+            train_loss = log_loss_torch(self.Y_gpu, probs).item()
+        self.training_loss.append(train_loss)
+        if i % self.eval_every_n_trees == 0:
+            self._sync_records(True)
+            self._advance_eval(i + 1)
+            eval_probs = softmax(self._eval_pred, dim=1)
+            yt = self._gather_cat(self._Y_eval)
+            if self._comm.on:
+                eval_probs = torch.cat(self._comm.gather_var(eval_probs.reshape(-1))).reshape(-1, self.num_classes)
+            if self.eval_metric == "accuracy":
+                eval_loss = 1.0 - accuracy_torch(yt, torch.argmax(eval_probs, dim=1)).item()
+            else:
+                eval_loss = log_loss_torch(yt, eval_probs).item()
+            self.eval_loss.append(eval_loss)
+            if len(self.eval_loss) > self.early_stopping_rounds:
+                if self.eval_loss[-(self.early_stopping_rounds + 1)] < self.eval_loss[-1]:
+                    self.stop = True
+            print(f"🌲 Round {i+1}/{self.n_estimators} ({self.num_classes} trees) | "
+                  f"Train LogLoss: {train_loss:.6f} | Eval {self.eval_metric}: {eval_loss:.6f}")
+
+    def _advance_eval(self, upto):
+        """Add the trees [_eval_upto, upto) to the running eval prediction
+        (tree order, so equal to predicting with the whole forest)."""
+        if upto <= self._eval_upto:
+            return
+        self._ensure_packed()
+        self._predict_into(self._eval_bins, self._eval_pred, self._eval_upto, upto)
+        self._eval_upto = upto
+
+    # ------------------------------------------------------------------
+    # prediction (core.py:917-1030)
+    # ------------------------------------------------------------------
+    def _flat_trees(self):
+        if self.objective == "regression":
+            return [t for t in self.forest if t]
+        return [t for rnd in self.forest if rnd for t in rnd]
+
+    def _ensure_packed(self):
+        if self._packed is None:
+            nodes, offs = pack_trees(self._flat_trees())
+            dev = getattr(self, "_dev", torch.device("cuda", torch.cuda.current_device()))
+            self._packed = (torch.from_numpy(nodes.reshape(-1)).to(dev),
+                            torch.from_numpy(offs).to(dev), offs)
+        return self._packed
+
+    def _predict_into(self, bins, out, r0, r1):
+        """out[:, class] += lr * leaf for the trees of rounds [r0, r1)."""
+        nodes, offs_d, offs = self._ensure_packed()
+        K = out.shape[1]
+        t0, t1 = r0 * K, min(r1 * K, len(offs) - 1)
+        if t1 <= t0:
+            return
+        _lib.call("wgb_predict_packed", bins.data_ptr(), bins.shape[0], bins.shape[1],
+                  nodes.data_ptr(), offs_d[t0:].data_ptr(), t1 - t0, K,
+                  float(np.float32(self.learning_rate)), out.data_ptr(),
+                  torch.cuda.current_stream().cuda_stream)
+
+    def _init_proba_logits(self, n):
+        """core.py:1001-1007: the prior of class k is 1/K (sic), computed on the host."""
+        Fm = torch.zeros((n, self.num_classes), dtype=torch.float32)
+        for c in range(self.num_classes):
+            prior_k = (self.classes_ == self.classes_[c]).sum() / len(self.classes_)
+            if prior_k > 0:
+                Fm[:, c] = torch.log(torch.tensor(prior_k + 1e-10))
+        return Fm.to(self._dev)
+
+    def bin_inference_data(self, X_np):
+        if not hasattr(self, "_dev"):
+            self._dev = torch.device("cuda", torch.cuda.current_device())
+        self._comm = getattr(self, "_comm", None) or _Comm(False)
+        if isinstance(self.bin_edges, np.ndarray):
+            self.bin_edges = torch.from_numpy(self.bin_edges)
+        self.bin_edges = self.bin_edges.to(self._dev)
+        return self._upload_bins(X_np, fit=False)[0]
+
+    def predict_binned(self, bins):
+        out = torch.zeros((bins.shape[0], 1), dtype=torch.float32, device=bins.device) + \
+            np.float32(self.base_prediction)
+        self._predict_into(bins, out, 0, len(self._flat_trees()))
+        return out[:, 0]
+
+    def predict_proba_binned(self, bins):
+        out = self._init_proba_logits(bins.shape[0])
+        self._predict_into(bins, out, 0, len([r for r in self.forest if r]))
+        return softmax(out, dim=1)
+
+    def predict(self, X_np):
+        if self.objective in ("multiclass", "binary"):
+            probs = self.predict_proba(X_np)
+            return self.label_encoder.inverse_transform(np.argmax(probs, axis=1))
+        with torch.cuda.device(self._device_for_predict()):
+            bins = self.bin_inference_data(X_np)
+            return self.predict_binned(bins).cpu().numpy()
+
+    def predict_proba(self, X_np):
+        if self.objective not in ["multiclass", "binary"]:
+            raise ValueError("predict_proba only available for classification objectives")
+        with torch.cuda.device(self._device_for_predict()):
+            bins = self.bin_inference_data(X_np)
+            return self.predict_proba_binned(bins).cpu().numpy()
+
+    def _device_for_predict(self):
+        if not hasattr(self, "_dev"):
+            self._dev = torch.device("cuda", torch.cuda.current_device())
+        return self._dev
+
+    # ------------------------------------------------------------------
+    # importance, save / load (core.py:1032-1213)
+    # ------------------------------------------------------------------
+    def get_feature_importance(self, importance_type="gain", normalize=True):
+        if self.feature_importance_ is None:
+            raise ValueError("Model has not been fitted yet.")
+        if importance_type != "gain":
+            raise ValueError(f"importance_type '{importance_type}' not supported. Use 'gain'.")
+        imp = self.feature_importance_.copy()
+        if normalize and imp.sum() > 0:
+            imp = imp / imp.sum()
+        return imp
+
+    def get_per_era_feature_importance(self, normalize=True):
+        if self.per_era_feature_importance_ is None:
+            raise ValueError("Model has not been fitted yet.")
+        imp = self.per_era_feature_importance_.copy()
+        if normalize:
+            for e in range(imp.shape[0]):
+                s = imp[e].sum()
+                if s > 0:
+                    imp[e] /= s
+        return imp
+
+    def save_model(self, path):
+        if not self._is_fitted:
+            raise ValueError("Cannot save unfitted model. Call fit() first.")
+        state = {k: getattr(self, k) for k in (
+            "objective", "num_bins", "max_depth", "learning_rate", "n_estimators",
+            "min_child_weight", "min_split_gain", "L2_reg", "colsample_bytree", "random_state",
+            "warm_start", "forest", "base_prediction", "num_features", "num_classes", "classes_",
+            "label_encoder", "feature_importance_", "per_era_feature_importance_", "_is_fitted",
+            "_trees_trained", "training_loss", "eval_loss")}
+        state["bin_edges"] = self.bin_edges.cpu() if torch.is_tensor(self.bin_edges) else self.bin_edges
+        with open(path, "wb") as f:
+            pickle.dump(state, f)
+        print(f"Model saved to {path}")
+
+    def load_model(self, path):
+        with open(path, "rb") as f:
+            state = pickle.load(f)
+        for k, v in state.items():
+            setattr(self, k, v)
+        self.training_loss = state.get("training_loss", [])
+        self.eval_loss = state.get("eval_loss", [])
+        self._packed = None
+        print(f"Model loaded from {path} ({self._trees_trained} trees)")
+        return self
+
+    def flatten_tree(self, tree, max_nodes):
+        """core.py:1215-1252 (pre-order, [max_nodes, 6], NaN-filled)."""
+        flat = torch.full((max_nodes, 6), float("nan"), dtype=torch.float32)
+        counter = [0]
+
+        def walk(nd):
+            i = counter[0]
+            counter[0] += 1
+            if "leaf_value" in nd:
+                flat[i, 4] = 1.0
+                flat[i, 5] = nd["leaf_value"]
+            else:
+                flat[i, 0] = float(nd["feature"])
+                flat[i, 1] = float(nd["bin"])
+                flat[i, 2] = counter[0]
+                walk(nd["left"])
+                flat[i, 3] = counter[0]
+                walk(nd["right"])
+                flat[i, 4] = 0.0
+        walk(tree)
+        return flat
+
+
+def ctypes_ptr(ws):
+    import ctypes
+    return ctypes.cast(ctypes.pointer(ws), ctypes.c_void_p)

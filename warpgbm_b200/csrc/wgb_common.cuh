@@ -1,0 +1,167 @@
+// Shared helpers of the warpgbm_b200 CUDA library (sm_100a).
+#pragma once
+
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include <climits>
+#include <cmath>
+
+#include "../../include/warpgbm_b200.h"
+
+namespace wgb {
+
+// ---------------------------------------------------------------- errors --
+void set_error(const char *fmt, ...);
+
+#define WGB_CHECK_ARG(cond, ...)                                              \
+    do {                                                                      \
+        if (!(cond)) {                                                        \
+            ::wgb::set_error(__VA_ARGS__);                                    \
+            return WGB_ERR_ARG;                                               \
+        }                                                                     \
+    } while (0)
+
+#define WGB_CUDA(call)                                                        \
+    do {                                                                      \
+        cudaError_t e_ = (call);                                              \
+        if (e_ != cudaSuccess) {                                              \
+            ::wgb::set_error("%s failed: %s (%s:%d)", #call,                  \
+                             cudaGetErrorString(e_), __FILE__, __LINE__);     \
+            return WGB_ERR_CUDA;                                              \
+        }                                                                     \
+    } while (0)
+
+#define WGB_LAUNCHED(name)                                                    \
+    do {                                                                      \
+        cudaError_t e_ = cudaGetLastError();                                  \
+        if (e_ != cudaSuccess) {                                              \
+            ::wgb::set_error("launch of %s failed: %s", name,                 \
+                             cudaGetErrorString(e_));                         \
+            return WGB_ERR_CUDA;                                              \
+        }                                                                     \
+    } while (0)
+
+inline cudaStream_t as_stream(void *s) { return reinterpret_cast<cudaStream_t>(s); }
+
+// ------------------------------------------------------------ constants --
+constexpr int HIST_FT = 128;        // features per histogram tile (one 128-B row segment)
+constexpr int HIST_R = 1024;        // rows per histogram chunk
+constexpr int HIST_THREADS = 256;
+constexpr int SPLIT_THREADS = 128;  // features per split block
+constexpr int PART_TILE = 2048;     // positions per partition tile
+constexpr int PART_THREADS = 256;
+
+// --------------------------------------------------------- fixed point --
+// Residual quantisation: q = rint(g * 2^s), s = 29 - e where max|g| = m*2^e,
+// m in [0.5, 1).  |q| <= 2^29, so a shared-memory cell may pack
+// count << 47 + sum(q) for up to 2^16 rows and int64 totals hold 2^33 rows.
+__host__ __device__ inline int quant_shift(float maxabs) {
+    if (!(maxabs > 0.0f) || isinf(maxabs)) return 0;
+    int e;
+    frexpf(maxabs, &e);
+    int s = 29 - e;
+    if (s > 126) s = 126;
+    if (s < -99) s = -99;
+    return s;
+}
+
+// 2^s as float for s in [-126, 127]
+__device__ __forceinline__ float pow2f(int s) { return __int_as_float((127 + s) << 23); }
+
+constexpr unsigned long long PACK_ONE = 1ull << 47;
+
+__device__ __forceinline__ void unpack_cell(unsigned long long w, long long &cnt, long long &gsum) {
+    unsigned long long c = (w + (1ull << 46)) >> 47;
+    cnt = (long long)c;
+    gsum = (long long)(w - (c << 47));
+}
+
+// Leaf value = mean residual of the node's rows from the exact sums
+// (fp32 ops: float(sum_q) * 2^-s, times 1/float(n)).
+__device__ __forceinline__ float canon_leaf(long long sumq, long long count, float inv) {
+    float sf = __fmul_rn(__ll2float_rn(sumq), inv);
+    float fac = __fdiv_rn(1.0f, __ll2float_rn(count));
+    return __fmul_rn(sf, fac);
+}
+
+// best_split_kernel.cu:42-50 with one IEEE rounding per operation.
+struct SplitEval {
+    float gain;
+    float dir;
+};
+__device__ __forceinline__ SplitEval eval_split(float GL, float HL, float GT, float HT, float mcw,
+                                                float eps) {
+    SplitEval r{0.0f, 0.0f};
+    float GR = __fsub_rn(GT, GL);
+    float HR = __fsub_rn(HT, HL);
+    if (HL >= mcw && HR >= mcw) {
+        float dl = __fadd_rn(HL, eps), dr = __fadd_rn(HR, eps), dt = __fadd_rn(HT, eps);
+        float t1 = __fdiv_rn(__fmul_rn(GL, GL), dl);
+        float t2 = __fdiv_rn(__fmul_rn(GR, GR), dr);
+        float t3 = __fdiv_rn(__fmul_rn(GT, GT), dt);
+        r.gain = __fsub_rn(__fadd_rn(t1, t2), t3);
+        float lv = __fdiv_rn(GL, dl), rv = __fdiv_rn(GR, dr);
+        r.dir = (lv > rv) ? 1.0f : -1.0f;
+    }
+    return r;
+}
+
+// Arg-max key of the directional era split (core.py:577-594): higher
+// agreement first (max over every candidate), then higher masked criterion
+// (-inf where crit <= min_split_gain), then the lower flat index.
+struct Key {
+    int A;
+    float c;
+    int idx;
+};
+__device__ __forceinline__ bool key_better(const Key &a, const Key &b) {
+    if (a.A != b.A) return a.A > b.A;
+    if (a.c != b.c) return a.c > b.c;
+    return a.idx < b.idx;
+}
+__device__ __forceinline__ Key key_none() { return Key{-1, -INFINITY, INT_MAX}; }
+
+__device__ __forceinline__ Key warp_key_max(Key k) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+        Key t;
+        t.A = __shfl_xor_sync(0xffffffffu, k.A, o);
+        t.c = __shfl_xor_sync(0xffffffffu, k.c, o);
+        t.idx = __shfl_xor_sync(0xffffffffu, k.idx, o);
+        if (key_better(t, k)) k = t;
+    }
+    return k;
+}
+
+template <typename T>
+__device__ __forceinline__ T warp_sum(T v) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+    return v;
+}
+
+__device__ __forceinline__ int warp_min(int v) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v = min(v, __shfl_xor_sync(0xffffffffu, v, o));
+    return v;
+}
+
+// Block-wide minimum (every thread gets the result).  Contains barriers.
+__device__ __forceinline__ int block_min(int v, int *scratch /* >= 33 ints */) {
+    int lane = threadIdx.x & 31, w = threadIdx.x >> 5, nw = (blockDim.x + 31) >> 5;
+    v = warp_min(v);
+    if (lane == 0) scratch[w] = v;
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        int m = INT_MAX;
+        for (int i = 0; i < nw; ++i) m = min(m, scratch[i]);
+        scratch[32] = m;
+    }
+    __syncthreads();
+    int r = scratch[32];
+    __syncthreads();
+    return r;
+}
+
+}  // namespace wgb

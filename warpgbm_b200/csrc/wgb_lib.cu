@@ -1,0 +1,4 @@
+// Single translation unit of libwgb_b200.so: the level-wise engine and the
+// binning / prediction / reference-compatible entry points share kernels.
+#include "wgb_engine.cu"
+#include "wgb_ops.cu"

@@ -1,0 +1,417 @@
+// Binning, prediction and the reference-compatible entry points of
+// warpgbm_b200 (sm_100a).  Compiled in the same translation unit as
+// wgb_engine.cu (see wgb_lib.cu): it reuses k_hist and k_chunk_plan.
+
+namespace wgb {
+
+// ====================================================================== //
+// binning                                                                //
+// ====================================================================== //
+
+// Row-major float [n][F] -> int8 [n][out_stride] in one pass.  CTA = 64 rows x
+// 128 features; the tile's edges sit in shared memory edge-major ([b][128])
+// so each thread reads its 4 features' edges as one conflict-free float4.
+// Per element the reference scan (binner.cu:20-23): count leading edges with
+// x >= edge, stopping at the first failure.
+constexpr int BIN_FT = 128, BIN_ROWS = 64;
+
+__global__ void __launch_bounds__(256) k_bin_matrix(const float *__restrict__ X, long long n, int F,
+                                                    long long xs, const float *__restrict__ edges,
+                                                    int nb, int8_t *__restrict__ out, long long os) {
+    extern __shared__ float4 s_e4[];  // [nb][BIN_FT/4]
+    float *s_e = reinterpret_cast<float *>(s_e4);
+    const int f0 = blockIdx.y * BIN_FT;
+    for (int t = threadIdx.x; t < nb * BIN_FT; t += blockDim.x) {
+        int b = t / BIN_FT, fl = t - b * BIN_FT;
+        int f = f0 + fl;
+        s_e[t] = f < F ? edges[(long long)f * nb + b] : 0.0f;
+    }
+    __syncthreads();
+    const int tl = threadIdx.x & 31;           // feature quad within the tile
+    const int f = f0 + 4 * tl;
+    if (f >= os) return;
+    const long long r0 = (long long)blockIdx.x * BIN_ROWS;
+    for (int rr = threadIdx.x >> 5; rr < BIN_ROWS; rr += blockDim.x >> 5) {
+        long long r = r0 + rr;
+        if (r >= n) break;
+        const float *xr = X + r * xs;
+        float v[4];
+#pragma unroll
+        for (int j = 0; j < 4; ++j) v[j] = (f + j < F) ? __ldg(xr + f + j) : 0.0f;
+        int bin[4] = {0, 0, 0, 0};
+        bool go[4] = {true, true, true, true};
+        for (int b = 0; b < nb; ++b) {
+            float4 e = s_e4[b * (BIN_FT / 4) + tl];
+            go[0] = go[0] && (v[0] >= e.x);
+            go[1] = go[1] && (v[1] >= e.y);
+            go[2] = go[2] && (v[2] >= e.z);
+            go[3] = go[3] && (v[3] >= e.w);
+            bin[0] += go[0];
+            bin[1] += go[1];
+            bin[2] += go[2];
+            bin[3] += go[3];
+        }
+        uint32_t w = 0;
+#pragma unroll
+        for (int j = 0; j < 4; ++j)
+            if (f + j < F) w |= (uint32_t)(uint8_t)bin[j] << (8 * j);
+        *reinterpret_cast<uint32_t *>(out + r * os + f) = w;
+    }
+}
+
+__global__ void k_bin_column(const float *__restrict__ X, long long n, const float *__restrict__ e,
+                             int nb, int8_t *__restrict__ out) {
+    long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x;
+    if (i >= n) return;
+    float v = X[i];
+    int b = 0;
+    while (b < nb && v >= e[b]) ++b;
+    out[i] = (int8_t)b;
+}
+
+// ====================================================================== //
+// prediction                                                             //
+// ====================================================================== //
+
+// Packed forest: node = int2; internal {feature >= 0, bin | right << 8}
+// (left child = node + 1, pre-order), leaf {-1, float bits of value}.
+// One thread per row; the CTA stages its rows' bins in shared memory
+// (row stride S + 4 bytes: the same feature of consecutive rows falls in
+// consecutive banks).  Trees are walked PG at a time (independent chains for
+// latency hiding) and their leaves added strictly in tree order.
+constexpr int PRED_ROWS = 128, PRED_G = 4;
+
+__global__ void __launch_bounds__(PRED_ROWS) k_predict_packed(
+    const int8_t *__restrict__ bins, long long n, long long S, const int2 *__restrict__ nodes,
+    const int *__restrict__ tree_off, int T, int K, float lr, float *__restrict__ out) {
+    extern __shared__ uint32_t s_rows[];
+    const int SW = (int)(S / 4) + 1;  // words per staged row
+    const long long r0 = (long long)blockIdx.x * PRED_ROWS;
+    const int nrows = (int)min((long long)PRED_ROWS, n - r0);
+    for (int t = threadIdx.x; t < nrows * (SW - 1); t += PRED_ROWS) {
+        int rr = t / (SW - 1), w = t - rr * (SW - 1);
+        s_rows[rr * SW + w] = __ldg(reinterpret_cast<const uint32_t *>(bins + (r0 + rr) * S) + w);
+    }
+    __syncthreads();
+    if (threadIdx.x >= nrows) return;
+    const uint8_t *myrow = reinterpret_cast<const uint8_t *>(s_rows + threadIdx.x * SW);
+    const long long row = r0 + threadIdx.x;
+    for (int c = 0; c < K; ++c) {
+        float acc = out[row * K + c];
+        for (int t0 = c; t0 < T; t0 += K * PRED_G) {
+            float val[PRED_G];
+            int node[PRED_G], base[PRED_G], lim[PRED_G];
+            bool live[PRED_G];
+#pragma unroll
+            for (int u = 0; u < PRED_G; ++u) {
+                int t = t0 + u * K;
+                live[u] = t < T;
+                base[u] = live[u] ? tree_off[t] : 0;
+                lim[u] = live[u] ? tree_off[t + 1] - base[u] : 0;
+                node[u] = 0;
+                val[u] = 0.0f;
+            }
+            bool any = true;
+            while (any) {
+                any = false;
+#pragma unroll
+                for (int u = 0; u < PRED_G; ++u) {
+                    if (!live[u]) continue;
+                    int2 nd = __ldg(nodes + base[u] + node[u]);
+                    if (nd.x < 0) {
+                        val[u] = __int_as_float(nd.y);
+                        live[u] = false;
+                        continue;
+                    }
+                    if (nd.x >= S) {  // malformed feature index
+                        val[u] = __int_as_float(0x7fc00000);
+                        live[u] = false;
+                        continue;
+                    }
+                    int b = (int)(int8_t)myrow[nd.x];
+                    int nxt = (b <= (nd.y & 0xff)) ? node[u] + 1 : (nd.y >> 8);
+                    // pre-order ids only grow; anything else is a malformed tree
+                    if (nxt <= node[u] || nxt >= lim[u]) {
+                        val[u] = __int_as_float(0x7fc00000);
+                        live[u] = false;
+                        continue;
+                    }
+                    node[u] = nxt;
+                    any = true;
+                }
+            }
+#pragma unroll
+            for (int u = 0; u < PRED_G; ++u)
+                if (t0 + u * K < T) acc = __fadd_rn(acc, __fmul_rn(lr, val[u]));
+        }
+        out[row * K + c] = acc;
+    }
+}
+
+// The reference's flattened format (core.py:1215-1252): [T][max_nodes][6].
+__global__ void k_predict_flat(const int8_t *__restrict__ bins, long long n, long long F,
+                               const float *__restrict__ forest, int T, int max_nodes, float lr,
+                               float *__restrict__ out) {
+    long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x;
+    if (i >= n) return;
+    const int8_t *r = bins + i * F;
+    float acc = out[i];
+    for (int t = 0; t < T; ++t) {
+        const float *tree = forest + (long long)t * max_nodes * 6;
+        int node = 0;
+        float v = __int_as_float(0x7fc00000);
+        for (int step = 0; step < max_nodes; ++step) {
+            const float *nd = tree + node * 6;
+            if (nd[4] > 0.5f) {
+                v = nd[5];
+                break;
+            }
+            int f = (int)nd[0], sb = (int)nd[1];
+            if (f < 0 || f >= F) break;
+            int nxt = (r[f] <= sb) ? (int)nd[2] : (int)nd[3];
+            if (nxt <= node || nxt >= max_nodes) break;
+            node = nxt;
+        }
+        acc = __fadd_rn(acc, __fmul_rn(lr, v));
+    }
+    out[i] = acc;
+}
+
+// ====================================================================== //
+// reference-compatible split / histogram                                 //
+// ====================================================================== //
+
+__global__ void k_ref_split(const float *__restrict__ G, const float *__restrict__ H, int E, int k, int B,
+                            float mcs, float eps, float *__restrict__ gain, float *__restrict__ dir) {
+    int j = blockIdx.x * blockDim.x + threadIdx.x;
+    int e = blockIdx.y;
+    if (j >= k || e >= E) return;
+    const long long base = ((long long)e * k + j) * B;
+    const long long bg = ((long long)e * k + j) * (B - 1);
+    float GT = 0.0f, HT = 0.0f;
+    for (int b = 0; b < B; ++b) {
+        GT = __fadd_rn(GT, G[base + b]);
+        HT = __fadd_rn(HT, H[base + b]);
+    }
+    float GL = 0.0f, HL = 0.0f;
+    for (int b = 0; b < B - 1; ++b) {
+        GL = __fadd_rn(GL, G[base + b]);
+        HL = __fadd_rn(HL, H[base + b]);
+        SplitEval r = eval_split(GL, HL, GT, HT, mcs, eps);
+        gain[bg + b] = r.gain;
+        dir[bg + b] = r.dir;
+    }
+}
+
+__global__ void k_max_abs_rows(const float *__restrict__ g, const int *__restrict__ rows, long long n,
+                               long long nrows, float *maxabs) {
+    float m = 0.0f;
+    for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < n;
+         i += (long long)gridDim.x * blockDim.x) {
+        int r = rows[i];
+        if (r >= 0 && r < nrows) m = fmaxf(m, fabsf(g[r]));
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+    if ((threadIdx.x & 31) == 0) atomicMax(reinterpret_cast<int *>(maxabs), __float_as_int(m));
+}
+
+__global__ void k_single_node(const float *maxabs, int *shift, wgb_node *nd, int n, int *nn) {
+    *shift = quant_shift(*maxabs);
+    wgb_node r{};
+    r.lstart = 0;
+    r.lcnt = n;
+    r.slot = 0;
+    r.built = 1;
+    r.fpos = -1;
+    r.child = -1;
+    *nd = r;
+    *nn = 1;
+}
+
+__global__ void k_kpos(const int *__restrict__ feats, int k, int F, int *__restrict__ kpos) {
+    int j = blockIdx.x * blockDim.x + threadIdx.x;
+    if (j >= k) return;
+    int f = feats[j];
+    if (f >= 0 && f < F) kpos[f] = j;
+}
+
+__global__ void k_hist_to_float(const long long *__restrict__ hg, const int *__restrict__ hc, long long m,
+                                int B, const int *shift, float *__restrict__ G, float *__restrict__ H) {
+    const float inv = pow2f(-*shift);
+    for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < m * B;
+         i += (long long)gridDim.x * blockDim.x) {
+        long long c = i / B;
+        int b = (int)(i - c * B);
+        long long src = c * (B + 1) + b;
+        G[i] = __fadd_rn(G[i], __fmul_rn(__ll2float_rn(hg[src]), inv));
+        H[i] = __fadd_rn(H[i], __int2float_rn(hc[src]));
+    }
+}
+
+int hist_ew_for(int B) {
+    // eras per shared window: keep the cells at <= 48 KB
+    int per = (B + 1) * HIST_FT * 8;
+    int ew = (48 * 1024) / per;
+    if (ew < 1) ew = 1;
+    if (ew > 8) ew = 8;
+    return ew;
+}
+
+static int grid_cap(long long n, int threads) {
+    long long b = (n + threads - 1) / threads;
+    if (b < 1) b = 1;
+    if (b > 148 * 16) b = 148 * 16;
+    return (int)b;
+}
+
+}  // namespace wgb
+
+using namespace wgb;
+
+extern "C" {
+
+int wgb_bin_matrix(const float *X, int64_t n, int32_t F, int64_t x_stride, const float *edges,
+                   int32_t num_bins, int8_t *out, int64_t out_stride, void *stream) {
+    WGB_CHECK_ARG(n >= 0 && F >= 1, "bad shape n=%lld F=%d", (long long)n, F);
+    WGB_CHECK_ARG(num_bins >= 2 && num_bins <= 127, "num_bins must be in [2, 127]");
+    WGB_CHECK_ARG(x_stride >= F, "x_stride < F");
+    WGB_CHECK_ARG(out_stride >= F && out_stride % 4 == 0, "out_stride must be >= F and a multiple of 4");
+    if (n == 0) return WGB_OK;
+    WGB_CHECK_ARG(X && edges && out, "NULL pointer");
+    const int nb = num_bins - 1;
+    size_t smem = (size_t)nb * BIN_FT * sizeof(float);
+    dim3 grid((unsigned)((n + BIN_ROWS - 1) / BIN_ROWS), (unsigned)((out_stride + BIN_FT - 1) / BIN_FT));
+    WGB_CUDA(cudaFuncSetAttribute(k_bin_matrix, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+    k_bin_matrix<<<grid, 256, smem, as_stream(stream)>>>(X, n, F, x_stride, edges, nb, out, out_stride);
+    WGB_LAUNCHED("k_bin_matrix");
+    return WGB_OK;
+}
+
+int wgb_custom_cuda_binner(const float *X, int64_t n, const float *bin_edges, int32_t num_edges,
+                           int8_t *bin_indices, void *stream) {
+    WGB_CHECK_ARG(n >= 0 && num_edges >= 0, "bad sizes");
+    if (n == 0) return WGB_OK;
+    WGB_CHECK_ARG(X && bin_indices && (bin_edges || num_edges == 0), "NULL pointer");
+    k_bin_column<<<(unsigned)((n + 255) / 256), 256, 0, as_stream(stream)>>>(X, n, bin_edges, num_edges,
+                                                                              bin_indices);
+    WGB_LAUNCHED("k_bin_column");
+    return WGB_OK;
+}
+
+int wgb_predict_packed(const int8_t *bins, int64_t n, int64_t S, const int32_t *nodes,
+                       const int32_t *tree_off, int32_t T, int32_t K, float lr, float *out,
+                       void *stream) {
+    WGB_CHECK_ARG(n >= 0 && S >= 4 && S % 4 == 0, "bad bins shape (stride must be a multiple of 4)");
+    WGB_CHECK_ARG(T >= 0 && K >= 1, "bad forest shape");
+    if (n == 0 || T == 0) return WGB_OK;
+    size_t smem = (size_t)PRED_ROWS * (S + 4);
+    WGB_CHECK_ARG(smem <= 200 * 1024, "rows too wide for the staged predictor (S=%lld)", (long long)S);
+    WGB_CUDA(cudaFuncSetAttribute(k_predict_packed, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+    k_predict_packed<<<(unsigned)((n + PRED_ROWS - 1) / PRED_ROWS), PRED_ROWS, smem, as_stream(stream)>>>(
+        bins, n, S, reinterpret_cast<const int2 *>(nodes), tree_off, T, K, lr, out);
+    WGB_LAUNCHED("k_predict_packed");
+    return WGB_OK;
+}
+
+int wgb_predict_forest(const int8_t *bin_indices, int64_t n, int64_t F, const float *tree_tensor,
+                       int32_t T, int32_t max_nodes, float learning_rate, float *out, void *stream) {
+    WGB_CHECK_ARG(n >= 0 && F >= 1 && T >= 0 && max_nodes >= 1, "bad shapes");
+    if (n == 0 || T == 0) return WGB_OK;
+    k_predict_flat<<<(unsigned)((n + 255) / 256), 256, 0, as_stream(stream)>>>(
+        bin_indices, n, F, tree_tensor, T, max_nodes, learning_rate, out);
+    WGB_LAUNCHED("k_predict_flat");
+    return WGB_OK;
+}
+
+int wgb_compute_split(const float *G, const float *H, int32_t num_eras, int32_t k, int32_t num_bins,
+                      float min_split_gain, float min_child_samples, float eps, float *per_era_gain,
+                      float *per_era_direction, int32_t threads, void *stream) {
+    (void)min_split_gain;  // unused by the reference kernel as well
+    WGB_CHECK_ARG(num_eras >= 1 && k >= 0 && num_bins >= 2, "bad histogram shape");
+    WGB_CHECK_ARG(threads >= 1 && threads <= 1024, "threads must be in [1, 1024]");
+    if (k == 0) return WGB_OK;
+    dim3 grid((unsigned)((k + threads - 1) / threads), (unsigned)num_eras);
+    k_ref_split<<<grid, threads, 0, as_stream(stream)>>>(G, H, num_eras, k, num_bins, min_child_samples, eps,
+                                                         per_era_gain, per_era_direction);
+    WGB_LAUNCHED("k_ref_split");
+    return WGB_OK;
+}
+
+int wgb_compute_histogram3(const int8_t *bin_indices, int64_t num_rows, int64_t F_master,
+                           const float *residuals, const int32_t *sample_indices, int64_t n,
+                           const int32_t *feature_indices, int32_t k, const int32_t *era_indices,
+                           float *grad_hist, float *hess_hist, int32_t num_eras, int32_t num_bins,
+                           int32_t threads_per_block, int32_t rows_per_thread, void *stream) {
+    WGB_CHECK_ARG(threads_per_block > 0 && threads_per_block % 32 == 0,
+                  "threads_per_block should be a positive multiple of 32");
+    WGB_CHECK_ARG(rows_per_thread >= 1 && rows_per_thread <= 16, "rows_per_thread must be in [1, 16]");
+    WGB_CHECK_ARG(num_bins >= 2 && num_bins <= 127, "num_bins must be in [2, 127]");
+    WGB_CHECK_ARG(num_eras >= 1 && k >= 0 && n >= 0 && num_rows >= 0 && F_master >= 1, "bad sizes");
+    WGB_CHECK_ARG(n < (1ll << 31), "too many samples");
+    if (n == 0 || k == 0) return WGB_OK;
+    cudaStream_t st = as_stream(stream);
+    const long long se = (long long)num_eras * k * (num_bins + 1);
+    const int nchunk = (int)((n + HIST_R - 1) / HIST_R);
+    // scratch from the stream-ordered pool
+    long long *hg = nullptr;
+    int *hc = nullptr, *kpos = nullptr, *small = nullptr;
+    int4 *chunks = nullptr;
+    wgb_node *nd = nullptr;
+    WGB_CUDA(cudaMallocAsync((void **)&hg, sizeof(long long) * se, st));
+    WGB_CUDA(cudaMallocAsync((void **)&hc, sizeof(int) * se, st));
+    WGB_CUDA(cudaMallocAsync((void **)&kpos, sizeof(int) * F_master, st));
+    WGB_CUDA(cudaMallocAsync((void **)&chunks, sizeof(int4) * nchunk, st));
+    WGB_CUDA(cudaMallocAsync((void **)&small, sizeof(int) * 8, st));
+    WGB_CUDA(cudaMallocAsync((void **)&nd, sizeof(wgb_node), st));
+    int *nchunks = small, *shift = small + 1, *nn = small + 2;
+    float *maxabs = reinterpret_cast<float *>(small + 3);
+    int rc = WGB_OK;
+    do {
+        if (cudaMemsetAsync(hg, 0, sizeof(long long) * se, st) != cudaSuccess ||
+            cudaMemsetAsync(hc, 0, sizeof(int) * se, st) != cudaSuccess ||
+            cudaMemsetAsync(kpos, 0xff, sizeof(int) * F_master, st) != cudaSuccess ||
+            cudaMemsetAsync(small, 0, sizeof(int) * 8, st) != cudaSuccess) {
+            set_error("cudaMemsetAsync failed");
+            rc = WGB_ERR_CUDA;
+            break;
+        }
+        k_kpos<<<(k + 255) / 256, 256, 0, st>>>(feature_indices, k, (int)F_master, kpos);
+        k_max_abs_rows<<<grid_cap(n, 256), 256, 0, st>>>(residuals, sample_indices, n, num_rows, maxabs);
+        k_single_node<<<1, 1, 0, st>>>(maxabs, shift, nd, (int)n, nn);
+        k_chunk_plan<<<1, 1024, 0, st>>>(nd, nn, chunks, nchunks, nchunk);
+        dim3 grid((unsigned)nchunk, (unsigned)((F_master + HIST_FT - 1) / HIST_FT));
+        if (num_eras == 1) {
+            size_t smem = hist_smem_bytes(num_bins, 1);
+            cudaFuncSetAttribute(k_hist<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+            k_hist<false><<<grid, HIST_THREADS, smem, st>>>(bin_indices, F_master, (int)F_master, sample_indices,
+                                                            nullptr, residuals, shift, nullptr, kpos, k, 1,
+                                                            num_bins, 1, chunks, nchunks, nd, hg, hc, se,
+                                                            num_rows);
+        } else {
+            int EW = hist_ew_for(num_bins);
+            size_t smem = hist_smem_bytes(num_bins, EW);
+            cudaFuncSetAttribute(k_hist<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+            k_hist<true><<<grid, HIST_THREADS, smem, st>>>(bin_indices, F_master, (int)F_master, sample_indices,
+                                                           nullptr, residuals, shift, era_indices, kpos, k,
+                                                           num_eras, num_bins, EW, chunks, nchunks, nd, hg, hc,
+                                                           se, num_rows);
+        }
+        k_hist_to_float<<<grid_cap((long long)num_eras * k * num_bins, 256), 256, 0, st>>>(
+            hg, hc, (long long)num_eras * k, num_bins, shift, grad_hist, hess_hist);
+        cudaError_t e = cudaGetLastError();
+        if (e != cudaSuccess) {
+            set_error("wgb_compute_histogram3 launch failed: %s", cudaGetErrorString(e));
+            rc = WGB_ERR_CUDA;
+        }
+    } while (0);
+    cudaFreeAsync(hg, st);
+    cudaFreeAsync(hc, st);
+    cudaFreeAsync(kpos, st);
+    cudaFreeAsync(chunks, st);
+    cudaFreeAsync(small, st);
+    cudaFreeAsync(nd, st);
+    return rc;
+}
+
+}  // extern "C"
