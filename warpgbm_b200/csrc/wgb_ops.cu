@@ -86,9 +86,10 @@ __global__ void __launch_bounds__(PRED_ROWS) k_predict_packed(
     const int *__restrict__ tree_off, int T, int K, float lr, float *__restrict__ out) {
     extern __shared__ uint32_t s_rows[];
     const int SW = (int)(S / 4) + 1;  // words per staged row
-    const long long r0 = (long long)blockIdx.x * PRED_ROWS;
-    const int nrows = (int)min((long long)PRED_ROWS, n - r0);
-    for (int t = threadIdx.x; t < nrows * (SW - 1); t += PRED_ROWS) {
+    const int RP = blockDim.x;        // rows per CTA (<= PRED_ROWS, fewer for wide rows)
+    const long long r0 = (long long)blockIdx.x * RP;
+    const int nrows = (int)min((long long)RP, n - r0);
+    for (int t = threadIdx.x; t < nrows * (SW - 1); t += RP) {
         int rr = t / (SW - 1), w = t - rr * (SW - 1);
         s_rows[rr * SW + w] = __ldg(reinterpret_cast<const uint32_t *>(bins + (r0 + rr) * S) + w);
     }
@@ -305,10 +306,13 @@ int wgb_predict_packed(const int8_t *bins, int64_t n, int64_t S, const int32_t *
     WGB_CHECK_ARG(n >= 0 && S >= 4 && S % 4 == 0, "bad bins shape (stride must be a multiple of 4)");
     WGB_CHECK_ARG(T >= 0 && K >= 1, "bad forest shape");
     if (n == 0 || T == 0) return WGB_OK;
-    size_t smem = (size_t)PRED_ROWS * (S + 4);
+    // rows per CTA: up to PRED_ROWS, fewer (multiple of 32) when rows are wide
+    int rp = PRED_ROWS;
+    while (rp > 32 && (size_t)rp * (S + 4) > 200 * 1024) rp -= 32;
+    size_t smem = (size_t)rp * (S + 4);
     WGB_CHECK_ARG(smem <= 200 * 1024, "rows too wide for the staged predictor (S=%lld)", (long long)S);
     WGB_CUDA(cudaFuncSetAttribute(k_predict_packed, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
-    k_predict_packed<<<(unsigned)((n + PRED_ROWS - 1) / PRED_ROWS), PRED_ROWS, smem, as_stream(stream)>>>(
+    k_predict_packed<<<(unsigned)((n + rp - 1) / rp), rp, smem, as_stream(stream)>>>(
         bins, n, S, reinterpret_cast<const int2 *>(nodes), tree_off, T, K, lr, out);
     WGB_LAUNCHED("k_predict_packed");
     return WGB_OK;
