@@ -177,7 +177,8 @@ typedef struct wgb_ws {
     int32_t F, k, E, B, D, K;
     int32_t cls;             /* output column updated by this tree            */
     int32_t chunk_cap, ntiles, ncand_blk;
-    int32_t hist_ew;         /* eras per shared-memory window                 */
+    int32_t hist_ew;         /* max eras per shared-memory window (0 = auto)  */
+    int32_t regular;         /* 1 if every bin is known to lie in [0, B)      */
     /* hyper-parameters (fp32 as the reference passes them) */
     float mcw, eps, msg, lr, mean_factor;
 } wgb_ws;

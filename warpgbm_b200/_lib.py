@@ -50,7 +50,7 @@ class WgbWs(ctypes.Structure):
         ("F", _i32), ("k", _i32), ("E", _i32), ("B", _i32), ("D", _i32), ("K", _i32),
         ("cls", _i32),
         ("chunk_cap", _i32), ("ntiles", _i32), ("ncand_blk", _i32),
-        ("hist_ew", _i32),
+        ("hist_ew", _i32), ("regular", _i32),
         ("mcw", _f32), ("eps", _f32), ("msg", _f32), ("lr", _f32), ("mean_factor", _f32),
     ]
 

@@ -451,12 +451,23 @@ class WarpGBM(BaseEstimator, RegressorMixin):
                 bins[:, :F] = Xi.to(torch.int8)
                 if fit:
                     self.bin_edges = torch.arange(1, B, dtype=torch.float32, device=dev).repeat(F, 1)
+                    # regular = every stored bin in [0, B) (negative or wrapped
+                    # pre-binned values take the kernel's slower checked path)
+                    mn = torch.zeros(1, dtype=torch.int64, device=dev)
+                    mxb = torch.zeros(1, dtype=torch.int64, device=dev)
+                    if n:
+                        mn[0] = bins[:, :F].amin()
+                        mxb[0] = bins[:, :F].amax()
+                    self._comm.max_(mxb)
+                    mn = -self._comm.max_(-mn)
+                    self._bins_regular = bool(mn.item() >= 0 and mxb.item() < B)
                 return bins, True
             Xd = Xi.to(torch.float32)
         else:
             Xd = _to_dev(X_np, dev, torch.float32)
         if fit:
             print("quantile binning.")
+            self._bins_regular = True  # binner output is always in [0, B)
             q = torch.linspace(0, 1, B + 1, device=dev, dtype=torch.float32)[1:-1]
             self.bin_edges = sharded_quantile_edges(Xd, q, self._comm)
         bins = torch.empty((n, S), dtype=torch.int8, device=dev)
@@ -516,7 +527,8 @@ class WarpGBM(BaseEstimator, RegressorMixin):
             setattr(ws, name, t[name].data_ptr())
         ws.N, ws.S, ws.F, ws.k, ws.E, ws.B, ws.D, ws.K = N, S, F, k, E, B, D, K
         ws.chunk_cap, ws.ntiles, ws.ncand_blk = max(chunk_cap, 1), ntiles, ncand
-        ws.hist_ew = hist_ew_for(B)
+        ws.hist_ew = 0  # automatic
+        ws.regular = 1 if self._bins_regular else 0
         ws.mcw = float(np.float32(self.min_child_weight))
         ws.eps = float(np.float32(self.L2_reg))
         ws.msg = float(np.float32(self.min_split_gain))

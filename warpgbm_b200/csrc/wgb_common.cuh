@@ -45,8 +45,8 @@ void set_error(const char *fmt, ...);
 inline cudaStream_t as_stream(void *s) { return reinterpret_cast<cudaStream_t>(s); }
 
 // ------------------------------------------------------------ constants --
-constexpr int HIST_FT = 128;        // features per histogram tile (one 128-B row segment)
-constexpr int HIST_R = 1024;        // rows per histogram chunk
+constexpr int HIST_R = 1024;        // rows per histogram chunk (cell packing needs <= 1024)
+#define HIST_ERA_R(has_era) ((has_era) ? HIST_R : 1)
 constexpr int HIST_THREADS = 256;
 constexpr int SPLIT_THREADS = 128;  // features per split block
 constexpr int PART_TILE = 2048;     // positions per partition tile
@@ -54,8 +54,9 @@ constexpr int PART_THREADS = 256;
 
 // --------------------------------------------------------- fixed point --
 // Residual quantisation: q = rint(g * 2^s), s = 29 - e where max|g| = m*2^e,
-// m in [0.5, 1).  |q| <= 2^29, so a shared-memory cell may pack
-// count << 47 + sum(q) for up to 2^16 rows and int64 totals hold 2^33 rows.
+// m in [0.5, 1).  |q| <= 2^29, so int64 totals hold 2^33 rows and the
+// histogram kernel's two 32-bit shared words per cell stay exact for
+// HIST_R rows.
 __host__ __device__ inline int quant_shift(float maxabs) {
     if (!(maxabs > 0.0f) || isinf(maxabs)) return 0;
     int e;
@@ -68,14 +69,6 @@ __host__ __device__ inline int quant_shift(float maxabs) {
 
 // 2^s as float for s in [-126, 127]
 __device__ __forceinline__ float pow2f(int s) { return __int_as_float((127 + s) << 23); }
-
-constexpr unsigned long long PACK_ONE = 1ull << 47;
-
-__device__ __forceinline__ void unpack_cell(unsigned long long w, long long &cnt, long long &gsum) {
-    unsigned long long c = (w + (1ull << 46)) >> 47;
-    cnt = (long long)c;
-    gsum = (long long)(w - (c << 47));
-}
 
 // Leaf value = mean residual of the node's rows from the exact sums
 // (fp32 ops: float(sum_q) * 2^-s, times 1/float(n)).

@@ -25,6 +25,7 @@ namespace wgb {
 
 static thread_local char g_err[1024];
 
+
 void set_error(const char *fmt, ...) {
     va_list ap;
     va_start(ap, fmt);
@@ -164,36 +165,83 @@ __global__ void __launch_bounds__(1024) k_chunk_plan(const wgb_node *__restrict_
     if (threadIdx.x == 0) *nchunks = min(s_base, cap);
 }
 
-// One CTA = one chunk (<= HIST_R rows of one node) x one 128-feature tile.
-// Lane l of every warp owns features 4l..4l+3 of the tile (one 32-bit load
-// per row); shared cells are [era window][slot b][j][lane] u64, so a warp's
-// 64-bit atomics touch 32 consecutive words (2 wavefronts, no conflicts).
-// Slot b == B collects negative bins; bins >= B are skipped
-// (histogram_kernel.cu:41).  When q == nullptr the residual g is quantised
-// on the fly with 2^shift (used by the drop-in wgb_compute_histogram3).
-template <bool HAS_ERA>
-__global__ void __launch_bounds__(HIST_THREADS) k_hist(
+// One CTA = one chunk (<= HIST_R rows of one node) x one tile of 32*FPL
+// features.  Lane l of every warp owns features FPL*l .. FPL*l+FPL-1 of the
+// tile (one FPL-byte load per row).  Every histogram cell is two 32-bit
+// shared words updated with native 32-bit reductions (64-bit shared atomics
+// are several times slower on sm_100):
+//     A  += (1 << 21) + (q & 0x7FF)       count (<= 1024) | low 11 bits of q
+//     Bw += q >> 11                       high bits of q (arithmetic shift)
+// so sum(q) = Bw * 2048 + (A & 0x1FFFFF) and count = A >> 21 exactly for up
+// to HIST_R = 1024 rows per chunk.
+// Shared layout of each word array: [era slot][j/2][bin slot 0..NSC-1][j%2][lane]
+// -- a bin slot is 256 bytes, so one byte-permute turns a bin into its byte
+// offset, the feature term is an immediate, and a warp's 32 reductions hit
+// 32 consecutive words (no bank conflicts).  Slots: 0..B-1 bins, B negative
+// bins (they always go left, core.py:629), B+1 trash for bins >= B (skipped
+// by the reference, histogram_kernel.cu:41); REGULAR instantiations know
+// every bin lies in [0, B).  Every feature of a lane is accumulated
+// unconditionally -- cells of unselected or padding features are never
+// flushed -- so an update is four instructions: permute, add, two reductions.
+// When q == nullptr the residual g is quantised on the fly with 2^shift (the
+// drop-in wgb_compute_histogram3).
+template <int IMM>
+__device__ __forceinline__ void red_shared(uint32_t addr, uint32_t v) {
+    asm volatile("red.shared.add.u32 [%0+%2], %1;" ::"r"(addr), "r"(v), "n"(IMM) : "memory");
+}
+
+template <int FPL, int NSC, int J>
+__device__ __forceinline__ void hist_update(uint32_t ra, uint32_t b8, uint32_t pa, uint32_t pb) {
+    constexpr int OFF = (J >> 1) * NSC * 256 + (J & 1) * 128;
+    constexpr int BOFF = (FPL / 2) * NSC * 256;  // word array B follows A within an era slot
+    const uint32_t a = ra + b8;
+    red_shared<OFF>(a, pa);
+    red_shared<BOFF + OFF>(a, pb);
+}
+
+template <int FPL, int NSC, bool REGULAR, int J = 0>
+__device__ __forceinline__ void hist_row(const uint32_t (&w)[FPL / 4], uint32_t ra, uint32_t pa, uint32_t pb,
+                                         int B) {
+    if constexpr (J < FPL) {
+        uint32_t b8;
+        if constexpr (REGULAR) {
+            b8 = __byte_perm(w[J >> 2], 0u, 0x4404u | ((J & 3) << 4));  // bin << 8
+        } else {
+            const int sb = (int)(int8_t)__byte_perm(w[J >> 2], 0u, 0x4440u | (J & 3));
+            b8 = (uint32_t)(sb < 0 ? B : (sb >= B ? B + 1 : sb)) << 8;
+        }
+        hist_update<FPL, NSC, J>(ra, b8, pa, pb);
+        hist_row<FPL, NSC, REGULAR, J + 1>(w, ra, pa, pb, B);
+    }
+}
+
+template <int FPL, int NT, int MINB, int NSC, int EWC, bool HAS_ERA, bool REGULAR>
+__global__ void __launch_bounds__(NT, MINB) k_hist(
     const int8_t *__restrict__ bins, long long S, int F, const int *__restrict__ order,
     const int *__restrict__ q, const float *__restrict__ g, const int *shift,
     const int *__restrict__ era, const int *__restrict__ kpos, int k, int E, int B, int EW,
     const int4 *__restrict__ chunks, const int *nchunks, const wgb_node *__restrict__ lvl,
     long long *__restrict__ hg, int *__restrict__ hc, long long slot_elems, long long nrows) {
-    extern __shared__ unsigned long long sh[];  // [EW][B+1][4][32]
-    __shared__ int s_kp[HIST_FT];
-    __shared__ int s_row[HIST_R];
-    __shared__ int s_q[HIST_R];
-    __shared__ int s_era[HIST_R];
+    constexpr int FT = 32 * FPL;             // features per tile
+    constexpr int U = (FPL >= 16 || MINB > 1) ? 4 : 8;  // rows per pipeline step per warp
+    constexpr int NW = NT / 32;
+    constexpr int WPR = FPL / 4;             // 32-bit words per lane per row
+    constexpr int ESLOT = 2 * NSC * FT;      // words per era slot (A and B arrays)
+    extern __shared__ uint32_t sh32[];       // [EWC][A|B][j/2][NSC][j%2][32]
+    __shared__ int s_kp[FT];                 // lane-major: [j][lane]
+    __shared__ int2 s_rec[HIST_R];           // {row or -1, q}
+    __shared__ int s_era[HIST_ERA_R(HAS_ERA)];
     __shared__ int s_red[33];
 
     const int c = blockIdx.x;
     if (c >= *nchunks) return;
-    const int f0 = blockIdx.y * HIST_FT;
+    const int f0 = blockIdx.y * FT;
     int any = 0;
-    if (threadIdx.x < HIST_FT) {
-        int f = f0 + threadIdx.x;
+    for (int t = threadIdx.x; t < FT; t += NT) {
+        int f = f0 + t;
         int kp = f < F ? kpos[f] : -1;
-        s_kp[threadIdx.x] = kp;
-        any = kp >= 0;
+        s_kp[(t % FPL) * 32 + t / FPL] = kp;
+        any |= kp >= 0;
     }
     if (!__syncthreads_or(any)) return;
 
@@ -204,7 +252,7 @@ __global__ void __launch_bounds__(HIST_THREADS) k_hist(
     if (!q) sc = pow2f(*shift);
     // rows outside [0, nrows) or eras outside [0, E) are skipped (only the
     // drop-in entry point can receive them; the engine never produces them)
-    for (int i = threadIdx.x; i < cnt; i += HIST_THREADS) {
+    for (int i = threadIdx.x; i < cnt; i += NT) {
         int r = order[ch.y + i];
         bool ok = r >= 0 && r < nrows;
         int e = 0;
@@ -212,96 +260,171 @@ __global__ void __launch_bounds__(HIST_THREADS) k_hist(
             e = era[r];
             ok = e >= 0 && e < E;
         }
-        s_row[i] = ok ? r : -1;
-        s_q[i] = ok ? (q ? q[r] : __float2int_rn(__fmul_rn(g[r], sc))) : 0;
+        const int qv = ok ? (q ? q[r] : __float2int_rn(__fmul_rn(g[r], sc))) : 0;
+        s_rec[i] = make_int2(ok ? r : -1, qv);
         if (HAS_ERA) s_era[i] = ok ? e : INT_MAX;
     }
     __syncthreads();
-    const bool aligned4 = (S & 3) == 0;
+    const bool aligned = (S % FPL) == 0;
+    const int ew_n = HAS_ERA ? min(EW, EWC) : 1;
 
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-    unsigned vmask = 0;
+    bool lane_live = false;
 #pragma unroll
-    for (int j = 0; j < 4; ++j)
-        if (s_kp[4 * lane + j] >= 0) vmask |= 1u << j;
+    for (int j = 0; j < FPL; ++j) lane_live |= s_kp[j * 32 + lane] >= 0;
     const int B1 = B + 1;
-    const int win = B1 * HIST_FT;
-    const int8_t *tile = bins + f0 + 4 * lane;
+    const uint32_t sbase = (uint32_t)__cvta_generic_to_shared(sh32) + 4u * lane;
+    const int8_t *tile = bins + f0 + FPL * lane;
 
     int e_lo = 0;
     if (HAS_ERA) {
         int m = INT_MAX;
-        for (int i = threadIdx.x; i < cnt; i += HIST_THREADS) m = min(m, s_era[i]);
+        for (int i = threadIdx.x; i < cnt; i += NT) m = min(m, s_era[i]);
         e_lo = block_min(m, s_red);
         if (e_lo == INT_MAX) return;  // no valid row (uniform)
     }
     for (;;) {
-        for (int t = threadIdx.x; t < EW * win; t += HIST_THREADS) sh[t] = 0ull;
+        {
+            uint4 *z = reinterpret_cast<uint4 *>(sh32);
+            const uint4 zero = make_uint4(0u, 0u, 0u, 0u);
+            for (int t = threadIdx.x; t < (ew_n * ESLOT) / 4; t += NT) z[t] = zero;
+        }
         __syncthreads();
-        if (vmask) {
-            for (int i0 = warp; i0 < cnt; i0 += 32) {
-                uint32_t w[4];
-                int ew[4];
-                bool ok[4];
+        if (lane_live) {
+            // software pipeline: rows of step k+1 are loaded while step k's
+            // cells are updated
+            uint32_t w[U][WPR], wn[U][WPR];
+            int4 rec[U], recn[U];                // {row or -1, q, era slot, -}
+            auto fetch = [&](int i0, int4 (&rr)[U], uint32_t (&ww)[U][WPR]) {
 #pragma unroll
-                for (int u = 0; u < 4; ++u) {
-                    int i = i0 + 8 * u;
-                    ok[u] = i < cnt && s_row[i] >= 0;
-                    ew[u] = 0;
-                    if (HAS_ERA && ok[u]) {
-                        int e = s_era[i] - e_lo;
-                        ok[u] = e >= 0 && e < EW;
-                        ew[u] = e;
+                for (int u = 0; u < U; ++u) {
+                    const int i = i0 + NW * u;
+                    const int2 rq = i < cnt ? s_rec[i] : make_int2(-1, 0);
+                    int4 r4 = make_int4(rq.x, rq.y, 0, 0);
+                    if (HAS_ERA && r4.x >= 0) {
+                        const int e = s_era[i] - e_lo;
+                        if (e < 0 || e >= ew_n) r4.x = -1;
+                        r4.z = e;
                     }
-                    w[u] = 0u;
-                    if (ok[u]) {
-                        const int8_t *src = tile + (long long)s_row[i] * S;
-                        if (aligned4) {
-                            w[u] = __ldg(reinterpret_cast<const uint32_t *>(src));
-                        } else {
+                    rr[u] = r4;
 #pragma unroll
-                            for (int j = 0; j < 4; ++j)
-                                if ((vmask >> j) & 1u) w[u] |= (uint32_t)(uint8_t)__ldg(src + j) << (8 * j);
+                    for (int x = 0; x < WPR; ++x) ww[u][x] = 0u;
+                    if (r4.x >= 0) {
+                        const int8_t *src = tile + (long long)r4.x * S;
+                        if (aligned) {
+                            if constexpr (FPL == 16) {
+                                const uint4 v = __ldg(reinterpret_cast<const uint4 *>(src));
+                                ww[u][0] = v.x; ww[u][1] = v.y; ww[u][2] = v.z; ww[u][3] = v.w;
+                            } else if constexpr (FPL == 8) {
+                                const uint2 v = __ldg(reinterpret_cast<const uint2 *>(src));
+                                ww[u][0] = v.x; ww[u][1] = v.y;
+                            } else {
+                                ww[u][0] = __ldg(reinterpret_cast<const uint32_t *>(src));
+                            }
+                        } else {
+                            const int nv = min(FPL, F - (f0 + FPL * lane));  // bytes inside the row
+#pragma unroll
+                            for (int j = 0; j < FPL; ++j)
+                                if (j < nv) ww[u][j >> 2] |= (uint32_t)(uint8_t)__ldg(src + j) << (8 * (j & 3));
                         }
                     }
                 }
+            };
+            fetch(warp, rec, w);
+            for (int i0 = warp; i0 < cnt; i0 += NW * U) {
+                const int i1 = i0 + NW * U;
+                if (i1 < cnt) fetch(i1, recn, wn);
 #pragma unroll
-                for (int u = 0; u < 4; ++u) {
-                    if (!ok[u]) continue;
-                    unsigned long long pk = PACK_ONE + (unsigned long long)(long long)s_q[i0 + 8 * u];
-                    unsigned long long *base = sh + ew[u] * win + lane;
+                for (int u = 0; u < U; ++u) {
+                    if (rec[u].x < 0) continue;
+                    const uint32_t ra = sbase + (HAS_ERA ? (uint32_t)rec[u].z * (ESLOT * 4) : 0u);
+                    const int qv = rec[u].y;
+                    hist_row<FPL, NSC, REGULAR>(w[u], ra, (1u << 21) + (uint32_t)(qv & 0x7FF),
+                                                (uint32_t)(qv >> 11), B);
+                }
 #pragma unroll
-                    for (int j = 0; j < 4; ++j) {
-                        int b = (int)(int8_t)(w[u] >> (8 * j));
-                        if (((vmask >> j) & 1u) && b < B) {
-                            int sl = b < 0 ? B : b;
-                            atomicAdd(base + (sl * 4 + j) * 32, pk);
-                        }
-                    }
+                for (int u = 0; u < U; ++u) {
+                    rec[u] = recn[u];
+#pragma unroll
+                    for (int x = 0; x < WPR; ++x) w[u][x] = wn[u][x];
                 }
             }
         }
         __syncthreads();
-        for (int t = threadIdx.x; t < EW * win; t += HIST_THREADS) {
-            unsigned long long w = sh[t];
-            if (w == 0ull) continue;
-            long long cntv, gs;
-            unpack_cell(w, cntv, gs);
-            int ew = t / win, rem = t - ew * win;
-            int sl = rem >> 7, jl = rem & 127;
-            int fl = 4 * (jl & 31) + (jl >> 5);
-            long long idx = slot * slot_elems + ((long long)(e_lo + ew) * k + s_kp[fl]) * B1 + sl;
-            atomicAdd(reinterpret_cast<unsigned long long *>(hg + idx), (unsigned long long)gs);
-            atomicAdd(hc + idx, (int)cntv);
+        // flush bins 0..B of every feature (the trash slot is dropped),
+        // walking the words in layout order (conflict-free reads)
+        for (int ew = 0; ew < ew_n; ++ew) {
+            const uint32_t *Ae = sh32 + ew * ESLOT;
+            const uint32_t *Be = Ae + NSC * FT;
+            const long long ebase = slot * slot_elems + (long long)(e_lo + ew) * k * B1;
+            for (int wi = threadIdx.x; wi < NSC * FT; wi += NT) {
+                const int jb = wi / (NSC * 64), rem = wi % (NSC * 64);
+                const int sl = rem >> 6, r2 = rem & 63;
+                if (sl > B) continue;
+                const int jj = 2 * jb + (r2 >> 5), lj = r2 & 31;
+                const int kp = s_kp[jj * 32 + lj];
+                if (kp < 0) continue;
+                const uint32_t a = Ae[wi];
+                if (a == 0u) continue;
+                const int cntv = (int)(a >> 21);
+                const long long gs = (long long)(int)Be[wi] * 2048 + (long long)(a & 0x1FFFFFu);
+                const long long idx = ebase + (long long)kp * B1 + sl;
+                atomicAdd(reinterpret_cast<unsigned long long *>(hg + idx), (unsigned long long)gs);
+                atomicAdd(hc + idx, cntv);
+            }
         }
         if (!HAS_ERA) break;
         int m = INT_MAX;
-        for (int i = threadIdx.x; i < cnt; i += HIST_THREADS)
-            if (s_era[i] >= e_lo + EW) m = min(m, s_era[i]);
+        for (int i = threadIdx.x; i < cnt; i += NT)
+            if (s_era[i] >= e_lo + ew_n) m = min(m, s_era[i]);
         m = block_min(m, s_red);  // also orders the flush before the next zeroing
         if (m == INT_MAX) break;
         e_lo = m;
     }
+}
+
+// Launch of the histogram kernel for one level: picks the feature width per
+// lane, the bin-slot capacity and the era window from the row alignment,
+// feature count, num_bins and era count.  Returns a cudaError_t.
+static cudaError_t launch_hist(int grid_x, const int8_t *bins, long long S, int F, const int *order,
+                               const int *q, const float *g, const int *shift, const int *era,
+                               const int *kpos, int k, int E, int B, int EW, bool regular,
+                               const int4 *chunks, const int *nchunks, const wgb_node *lvl,
+                               long long *hg, int *hc, long long slot_elems, long long nrows,
+                               cudaStream_t st) {
+    const bool has_era = E > 1;
+    int fpl = 4;
+    if (S % 8 == 0 && F > 128 && B <= 32) fpl = 8;
+    const int nsc = (B + 2 <= 8) ? 8 : (B + 2 <= 34 ? 34 : 130);
+#define WGB_HIST_CASE(FPL_, NT_, MINB_, NSC_, EWC_, ERA_, REG_)                                       \
+    if (fpl == FPL_ && nsc == NSC_ && has_era == ERA_ && regular == REG_) {                            \
+        auto fn = k_hist<FPL_, NT_, MINB_, NSC_, EWC_, ERA_, REG_>;                                    \
+        const int ew = ERA_ ? (EW > 0 ? min(EW, EWC_) : EWC_) : 1;                                     \
+        size_t smem = (size_t)EWC_ * 2 * NSC_ * 32 * FPL_ * 4;                                         \
+        cudaError_t e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem); \
+        if (e != cudaSuccess) return e;                                                                \
+        dim3 grid((unsigned)grid_x, (unsigned)((F + 32 * FPL_ - 1) / (32 * FPL_)));                    \
+        fn<<<grid, NT_, smem, st>>>(bins, S, F, order, q, g, shift, era, kpos, k, E, B, ew, chunks,   \
+                                    nchunks, lvl, hg, hc, slot_elems, nrows);                          \
+        return cudaGetLastError();                                                                     \
+    }
+#define WGB_HIST_REG(FPL_, NT_, MINB_, NSC_, EWC_, ERA_) \
+    WGB_HIST_CASE(FPL_, NT_, MINB_, NSC_, EWC_, ERA_, true) WGB_HIST_CASE(FPL_, NT_, MINB_, NSC_, EWC_, ERA_, false)
+    // one era: 2 CTAs x 16 warps per SM
+    WGB_HIST_REG(8, 512, 2, 34, 1, false)
+    WGB_HIST_REG(8, 512, 2, 8, 1, false)
+    WGB_HIST_REG(4, 256, 1, 34, 1, false)
+    WGB_HIST_REG(4, 256, 1, 8, 1, false)
+    WGB_HIST_REG(4, 256, 1, 130, 1, false)
+    // eras: several era slots per window
+    WGB_HIST_REG(8, 512, 1, 8, 8, true)
+    WGB_HIST_REG(8, 512, 1, 34, 2, true)
+    WGB_HIST_REG(4, 256, 1, 8, 8, true)
+    WGB_HIST_REG(4, 256, 1, 34, 4, true)
+    WGB_HIST_REG(4, 256, 1, 130, 1, true)
+#undef WGB_HIST_REG
+#undef WGB_HIST_CASE
+    return cudaErrorInvalidValue;
 }
 
 // sibling = parent - built, in place of the parent's slot (the sibling
@@ -747,7 +870,7 @@ static int grid_for(long long n, int threads, int cap = 148 * 16) {
     return (int)(b < cap ? b : cap);
 }
 
-size_t hist_smem_bytes(int B, int EW) { return (size_t)EW * (B + 1) * HIST_FT * 8; }
+
 
 }  // namespace wgb
 
@@ -778,7 +901,7 @@ static int check_ws(const wgb_ws *ws) {
     WGB_CHECK_ARG(ws->E >= 1, "num_eras must be >= 1");
     WGB_CHECK_ARG(ws->N >= 0 && ws->N < (1ll << 31), "rows per rank must be < 2^31");
     WGB_CHECK_ARG(ws->S >= ws->F && ws->S % 4 == 0, "bins row stride must be >= F and a multiple of 4");
-    WGB_CHECK_ARG(ws->hist_ew >= 1, "hist_ew must be >= 1");
+    WGB_CHECK_ARG(ws->hist_ew >= 0, "hist_ew must be >= 0");
     return WGB_OK;
 }
 
@@ -835,22 +958,16 @@ int wgb_level_hist(const wgb_ws *ws, int32_t d, void *stream) {
     if (ws->N == 0) return WGB_OK;
     long long max_chunks = (ws->N + HIST_R - 1) / HIST_R + count;
     if (max_chunks > ws->chunk_cap) max_chunks = ws->chunk_cap;
-    dim3 grid((unsigned)max_chunks, (unsigned)((ws->F + HIST_FT - 1) / HIST_FT));
-    int EW = ws->E == 1 ? 1 : ws->hist_ew;
-    size_t smem = hist_smem_bytes(ws->B, EW);
     const int *ord = level_order(ws, d);
-    if (ws->E == 1) {
-        WGB_CUDA(cudaFuncSetAttribute(k_hist<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
-        k_hist<false><<<grid, HIST_THREADS, smem, st>>>(
-            ws->bins, ws->S, ws->F, ord, ws->qg, nullptr, nullptr, nullptr, ws->kpos, ws->k, ws->E, ws->B,
-            1, reinterpret_cast<const int4 *>(ws->chunks), ws->nchunks, lvl, LL(ws->hg), ws->hc, se, ws->N);
-    } else {
-        WGB_CUDA(cudaFuncSetAttribute(k_hist<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
-        k_hist<true><<<grid, HIST_THREADS, smem, st>>>(
-            ws->bins, ws->S, ws->F, ord, ws->qg, nullptr, nullptr, ws->era, ws->kpos, ws->k, ws->E, ws->B,
-            EW, reinterpret_cast<const int4 *>(ws->chunks), ws->nchunks, lvl, LL(ws->hg), ws->hc, se, ws->N);
+    cudaError_t e = launch_hist((int)max_chunks, ws->bins, ws->S, ws->F, ord, ws->qg, nullptr, nullptr,
+                                ws->E > 1 ? ws->era : nullptr, ws->kpos, ws->k, ws->E, ws->B, ws->hist_ew,
+                                ws->regular != 0, reinterpret_cast<const int4 *>(ws->chunks), ws->nchunks,
+                                lvl, LL(ws->hg), ws->hc, se, ws->N, st);
+    if (e != cudaSuccess) {
+        set_error("k_hist launch failed: %s", cudaGetErrorString(e));
+        return WGB_ERR_CUDA;
     }
-    WGB_LAUNCHED("k_hist");
+
     return WGB_OK;
 }
 

@@ -250,15 +250,6 @@ __global__ void k_hist_to_float(const long long *__restrict__ hg, const int *__r
     }
 }
 
-int hist_ew_for(int B) {
-    // eras per shared window: keep the cells at <= 48 KB
-    int per = (B + 1) * HIST_FT * 8;
-    int ew = (48 * 1024) / per;
-    if (ew < 1) ew = 1;
-    if (ew > 8) ew = 8;
-    return ew;
-}
-
 static int grid_cap(long long n, int threads) {
     long long b = (n + threads - 1) / threads;
     if (b < 1) b = 1;
@@ -384,22 +375,14 @@ int wgb_compute_histogram3(const int8_t *bin_indices, int64_t num_rows, int64_t 
         k_max_abs_rows<<<grid_cap(n, 256), 256, 0, st>>>(residuals, sample_indices, n, num_rows, maxabs);
         k_single_node<<<1, 1, 0, st>>>(maxabs, shift, nd, (int)n, nn);
         k_chunk_plan<<<1, 1024, 0, st>>>(nd, nn, chunks, nchunks, nchunk);
-        dim3 grid((unsigned)nchunk, (unsigned)((F_master + HIST_FT - 1) / HIST_FT));
-        if (num_eras == 1) {
-            size_t smem = hist_smem_bytes(num_bins, 1);
-            cudaFuncSetAttribute(k_hist<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-            k_hist<false><<<grid, HIST_THREADS, smem, st>>>(bin_indices, F_master, (int)F_master, sample_indices,
-                                                            nullptr, residuals, shift, nullptr, kpos, k, 1,
-                                                            num_bins, 1, chunks, nchunks, nd, hg, hc, se,
-                                                            num_rows);
-        } else {
-            int EW = hist_ew_for(num_bins);
-            size_t smem = hist_smem_bytes(num_bins, EW);
-            cudaFuncSetAttribute(k_hist<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-            k_hist<true><<<grid, HIST_THREADS, smem, st>>>(bin_indices, F_master, (int)F_master, sample_indices,
-                                                           nullptr, residuals, shift, era_indices, kpos, k,
-                                                           num_eras, num_bins, EW, chunks, nchunks, nd, hg, hc,
-                                                           se, num_rows);
+        cudaError_t le = launch_hist(nchunk, bin_indices, F_master, (int)F_master, sample_indices, nullptr,
+                                     residuals, shift, num_eras > 1 ? era_indices : nullptr, kpos, k,
+                                     num_eras, num_bins, 0, false, chunks, nchunks, nd, hg, hc, se, num_rows,
+                                     st);
+        if (le != cudaSuccess) {
+            set_error("k_hist launch failed: %s", cudaGetErrorString(le));
+            rc = WGB_ERR_CUDA;
+            break;
         }
         k_hist_to_float<<<grid_cap((long long)num_eras * k * num_bins, 256), 256, 0, st>>>(
             hg, hc, (long long)num_eras * k, num_bins, shift, grad_hist, hess_hist);
