@@ -207,6 +207,13 @@ int wgb_level_partition(const wgb_ws *ws, int32_t d, void *stream);
 /* Level D: every remaining row gets its leaf update. */
 int wgb_tree_finish(const wgb_ws *ws, void *stream);
 
+/* Host -> device copy of `bytes` from pageable host memory, pipelined
+ * through pinned staging buffers (parallel host copies overlapped with the
+ * DMA, one cudaMemcpyAsync per 64 MiB chunk).  Returns once the source has
+ * been read; the device copies complete in stream order.  Ingest path of
+ * warpgbm/core.py:487-538 (the reference copies column by column). */
+int wgb_h2d(void *dst, const void *src, int64_t bytes, void *stream);
+
 /* Forest prediction with trees packed by warpgbm_b200 (pre-order, 8 bytes per
  * node: internal = {feature, bin | right_id << 8}, leaf = {-1, value bits}).
  * out[i*K + class_of_tree(t)] += lr * leaf_t(i), trees in order t = 0..T-1,

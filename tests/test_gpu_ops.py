@@ -159,3 +159,12 @@ def test_root_histogram_full_width(cuda):
     assert np.array_equal(Hd.cpu().numpy(), Hf)
     assert np.array_equal(Gd.cpu().numpy(), Gf)
     assert (Hf.sum(axis=2) == n).all()
+
+
+@pytest.mark.parametrize("nbytes", [1, 4097, (64 << 20) + 3, (200 << 20) + 12345])
+def test_pipelined_h2d_copy_is_exact(cuda, nbytes):
+    rng = np.random.default_rng(nbytes % 1000)
+    src = rng.integers(0, 256, nbytes, dtype=np.uint8)
+    dst = torch.empty(nbytes, dtype=torch.uint8, device=cuda)
+    _lib.call("wgb_h2d", dst.data_ptr(), src.ctypes.data, nbytes, _st())
+    assert np.array_equal(dst.cpu().numpy(), src)

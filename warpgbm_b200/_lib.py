@@ -76,6 +76,7 @@ _SIGS = {
     "wgb_level_partition": ([_p, _i32, _p], _i32),
     "wgb_tree_finish": ([_p, _p], _i32),
     "wgb_predict_packed": ([_p, _i64, _i64, _p, _p, _i32, _i32, _f32, _p, _p], _i32),
+    "wgb_h2d": ([_p, _p, _i64, _p], _i32),
 }
 
 EXPORTED = tuple(_SIGS)

@@ -182,9 +182,26 @@ def _quantile_columns(Xd: torch.Tensor, q: torch.Tensor, chunk_elems: int = 1 <<
     return out
 
 
+_NP2T = {np.dtype(np.float32): torch.float32, np.dtype(np.int8): torch.int8,
+         np.dtype(np.int32): torch.int32, np.dtype(np.int64): torch.int64,
+         np.dtype(np.int16): torch.int16, np.dtype(np.uint8): torch.uint8,
+         np.dtype(np.float64): torch.float64}
+
+
 def _to_dev(a, dev, dtype=None):
-    """numpy array or tensor -> contiguous tensor on dev (pinned staging for
-    large host arrays so the copy runs at full PCIe bandwidth)."""
+    """numpy array or tensor -> contiguous tensor on dev.  Large host arrays
+    go through wgb_h2d (pinned staging, parallel host copies overlapped with
+    the DMA) instead of the driver's single pageable staging buffer."""
+    if isinstance(a, np.ndarray) and a.nbytes >= (32 << 20):
+        tdt = dtype if dtype is not None else _NP2T.get(a.dtype)
+        if tdt is not None:
+            ndt = np.dtype(str(tdt).replace("torch.", ""))
+            src = np.ascontiguousarray(a, dtype=ndt)
+            out = torch.empty(src.shape, dtype=tdt, device=dev)
+            with torch.cuda.device(dev):
+                _lib.call("wgb_h2d", out.data_ptr(), src.ctypes.data, src.nbytes,
+                          torch.cuda.current_stream().cuda_stream)
+            return out
     if torch.is_tensor(a):
         t = a
     else:

@@ -2,3 +2,4 @@
 // binning / prediction / reference-compatible entry points share kernels.
 #include "wgb_engine.cu"
 #include "wgb_ops.cu"
+#include "wgb_io.cu"
