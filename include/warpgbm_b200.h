@@ -112,6 +112,17 @@ int wgb_bin_matrix(const float *X, int64_t n, int32_t F, int64_t x_stride,
                    const float *edges, int32_t num_bins, int8_t *out,
                    int64_t out_stride, void *stream);
 
+/* Quantile edges of every column of a row-major float32 matrix X [n][F]
+ * (row stride x_stride elements): edges[f][j] = torch.quantile(X[:, f],
+ * q[j]) with linear interpolation, bit for bit (q = linspace(0, 1, B+1)[1:-1]
+ * as the reference builds it, warpgbm/core.py:529-534; any NaN in a column
+ * makes its edges NaN).  Radix selection of the 2*nq order statistics, no
+ * sort.  XT is caller scratch of n*F floats (the column-major copy).
+ * n <= 2^24 (torch's limit). */
+int wgb_quantile_edges(const float *X, int64_t n, int32_t F, int64_t x_stride,
+                       const float *q, int32_t nq, float *XT, float *edges,
+                       void *stream);
+
 /* One node of one tree level (64 bytes).  Global quantities (summed over all
  * ranks of a row-sharded job) and local ones (this rank's rows). */
 typedef struct wgb_node {

@@ -168,3 +168,40 @@ def test_pipelined_h2d_copy_is_exact(cuda, nbytes):
     dst = torch.empty(nbytes, dtype=torch.uint8, device=cuda)
     _lib.call("wgb_h2d", dst.data_ptr(), src.ctypes.data, nbytes, _st())
     assert np.array_equal(dst.cpu().numpy(), src)
+
+
+def _quantile_cases(rng):
+    n_list = [1, 2, 3, 7, 100, 4097, 300_000]
+    for n in n_list:
+        yield "normal", rng.standard_normal(n).astype(np.float32) * 3
+    n = 50_000
+    yield "ties", rng.integers(0, 5, n).astype(np.float32)
+    yield "constant", np.full(n, -2.5, np.float32)
+    yield "signed_zeros", np.where(rng.random(n) < 0.5, 0.0, -0.0).astype(np.float32)
+    yield "inf", np.where(rng.random(n) < 0.05, np.inf, rng.standard_normal(n)).astype(np.float32)
+    yield "neg_inf", np.where(rng.random(n) < 0.3, -np.inf, rng.standard_normal(n)).astype(np.float32)
+    yield "nan", np.where(rng.random(n) < 0.001, np.nan, rng.standard_normal(n)).astype(np.float32)
+    yield "tiny", (rng.standard_normal(n) * 1e-38).astype(np.float32)
+    yield "heavy", rng.standard_cauchy(n).astype(np.float32)
+    yield "clustered", (np.round(rng.standard_normal(n) * 4) / 4 + 1e6).astype(np.float32)
+
+
+@pytest.mark.parametrize("B", [2, 5, 32, 127])
+def test_quantile_edges_kernel_equals_torch_quantile(cuda, B):
+    """wgb_quantile_edges (radix select) against torch.quantile on the B200,
+    the op the reference calls (core.py:532), bit for bit."""
+    from warpgbm_b200.core import _quantile_columns
+    rng = np.random.default_rng(B)
+    q = torch.linspace(0, 1, B + 1, device=cuda, dtype=torch.float32)[1:-1]
+    for name, col in _quantile_cases(rng):
+        x = torch.from_numpy(col).to(cuda)
+        got = _quantile_columns(x[:, None], q)[0].cpu().numpy()
+        ref = torch.quantile(x, q).cpu().numpy()
+        assert np.array_equal(got, ref, equal_nan=True), (name, len(col), got, ref)
+    # a multi-column matrix (transpose path, column chunking)
+    X = rng.standard_normal((20_000, 37)).astype(np.float32)
+    X[:, 5] = np.round(X[:, 5])
+    Xd = torch.from_numpy(X).to(cuda)
+    got = _quantile_columns(Xd, q, chunk_elems=20_000 * 8).cpu().numpy()
+    ref = torch.quantile(Xd, q, dim=0).T.cpu().numpy()
+    assert np.array_equal(got, ref, equal_nan=True)

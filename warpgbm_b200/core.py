@@ -169,16 +169,23 @@ def sharded_quantile_edges(Xd: torch.Tensor, q: torch.Tensor, comm: _Comm) -> to
     return torch.cat(outs, 0)[:F].contiguous()
 
 
-def _quantile_columns(Xd: torch.Tensor, q: torch.Tensor, chunk_elems: int = 1 << 27):
-    """torch.quantile(X[:, f], q) for every column, in column chunks."""
+def _quantile_columns(Xd: torch.Tensor, q: torch.Tensor, chunk_elems: int = 1 << 28):
+    """Edges [F, B-1] = torch.quantile(X[:, f], q) for every column, bit for
+    bit, by wgb_quantile_edges (radix selection, no sort), in column chunks of
+    at most chunk_elems elements of column-major scratch."""
     n, F = Xd.shape
     if n > (1 << 24):
         raise ValueError("quantile() input tensor is too large")  # torch's own limit
+    Xd = Xd.contiguous()
     out = torch.empty((F, q.numel()), dtype=torch.float32, device=Xd.device)
-    step = max(1, chunk_elems // max(n, 1))
+    step = max(1, min(F, chunk_elems // max(n, 1)))
+    XT = torch.empty(n * step, dtype=torch.float32, device=Xd.device)
+    qd = q.contiguous()
+    st = torch.cuda.current_stream().cuda_stream
     for c0 in range(0, F, step):
         c1 = min(F, c0 + step)
-        out[c0:c1] = torch.quantile(Xd[:, c0:c1], q, dim=0).T
+        _lib.call("wgb_quantile_edges", Xd.data_ptr() + 4 * c0, n, c1 - c0, F, qd.data_ptr(),
+                  q.numel(), XT.data_ptr(), out[c0:c1].data_ptr(), st)
     return out
 
 

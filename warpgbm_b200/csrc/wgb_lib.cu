@@ -3,3 +3,4 @@
 #include "wgb_engine.cu"
 #include "wgb_ops.cu"
 #include "wgb_io.cu"
+#include "wgb_quantile.cu"
