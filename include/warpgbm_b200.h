@@ -69,6 +69,29 @@ int wgb_compute_histogram3(const int8_t *bin_indices, int64_t num_rows,
                            int32_t num_bins, int32_t threads_per_block,
                            int32_t rows_per_thread, void *stream);
 
+/* wgb_compute_histogram3 for callers that may not allocate device memory.
+ * No counterpart in the reference: it exists for hosts that give this
+ * library a fixed memory budget, or run it where an allocation must not
+ * happen (an allocator call can stall or fail there), and so cannot let
+ * wgb_compute_histogram3 take its scratch from the stream-ordered pool.
+ * Same arguments and result as wgb_compute_histogram3; its scratch is a
+ * fixed 64 MiB block inside the library (reserved on every GPU where the
+ * library's kernels are loaded, until the process exits).  A call needs
+ * num_eras*k*(num_bins+1)*12 + F_master*4 + ceil(n/1024)*16 + 96 bytes (each
+ * part rounded up to 256); larger calls return WGB_ERR_ARG.  Calls share the
+ * block, so calls that may overlap on the GPU race; calls on one stream are
+ * safe.  The first call on a device looks up the block's address and should
+ * come before any stream capture. */
+int wgb_compute_histogram3_noalloc(const int8_t *bin_indices, int64_t num_rows,
+                                   int64_t F_master, const float *residuals,
+                                   const int32_t *sample_indices, int64_t n,
+                                   const int32_t *feature_indices, int32_t k,
+                                   const int32_t *era_indices,
+                                   float *grad_hist, float *hess_hist,
+                                   int32_t num_eras, int32_t num_bins,
+                                   int32_t threads_per_block,
+                                   int32_t rows_per_thread, void *stream);
+
 /* Replaces node_kernel.compute_split = launch_directional_split_kernel
  * (warpgbm/cuda/best_split_kernel.cu:57-88, node_kernel.cpp:6-14,43).
  * Per (era, feature): totals over all B bins, prefix over b < B-1;

@@ -62,6 +62,8 @@ _SIGS = {
     "wgb_sizeof_ws": ([], _i32),
     "wgb_compute_histogram3": ([_p, _i64, _i64, _p, _p, _i64, _p, _i32, _p, _p, _p, _i32, _i32,
                                 _i32, _i32, _p], _i32),
+    "wgb_compute_histogram3_noalloc": ([_p, _i64, _i64, _p, _p, _i64, _p, _i32, _p, _p, _p, _i32, _i32,
+                                        _i32, _i32, _p], _i32),
     "wgb_compute_split": ([_p, _p, _i32, _i32, _i32, _f32, _f32, _f32, _p, _p, _i32, _p], _i32),
     "wgb_custom_cuda_binner": ([_p, _i64, _p, _i32, _p, _p], _i32),
     "wgb_predict_forest": ([_p, _i64, _i64, _p, _i32, _i32, _f32, _p, _p], _i32),
@@ -120,7 +122,7 @@ def check(rc: int, what: str = "") -> None:
 _KERNELS = {
     "wgb_tree_reset": 1, "wgb_tree_residual": 1, "wgb_tree_quantize": 1, "wgb_tree_root": 1,
     "wgb_level_hist": 2, "wgb_level_split": 4, "wgb_level_partition": 4, "wgb_tree_finish": 1,
-    "wgb_bin_matrix": 1, "wgb_predict_packed": 1, "wgb_quantile_edges": 2, "wgb_compute_histogram3": 6,
+    "wgb_bin_matrix": 1, "wgb_predict_packed": 1, "wgb_quantile_edges": 2, "wgb_compute_histogram3": 6, "wgb_compute_histogram3_noalloc": 6,
     "wgb_compute_split": 1, "wgb_custom_cuda_binner": 1, "wgb_predict_forest": 1,
 }
 LAUNCHES = [0]

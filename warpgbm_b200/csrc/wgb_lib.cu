@@ -4,3 +4,4 @@
 #include "wgb_ops.cu"
 #include "wgb_io.cu"
 #include "wgb_quantile.cu"
+#include "wgb_noalloc.cu"
