@@ -75,21 +75,51 @@ class _Comm:
             and dist.get_world_size() > 1
         self.world = dist.get_world_size() if self.on else 1
         self.rank = dist.get_rank() if self.on else 0
+        # a gloo group moves CUDA tensors through host memory (NCCL uses them in place)
+        self.host_staging = self.on and dist.get_backend() == "gloo"
+
+    def _inplace(self, t, op):
+        if self.host_staging and t.is_cuda:
+            h = t.cpu()
+            op(h)
+            t.copy_(h)
+        else:
+            op(t)
+        return t
 
     def max_(self, t):
         if self.on:
-            self.dist.all_reduce(t, op=self.dist.ReduceOp.MAX)
+            self._inplace(t, lambda x: self.dist.all_reduce(x, op=self.dist.ReduceOp.MAX))
         return t
 
     def sum_(self, t):
         if self.on:
-            self.dist.all_reduce(t, op=self.dist.ReduceOp.SUM)
+            self._inplace(t, lambda x: self.dist.all_reduce(x, op=self.dist.ReduceOp.SUM))
         return t
 
     def bcast_(self, t, src=0):
         if self.on:
-            self.dist.broadcast(t, src)
+            self._inplace(t, lambda x: self.dist.broadcast(x, src))
         return t
+
+    def all_gather(self, outs, t):
+        if self.host_staging and t.is_cuda:
+            ho = [torch.empty_like(o, device="cpu") for o in outs]
+            self.dist.all_gather(ho, t.cpu())
+            for o, h in zip(outs, ho):
+                o.copy_(h)
+        else:
+            self.dist.all_gather(outs, t)
+
+    def all_to_all_single(self, out, inp, out_splits, in_splits):
+        if self.host_staging and inp.is_cuda:
+            ho = torch.empty_like(out, device="cpu")
+            self.dist.all_to_all_single(ho, inp.cpu(), output_split_sizes=out_splits,
+                                        input_split_sizes=in_splits)
+            out.copy_(ho)
+        else:
+            self.dist.all_to_all_single(out, inp, output_split_sizes=out_splits,
+                                        input_split_sizes=in_splits)
 
     def gather_var(self, t: torch.Tensor) -> List[torch.Tensor]:
         """all_gather of 1-D tensors of different lengths."""
@@ -97,13 +127,13 @@ class _Comm:
             return [t]
         n = torch.tensor([t.numel()], dtype=torch.int64, device=t.device)
         ns = [torch.zeros_like(n) for _ in range(self.world)]
-        self.dist.all_gather(ns, n)
+        self.all_gather(ns, n)
         ns = [int(x.item()) for x in ns]
         m = max(ns)
         pad = torch.zeros(m, dtype=t.dtype, device=t.device)
         pad[: t.numel()] = t
         outs = [torch.empty_like(pad) for _ in range(self.world)]
-        self.dist.all_gather(outs, pad)
+        self.all_gather(outs, pad)
         return [o[:c] for o, c in zip(outs, ns)]
 
 
@@ -142,6 +172,23 @@ def exact_mean(y: torch.Tensor, comm: _Comm) -> float:
     return float(np.float32(math.ldexp(float(int(q.item())), -t) / float(n)))
 
 
+def exchange_columns(Xd: torch.Tensor, comm: _Comm):
+    """Row shards in, column slices out: rank r receives every rank's rows
+    (in rank order) of columns [r*per, (r+1)*per), per = ceil(F / world)
+    (padding columns are zero).  One all_to_all."""
+    n, F = Xd.shape
+    W = comm.world
+    per = (F + W - 1) // W
+    Xp = torch.zeros((n, per * W), dtype=Xd.dtype, device=Xd.device)
+    Xp[:, :F] = Xd
+    send = Xp.reshape(n, W, per).permute(1, 0, 2).contiguous().reshape(-1, per)
+    ns = comm.gather_var(torch.tensor([n], dtype=torch.int64, device=Xd.device))
+    counts = [int(c.item()) for c in ns]
+    recv = torch.empty((sum(counts), per), dtype=Xd.dtype, device=Xd.device)
+    comm.all_to_all_single(recv, send, counts, [n] * W)
+    return recv, per
+
+
 def sharded_quantile_edges(Xd: torch.Tensor, q: torch.Tensor, comm: _Comm) -> torch.Tensor:
     """Quantile edges [F, B-1] of every column of the row-sharded float
     matrix, bit-identical to torch.quantile over the full column
@@ -150,22 +197,10 @@ def sharded_quantile_edges(Xd: torch.Tensor, q: torch.Tensor, comm: _Comm) -> to
     F = Xd.shape[1]
     if not comm.on:
         return _quantile_columns(Xd, q)
-    W = comm.world
-    per = (F + W - 1) // W
-    Fp = per * W
-    Xp = torch.zeros((Xd.shape[0], Fp), dtype=Xd.dtype, device=Xd.device)
-    Xp[:, :F] = Xd
-    # send block w = my rows of columns [w*per, (w+1)*per)
-    send = Xp.reshape(Xd.shape[0], W, per).permute(1, 0, 2).contiguous()
-    ns = comm.gather_var(torch.tensor([Xd.shape[0]], dtype=torch.int64, device=Xd.device))
-    counts = [int(c.item()) for c in ns]
-    recv = torch.empty((sum(counts), per), dtype=Xd.dtype, device=Xd.device)
-    comm.dist.all_to_all_single(recv, send.reshape(-1, per),
-                                output_split_sizes=counts,
-                                input_split_sizes=[Xd.shape[0]] * W)
-    mine = _quantile_columns(recv, q)                      # [per, B-1]
-    outs = [torch.empty_like(mine) for _ in range(W)]
-    comm.dist.all_gather(outs, mine)
+    cols, per = exchange_columns(Xd, comm)
+    mine = _quantile_columns(cols, q)                      # [per, B-1]
+    outs = [torch.empty_like(mine) for _ in range(comm.world)]
+    comm.all_gather(outs, mine)
     return torch.cat(outs, 0)[:F].contiguous()
 
 
