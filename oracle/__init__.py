@@ -57,6 +57,7 @@ def lib():
     sig = {
         "orc_bin_matrix": [_p, _i64, _i64, _i64, _p, _i32, _p, _i64],
         "orc_quantile_edges": [_p, _i64, _i64, _p, _i32, _p],
+        "orc_quantile_edges_matrix": [_p, _i64, _i64, _i64, _p, _i32, _p],
         "orc_hist_ref": [_p, _i64, _p, _p, _i64, _p, _i32, _p, _i32, _i32, _p, _p],
         "orc_quant_shift": [_f32],
         "orc_quantize": [_p, _i64, _i32, _p],
@@ -115,6 +116,16 @@ def quantile_edges(col: np.ndarray, q: np.ndarray) -> np.ndarray:
     q = _c(q, np.float32)
     out = np.empty(len(q), np.float32)
     lib().orc_quantile_edges(_ptr(col), col.shape[0], 1, _ptr(q), len(q), _ptr(out))
+    return out
+
+
+def quantile_edges_matrix(X: np.ndarray, q: np.ndarray) -> np.ndarray:
+    """quantile_edges of every column (OpenMP over columns), [F, len(q)]."""
+    X = _c(X, np.float32)
+    q = _c(q, np.float32)
+    n, F = X.shape
+    out = np.empty((F, len(q)), np.float32)
+    lib().orc_quantile_edges_matrix(_ptr(X), n, F, F, _ptr(q), len(q), _ptr(out))
     return out
 
 

@@ -87,6 +87,17 @@ void orc_quantile_edges(const float *col, int64_t n, int64_t stride,
     free(s);
 }
 
+/* Every column of a row-major matrix, parallel over columns (the CPU
+ * baseline's binning step; each column as orc_quantile_edges). */
+void orc_quantile_edges_matrix(const float *X, int64_t n, int64_t F,
+                               int64_t x_stride, const float *q, int nq,
+                               float *out)
+{
+#pragma omp parallel for schedule(dynamic, 1)
+    for (int64_t f = 0; f < F; ++f)
+        orc_quantile_edges(X + f, n, x_stride, q, nq, out + f * nq);
+}
+
 /* ------------------------------------------------------------------------ */
 /* Histograms                                                                */
 /* ------------------------------------------------------------------------ */
