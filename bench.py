@@ -26,6 +26,7 @@ import os
 import statistics
 import subprocess
 import sys
+import tempfile
 import time
 
 import numpy as np
@@ -79,11 +80,11 @@ class Clocks:
     def __init__(self, index: int):
         self.index = index
         self.proc = None
-        self.path = os.path.join(ROOT, "gpurun_out", f"clocks_{os.getpid()}.csv")
+        fd, self.path = tempfile.mkstemp(prefix="wgb_clocks_", suffix=".csv")
+        os.close(fd)
 
     def __enter__(self):
         try:
-            os.makedirs(os.path.dirname(self.path), exist_ok=True)
             self.f = open(self.path, "w")
             self.proc = subprocess.Popen(
                 ["nvidia-smi", f"--id={self.index}",
@@ -196,8 +197,8 @@ def run_reference(args, rank):
     yh = (Xh[:, :20] @ w + 0.3 * np.sin(Xh[:, 20:30]).sum(1) + rng.normal(0, 0.5, n)).astype(np.float32)
     import oracle as O
     q = O.linspace_q(CONFIG["num_bins"])
-    # edges for the sample tree's bins from a 50k-row subsample (the timed
-    # sample below recomputes exact edges for 20 columns)
+    # bins for the sample tree from edges of a 50k-row subsample (untimed;
+    # the timed sample recomputes exact edges of every column)
     sub = Xh[:: max(1, n // 50_000)]
     edges = np.stack([O.quantile_edges(sub[:, f], q) for f in range(F)])
     bins = O.bin_matrix(Xh, edges)
