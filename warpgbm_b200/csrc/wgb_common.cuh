@@ -157,4 +157,34 @@ __device__ __forceinline__ int block_min(int v, int *scratch /* >= 33 ints */) {
     return r;
 }
 
+// Exclusive prefix sum over the block (blockDim.x a multiple of 32, at most
+// 1024); `total` receives the block's sum.  Every thread calls it.
+__device__ __forceinline__ int block_scan_excl(int v, int *scratch /* >= 33 ints */, int &total) {
+    const int lane = threadIdx.x & 31, w = threadIdx.x >> 5, nw = blockDim.x >> 5;
+    int incl = v;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+        const int t = __shfl_up_sync(0xffffffffu, incl, o);
+        if (lane >= o) incl += t;
+    }
+    if (lane == 31) scratch[w] = incl;
+    __syncthreads();
+    if (w == 0) {
+        const int t = lane < nw ? scratch[lane] : 0;
+        int ti = t;
+#pragma unroll
+        for (int o = 1; o < 32; o <<= 1) {
+            const int u = __shfl_up_sync(0xffffffffu, ti, o);
+            if (lane >= o) ti += u;
+        }
+        scratch[lane] = ti - t;
+        if (lane == 31) scratch[32] = ti;
+    }
+    __syncthreads();
+    const int r = scratch[w] + incl - v;
+    total = scratch[32];
+    __syncthreads();
+    return r;
+}
+
 }  // namespace wgb

@@ -124,24 +124,18 @@ __global__ void __launch_bounds__(1024) k_chunk_plan(const wgb_node *__restrict_
                                                      int *nchunks, int cap) {
     __shared__ int s_cnt[1024];
     __shared__ int s_off[1025];
-    __shared__ int s_base;
+    __shared__ int s_scan[33];
     int nnd = *nn_d;
-    if (threadIdx.x == 0) s_base = 0;
-    __syncthreads();
+    int base = 0;
     for (int b0 = 0; b0 < nnd; b0 += 1024) {
         int i = b0 + threadIdx.x;
         int c = 0;
         if (i < nnd && lvl[i].built) c = (lvl[i].lcnt + HIST_R - 1) / HIST_R;
         s_cnt[threadIdx.x] = c;
-        __syncthreads();
-        if (threadIdx.x == 0) {
-            int acc = s_base;
-            for (int t = 0; t < 1024; ++t) {
-                s_off[t] = acc;
-                acc += s_cnt[t];
-            }
-            s_off[1024] = acc;
-        }
+        int tot;
+        const int ex = block_scan_excl(c, s_scan, tot);
+        s_off[threadIdx.x] = base + ex;
+        if (threadIdx.x == 0) s_off[1024] = base + tot;
         __syncthreads();
         int lo = s_off[0], hi = s_off[1024];
         for (int c2 = lo + threadIdx.x; c2 < hi; c2 += 1024) {
@@ -159,10 +153,9 @@ __global__ void __launch_bounds__(1024) k_chunk_plan(const wgb_node *__restrict_
             if (c2 < cap) chunks[c2] = make_int4(node, p0, p1, 0);
         }
         __syncthreads();
-        if (threadIdx.x == 0) s_base = hi;
-        __syncthreads();
+        base = hi;
     }
-    if (threadIdx.x == 0) *nchunks = min(s_base, cap);
+    if (threadIdx.x == 0) *nchunks = min(base, cap);
 }
 
 // One CTA = one chunk (<= HIST_R rows of one node) x one tile of 32*FPL
@@ -606,25 +599,15 @@ __global__ void __launch_bounds__(256) k_split_final(
 // child in a fresh slot 2^d + r, the sibling in the parent's slot.
 __global__ void __launch_bounds__(1024) k_plan_next(wgb_node *__restrict__ lvl, wgb_node *__restrict__ nxt,
                                                     int *nn, int d, const int *shift) {
-    __shared__ int s_f[1024];
-    __shared__ int s_base;
+    __shared__ int s_scan[33];
     const int nnd = nn[d];
     const float inv = pow2f(-*shift);
-    if (threadIdx.x == 0) s_base = 0;
-    __syncthreads();
+    int base = 0;
     for (int b0 = 0; b0 < nnd; b0 += 1024) {
         int i = b0 + threadIdx.x;
         int f = (i < nnd && lvl[i].fpos >= 0) ? 1 : 0;
-        s_f[threadIdx.x] = f;
-        __syncthreads();
-        // inclusive scan (Hillis-Steele)
-        for (int o = 1; o < 1024; o <<= 1) {
-            int v = threadIdx.x >= o ? s_f[threadIdx.x - o] : 0;
-            __syncthreads();
-            s_f[threadIdx.x] += v;
-            __syncthreads();
-        }
-        int r = s_base + s_f[threadIdx.x] - f;
+        int tot;
+        int r = base + block_scan_excl(f, s_scan, tot);
         if (f) {
             wgb_node &p = lvl[i];
             p.child = 2 * r;
@@ -647,11 +630,9 @@ __global__ void __launch_bounds__(1024) k_plan_next(wgb_node *__restrict__ lvl, 
         } else if (i < nnd) {
             lvl[i].child = -1;
         }
-        __syncthreads();
-        if (threadIdx.x == 1023) s_base = r + f;
-        __syncthreads();
+        base += tot;
     }
-    if (threadIdx.x == 0) nn[d + 1] = 2 * s_base;
+    if (threadIdx.x == 0) nn[d + 1] = 2 * base;
 }
 
 // ====================================================================== //
@@ -692,27 +673,17 @@ __global__ void __launch_bounds__(PART_THREADS) k_flags(
 
 // exclusive scan of tile counts (one block)
 __global__ void __launch_bounds__(1024) k_scan_tiles(const int *tile_cnt, int *tile_off, int ntiles) {
-    __shared__ int s[1024];
-    __shared__ int s_base;
-    if (threadIdx.x == 0) s_base = 0;
-    __syncthreads();
+    __shared__ int s_scan[33];
+    int base = 0;
     for (int b0 = 0; b0 < ntiles; b0 += 1024) {
         int i = b0 + threadIdx.x;
         int v = i < ntiles ? tile_cnt[i] : 0;
-        s[threadIdx.x] = v;
-        __syncthreads();
-        for (int o = 1; o < 1024; o <<= 1) {
-            int t = threadIdx.x >= o ? s[threadIdx.x - o] : 0;
-            __syncthreads();
-            s[threadIdx.x] += t;
-            __syncthreads();
-        }
-        if (i < ntiles) tile_off[i] = s_base + s[threadIdx.x] - v;
-        __syncthreads();
-        if (threadIdx.x == 1023) s_base += s[1023];
-        __syncthreads();
+        int tot;
+        const int ex = block_scan_excl(v, s_scan, tot);
+        if (i < ntiles) tile_off[i] = base + ex;
+        base += tot;
     }
-    if (threadIdx.x == 0) tile_off[ntiles] = s_base;  // total, for p == end
+    if (threadIdx.x == 0) tile_off[ntiles] = base;  // total, for p == end
 }
 
 // lefts before position p (p may equal nact)
@@ -742,23 +713,15 @@ __global__ void __launch_bounds__(1024) k_node_offsets(wgb_node *__restrict__ lv
         if (lane == 0) part[n] = make_int4(a, 0, b - a, 0);
     }
     __syncthreads();
-    __shared__ int s[1024];
-    __shared__ int s_base;
-    if (threadIdx.x == 0) s_base = 0;
-    __syncthreads();
+    __shared__ int s_scan[33];
+    int base = 0;
     for (int b0 = 0; b0 < nnd; b0 += 1024) {
         int i = b0 + threadIdx.x;
         int v = (i < nnd && lvl[i].fpos >= 0) ? lvl[i].lcnt : 0;
-        s[threadIdx.x] = v;
-        __syncthreads();
-        for (int o = 1; o < 1024; o <<= 1) {
-            int t = threadIdx.x >= o ? s[threadIdx.x - o] : 0;
-            __syncthreads();
-            s[threadIdx.x] += t;
-            __syncthreads();
-        }
+        int tot;
+        const int ex = block_scan_excl(v, s_scan, tot);
         if (v > 0 || (i < nnd && lvl[i].fpos >= 0)) {
-            int ns = s_base + s[threadIdx.x] - v;
+            int ns = base + ex;
             int4 pr = part[i];
             pr.y = ns;
             part[i] = pr;
@@ -768,11 +731,9 @@ __global__ void __launch_bounds__(1024) k_node_offsets(wgb_node *__restrict__ lv
             nxt[c + 1].lstart = ns + pr.z;
             nxt[c + 1].lcnt = v - pr.z;
         }
-        __syncthreads();
-        if (threadIdx.x == 1023) s_base += s[1023];
-        __syncthreads();
+        base += tot;
     }
-    if (threadIdx.x == 0) nact[d + 1] = s_base;
+    if (threadIdx.x == 0) nact[d + 1] = base;
 }
 
 // Scatter rows into the next level's order; finished rows get their leaf

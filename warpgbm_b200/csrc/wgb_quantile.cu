@@ -16,6 +16,7 @@
 namespace wgb {
 
 constexpr int QS_NT = 512;      // threads per column CTA
+constexpr int QS_U = 8;         // elements per thread per sweep step (loads in flight)
 constexpr int QS_MAXQ = 32;     // quantiles per sweep (64 target ranks)
 constexpr int QS_MAXT = 2 * QS_MAXQ;
 constexpr size_t QS_SMEM = QS_MAXT * 256 * 4 + 2 * QS_MAXT * 256 * 2;
@@ -130,15 +131,19 @@ __global__ void __launch_bounds__(QS_NT) k_qselect(const float *__restrict__ XT,
         if (tid == 0) s_nan = 0;
         __syncthreads();
         int nan_seen = 0;
-        for (long long base = (long long)warp * 32; base < n; base += QS_NT) {
-            const long long i = base + lane;
-            int key = -1;
-            if (i < n) {
-                const uint32_t b = __ldg(colb + i);
-                nan_seen |= (b & 0x7FFFFFFFu) > 0x7F800000u;
-                key = (int)(f2key(b) >> 24);
+        for (long long base = (long long)warp * 32 * QS_U; base < n; base += (long long)QS_NT * QS_U) {
+            uint32_t b[QS_U];
+#pragma unroll
+            for (int u = 0; u < QS_U; ++u) {
+                const long long i = base + 32 * u + lane;
+                b[u] = i < n ? __ldg(colb + i) : 0xFFFFFFFFu;  // marker: past the column end
             }
-            qs_count(hist + warp * 256, key);
+#pragma unroll
+            for (int u = 0; u < QS_U; ++u) {
+                const bool in = base + 32 * u + lane < n;
+                nan_seen |= in && (b[u] & 0x7FFFFFFFu) > 0x7F800000u;
+                qs_count(hist + warp * 256, in ? (int)(f2key(b[u]) >> 24) : -1);
+            }
         }
         if (__syncthreads_or(nan_seen)) {  // torch: every rank -> n-1 (the NaN)
             for (int j = tid; j < nq; j += QS_NT) edges[(long long)f * nq + j] = __int_as_float(0x7fc00000);
@@ -203,17 +208,25 @@ __global__ void __launch_bounds__(QS_NT) k_qselect(const float *__restrict__ XT,
                 }
             }
             __syncthreads();
-            for (long long base = (long long)warp * 32; base < n; base += QS_NT) {
-                const long long i = base + lane;
-                int key = -1;
-                if (i < n) {
-                    const uint32_t k = f2key(__ldg(colb + i));
-                    int s = tbl1[k >> 24];
-                    if (s >= 0 && p >= 2) s = tbl2[s * 256 + ((k >> 16) & 0xFF)];
-                    if (s >= 0 && p >= 3) s = tbl3[s * 256 + ((k >> 8) & 0xFF)];
-                    if (s >= 0) key = s * 256 + (int)((k >> (sh_hi - 8)) & 0xFF);
+            for (long long base = (long long)warp * 32 * QS_U; base < n; base += (long long)QS_NT * QS_U) {
+                uint32_t b[QS_U];
+#pragma unroll
+                for (int u = 0; u < QS_U; ++u) {
+                    const long long i = base + 32 * u + lane;
+                    b[u] = i < n ? __ldg(colb + i) : 0u;
                 }
-                qs_count(hist, key);
+#pragma unroll
+                for (int u = 0; u < QS_U; ++u) {
+                    int key = -1;
+                    if (base + 32 * u + lane < n) {
+                        const uint32_t k = f2key(b[u]);
+                        int s = tbl1[k >> 24];
+                        if (s >= 0 && p >= 2) s = tbl2[s * 256 + ((k >> 16) & 0xFF)];
+                        if (s >= 0 && p >= 3) s = tbl3[s * 256 + ((k >> 8) & 0xFF)];
+                        if (s >= 0) key = s * 256 + (int)((k >> (sh_hi - 8)) & 0xFF);
+                    }
+                    if (__any_sync(0xffffffffu, key >= 0)) qs_count(hist, key);  // warp-uniform
+                }
             }
             __syncthreads();
             for (int t = warp; t < nt; t += NW) {
