@@ -140,7 +140,8 @@ int wgb_bin_matrix(const float *X, int64_t n, int32_t F, int64_t x_stride,
  * q[j]) with linear interpolation, bit for bit (q = linspace(0, 1, B+1)[1:-1]
  * as the reference builds it, warpgbm/core.py:529-534; any NaN in a column
  * makes its edges NaN).  Radix selection of the 2*nq order statistics, no
- * sort.  XT is caller scratch of n*F floats (the column-major copy).
+ * sort.  XT is caller scratch of F*ld floats, ld = n rounded up to a
+ * multiple of 4 (the column-major copy), 16-byte aligned.
  * n <= 2^24 (torch's limit). */
 int wgb_quantile_edges(const float *X, int64_t n, int32_t F, int64_t x_stride,
                        const float *q, int32_t nq, float *XT, float *edges,

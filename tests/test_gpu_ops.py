@@ -42,6 +42,44 @@ def test_bin_matrix_matches_oracle(cuda, n, F, B):
     assert (got[:, F:] == 0).all()
 
 
+@pytest.mark.parametrize("F,xs", [(64, 64), (61, 61), (40, 45)])
+@pytest.mark.parametrize("B", [2, 9, 32, 127])
+def test_bin_matrix_edge_lists(cuda, F, xs, B):
+    """Binning against the oracle's leading-edge scan for edge lists of every
+    shape: sorted, with ties, with infinities, unsorted, all-NaN, one NaN;
+    aligned (16-byte row loads) and unaligned rows."""
+    rng = np.random.default_rng(F * 1000 + B)
+    n, nb = 3001, B - 1
+    Xw = rng.standard_normal((n, xs)).astype(np.float32) * 2
+    Xw[rng.random((n, xs)) < 0.02] = np.nan
+    Xw[rng.random((n, xs)) < 0.02] = np.inf
+    Xw[rng.random((n, xs)) < 0.02] = -np.inf
+    Xw[rng.random((n, xs)) < 0.05] = 0.0
+    edges = np.sort(rng.standard_normal((F, nb)).astype(np.float32) * 2, axis=1)
+    for f in range(F):
+        kind = f % 6
+        if kind == 1:
+            edges[f] = np.round(edges[f])                        # ties
+        elif kind == 2:
+            edges[f, : nb // 3] = -np.inf                        # infinities
+            edges[f, nb - nb // 4:] = np.inf
+        elif kind == 3 and nb > 1:
+            edges[f] = rng.permutation(edges[f])                 # unsorted
+        elif kind == 4:
+            edges[f] = np.nan                                    # all NaN
+        elif kind == 5 and nb > 2:
+            edges[f, nb // 2] = np.nan                           # one NaN
+    S = bins_stride(F)
+    out = torch.full((n, S), 99, dtype=torch.int8, device=cuda)
+    Xd = torch.from_numpy(Xw).to(cuda)
+    ed = torch.from_numpy(edges).to(cuda)
+    _lib.call("wgb_bin_matrix", Xd.data_ptr(), n, F, xs, ed.data_ptr(), B, out.data_ptr(), S, _st())
+    got = out.cpu().numpy()
+    ref = O.bin_matrix(np.ascontiguousarray(Xw[:, :F]), edges)
+    assert np.array_equal(got[:, :F], ref)
+    assert (got[:, F:] == 0).all()
+
+
 def test_torch_cuda_quantile_equals_oracle(cuda):
     """Pins the oracle's quantile restatement (FMA lerp, linspace formula) to
     torch.quantile on the B200 -- the op the reference calls at core.py:532."""

@@ -213,8 +213,9 @@ def _quantile_columns(Xd: torch.Tensor, q: torch.Tensor, chunk_elems: int = 1 <<
         raise ValueError("quantile() input tensor is too large")  # torch's own limit
     Xd = Xd.contiguous()
     out = torch.empty((F, q.numel()), dtype=torch.float32, device=Xd.device)
-    step = max(1, min(F, chunk_elems // max(n, 1)))
-    XT = torch.empty(n * step, dtype=torch.float32, device=Xd.device)
+    step = max(1, min(F, chunk_elems // max(n + 3, 1)))
+    ld = (n + 3) // 4 * 4                                  # 16-byte aligned columns
+    XT = torch.empty(ld * step, dtype=torch.float32, device=Xd.device)
     qd = q.contiguous()
     st = torch.cuda.current_stream().cuda_stream
     for c0 in range(0, F, step):

@@ -8,53 +8,77 @@ namespace wgb {
 // binning                                                                //
 // ====================================================================== //
 
-// Row-major float [n][F] -> int8 [n][out_stride] in one pass.  CTA = 64 rows x
-// 128 features; the tile's edges sit in shared memory edge-major ([b][128])
-// so each thread reads its 4 features' edges as one conflict-free float4.
-// Per element the reference scan (binner.cu:20-23): count leading edges with
-// x >= edge, stopping at the first failure.
-constexpr int BIN_FT = 128, BIN_ROWS = 64;
+// Row-major float [n][F] -> int8 [n][out_stride] in one pass.  CTA = 256
+// rows x 128 features; lane l of a warp bins features 4l..4l+3 of one row.
+// Per element the reference scan (binner.cu:20-23) counts leading edges with
+// x >= edge, stopping at the first failure.  When a feature's edges are
+// non-decreasing (always true for quantile edges; all-NaN edges included,
+// where every comparison fails) that count is found by binary search; any
+// other edge list keeps the linear scan.  Edges sit in shared memory
+// feature-major with an odd stride ([128][nb | 1]).
+constexpr int BIN_FT = 128, BIN_ROWS = 256;
+
+__device__ __forceinline__ int bin_linear(float x, const float *e, int nb) {
+    int b = 0;
+    while (b < nb && x >= e[b]) ++b;
+    return b;
+}
 
 __global__ void __launch_bounds__(256) k_bin_matrix(const float *__restrict__ X, long long n, int F,
                                                     long long xs, const float *__restrict__ edges,
                                                     int nb, int8_t *__restrict__ out, long long os) {
-    extern __shared__ float4 s_e4[];  // [nb][BIN_FT/4]
-    float *s_e = reinterpret_cast<float *>(s_e4);
+    extern __shared__ float s_e[];  // [BIN_FT][es]
+    __shared__ int s_mono[BIN_FT];
+    const int es = nb | 1;
     const int f0 = blockIdx.y * BIN_FT;
-    for (int t = threadIdx.x; t < nb * BIN_FT; t += blockDim.x) {
-        int b = t / BIN_FT, fl = t - b * BIN_FT;
-        int f = f0 + fl;
-        s_e[t] = f < F ? edges[(long long)f * nb + b] : 0.0f;
+    for (int t = threadIdx.x; t < BIN_FT * nb; t += blockDim.x) {
+        const int fl = t / nb, b = t - fl * nb;
+        const int f = f0 + fl;
+        s_e[fl * es + b] = f < F ? edges[(long long)f * nb + b] : 0.0f;
     }
     __syncthreads();
-    const int tl = threadIdx.x & 31;           // feature quad within the tile
+    for (int fl = threadIdx.x; fl < BIN_FT; fl += blockDim.x) {
+        const float *e = s_e + fl * es;
+        bool all_nan = true, mono = true;
+        for (int b = 0; b < nb; ++b) all_nan &= isnan(e[b]);
+        for (int b = 0; b + 1 < nb; ++b) mono &= e[b] <= e[b + 1];
+        s_mono[fl] = all_nan || mono;
+    }
+    __syncthreads();
+    const int tl = threadIdx.x & 31;  // feature quad within the tile
     const int f = f0 + 4 * tl;
     if (f >= os) return;
+    const bool vec = (xs % 4 == 0) && (f + 4 <= F);
+    const bool mono = s_mono[4 * tl] && s_mono[4 * tl + 1] && s_mono[4 * tl + 2] && s_mono[4 * tl + 3];
+    int top = 1;
+    while (top * 2 <= nb) top *= 2;  // largest power of two <= nb
     const long long r0 = (long long)blockIdx.x * BIN_ROWS;
     for (int rr = threadIdx.x >> 5; rr < BIN_ROWS; rr += blockDim.x >> 5) {
-        long long r = r0 + rr;
+        const long long r = r0 + rr;
         if (r >= n) break;
         const float *xr = X + r * xs;
         float v[4];
+        if (vec) {
+            const float4 x4 = __ldg(reinterpret_cast<const float4 *>(xr + f));
+            v[0] = x4.x; v[1] = x4.y; v[2] = x4.z; v[3] = x4.w;
+        } else {
 #pragma unroll
-        for (int j = 0; j < 4; ++j) v[j] = (f + j < F) ? __ldg(xr + f + j) : 0.0f;
-        int bin[4] = {0, 0, 0, 0};
-        bool go[4] = {true, true, true, true};
-        for (int b = 0; b < nb; ++b) {
-            float4 e = s_e4[b * (BIN_FT / 4) + tl];
-            go[0] = go[0] && (v[0] >= e.x);
-            go[1] = go[1] && (v[1] >= e.y);
-            go[2] = go[2] && (v[2] >= e.z);
-            go[3] = go[3] && (v[3] >= e.w);
-            bin[0] += go[0];
-            bin[1] += go[1];
-            bin[2] += go[2];
-            bin[3] += go[3];
+            for (int j = 0; j < 4; ++j) v[j] = (f + j < F) ? __ldg(xr + f + j) : 0.0f;
         }
         uint32_t w = 0;
 #pragma unroll
-        for (int j = 0; j < 4; ++j)
-            if (f + j < F) w |= (uint32_t)(uint8_t)bin[j] << (8 * j);
+        for (int j = 0; j < 4; ++j) {
+            const float *e = s_e + (4 * tl + j) * es;
+            int b;
+            if (mono) {
+                b = 0;
+                for (int step = top; step >= 1; step >>= 1)
+                    if (b + step <= nb && v[j] >= e[b + step - 1]) b += step;
+            } else {
+                b = bin_linear(v[j], e, nb);
+            }
+            if (f + j < F) w |= (uint32_t)(uint8_t)b << (8 * j);
+        }
         *reinterpret_cast<uint32_t *>(out + r * os + f) = w;
     }
 }
@@ -272,7 +296,7 @@ int wgb_bin_matrix(const float *X, int64_t n, int32_t F, int64_t x_stride, const
     if (n == 0) return WGB_OK;
     WGB_CHECK_ARG(X && edges && out, "NULL pointer");
     const int nb = num_bins - 1;
-    size_t smem = (size_t)nb * BIN_FT * sizeof(float);
+    size_t smem = (size_t)(nb | 1) * BIN_FT * sizeof(float);
     dim3 grid((unsigned)((n + BIN_ROWS - 1) / BIN_ROWS), (unsigned)((out_stride + BIN_FT - 1) / BIN_FT));
     WGB_CUDA(cudaFuncSetAttribute(k_bin_matrix, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
     k_bin_matrix<<<grid, 256, smem, as_stream(stream)>>>(X, n, F, x_stride, edges, nb, out, out_stride);

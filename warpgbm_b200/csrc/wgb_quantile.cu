@@ -7,26 +7,32 @@
 // lerp(sorted[below], sorted[above], w); any NaN in the column sets every
 // rank to n - 1 (the NaN), so all edges are NaN.  Only the 2 (B - 1) order
 // statistics are needed, so instead of a sort each column does a radix
-// select: four passes over the column, one 8-bit digit of the
+// select: four passes over the column, one digit of the
 // order-preserving key per pass, histogramming only elements whose higher
 // digits match a still-active target prefix.  Keys order exactly like the
 // radix sort torch uses (-0.0 before +0.0), so the selected elements -- and
 // the edges, computed with torch's lerp formula and one fused multiply-add
-// per branch -- are bit-identical.
+// per branch -- are bit-identical.  Digits are 12, 8, 8 and 4 bits wide.
 namespace wgb {
 
+// Digits of the 32-bit order-preserving key, high to low: 12, 8, 8, 4 bits.
+// The first digit (sign, exponent, 3 mantissa bits) spreads typical float
+// columns over many buckets, so plain shared atomics see little contention.
 constexpr int QS_NT = 512;      // threads per column CTA
-constexpr int QS_U = 8;         // elements per thread per sweep step (loads in flight)
+constexpr int QS_V = 4;         // 16-byte loads in flight per thread per sweep step
 constexpr int QS_MAXQ = 32;     // quantiles per sweep (64 target ranks)
 constexpr int QS_MAXT = 2 * QS_MAXQ;
-constexpr size_t QS_SMEM = QS_MAXT * 256 * 4 + 2 * QS_MAXT * 256 * 2;
+constexpr int QS_H0 = 4096;     // buckets of the first digit
+constexpr size_t QS_SMEM = QS_MAXT * 256 * 4 + QS_H0 + 2 * QS_MAXT * 256;  // hist | tbl12 | tbl8a | tbl8b
+constexpr uint8_t QS_NONE = 0xFF;
 
 __device__ __forceinline__ uint32_t f2key(uint32_t b) { return b ^ ((b >> 31) ? 0xFFFFFFFFu : 0x80000000u); }
 __device__ __forceinline__ uint32_t key2f(uint32_t k) { return k ^ ((k >> 31) ? 0x80000000u : 0xFFFFFFFFu); }
 
-// [f][r] = X[r][f]: 32 x 32 tiles through shared memory.
+// XT[f * ld + r] = X[r][f], ld = n rounded up to a multiple of 4 (every
+// column starts 16-byte aligned): 32 x 32 tiles through shared memory.
 __global__ void __launch_bounds__(256) k_transpose(const float *__restrict__ X, long long n, int F, long long xs,
-                                                   float *__restrict__ XT) {
+                                                   long long ld, float *__restrict__ XT) {
     __shared__ float t[32][33];
     const long long r0 = (long long)blockIdx.x * 32;
     const int f0 = blockIdx.y * 32;
@@ -40,37 +46,25 @@ __global__ void __launch_bounds__(256) k_transpose(const float *__restrict__ X, 
     for (int y = ty; y < 32; y += 8) {
         int f = f0 + y;
         long long r = r0 + tx;
-        if (f < F && r < n) XT[(long long)f * n + r] = t[tx][y];
+        if (f < F && r < n) XT[(long long)f * ld + r] = t[tx][y];
     }
 }
 
-// warp-aggregated histogram increment; key < 0 = no increment.  Every lane
-// of the warp calls it.
-__device__ __forceinline__ void qs_count(uint32_t *hist, int key) {
-    const unsigned m = __match_any_sync(0xffffffffu, key);
-    const int lane = threadIdx.x & 31;
-    if (key >= 0 && lane == __ffs(m) - 1) atomicAdd(hist + key, (uint32_t)__popc(m));
-}
-
-// Cumulative search of one 256-bucket row by one warp: bucket holding the
-// resid-th element (0-based), and the count before it.
+// Cumulative search of one L-bucket row by one warp: bucket holding the
+// resid-th element (0-based) and the count before it.
+template <int L>
 __device__ __forceinline__ void qs_find(const uint32_t *row, uint32_t resid, int &digit, uint32_t &before) {
+    constexpr int PER = L / 32;
     const int lane = threadIdx.x & 31;
-    uint32_t c[8];
     uint32_t s = 0;
-#pragma unroll
-    for (int i = 0; i < 8; ++i) {
-        c[i] = row[lane * 8 + i];
-        s += c[i];
-    }
+    for (int i = 0; i < PER; ++i) s += row[lane * PER + i];
     uint32_t incl = s;
 #pragma unroll
     for (int o = 1; o < 32; o <<= 1) {
         uint32_t v = __shfl_up_sync(0xffffffffu, incl, o);
         if (lane >= o) incl += v;
     }
-    uint32_t excl = incl - s;
-    // lane whose range [excl, incl) holds resid
+    const uint32_t excl = incl - s;
     const bool mine = resid >= excl && resid < incl;
     const unsigned who = __ballot_sync(0xffffffffu, mine);
     const int src = who ? __ffs(who) - 1 : 31;
@@ -78,14 +72,14 @@ __device__ __forceinline__ void qs_find(const uint32_t *row, uint32_t resid, int
     uint32_t b = 0;
     if (lane == src) {
         uint32_t acc = excl;
-        d = lane * 8 + 7;
-#pragma unroll
-        for (int i = 0; i < 8; ++i) {
-            if (resid < acc + c[i]) {
-                d = lane * 8 + i;
+        d = lane * PER + PER - 1;
+        for (int i = 0; i < PER; ++i) {
+            const uint32_t c = row[lane * PER + i];
+            if (resid < acc + c) {
+                d = lane * PER + i;
                 break;
             }
-            acc += c[i];
+            acc += c;
         }
         b = acc;
     }
@@ -93,26 +87,80 @@ __device__ __forceinline__ void qs_find(const uint32_t *row, uint32_t resid, int
     before = __shfl_sync(0xffffffffu, b, src);
 }
 
-__global__ void __launch_bounds__(QS_NT) k_qselect(const float *__restrict__ XT, long long n, const float *__restrict__ q,
-                                                   int nq, float *__restrict__ edges) {
-    extern __shared__ uint32_t qs_dyn[];        // hist | tbl2 | tbl3 (QS_SMEM bytes)
-    uint32_t *hist = qs_dyn;                    // [QS_MAXT][256]; pass 0: per-warp rows
-    short *tbl2 = reinterpret_cast<short *>(qs_dyn + QS_MAXT * 256);  // [QS_MAXT][256]
-    short *tbl3 = tbl2 + QS_MAXT * 256;                               // [QS_MAXT][256]
-    __shared__ short tbl1[256];
+// One sweep over the column for digit pass P (0..3): counts the digit of
+// every element whose higher digits match a target prefix (slot tables of
+// the previous passes).  Pass 0 also reports NaNs.
+template <int P>
+__device__ __forceinline__ int qs_sweep(const uint4 *__restrict__ colv, long long n, uint32_t *hist,
+                                        const uint8_t *tbl12, const uint8_t *tbl8a, const uint8_t *tbl8b) {
+    const long long nvec = (n + 3) >> 2;
+    int nan_seen = 0;
+    for (long long v0 = threadIdx.x; v0 < nvec; v0 += (long long)QS_NT * QS_V) {
+        uint4 x[QS_V];
+#pragma unroll
+        for (int u = 0; u < QS_V; ++u) {
+            const long long v = v0 + (long long)u * QS_NT;
+            x[u] = v < nvec ? __ldg(colv + v) : make_uint4(0u, 0u, 0u, 0u);
+        }
+        uint32_t last = 0xFFFFFFFFu, run = 0;  // pass 0: runs of one bucket, one atomic per run
+#pragma unroll
+        for (int u = 0; u < QS_V; ++u) {
+            const long long e0 = (v0 + (long long)u * QS_NT) * 4;
+#pragma unroll
+            for (int c = 0; c < 4; ++c) {
+                if (e0 + c >= n) continue;
+                const uint32_t b = c == 0 ? x[u].x : c == 1 ? x[u].y : c == 2 ? x[u].z : x[u].w;
+                const uint32_t k = f2key(b);
+                if (P == 0) {
+                    nan_seen |= (b & 0x7FFFFFFFu) > 0x7F800000u;
+                    const uint32_t d = k >> 20;
+                    if (d != last) {
+                        if (run) atomicAdd(hist + last, run);
+                        last = d;
+                        run = 0;
+                    }
+                    ++run;
+                    continue;
+                }
+                uint32_t sl = tbl12[k >> 20];
+                if (sl == QS_NONE) continue;
+                if (P >= 2) {
+                    sl = tbl8a[sl * 256 + ((k >> 12) & 0xFF)];
+                    if (sl == QS_NONE) continue;
+                }
+                if (P >= 3) {
+                    sl = tbl8b[sl * 256 + ((k >> 4) & 0xFF)];
+                    if (sl == QS_NONE) continue;
+                }
+                const uint32_t d = P == 1 ? (k >> 12) & 0xFF : P == 2 ? (k >> 4) & 0xFF : k & 0xF;
+                atomicAdd(hist + sl * 256 + d, 1u);
+            }
+        }
+        if (P == 0 && run) atomicAdd(hist + last, run);
+    }
+    return nan_seen;
+}
+
+__global__ void __launch_bounds__(QS_NT, 2) k_qselect(const float *__restrict__ XT, long long n, long long ld,
+                                                      const float *__restrict__ q, int nq, float *__restrict__ edges) {
+    extern __shared__ __align__(16) uint32_t qs_dyn[];
+    uint32_t *hist = qs_dyn;                                            // [QS_MAXT][256] (pass 0: [QS_H0])
+    uint8_t *tbl12 = reinterpret_cast<uint8_t *>(qs_dyn + QS_MAXT * 256);  // 12-bit prefix -> pass-1 slot
+    uint8_t *tbl8a = tbl12 + QS_H0;                                     // [pass-1 slot][8 bits] -> pass-2 slot
+    uint8_t *tbl8b = tbl8a + QS_MAXT * 256;                             // [pass-2 slot][8 bits] -> pass-3 slot
     __shared__ int t_rank[QS_MAXT];
     __shared__ uint32_t t_key[QS_MAXT];     // resolved key prefix (high digits)
     __shared__ uint32_t t_resid[QS_MAXT];   // rank within the prefix's elements
     __shared__ int t_slot[QS_MAXT];
     __shared__ float t_w[QS_MAXQ];
-    __shared__ int s_nan, s_nslot;
+    __shared__ int s_nslot;
     __shared__ uint32_t s_pre[QS_MAXT];
 
     const int f = blockIdx.x;
-    const float *col = XT + (long long)f * n;
+    const uint4 *colv = reinterpret_cast<const uint4 *>(XT + (long long)f * ld);
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     constexpr int NW = QS_NT / 32;
-    const uint32_t *colb = reinterpret_cast<const uint32_t *>(col);
+    constexpr int SHIFT[4] = {20, 12, 4, 0};  // low bit of each pass's digit
 
     for (int q0 = 0; q0 < nq; q0 += QS_MAXQ) {
         const int nqs = min(QS_MAXQ, nq - q0);
@@ -126,115 +174,73 @@ __global__ void __launch_bounds__(QS_NT) k_qselect(const float *__restrict__ XT,
             t_rank[2 * tid + 1] = (int)hi;
             t_w[tid] = __fsub_rn(rank, (float)lo);
         }
-        // ---- pass 0: digit 0 histogram (per warp), NaN detection
-        for (int t = tid; t < NW * 256; t += QS_NT) hist[t] = 0;
-        if (tid == 0) s_nan = 0;
+        // ---- pass 0: first digit, NaN detection
+        for (int t = tid; t < QS_H0; t += QS_NT) hist[t] = 0;
         __syncthreads();
-        int nan_seen = 0;
-        for (long long base = (long long)warp * 32 * QS_U; base < n; base += (long long)QS_NT * QS_U) {
-            uint32_t b[QS_U];
-#pragma unroll
-            for (int u = 0; u < QS_U; ++u) {
-                const long long i = base + 32 * u + lane;
-                b[u] = i < n ? __ldg(colb + i) : 0xFFFFFFFFu;  // marker: past the column end
-            }
-#pragma unroll
-            for (int u = 0; u < QS_U; ++u) {
-                const bool in = base + 32 * u + lane < n;
-                nan_seen |= in && (b[u] & 0x7FFFFFFFu) > 0x7F800000u;
-                qs_count(hist + warp * 256, in ? (int)(f2key(b[u]) >> 24) : -1);
-            }
-        }
+        const int nan_seen = qs_sweep<0>(colv, n, hist, tbl12, tbl8a, tbl8b);
         if (__syncthreads_or(nan_seen)) {  // torch: every rank -> n-1 (the NaN)
             for (int j = tid; j < nq; j += QS_NT) edges[(long long)f * nq + j] = __int_as_float(0x7fc00000);
             return;
         }
-        // fold warp rows into row 0
-        for (int d = tid; d < 256; d += QS_NT) {
-            uint32_t s = 0;
-            for (int w = 0; w < NW; ++w) s += hist[w * 256 + d];
-            hist[d] = s;
-        }
-        __syncthreads();
-        // each target: digit 0 and residual rank (one warp per target)
         for (int t = warp; t < nt; t += NW) {
             int d;
             uint32_t before;
-            qs_find(hist, (uint32_t)t_rank[t], d, before);
+            qs_find<QS_H0>(hist, (uint32_t)t_rank[t], d, before);
             if (lane == 0) {
-                t_key[t] = (uint32_t)d << 24;
+                t_key[t] = (uint32_t)d << 20;
                 t_resid[t] = (uint32_t)t_rank[t] - before;
             }
         }
         __syncthreads();
         // ---- passes 1..3
+#pragma unroll
         for (int p = 1; p <= 3; ++p) {
-            const int sh_hi = 32 - 8 * p;        // bits above the digit of this pass
-            // distinct prefixes of this level -> slots (one thread, <= 64 targets)
-            if (tid == 0) {
+            const int sh = SHIFT[p - 1];     // the resolved prefix is key >> sh
+            if (tid == 0) {                  // distinct prefixes -> slots (<= 64 targets)
                 int ns = 0;
                 for (int t = 0; t < nt; ++t) {
-                    const uint32_t pre = t_key[t] >> sh_hi;
-                    int s = -1;
+                    const uint32_t pre = t_key[t] >> sh;
+                    int sl = -1;
                     for (int u = 0; u < ns; ++u)
-                        if (s_pre[u] == pre) { s = u; break; }
-                    if (s < 0) { s = ns; s_pre[ns++] = pre; }
-                    t_slot[t] = s;
+                        if (s_pre[u] == pre) { sl = u; break; }
+                    if (sl < 0) { sl = ns; s_pre[ns++] = pre; }
+                    t_slot[t] = sl;
                 }
                 s_nslot = ns;
             }
             __syncthreads();
             const int ns = s_nslot;
-            // lookup table of this level: element prefix -> slot
             if (p == 1) {
-                for (int t = tid; t < 256; t += QS_NT) tbl1[t] = -1;
-            } else if (p == 2) {
-                for (int t = tid; t < QS_MAXT * 256; t += QS_NT) tbl2[t] = -1;
+                for (int t = tid; t < QS_H0; t += QS_NT) tbl12[t] = QS_NONE;
             } else {
-                for (int t = tid; t < QS_MAXT * 256; t += QS_NT) tbl3[t] = -1;
+                uint8_t *tb = p == 2 ? tbl8a : tbl8b;
+                for (int t = tid; t < QS_MAXT * 256; t += QS_NT) tb[t] = QS_NONE;
             }
             for (int t = tid; t < ns * 256; t += QS_NT) hist[t] = 0;
             __syncthreads();
             if (tid < ns) {
                 const uint32_t pre = s_pre[tid];
                 if (p == 1) {
-                    tbl1[pre & 0xFF] = (short)tid;
+                    tbl12[pre] = (uint8_t)tid;
                 } else if (p == 2) {
-                    tbl2[tbl1[(pre >> 8) & 0xFF] * 256 + (pre & 0xFF)] = (short)tid;
+                    tbl8a[tbl12[pre >> 8] * 256 + (pre & 0xFF)] = (uint8_t)tid;
                 } else {
-                    const int s1 = tbl1[(pre >> 16) & 0xFF];
-                    const int s2 = tbl2[s1 * 256 + ((pre >> 8) & 0xFF)];
-                    tbl3[s2 * 256 + (pre & 0xFF)] = (short)tid;
+                    const int s1 = tbl12[pre >> 16];
+                    const int s2 = tbl8a[s1 * 256 + ((pre >> 8) & 0xFF)];
+                    tbl8b[s2 * 256 + (pre & 0xFF)] = (uint8_t)tid;
                 }
             }
             __syncthreads();
-            for (long long base = (long long)warp * 32 * QS_U; base < n; base += (long long)QS_NT * QS_U) {
-                uint32_t b[QS_U];
-#pragma unroll
-                for (int u = 0; u < QS_U; ++u) {
-                    const long long i = base + 32 * u + lane;
-                    b[u] = i < n ? __ldg(colb + i) : 0u;
-                }
-#pragma unroll
-                for (int u = 0; u < QS_U; ++u) {
-                    int key = -1;
-                    if (base + 32 * u + lane < n) {
-                        const uint32_t k = f2key(b[u]);
-                        int s = tbl1[k >> 24];
-                        if (s >= 0 && p >= 2) s = tbl2[s * 256 + ((k >> 16) & 0xFF)];
-                        if (s >= 0 && p >= 3) s = tbl3[s * 256 + ((k >> 8) & 0xFF)];
-                        if (s >= 0) key = s * 256 + (int)((k >> (sh_hi - 8)) & 0xFF);
-                    }
-                    if (__any_sync(0xffffffffu, key >= 0)) qs_count(hist, key);  // warp-uniform
-                }
-            }
+            if (p == 1) qs_sweep<1>(colv, n, hist, tbl12, tbl8a, tbl8b);
+            else if (p == 2) qs_sweep<2>(colv, n, hist, tbl12, tbl8a, tbl8b);
+            else qs_sweep<3>(colv, n, hist, tbl12, tbl8a, tbl8b);
             __syncthreads();
             for (int t = warp; t < nt; t += NW) {
                 int d;
                 uint32_t before;
-                qs_find(hist + t_slot[t] * 256, t_resid[t], d, before);
+                qs_find<256>(hist + t_slot[t] * 256, t_resid[t], d, before);
                 if (lane == 0) {
-                    t_key[t] |= (uint32_t)d << (sh_hi - 8);
+                    t_key[t] |= (uint32_t)d << SHIFT[p];
                     t_resid[t] -= before;
                 }
             }
@@ -263,12 +269,14 @@ extern "C" int wgb_quantile_edges(const float *X, int64_t n, int32_t F, int64_t 
     WGB_CHECK_ARG(n <= (1ll << 24), "quantile() input tensor is too large");
     WGB_CHECK_ARG(x_stride >= F, "x_stride < F");
     WGB_CHECK_ARG(X && q && XT && edges, "NULL pointer");
+    WGB_CHECK_ARG((reinterpret_cast<uintptr_t>(XT) & 15) == 0, "XT must be 16-byte aligned");
     cudaStream_t st = as_stream(stream);
+    const long long ld = (n + 3) & ~3ll;
     dim3 tg((unsigned)((n + 31) / 32), (unsigned)((F + 31) / 32));
-    k_transpose<<<tg, 256, 0, st>>>(X, n, F, x_stride, XT);
+    k_transpose<<<tg, 256, 0, st>>>(X, n, F, x_stride, ld, XT);
     WGB_LAUNCHED("k_transpose");
     WGB_CUDA(cudaFuncSetAttribute(k_qselect, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)QS_SMEM));
-    k_qselect<<<(unsigned)F, QS_NT, QS_SMEM, st>>>(XT, n, q, nq, edges);
+    k_qselect<<<(unsigned)F, QS_NT, QS_SMEM, st>>>(XT, n, ld, q, nq, edges);
     WGB_LAUNCHED("k_qselect");
     return WGB_OK;
 }
