@@ -37,6 +37,10 @@ sys.path.insert(0, ROOT)
 
 CONFIG = dict(n=1_000_000, F=1000, num_bins=32, max_depth=5, n_estimators=100,
               learning_rate=0.01)
+# DRAM bytes (read + write) per algorithmic byte of a k_hist launch, from an
+# ncu capture of a 300k-row x 1000-feature root launch (317.6 MB measured for
+# 302.8 MB algorithmic); the traffic grows with the rows processed.
+HIST_TRAFFIC_PER_ALG_BYTE = 1.049
 
 
 def parse():
@@ -322,7 +326,10 @@ def main():
             "roofline": {"bound": "hbm", "kernel": "k_hist (wgb_level_hist)",
                          "achieved": round(achieved, 1) if achieved else None, "peak": peak,
                          "unit": "GB/s", "frac": round(achieved / peak, 4) if achieved else None,
-                         "peak_kind": peak_kind, "traffic": None,
+                         "peak_kind": peak_kind,
+                         "traffic": round(HIST_TRAFFIC_PER_ALG_BYTE * hist_bytes / max(nlaunch * args.steps, 1))
+                         if hist_bytes else None,
+                         "traffic_unit": "bytes per launch (ncu ratio 1.049 x algorithmic)",
                          "launches_timed": nlaunch * args.steps,
                          "avg_launch_ms": round(hist_ms / max(nlaunch * args.steps, 1), 4)},
             "e2e": e2e,
