@@ -131,11 +131,13 @@ class Clocks:
                 "reasons": sorted(reasons), "samples": len(sm)}
 
 
-def hist_algorithmic_bytes(model, n_total: int, k: int, E: int, B: int) -> float:
-    """Bytes the histogram builds must move (algorithmic, from the grown
-    trees): per built node n_rows * (k bins + 4 B q + 4 B row id [+4 B era])
-    + its E*k*B*(8+4) B histogram; built nodes = root + the smaller child of
-    every split above the last level."""
+def hist_algorithmic_bytes(model, n_total: int, k: int, E: int, B: int, world: int = 1) -> float:
+    """Bytes the histogram builds of one rank must move (algorithmic, from
+    the grown trees): per built node n_rows * (k bins + 4 B q + 4 B row id
+    [+4 B era]) + its E*k*B*(8+4) B histogram; built nodes = root + the
+    smaller child of every split above the last level.  Node sizes in the
+    trees are global; with `world` ranks of equal shards a rank holds
+    1/world of each node's rows."""
     D = model.max_depth
     per_row = k + 8 + (4 if E > 1 else 0)
     per_node = E * k * B * 12
@@ -150,12 +152,12 @@ def hist_algorithmic_bytes(model, n_total: int, k: int, E: int, B: int) -> float
         if "leaf_value" in nd or d + 1 >= D:
             return
         cl, cr = count(nd["left"]), count(nd["right"])
-        total += (cl if cl <= cr else cr) * per_row + per_node
+        total += (cl if cl <= cr else cr) * per_row / world + per_node
         walk(nd["left"], d + 1)
         walk(nd["right"], d + 1)
 
     for t in model._flat_trees():
-        total += n_total * per_row + per_node
+        total += n_total * per_row / world + per_node
         walk(t, 0)
     return total
 
@@ -272,8 +274,8 @@ def main():
                 model._hist_events = []
                 model.fit(X, y)
                 hist_ms += sum(a.elapsed_time(b) for a, b in model._hist_events)
-                hist_bytes += hist_algorithmic_bytes(model, model._n_global // max(world, 1) if world > 1 else n,
-                                                     F, 1, CONFIG["num_bins"])
+                hist_bytes += hist_algorithmic_bytes(model, model._n_global if world > 1 else n,
+                                                     F, 1, CONFIG["num_bins"], world)
         e1.record()
         barrier()
     launches = _lib.LAUNCHES[0] - launches0

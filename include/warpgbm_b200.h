@@ -77,7 +77,7 @@ int wgb_compute_histogram3(const int8_t *bin_indices, int64_t num_rows,
  * Same arguments and result as wgb_compute_histogram3; its scratch is a
  * fixed 64 MiB block inside the library (reserved on every GPU where the
  * library's kernels are loaded, until the process exits).  A call needs
- * num_eras*k*(num_bins+1)*12 + F_master*4 + ceil(n/1024)*16 + 96 bytes (each
+ * num_eras*k*(num_bins+1)*16 + F_master*4 + ceil(n/1024)*16 + 96 bytes (each
  * part rounded up to 256); larger calls return WGB_ERR_ARG.  Calls share the
  * block, so calls that may overlap on the GPU race; calls on one stream are
  * safe.  The first call on a device looks up the block's address and should
@@ -190,8 +190,9 @@ typedef struct wgb_ws {
     int32_t *tile_off;       /* [ntiles]                                      */
     int32_t *part;           /* [2^D][4] per-node partition scratch           */
     /* histograms */
-    int64_t *hg;             /* [2^(D-1)][E][k][B+1] quantised grad sums      */
-    int32_t *hc;             /* [2^(D-1)][E][k][B+1] counts                   */
+    int64_t *hg;             /* histogram pool, 2^(D-1) slots of           */
+                             /*   2*E*k*(B+1) + 2 int64: [E][k][B+1] sums of */
+                             /*   q, [E][k][B+1] counts, root sum, spare     */
     /* chunk work list of the histogram build */
     int32_t *chunks;         /* [chunk_cap][4] = node, p0, p1, -              */
     int32_t *nchunks;        /* [1]                                           */
@@ -226,11 +227,15 @@ int wgb_tree_reset(const wgb_ws *ws, void *stream);
 /* Quantise g (shift from *maxabs, which must already be the global max),
  * sum q over local rows into *rootsum. */
 int wgb_tree_quantize(const wgb_ws *ws, void *stream);
-/* Root record (needs the global *rootsum) and level counters. */
+/* Root record (its sum and leaf are set at level 0's split) and level
+ * counters. */
 int wgb_tree_root(const wgb_ws *ws, void *stream);
 /* Level d: chunk plan, zero of the built slots, histogram build of the
  * built nodes from local rows.  Built slots of level d are the contiguous
- * range returned by wgb_built_slots (an all-reduce over ranks goes there). */
+ * range returned by wgb_built_slots; one int64 SUM all-reduce over ranks of
+ * hg[first*P, (first+count)*P), P = 2*E*k*(B+1) + 2, covers sums, counts
+ * and (level 0) the root's sum of q, which wgb_level_hist copies from
+ * *rootsum into the first spare cell of slot 0. */
 int wgb_level_hist(const wgb_ws *ws, int32_t d, void *stream);
 void wgb_built_slots(int32_t d, int32_t *first, int32_t *count);
 /* Level d: sibling = parent - built (in place), split search, per-era gains,

@@ -52,7 +52,7 @@ def test_noalloc_matches_regular_entry_point_twice(n, F, k, E, B):
 
 def test_noalloc_rejects_work_beyond_its_block():
     L = _lib.lib()
-    # 600 eras x 2000 features x 33 bins x 12 B = 475 MB of cells > 64 MiB;
+    # 600 eras x 2000 features x 33 bins x 16 B = 634 MB of cells > 64 MiB;
     # rejected before any pointer is touched
     rc = L.wgb_compute_histogram3_noalloc(None, 1, 2000, None, None, 10, None, 2000, None, None,
                                           None, 600, 32, 64, 4, None)

@@ -41,7 +41,7 @@ class WgbWs(ctypes.Structure):
         ("feats", _p), ("kpos", _p),
         ("order", _p * 2), ("posnode", _p * 2), ("flags", _p),
         ("tile_cnt", _p), ("tile_off", _p), ("part", _p),
-        ("hg", _p), ("hc", _p),
+        ("hg", _p),
         ("chunks", _p), ("nchunks", _p),
         ("cand", _p), ("era_gain", _p),
         ("nodes", _p), ("nn", _p), ("nact", _p),

@@ -541,7 +541,8 @@ class WarpGBM(BaseEstimator, RegressorMixin):
         S = bins_stride(F)
         nslots = 1 << (D - 1)
         se = E * k * (B + 1)
-        hist_bytes = nslots * se * 12
+        P = 2 * se + 2                  # int64 per slot: sums, counts, root sum, spare
+        hist_bytes = nslots * P * 8
         free, _ = torch.cuda.mem_get_info(dev)
         if hist_bytes > 0.6 * free:
             raise MemoryError(
@@ -559,8 +560,7 @@ class WarpGBM(BaseEstimator, RegressorMixin):
         t["tile_cnt"] = torch.empty(ntiles, **i32)
         t["tile_off"] = torch.empty(ntiles + 1, **i32)
         t["part"] = torch.empty((max(nslots, 1), 4), **i32)
-        t["hg"] = torch.empty(nslots * se, dtype=torch.int64, device=dev)
-        t["hc"] = torch.empty(nslots * se, **i32)
+        t["hg"] = torch.empty(nslots * P, dtype=torch.int64, device=dev)
         chunk_cap = (N + HIST_R - 1) // HIST_R + nslots
         t["chunks"] = torch.empty((max(chunk_cap, 1), 4), **i32)
         ncand = (k + SPLIT_THREADS - 1) // SPLIT_THREADS
@@ -581,7 +581,7 @@ class WarpGBM(BaseEstimator, RegressorMixin):
         ws = _lib.WgbWs()
         ws.order[0], ws.order[1] = t["order0"].data_ptr(), t["order1"].data_ptr()
         ws.posnode[0], ws.posnode[1] = t["posnode0"].data_ptr(), t["posnode1"].data_ptr()
-        for name in ("flags", "tile_cnt", "tile_off", "part", "hg", "hc", "chunks", "cand",
+        for name in ("flags", "tile_cnt", "tile_off", "part", "hg", "chunks", "cand",
                      "era_gain", "nodes", "rootsum", "g", "qg", "feats", "kpos", "nn", "nact",
                      "nchunks", "shift", "maxabs"):
             setattr(ws, name, t[name].data_ptr())
@@ -735,10 +735,8 @@ class WarpGBM(BaseEstimator, RegressorMixin):
         if comm.on:
             comm.max_(self._t["maxabs"])
         _lib.call("wgb_tree_quantize", p, st())
-        if comm.on:
-            comm.sum_(self._t["rootsum"])
         _lib.call("wgb_tree_root", p, st())
-        se = ws.E * ws.k * (ws.B + 1)
+        P = 2 * ws.E * ws.k * (ws.B + 1) + 2
         timer = getattr(self, "_hist_events", None)
         for d in range(self.max_depth):
             if timer is not None:
@@ -751,8 +749,7 @@ class WarpGBM(BaseEstimator, RegressorMixin):
                 timer.append((ev0, ev1))
             if comm.on:
                 first, count = _lib.built_slots(d)
-                comm.sum_(self._t["hg"][first * se:(first + count) * se])
-                comm.sum_(self._t["hc"][first * se:(first + count) * se])
+                comm.sum_(self._t["hg"][first * P:(first + count) * P])
             _lib.call("wgb_level_split", p, d, st())
             _lib.call("wgb_level_partition", p, d, st())
         _lib.call("wgb_tree_finish", p, st())

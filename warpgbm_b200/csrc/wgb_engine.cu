@@ -91,10 +91,12 @@ __global__ void k_quantize(const float *__restrict__ g, int *__restrict__ qg, lo
     }
 }
 
+// Root record; its sum of q and leaf are filled by k_root_total once the
+// level-0 histograms (which carry the root sum) are complete on every rank.
 __global__ void k_root(wgb_node *nodes, int *nn, int *nact, int D, long long n_local,
-                       long long n_global, const long long *rootsum, const int *shift) {
+                       long long n_global) {
     wgb_node r;
-    r.sumq = *rootsum;
+    r.sumq = 0;
     r.count = n_global;
     r.lsumq = 0;
     r.lcount = 0;
@@ -105,12 +107,18 @@ __global__ void k_root(wgb_node *nodes, int *nn, int *nact, int D, long long n_l
     r.fpos = -1;
     r.bin = 0;
     r.child = -1;
-    r.leaf = canon_leaf(r.sumq, r.count, pow2f(-*shift));
+    r.leaf = 0.0f;
     nodes[0] = r;
     for (int d = 0; d <= D; ++d) {
         nn[d] = d == 0 ? 1 : 0;
         nact[d] = d == 0 ? (int)n_local : 0;
     }
+}
+
+__global__ void k_root_total(wgb_node *nodes, const long long *root_cell, const int *shift) {
+    wgb_node &r = nodes[0];
+    r.sumq = *root_cell;
+    r.leaf = canon_leaf(r.sumq, r.count, pow2f(-*shift));
 }
 
 // ====================================================================== //
@@ -214,7 +222,7 @@ __global__ void __launch_bounds__(NT, MINB) k_hist(
     const int *__restrict__ q, const float *__restrict__ g, const int *shift,
     const int *__restrict__ era, const int *__restrict__ kpos, int k, int E, int B, int EW,
     const int4 *__restrict__ chunks, const int *nchunks, const wgb_node *__restrict__ lvl,
-    long long *__restrict__ hg, int *__restrict__ hc, long long slot_elems, long long nrows) {
+    long long *__restrict__ hg, long long *__restrict__ hc, long long slot_elems, long long nrows) {
     constexpr int FT = 32 * FPL;             // features per tile
     constexpr int U = (FPL >= 16 || MINB > 1) ? 4 : 8;  // rows per pipeline step per warp
     constexpr int NW = NT / 32;
@@ -363,7 +371,7 @@ __global__ void __launch_bounds__(NT, MINB) k_hist(
                 const long long gs = (long long)(int)Be[wi] * 2048 + (long long)(a & 0x1FFFFFu);
                 const long long idx = ebase + (long long)kp * B1 + sl;
                 atomicAdd(reinterpret_cast<unsigned long long *>(hg + idx), (unsigned long long)gs);
-                atomicAdd(hc + idx, cntv);
+                atomicAdd(reinterpret_cast<unsigned long long *>(hc + idx), (unsigned long long)cntv);
             }
         }
         if (!HAS_ERA) break;
@@ -383,7 +391,7 @@ static cudaError_t launch_hist(int grid_x, const int8_t *bins, long long S, int 
                                const int *q, const float *g, const int *shift, const int *era,
                                const int *kpos, int k, int E, int B, int EW, bool regular,
                                const int4 *chunks, const int *nchunks, const wgb_node *lvl,
-                               long long *hg, int *hc, long long slot_elems, long long nrows,
+                               long long *hg, long long *hc, long long slot_elems, long long nrows,
                                cudaStream_t st) {
     const bool has_era = E > 1;
     int fpl = 4;
@@ -422,8 +430,8 @@ static cudaError_t launch_hist(int grid_x, const int8_t *bins, long long S, int 
 
 // sibling = parent - built, in place of the parent's slot (the sibling
 // inherits it).  grid.y = pair.
-__global__ void k_subtract(const wgb_node *__restrict__ lvl, const int *nn_d, long long *hg, int *hc,
-                           long long slot_elems) {
+__global__ void k_subtract(const wgb_node *__restrict__ lvl, const int *nn_d, long long *hg, long long *hc,
+                           long long slot_elems, long long ncell) {
     int p = blockIdx.y;
     if (2 * p + 1 >= *nn_d) return;
     const wgb_node &a = lvl[2 * p], &b = lvl[2 * p + 1];
@@ -431,9 +439,9 @@ __global__ void k_subtract(const wgb_node *__restrict__ lvl, const int *nn_d, lo
     long long bb = a.built ? a.slot : b.slot;  // built slot
     long long *gs = hg + sb * slot_elems;
     const long long *gb = hg + bb * slot_elems;
-    int *cs = hc + sb * slot_elems;
-    const int *cb = hc + bb * slot_elems;
-    for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < slot_elems;
+    long long *cs = hc + sb * slot_elems;
+    const long long *cb = hc + bb * slot_elems;
+    for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < ncell;
          i += (long long)gridDim.x * blockDim.x) {
         gs[i] -= gb[i];
         cs[i] -= cb[i];
@@ -451,7 +459,7 @@ __global__ void k_subtract(const wgb_node *__restrict__ lvl, const int *nn_d, lo
 template <int NB, bool MULTI>
 __global__ void __launch_bounds__(SPLIT_THREADS) k_split(
     const wgb_node *__restrict__ lvl, const int *nn_d, const long long *__restrict__ hg,
-    const int *__restrict__ hc, long long slot_elems, int k, int E, int B, const int *shift,
+    const long long *__restrict__ hc, long long slot_elems, int k, int E, int B, const int *shift,
     float mcw, float eps, float msg, float factor, int4 *cand, int nblk) {
     const int n = blockIdx.y;
     if (n >= *nn_d) return;
@@ -473,17 +481,17 @@ __global__ void __launch_bounds__(SPLIT_THREADS) k_split(
         for (int e = 0; e < E; ++e) {
             const long long off = slot * slot_elems + ((long long)e * k + j) * B1;
             const long long *gp = hg + off;
-            const int *cp = hc + off;
+            const long long *cp = hc + off;
             float GT = 0.0f, HT = 0.0f;
             for (int b = 0; b < B; ++b) {
                 GT = __fadd_rn(GT, __fmul_rn(__ll2float_rn(__ldg(gp + b)), inv));
-                HT = __fadd_rn(HT, __int2float_rn(__ldg(cp + b)));
+                HT = __fadd_rn(HT, __ll2float_rn(__ldg(cp + b)));
             }
             float GL = 0.0f, HL = 0.0f;
 #pragma unroll 4
             for (int b = 0; b < nb; ++b) {
                 GL = __fadd_rn(GL, __fmul_rn(__ll2float_rn(__ldg(gp + b)), inv));
-                HL = __fadd_rn(HL, __int2float_rn(__ldg(cp + b)));
+                HL = __fadd_rn(HL, __ll2float_rn(__ldg(cp + b)));
                 SplitEval r = eval_split(GL, HL, GT, HT, mcw, eps);
                 if (MULTI) {
                     if (b < NB) {
@@ -523,7 +531,7 @@ __global__ void __launch_bounds__(SPLIT_THREADS) k_split(
 // negative-bin slot, which always goes left).
 __global__ void __launch_bounds__(256) k_split_final(
     wgb_node *__restrict__ lvl, const int *nn_d, const long long *__restrict__ hg,
-    const int *__restrict__ hc, long long slot_elems, int k, int E, int B, const int *shift,
+    const long long *__restrict__ hc, long long slot_elems, int k, int E, int B, const int *shift,
     float mcw, float eps, const int4 *__restrict__ cand, int nblk, float *era_gain) {
     const int n = blockIdx.x;
     if (n >= *nn_d) return;
@@ -557,11 +565,11 @@ __global__ void __launch_bounds__(256) k_split_final(
     for (int e = threadIdx.x; e < E; e += blockDim.x) {
         const long long off = slot * slot_elems + ((long long)e * k + fpos) * B1;
         const long long *gp = hg + off;
-        const int *cp = hc + off;
+        const long long *cp = hc + off;
         float GT = 0.0f, HT = 0.0f, GL = 0.0f, HL = 0.0f;
         for (int b = 0; b < B; ++b) {
             float gv = __fmul_rn(__ll2float_rn(gp[b]), inv);
-            float hv = __int2float_rn(cp[b]);
+            float hv = __ll2float_rn(cp[b]);
             GT = __fadd_rn(GT, gv);
             HT = __fadd_rn(HT, hv);
             if (b <= bin) {
@@ -823,7 +831,11 @@ static inline const int *level_order(const wgb_ws *ws, int d) {
 static inline const int *level_posnode(const wgb_ws *ws, int d) {
     return d == 0 ? nullptr : ws->posnode[(d - 1) & 1];
 }
-static inline long long slot_elems(const wgb_ws *ws) { return (long long)ws->E * ws->k * (ws->B + 1); }
+// Histogram pool: one int64 region per slot, [sums E*k*(B+1)][counts E*k*(B+1)][2 spare];
+// slot 0's first spare cell carries the root's sum of q through the level-0
+// reduction, so one collective per level covers sums, counts and the root.
+static inline long long hist_cells(const wgb_ws *ws) { return (long long)ws->E * ws->k * (ws->B + 1); }
+static inline long long slot_elems(const wgb_ws *ws) { return 2 * hist_cells(ws) + 2; }
 
 static int grid_for(long long n, int threads, int cap = 148 * 16) {
     long long b = (n + threads - 1) / threads;
@@ -896,8 +908,7 @@ int wgb_tree_quantize(const wgb_ws *ws, void *stream) {
 int wgb_tree_root(const wgb_ws *ws, void *stream) {
     int rc = check_ws(ws);
     if (rc) return rc;
-    k_root<<<1, 1, 0, as_stream(stream)>>>(ws->nodes, ws->nn, ws->nact, ws->D, ws->N, ws->N_global,
-                                           LL(ws->rootsum), ws->shift);
+    k_root<<<1, 1, 0, as_stream(stream)>>>(ws->nodes, ws->nn, ws->nact, ws->D, ws->N, ws->N_global);
     WGB_LAUNCHED("k_root");
     return WGB_OK;
 }
@@ -909,9 +920,10 @@ int wgb_level_hist(const wgb_ws *ws, int32_t d, void *stream) {
     cudaStream_t st = as_stream(stream);
     int first, count;
     wgb_built_slots(d, &first, &count);
-    const long long se = slot_elems(ws);
+    const long long se = slot_elems(ws), nc = hist_cells(ws);
     WGB_CUDA(cudaMemsetAsync(ws->hg + (long long)first * se, 0, sizeof(int64_t) * se * count, st));
-    WGB_CUDA(cudaMemsetAsync(ws->hc + (long long)first * se, 0, sizeof(int32_t) * se * count, st));
+    if (d == 0)  // this rank's root sum rides along with the level-0 reduction
+        WGB_CUDA(cudaMemcpyAsync(ws->hg + 2 * nc, ws->rootsum, sizeof(int64_t), cudaMemcpyDeviceToDevice, st));
     wgb_node *lvl = level_nodes(ws, d);
     k_chunk_plan<<<1, 1024, 0, st>>>(lvl, ws->nn + d, reinterpret_cast<int4 *>(ws->chunks),
                                      ws->nchunks, ws->chunk_cap);
@@ -923,7 +935,7 @@ int wgb_level_hist(const wgb_ws *ws, int32_t d, void *stream) {
     cudaError_t e = launch_hist((int)max_chunks, ws->bins, ws->S, ws->F, ord, ws->qg, nullptr, nullptr,
                                 ws->E > 1 ? ws->era : nullptr, ws->kpos, ws->k, ws->E, ws->B, ws->hist_ew,
                                 ws->regular != 0, reinterpret_cast<const int4 *>(ws->chunks), ws->nchunks,
-                                lvl, LL(ws->hg), ws->hc, se, ws->N, st);
+                                lvl, LL(ws->hg), LL(ws->hg) + nc, se, ws->N, st);
     if (e != cudaSuccess) {
         set_error("k_hist launch failed: %s", cudaGetErrorString(e));
         return WGB_ERR_CUDA;
@@ -937,14 +949,18 @@ int wgb_level_split(const wgb_ws *ws, int32_t d, void *stream) {
     if (rc) return rc;
     WGB_CHECK_ARG(d >= 0 && d < ws->D, "level %d out of range", d);
     cudaStream_t st = as_stream(stream);
-    const long long se = slot_elems(ws);
+    const long long se = slot_elems(ws), nc = hist_cells(ws);
+    long long *hg = LL(ws->hg), *hc = hg + nc;
     wgb_node *lvl = level_nodes(ws, d);
     const int cap = 1 << d;
-    if (d > 0) {
-        int bx = (int)((se + 255) / 256);
+    if (d == 0) {
+        k_root_total<<<1, 1, 0, st>>>(ws->nodes, hg + 2 * nc, ws->shift);
+        WGB_LAUNCHED("k_root_total");
+    } else {
+        int bx = (int)((nc + 255) / 256);
         if (bx > 64) bx = 64;
         dim3 g(bx, cap / 2);
-        k_subtract<<<g, 256, 0, st>>>(lvl, ws->nn + d, LL(ws->hg), ws->hc, se);
+        k_subtract<<<g, 256, 0, st>>>(lvl, ws->nn + d, hg, hc, se, nc);
         WGB_LAUNCHED("k_subtract");
     }
     const int nblk = (ws->k + SPLIT_THREADS - 1) / SPLIT_THREADS;
@@ -953,7 +969,7 @@ int wgb_level_split(const wgb_ws *ws, int32_t d, void *stream) {
     const int nb = ws->B - 1;
     int4 *cand = reinterpret_cast<int4 *>(ws->cand);
 #define WGB_SPLIT_ARGS                                                                       \
-    lvl, ws->nn + d, LL(ws->hg), ws->hc, se, ws->k, ws->E, ws->B, ws->shift, ws->mcw, ws->eps, \
+    lvl, ws->nn + d, hg, hc, se, ws->k, ws->E, ws->B, ws->shift, ws->mcw, ws->eps, \
         ws->msg, ws->mean_factor, cand, nblk
     if (ws->E == 1) {
         k_split<1, false><<<g, SPLIT_THREADS, 0, st>>>(WGB_SPLIT_ARGS);
@@ -967,7 +983,7 @@ int wgb_level_split(const wgb_ws *ws, int32_t d, void *stream) {
 #undef WGB_SPLIT_ARGS
     WGB_LAUNCHED("k_split");
     float *eg = ws->era_gain + (long long)((1 << d) - 1) * ws->E;
-    k_split_final<<<cap, 256, 0, st>>>(lvl, ws->nn + d, LL(ws->hg), ws->hc, se, ws->k, ws->E, ws->B,
+    k_split_final<<<cap, 256, 0, st>>>(lvl, ws->nn + d, hg, hc, se, ws->k, ws->E, ws->B,
                                        ws->shift, ws->mcw, ws->eps, cand, nblk, eg);
     WGB_LAUNCHED("k_split_final");
     k_plan_next<<<1, 1024, 0, st>>>(lvl, level_nodes(ws, d + 1), ws->nn, d, ws->shift);

@@ -10,7 +10,7 @@
 // part of the library image instead.  Its limits:
 //   * the block is WGB_NOALLOC_SCRATCH_BYTES (64 MiB); every GPU on which the
 //     library's kernels are loaded keeps it reserved until the process exits;
-//   * a call needs num_eras * k * (num_bins + 1) * 12 bytes of histogram
+//   * a call needs num_eras * k * (num_bins + 1) * 16 bytes of histogram
 //     cells plus F_master * 4 + ceil(n / 1024) * 16 + 96 bytes, each part
 //     rounded up to 256 bytes; larger calls are rejected with WGB_ERR_ARG
 //     before any work is queued;
@@ -60,7 +60,7 @@ extern "C" int wgb_compute_histogram3_noalloc(const int8_t *bin_indices, int64_t
     const long long se = (long long)num_eras * k * (num_bins + 1);
     const int nchunk = (int)((n + HIST_R - 1) / HIST_R);
     const size_t off_hc = round256((size_t)se * 8);
-    const size_t off_kpos = off_hc + round256((size_t)se * 4);
+    const size_t off_kpos = off_hc + round256((size_t)se * 8);
     const size_t off_chunks = off_kpos + round256((size_t)F_master * 4);
     const size_t off_small = off_chunks + round256((size_t)nchunk * sizeof(int4));
     const size_t off_nd = off_small + 256;
@@ -84,7 +84,7 @@ extern "C" int wgb_compute_histogram3_noalloc(const int8_t *bin_indices, int64_t
         base = static_cast<unsigned char *>(g_noalloc_addr.ptr[dev]);
     }
     long long *hg = reinterpret_cast<long long *>(base);
-    int *hc = reinterpret_cast<int *>(base + off_hc);
+    long long *hc = reinterpret_cast<long long *>(base + off_hc);
     int *kpos = reinterpret_cast<int *>(base + off_kpos);
     int4 *chunks = reinterpret_cast<int4 *>(base + off_chunks);
     int *small = reinterpret_cast<int *>(base + off_small);
@@ -95,7 +95,7 @@ extern "C" int wgb_compute_histogram3_noalloc(const int8_t *bin_indices, int64_t
     cudaStream_t st = as_stream(stream);
     // the block keeps the previous call's contents: clear what must start at 0
     WGB_CUDA(cudaMemsetAsync(hg, 0, sizeof(long long) * se, st));
-    WGB_CUDA(cudaMemsetAsync(hc, 0, sizeof(int) * se, st));
+    WGB_CUDA(cudaMemsetAsync(hc, 0, sizeof(long long) * se, st));
     WGB_CUDA(cudaMemsetAsync(kpos, 0xff, sizeof(int) * F_master, st));
     WGB_CUDA(cudaMemsetAsync(small, 0, 256, st));
     k_kpos<<<(k + 255) / 256, 256, 0, st>>>(feature_indices, k, (int)F_master, kpos);

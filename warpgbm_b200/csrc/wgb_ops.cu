@@ -261,7 +261,7 @@ __global__ void k_kpos(const int *__restrict__ feats, int k, int F, int *__restr
     if (f >= 0 && f < F) kpos[f] = j;
 }
 
-__global__ void k_hist_to_float(const long long *__restrict__ hg, const int *__restrict__ hc, long long m,
+__global__ void k_hist_to_float(const long long *__restrict__ hg, const long long *__restrict__ hc, long long m,
                                 int B, const int *shift, float *__restrict__ G, float *__restrict__ H) {
     const float inv = pow2f(-*shift);
     for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < m * B;
@@ -270,7 +270,7 @@ __global__ void k_hist_to_float(const long long *__restrict__ hg, const int *__r
         int b = (int)(i - c * B);
         long long src = c * (B + 1) + b;
         G[i] = __fadd_rn(G[i], __fmul_rn(__ll2float_rn(hg[src]), inv));
-        H[i] = __fadd_rn(H[i], __int2float_rn(hc[src]));
+        H[i] = __fadd_rn(H[i], __ll2float_rn(hc[src]));
     }
 }
 
@@ -373,12 +373,12 @@ int wgb_compute_histogram3(const int8_t *bin_indices, int64_t num_rows, int64_t 
     const long long se = (long long)num_eras * k * (num_bins + 1);
     const int nchunk = (int)((n + HIST_R - 1) / HIST_R);
     // scratch from the stream-ordered pool
-    long long *hg = nullptr;
-    int *hc = nullptr, *kpos = nullptr, *small = nullptr;
+    long long *hg = nullptr, *hc = nullptr;
+    int *kpos = nullptr, *small = nullptr;
     int4 *chunks = nullptr;
     wgb_node *nd = nullptr;
     WGB_CUDA(cudaMallocAsync((void **)&hg, sizeof(long long) * se, st));
-    WGB_CUDA(cudaMallocAsync((void **)&hc, sizeof(int) * se, st));
+    WGB_CUDA(cudaMallocAsync((void **)&hc, sizeof(long long) * se, st));
     WGB_CUDA(cudaMallocAsync((void **)&kpos, sizeof(int) * F_master, st));
     WGB_CUDA(cudaMallocAsync((void **)&chunks, sizeof(int4) * nchunk, st));
     WGB_CUDA(cudaMallocAsync((void **)&small, sizeof(int) * 8, st));
@@ -388,7 +388,7 @@ int wgb_compute_histogram3(const int8_t *bin_indices, int64_t num_rows, int64_t 
     int rc = WGB_OK;
     do {
         if (cudaMemsetAsync(hg, 0, sizeof(long long) * se, st) != cudaSuccess ||
-            cudaMemsetAsync(hc, 0, sizeof(int) * se, st) != cudaSuccess ||
+            cudaMemsetAsync(hc, 0, sizeof(long long) * se, st) != cudaSuccess ||
             cudaMemsetAsync(kpos, 0xff, sizeof(int) * F_master, st) != cudaSuccess ||
             cudaMemsetAsync(small, 0, sizeof(int) * 8, st) != cudaSuccess) {
             set_error("cudaMemsetAsync failed");
