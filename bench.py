@@ -48,7 +48,7 @@ def parse():
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=3)
     ap.add_argument("--warmup", type=int, default=3)
-    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference", "reference-cuda"])
     ap.add_argument("--rows", type=int, default=CONFIG["n"])
     ap.add_argument("--trees", type=int, default=CONFIG["n_estimators"])
     ap.add_argument("--no-e2e", action="store_true")
@@ -227,6 +227,43 @@ def run_reference(args, rank):
     print(json.dumps(line), flush=True)
 
 
+def run_reference_cuda(args, rank):
+    """--impl reference-cuda: the reference's own CUDA kernels (compiled from
+    its sources into oracle/_ref/) driven by a restatement of its regression
+    fit loop, on this GPU, from numpy inputs like the reference's fit."""
+    if rank != 0:
+        return
+    from oracle.build_ref import load
+    from oracle.ref_cuda import RefCudaFit
+    ops = load()
+    rng = np.random.default_rng(0)
+    n, F = args.rows, CONFIG["F"]
+    Xh = rng.standard_normal((n, F), dtype=np.float32)
+    w = rng.standard_normal(20)
+    yh = (Xh[:, :20] @ w + 0.3 * np.sin(Xh[:, 20:30]).sum(1) + rng.normal(0, 0.5, n)).astype(np.float32)
+    params = dict(num_bins=CONFIG["num_bins"], max_depth=CONFIG["max_depth"],
+                  learning_rate=CONFIG["learning_rate"], n_estimators=args.trees)
+    runs = []
+    for i in range(args.warmup + args.steps):
+        m = RefCudaFit(ops, **params).fit(Xh, yh)
+        if i >= args.warmup:
+            runs.append(m.timings)
+    total = [r["ingest_s"] + r["grow_s"] for r in runs]
+    v = statistics.median(total) * 100.0 / args.trees
+    line = {"metric": "train sec/100 trees @1M×1K", "value": round(v, 3), "unit": "s/100 trees",
+            "impl": "reference-cuda", "n_gpus": 1, "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": round(statistics.median(total) * 1000.0, 1), "higher_is_better": False,
+            "dtype": "f32", "data": "synthetic (config 2 generator, numpy seed 0)",
+            "config": {"workload": "config2: 1M x 1000 f32 regression, B=32, depth 5, lr 0.01",
+                       "rows": n, "trees": args.trees},
+            "breakdown": {"ingest_binning_s": round(statistics.median(r["ingest_s"] for r in runs), 3),
+                          "growth_s_per_100_trees": round(statistics.median(r["grow_s"] for r in runs)
+                                                          * 100.0 / args.trees, 3)},
+            "note": "reference kernels (warpgbm/cuda/*.cu, compiled for sm_100a) under a restatement "
+                    "of the reference's fit loop; timed from numpy X, y like the reference's fit"}
+    print(json.dumps(line), flush=True)
+
+
 def main():
     args = parse()
     world = int(os.environ.get("WORLD_SIZE", "1"))
@@ -234,6 +271,9 @@ def main():
     local = int(os.environ.get("LOCAL_RANK", "0"))
     if args.impl == "reference":
         run_reference(args, rank)
+        return
+    if args.impl == "reference-cuda":
+        run_reference_cuda(args, rank)
         return
     import torch.distributed as dist
     from datetime import timedelta

@@ -134,6 +134,21 @@ def test_moderate_scale_bit_exact_and_deterministic(cuda):
     assert np.array_equal(p1, o.predict(X))
 
 
+@pytest.mark.parametrize("D,n,F", [(10, 60_000, 40), (13, 40_000, 12)])
+def test_deep_trees_bit_exact(cuda, D, n, F):
+    """BASELINE config 4's shape in miniature (pre-binned 0..31, depth 10) and a
+    depth-13 tree whose deep levels hold more than 1024 nodes."""
+    rng = np.random.default_rng(D)
+    X = rng.integers(0, 32, (n, F)).astype(np.int8)
+    w = rng.standard_normal(min(F, 25))
+    y = (X[:, :len(w)] / 31.0 @ w + rng.normal(0, 0.2, n)).astype(np.float32)
+    params = dict(num_bins=32, max_depth=D, n_estimators=3, learning_rate=0.05, min_child_weight=2)
+    m = WarpGBM(**params).fit(X, y)
+    o = _oracle_for(m, params, X, y, None)
+    assert _same(_flat(m, D), o.flat_forest())
+    assert np.array_equal(m.predict(X), o.predict(X))
+
+
 @pytest.mark.parametrize("kind", ["depth1", "bins2", "bins127", "constant_y", "tiny", "negative_bins"])
 def test_edge_cases_bit_exact(cuda, kind):
     rng = np.random.default_rng(1)

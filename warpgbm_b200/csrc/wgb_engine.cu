@@ -429,10 +429,10 @@ static cudaError_t launch_hist(int grid_x, const int8_t *bins, long long S, int 
 }
 
 // sibling = parent - built, in place of the parent's slot (the sibling
-// inherits it).  grid.y = pair.
+// inherits it).  Block b works on pair b / bpp (bpp blocks per pair).
 __global__ void k_subtract(const wgb_node *__restrict__ lvl, const int *nn_d, long long *hg, long long *hc,
-                           long long slot_elems, long long ncell) {
-    int p = blockIdx.y;
+                           long long slot_elems, long long ncell, int bpp) {
+    const int p = blockIdx.x / bpp, bx = blockIdx.x - p * bpp;
     if (2 * p + 1 >= *nn_d) return;
     const wgb_node &a = lvl[2 * p], &b = lvl[2 * p + 1];
     long long sb = a.built ? b.slot : a.slot;  // sibling (= parent) slot
@@ -441,8 +441,7 @@ __global__ void k_subtract(const wgb_node *__restrict__ lvl, const int *nn_d, lo
     const long long *gb = hg + bb * slot_elems;
     long long *cs = hc + sb * slot_elems;
     const long long *cb = hc + bb * slot_elems;
-    for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < ncell;
-         i += (long long)gridDim.x * blockDim.x) {
+    for (long long i = bx * (long long)blockDim.x + threadIdx.x; i < ncell; i += (long long)bpp * blockDim.x) {
         gs[i] -= gb[i];
         cs[i] -= cb[i];
     }
@@ -461,9 +460,9 @@ __global__ void __launch_bounds__(SPLIT_THREADS) k_split(
     const wgb_node *__restrict__ lvl, const int *nn_d, const long long *__restrict__ hg,
     const long long *__restrict__ hc, long long slot_elems, int k, int E, int B, const int *shift,
     float mcw, float eps, float msg, float factor, int4 *cand, int nblk) {
-    const int n = blockIdx.y;
+    const int n = blockIdx.x / nblk, jb = blockIdx.x - n * nblk;  // node, feature block
     if (n >= *nn_d) return;
-    const int j = blockIdx.x * SPLIT_THREADS + threadIdx.x;
+    const int j = jb * SPLIT_THREADS + threadIdx.x;
     const float inv = pow2f(-*shift);
     const int B1 = B + 1, nb = B - 1;
     const long long slot = lvl[n].slot;
@@ -522,7 +521,7 @@ __global__ void __launch_bounds__(SPLIT_THREADS) k_split(
     if (threadIdx.x == 0) {
         for (int w = 1; w < SPLIT_THREADS / 32; ++w)
             if (key_better(s_k[w], best)) best = s_k[w];
-        cand[(long long)n * nblk + blockIdx.x] = make_int4(best.A, __float_as_int(best.c), best.idx, 0);
+        cand[(long long)n * nblk + jb] = make_int4(best.A, __float_as_int(best.c), best.idx, 0);
     }
 }
 
@@ -959,13 +958,12 @@ int wgb_level_split(const wgb_ws *ws, int32_t d, void *stream) {
     } else {
         int bx = (int)((nc + 255) / 256);
         if (bx > 64) bx = 64;
-        dim3 g(bx, cap / 2);
-        k_subtract<<<g, 256, 0, st>>>(lvl, ws->nn + d, hg, hc, se, nc);
+        k_subtract<<<(unsigned)bx * (cap / 2), 256, 0, st>>>(lvl, ws->nn + d, hg, hc, se, nc, bx);
         WGB_LAUNCHED("k_subtract");
     }
     const int nblk = (ws->k + SPLIT_THREADS - 1) / SPLIT_THREADS;
     WGB_CHECK_ARG(nblk <= ws->ncand_blk, "candidate buffer too small");
-    dim3 g(nblk, cap);
+    const unsigned g = (unsigned)nblk * (unsigned)cap;  // node-major blocks
     const int nb = ws->B - 1;
     int4 *cand = reinterpret_cast<int4 *>(ws->cand);
 #define WGB_SPLIT_ARGS                                                                       \
