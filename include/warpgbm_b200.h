@@ -173,6 +173,8 @@ typedef struct wgb_node {
 typedef struct wgb_ws {
     /* data (fixed for the fit) */
     const int8_t *bins;      /* [N][S]                                       */
+    const int8_t *bins_fm;   /* [F][NT] feature-major copy, NT = N rounded up */
+                             /*   to 16 (wgb_bins_feature_major), or NULL     */
     const int32_t *era;      /* [N] dense era id per row, or NULL if E == 1   */
     const int32_t *root_order; /* [N] row ids sorted by era (stable)          */
     const float *y;          /* [N] regression target (NULL: g given)        */
@@ -241,6 +243,10 @@ void wgb_built_slots(int32_t d, int32_t *first, int32_t *count);
 /* Level d: sibling = parent - built (in place), split search, per-era gains,
  * child totals, next level's node records. */
 int wgb_level_split(const wgb_ws *ws, int32_t d, void *stream);
+/* Feature-major copy of ws->bins into out ([F][NT], NT = N rounded up to a
+ * multiple of 16, 16-byte aligned): the partition reads one feature of many
+ * rows, which this layout makes contiguous.  Set ws->bins_fm = out after. */
+int wgb_bins_feature_major(const wgb_ws *ws, int8_t *out, void *stream);
 /* Level d: stable partition of local rows into the next level's order; rows
  * of nodes that became leaves get pred[:, cls] += lr * leaf. */
 int wgb_level_partition(const wgb_ws *ws, int32_t d, void *stream);

@@ -621,6 +621,15 @@ class WarpGBM(BaseEstimator, RegressorMixin):
             ws.era = era_dense.data_ptr() if E > 1 else None
             ws.N_global = self._n_global
             keep = [bins, root_order, era_dense]
+            # feature-major copy for the partition's bin reads, when it fits
+            NT = (N + 15) // 16 * 16
+            if N and F * NT < 0.25 * torch.cuda.mem_get_info(dev)[0]:
+                bins_fm = torch.empty(F * NT, dtype=torch.int8, device=dev)
+                _lib.call("wgb_bins_feature_major", ctypes_ptr(ws), bins_fm.data_ptr(), st())
+                ws.bins_fm = bins_fm.data_ptr()
+                keep.append(bins_fm)
+            else:
+                ws.bins_fm = None
 
             resume = self.warm_start and self._is_fitted and self._trees_trained > 0
             if classification:

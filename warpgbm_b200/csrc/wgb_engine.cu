@@ -646,10 +646,42 @@ __global__ void __launch_bounds__(1024) k_plan_next(wgb_node *__restrict__ lvl, 
 // partition                                                              //
 // ====================================================================== //
 
+// bins [N][S] -> out [F][NT] (NT = N rounded up to 16).  Tile = 128 rows x
+// 128 features through shared memory; 16-byte loads and stores.
+__global__ void __launch_bounds__(256) k_bins_fm(const int8_t *__restrict__ bins, long long N, long long S, int F,
+                                                 long long NT, int8_t *__restrict__ out) {
+    __shared__ __align__(16) uint8_t t[128][144];
+    const long long r0 = (long long)blockIdx.x * 128;
+    const int f0 = blockIdx.y * 128;
+    for (int i = threadIdx.x; i < 128 * 8; i += 256) {
+        const int rr = i >> 3, c16 = (i & 7) * 16;
+        const long long r = r0 + rr;
+        uint4 v = make_uint4(0u, 0u, 0u, 0u);
+        if (r < N && f0 + c16 < S) v = __ldg(reinterpret_cast<const uint4 *>(bins + r * S + f0 + c16));
+        *reinterpret_cast<uint4 *>(&t[rr][c16]) = v;
+    }
+    __syncthreads();
+    for (int i = threadIdx.x; i < 128 * 8; i += 256) {
+        const int fl = i >> 3, r16 = (i & 7) * 16;
+        const int f = f0 + fl;
+        if (f >= F || r0 + r16 >= NT) continue;
+        uint32_t w[4];
+#pragma unroll
+        for (int q = 0; q < 4; ++q)
+            w[q] = (uint32_t)t[r16 + 4 * q][fl] | ((uint32_t)t[r16 + 4 * q + 1][fl] << 8) |
+                   ((uint32_t)t[r16 + 4 * q + 2][fl] << 16) | ((uint32_t)t[r16 + 4 * q + 3][fl] << 24);
+        *reinterpret_cast<uint4 *>(out + (long long)f * NT + r0 + r16) = make_uint4(w[0], w[1], w[2], w[3]);
+    }
+}
+
 // flag per position: 1 left, 0 right, 2 node is a leaf; left count per tile.
+// The split feature's bin comes from the feature-major copy when there is
+// one (rows of a node are ascending, so neighbouring positions read
+// neighbouring bytes), else from the row-major matrix.
 __global__ void __launch_bounds__(PART_THREADS) k_flags(
     const wgb_node *__restrict__ lvl, const int *nact_d, const int *__restrict__ order,
     const int *__restrict__ posnode, const int8_t *__restrict__ bins, long long S,
+    const int8_t *__restrict__ bins_fm, long long NT,
     const int *__restrict__ feats, uint8_t *flags, int *tile_cnt) {
     const int nact = *nact_d;
     const long long t0 = (long long)blockIdx.x * PART_TILE;
@@ -661,8 +693,8 @@ __global__ void __launch_bounds__(PART_THREADS) k_flags(
         int fp = lvl[n].fpos;
         uint8_t fl = 2;
         if (fp >= 0) {
-            int row = order[p];
-            int b = bins[(long long)row * S + feats[fp]];
+            const int row = order[p], feat = feats[fp];
+            const int b = bins_fm ? bins_fm[(long long)feat * NT + row] : bins[(long long)row * S + feat];
             fl = b <= lvl[n].bin ? 1 : 0;
             cnt += fl;
         }
@@ -989,6 +1021,20 @@ int wgb_level_split(const wgb_ws *ws, int32_t d, void *stream) {
     return WGB_OK;
 }
 
+int wgb_bins_feature_major(const wgb_ws *ws, int8_t *out, void *stream) {
+    int rc = check_ws(ws);
+    if (rc) return rc;
+    WGB_CHECK_ARG(out != nullptr && (reinterpret_cast<uintptr_t>(out) & 15) == 0,
+                  "out must be a 16-byte aligned buffer of F * NT bytes");
+    WGB_CHECK_ARG(ws->S % 16 == 0, "bins row stride must be a multiple of 16");
+    if (ws->N == 0) return WGB_OK;
+    const long long NT = (ws->N + 15) & ~15ll;
+    dim3 g((unsigned)((NT + 127) / 128), (unsigned)((ws->F + 127) / 128));
+    k_bins_fm<<<g, 256, 0, as_stream(stream)>>>(ws->bins, ws->N, ws->S, ws->F, NT, out);
+    WGB_LAUNCHED("k_bins_fm");
+    return WGB_OK;
+}
+
 int wgb_level_partition(const wgb_ws *ws, int32_t d, void *stream) {
     int rc = check_ws(ws);
     if (rc) return rc;
@@ -1000,8 +1046,8 @@ int wgb_level_partition(const wgb_ws *ws, int32_t d, void *stream) {
     WGB_CHECK_ARG(ntiles <= ws->ntiles, "tile buffer too small");
     const int *ord = level_order(ws, d);
     const int *pn = level_posnode(ws, d);
-    k_flags<<<ntiles, PART_THREADS, 0, st>>>(lvl, ws->nact + d, ord, pn, ws->bins, ws->S, ws->feats,
-                                              ws->flags, ws->tile_cnt);
+    k_flags<<<ntiles, PART_THREADS, 0, st>>>(lvl, ws->nact + d, ord, pn, ws->bins, ws->S, ws->bins_fm,
+                                              (ws->N + 15) & ~15ll, ws->feats, ws->flags, ws->tile_cnt);
     WGB_LAUNCHED("k_flags");
     k_scan_tiles<<<1, 1024, 0, st>>>(ws->tile_cnt, ws->tile_off, ntiles);
     WGB_LAUNCHED("k_scan_tiles");
