@@ -325,6 +325,7 @@ def run_c5(args, world, rank, local):
             with contextlib.redirect_stdout(io.StringIO()):
                 model = WarpGBM(**params)
                 model._hist_events = []
+                model._comm_events = []
                 model.fit(X, y)
             e1.record()
             pred = model.predict(X)
@@ -334,6 +335,7 @@ def run_c5(args, world, rank, local):
             pred_ms.append(max_over_ranks(e1.elapsed_time(e2)))
     launches = _lib.LAUNCHES[0] - launches0
     hist_ms = sum(a.elapsed_time(b) for a, b in model._hist_events)
+    comm_ms = sum(a.elapsed_time(b) for a, b in model._comm_events)
     hist_bytes = hist_algorithmic_bytes(model, n_total, F, 1, C5["num_bins"], world)
     peak, peak_kind = peaks()
     achieved = hist_bytes / (hist_ms / 1000.0) / 1e9 if hist_ms > 0 else None
@@ -349,6 +351,8 @@ def run_c5(args, world, rank, local):
                            "parallelism": f"row-shard dp{world}"},
                 "predict": {"value": round(statistics.median(pred_ms) / 1000.0, 4), "unit": "s",
                             "rows_per_rank": n, "trees": trees},
+                "breakdown_rank0_ms": {"histogram_kernels": round(hist_ms, 1), "collectives": round(comm_ms, 1),
+                                       "fit": round(fit_ms[-1], 1)},
                 "roofline": {"bound": "hbm", "kernel": "k_hist (wgb_level_hist)",
                              "achieved": round(achieved, 1) if achieved else None, "peak": peak,
                              "unit": "GB/s", "frac": round(achieved / peak, 4) if achieved else None,
@@ -400,23 +404,28 @@ def main():
             WarpGBM(**params).fit(X, y)
     barrier()
     model = None
-    times, hist_ms, hist_bytes = [], 0.0, 0.0
+    times, hist_ms, hist_bytes, comm_ms = [], 0.0, 0.0, 0.0
     launches0 = _lib.LAUNCHES[0]
     with Clocks(local) as clk:
         barrier()
         e0 = torch.cuda.Event(enable_timing=True)
         e1 = torch.cuda.Event(enable_timing=True)
         e0.record()
+        models = []
         with contextlib.redirect_stdout(io.StringIO()):
             for _ in range(args.steps):
                 model = WarpGBM(**params)
                 model._hist_events = []
+                model._comm_events = []
                 model.fit(X, y)
-                hist_ms += sum(a.elapsed_time(b) for a, b in model._hist_events)
-                hist_bytes += hist_algorithmic_bytes(model, model._n_global if world > 1 else n,
-                                                     F, 1, CONFIG["num_bins"], world)
+                models.append(model)
         e1.record()
         barrier()
+    for model in models:  # host-side accounting, outside the timed region
+        hist_ms += sum(a.elapsed_time(b) for a, b in model._hist_events)
+        comm_ms += sum(a.elapsed_time(b) for a, b in model._comm_events)
+        hist_bytes += hist_algorithmic_bytes(model, model._n_global if world > 1 else n,
+                                             F, 1, CONFIG["num_bins"], world)
     launches = _lib.LAUNCHES[0] - launches0
     t = e0.elapsed_time(e1) / args.steps
     tt = torch.tensor([t], device=dev)
@@ -474,6 +483,8 @@ def main():
                          "launches_timed": nlaunch * args.steps,
                          "avg_launch_ms": round(hist_ms / max(nlaunch * args.steps, 1), 4)},
             "e2e": e2e,
+            "breakdown_rank0_ms_per_step": {"histogram_kernels": round(hist_ms / args.steps, 1),
+                                            "collectives": round(comm_ms / args.steps, 1)},
             "gpu_launches": launches,
             "clocks": clk.summary(),
         }

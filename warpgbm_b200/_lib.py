@@ -131,10 +131,7 @@ LAUNCHES = [0]
 
 def call(name: str, *args) -> None:
     check(getattr(lib(), name)(*args), name)
-    n = _KERNELS.get(name, 0)
-    if name == "wgb_level_split" and args[1] == 0:
-        n -= 1  # no sibling subtraction at the root
-    LAUNCHES[0] += n
+    LAUNCHES[0] += _KERNELS.get(name, 0)
 
 
 def built_slots(d: int):

@@ -287,6 +287,93 @@ def pack_trees(trees) -> (np.ndarray, np.ndarray):
     return arr, np.array(offs, np.int32)
 
 
+def compact_tree(nodes, gains, feats, D, E):
+    """One tree's level-packed node records -> pre-order arrays, vectorised
+    per level (no per-node Python).  Returns (packed [n,2] int32 in the
+    wgb_predict_packed format, leaf values [n] f32, samples [n] int64,
+    split pre-order ids, split global features, split per-era gains [s, E]).
+    Only nodes reachable from the root are real (the record buffer keeps
+    stale entries of earlier trees)."""
+    fpos_all = nodes["fpos"].astype(np.int64)
+    child_all = nodes["child"].astype(np.int64)
+    base = [(1 << d) - 1 for d in range(D + 1)]
+    real = [np.zeros(1, np.int64)]                       # level-local ids of real nodes
+    split = []                                           # per level: bool mask over real
+    for d in range(D + 1):
+        r = real[d]
+        sp = (fpos_all[base[d] + r] >= 0) if d < D else np.zeros(r.shape, bool)
+        split.append(sp)
+        if d < D:
+            c = child_all[base[d] + r[sp]]
+            real.append(np.stack([c, c + 1], 1).reshape(-1))
+    # subtree sizes bottom-up (indexed by level-local id)
+    size = [None] * (D + 1)
+    for d in range(D, -1, -1):
+        r = real[d]
+        sz = np.ones(r.shape, np.int64)
+        if d < D and split[d].any():
+            c = child_all[base[d] + r[split[d]]]
+            sz[split[d]] += size[d + 1][c] + size[d + 1][c + 1]
+        full = np.zeros((1 << d), np.int64)
+        full[r] = sz
+        size[d] = full
+    n = int(size[0][0])
+    pre = [None] * (D + 1)
+    pre[0] = np.zeros(1, np.int64)
+    packed = np.zeros((n, 2), np.int32)
+    leaf = np.zeros(n, np.float32)
+    samples = np.zeros(n, np.int64)
+    sp_pre, sp_feat, sp_gain = [], [], []
+    leaf_bits = np.ascontiguousarray(nodes["leaf"]).view(np.int32)
+    for d in range(D + 1):
+        r = real[d]
+        full_pre = pre[d]
+        pr = full_pre[r]
+        g = base[d] + r
+        lf = ~split[d]
+        packed[pr[lf], 0] = -1
+        packed[pr[lf], 1] = leaf_bits[g[lf]]
+        leaf[pr[lf]] = nodes["leaf"][g[lf]]
+        samples[pr[lf]] = nodes["count"][g[lf]]
+        if d < D:
+            nxt = np.zeros((1 << (d + 1)), np.int64)
+            if split[d].any():
+                ps, gs = pr[split[d]], g[split[d]]
+                c = child_all[gs]
+                nxt[c] = ps + 1
+                nxt[c + 1] = ps + 1 + size[d + 1][c]
+                gfi = feats[fpos_all[gs]].astype(np.int64)
+                packed[ps, 0] = gfi
+                packed[ps, 1] = (nodes["bin"][gs].astype(np.int64) & 0xFF) | (nxt[c + 1] << 8)
+                sp_pre.append(ps)
+                sp_feat.append(gfi)
+                sp_gain.append(gains.reshape(-1, E)[gs])
+            pre[d + 1] = nxt
+    if sp_pre:
+        sp_pre = np.concatenate(sp_pre)
+        order = np.argsort(sp_pre, kind="stable")
+        sp_pre, sp_feat = sp_pre[order], np.concatenate(sp_feat)[order]
+        sp_gain = np.concatenate(sp_gain)[order]
+    else:
+        sp_pre = sp_feat = np.zeros(0, np.int64)
+        sp_gain = np.zeros((0, E), np.float32)
+    return packed, leaf, samples, sp_pre, sp_feat, sp_gain
+
+
+def tree_dict(packed, leaf, samples):
+    """Reference nested-dict tree from compact pre-order arrays."""
+    f = packed[:, 0].tolist()
+    w = packed[:, 1].tolist()
+    lv = leaf.tolist()
+    sm = samples.tolist()
+
+    def build(i):
+        if f[i] < 0:
+            return {"leaf_value": lv[i], "samples": sm[i]}
+        return {"feature": f[i], "bin": w[i] & 0xFF, "left": build(i + 1), "right": build(w[i] >> 8)}
+    return build(0)
+
+
 class WarpGBM(BaseEstimator, RegressorMixin):
     def __init__(
         self,
@@ -344,6 +431,30 @@ class WarpGBM(BaseEstimator, RegressorMixin):
         self._is_fitted = False
         self._trees_trained = 0
         self._packed = None
+
+    # ------------------------------------------------------------------
+    # forest: nested-dict trees (the reference's format), built on first
+    # access from the compact arrays that fit() and predict use
+    # ------------------------------------------------------------------
+    @property
+    def forest(self):
+        lazy = self.__dict__.get("_lazy")
+        if lazy:
+            f = self.__dict__["_forest"]
+            for (i, c) in sorted(lazy):
+                t = tree_dict(*self._compact[(i, c)][:3])
+                if isinstance(f[i], list):
+                    f[i][c] = t
+                else:
+                    f[i] = t
+            lazy.clear()
+        return self.__dict__.get("_forest")
+
+    @forest.setter
+    def forest(self, v):
+        self.__dict__["_forest"] = v
+        self.__dict__["_lazy"] = set()
+        self.__dict__["_compact"] = {}
 
     # ------------------------------------------------------------------
     # validation (core.py:83-143, 216-291)
@@ -697,6 +808,7 @@ class WarpGBM(BaseEstimator, RegressorMixin):
             self._rec_done = 0
             self._rec_decoded = 0
             self._rec_meta = []
+            self._rec_events = []
             self._residuals = []
             if not resume:
                 self.feature_subsets_ = []
@@ -741,8 +853,15 @@ class WarpGBM(BaseEstimator, RegressorMixin):
         p = ctypes_ptr(ws)
         _lib.call("wgb_tree_reset", p, st())
         _lib.call("wgb_tree_residual", p, st())
+        ctimer = getattr(self, "_comm_events", None)   # bench hook: device time of collectives
         if comm.on:
+            if ctimer is not None:
+                c0, c1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                c0.record()
             comm.max_(self._t["maxabs"])
+            if ctimer is not None:
+                c1.record()
+                ctimer.append((c0, c1))
         _lib.call("wgb_tree_quantize", p, st())
         _lib.call("wgb_tree_root", p, st())
         P = 2 * ws.E * ws.k * (ws.B + 1) + 2
@@ -758,7 +877,13 @@ class WarpGBM(BaseEstimator, RegressorMixin):
                 timer.append((ev0, ev1))
             if comm.on:
                 first, count = _lib.built_slots(d)
+                if ctimer is not None:
+                    c0, c1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                    c0.record()
                 comm.sum_(self._t["hg"][first * P:(first + count) * P])
+                if ctimer is not None:
+                    c1.record()
+                    ctimer.append((c0, c1))
             _lib.call("wgb_level_split", p, d, st())
             _lib.call("wgb_level_partition", p, d, st())
         _lib.call("wgb_tree_finish", p, st())
@@ -768,30 +893,38 @@ class WarpGBM(BaseEstimator, RegressorMixin):
         self._rec_nodes[j].copy_(self._t["nodes"], non_blocking=True)
         self._rec_gain[j, : self._t["era_gain"].numel()].copy_(self._t["era_gain"], non_blocking=True)
         self._rec_feats[j].copy_(self._t["feats"], non_blocking=True)
+        ev = torch.cuda.Event()
+        ev.record()
+        self._rec_events.append(ev)
         self._rec_meta.append((i, c))
         self._rec_done += 1
+        self._drain_records(self.objective != "regression")
 
     # ------------------------------------------------------------------
     # tree records -> reference dict trees, importance (core.py:623-658)
     # ------------------------------------------------------------------
     def _decode_tree(self, j):
+        """Record j -> compact pre-order arrays; per-era importance of its
+        splits accumulated in pre-order (core.py:624-627 adds them while
+        growing depth first, left before right)."""
         D, E = self.max_depth, self.num_eras
         nodes = self._rec_nodes[j].numpy().view(_lib.NODE_DTYPE)
-        gains = self._rec_gain[j].numpy()
+        gains = self._rec_gain[j].numpy()[: ((1 << D) - 1) * E]
         feats = self._rec_feats[j].numpy()
-        imp = self.per_era_feature_importance_
+        packed, leaf, samples, sp_pre, sp_feat, sp_gain = compact_tree(nodes, gains, feats, D, E)
+        if len(sp_feat):
+            np.add.at(self.per_era_feature_importance_, (slice(None), sp_feat), sp_gain.T)
+        return packed, leaf, samples
 
-        def rec(d, n):
-            nd = nodes[(1 << d) - 1 + n]
-            if d < D and nd["fpos"] >= 0:
-                gfi = int(feats[nd["fpos"]])
-                g0 = ((1 << d) - 1 + n) * E
-                imp[:, gfi] += gains[g0:g0 + E]
-                return {"feature": gfi, "bin": int(nd["bin"]),
-                        "left": rec(d + 1, int(nd["child"])),
-                        "right": rec(d + 1, int(nd["child"]) + 1)}
-            return {"leaf_value": float(nd["leaf"]), "samples": int(nd["count"])}
-        return rec(0, 0)
+    def _drain_records(self, classification):
+        """Decode the records whose device->host copies have landed, without
+        waiting: the host does it while the GPU grows the next trees."""
+        j = self._rec_decoded
+        while j < self._rec_done and self._rec_events[j].query():
+            self._store_tree(j, classification)
+            self._rec_events[j] = None
+            j += 1
+        self._rec_decoded = j
 
     def _finalize_records(self, classification):
         torch.cuda.current_stream().synchronize()
@@ -801,19 +934,19 @@ class WarpGBM(BaseEstimator, RegressorMixin):
 
     def _store_tree(self, j, classification):
         i, c = self._rec_meta[j]
-        tree = self._decode_tree(j)
+        compact = self._decode_tree(j)
         if not hasattr(self, "feature_subsets_"):
             self.feature_subsets_ = []
         if c == 0:
             while len(self.feature_subsets_) <= i:
                 self.feature_subsets_.append(None)
             self.feature_subsets_[i] = self._rec_feats[j].numpy().copy()
+        f = self.__dict__["_forest"]
         if classification:
-            while len(self.forest) <= i:
-                self.forest.append([None] * self.num_classes)
-            self.forest[i][c] = tree
-        else:
-            self.forest[i] = tree
+            while len(f) <= i:
+                f.append([None] * self.num_classes)
+        self._compact[(i, c)] = compact
+        self._lazy.add((i, c))
         self._packed = None
 
     def _sync_records(self, classification):
@@ -827,7 +960,7 @@ class WarpGBM(BaseEstimator, RegressorMixin):
         for name in ("_t", "_ws", "_keep", "_pred", "Y_gpu", "_eval_bins", "_eval_pred", "_Y_eval"):
             if hasattr(self, name):
                 delattr(self, name)
-        for name in ("_rec_nodes", "_rec_gain", "_rec_feats", "_rec_meta"):
+        for name in ("_rec_nodes", "_rec_gain", "_rec_feats", "_rec_meta", "_rec_events"):
             if hasattr(self, name):
                 delattr(self, name)
         self._rec_decoded = 0
@@ -917,9 +1050,31 @@ class WarpGBM(BaseEstimator, RegressorMixin):
             return [t for t in self.forest if t]
         return [t for rnd in self.forest if rnd for t in rnd]
 
+    def _tree_slots(self):
+        """(i, c) of every trained tree in prediction order (round-major)."""
+        f = self.__dict__.get("_forest") or []
+        lazy, out = self.__dict__.get("_lazy", set()), []
+        for i, r in enumerate(f):
+            if isinstance(r, list):
+                out.extend((i, c) for c, t in enumerate(r) if t or (i, c) in lazy)
+            elif r or (i, 0) in lazy:
+                out.append((i, 0))
+        return out
+
     def _ensure_packed(self):
         if self._packed is None:
-            nodes, offs = pack_trees(self._flat_trees())
+            compact, f = self.__dict__.get("_compact", {}), self.__dict__.get("_forest")
+            parts = []
+            for (i, c) in self._tree_slots():
+                if (i, c) in compact:
+                    parts.append(compact[(i, c)][0])
+                else:   # a tree given as a dict (loaded model)
+                    t = f[i][c] if isinstance(f[i], list) else f[i]
+                    parts.append(pack_trees([t])[0])
+            offs = np.zeros(len(parts) + 1, np.int32)
+            if parts:
+                offs[1:] = np.cumsum([len(p) for p in parts])
+            nodes = np.concatenate(parts) if parts else np.zeros((0, 2), np.int32)
             dev = getattr(self, "_dev", torch.device("cuda", torch.cuda.current_device()))
             self._packed = (torch.from_numpy(nodes.reshape(-1)).to(dev),
                             torch.from_numpy(offs).to(dev), offs)
@@ -958,12 +1113,12 @@ class WarpGBM(BaseEstimator, RegressorMixin):
     def predict_binned(self, bins):
         out = torch.zeros((bins.shape[0], 1), dtype=torch.float32, device=bins.device) + \
             np.float32(self.base_prediction)
-        self._predict_into(bins, out, 0, len(self._flat_trees()))
+        self._predict_into(bins, out, 0, len(self._tree_slots()))
         return out[:, 0]
 
     def predict_proba_binned(self, bins):
         out = self._init_proba_logits(bins.shape[0])
-        self._predict_into(bins, out, 0, len([r for r in self.forest if r]))
+        self._predict_into(bins, out, 0, len({i for i, _ in self._tree_slots()}))
         return softmax(out, dim=1)
 
     def predict(self, X_np):
