@@ -53,6 +53,8 @@ def parse():
     ap.add_argument("--trees", type=int, default=CONFIG["n_estimators"])
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu", action="store_true", help="skip the cpu_baseline sample")
+    ap.add_argument("--clock-ms", type=int, default=200,
+                    help="nvidia-smi sampling period during the timed region (0: no sampling)")
     ap.add_argument("--config", default="c2", choices=["c2", "c5"],
                     help="c5: 20M x 500 pre-binned rows split over the GPUs (strong scaling), "
                          "depth 10, 50 trees, then batch predict")
@@ -84,13 +86,16 @@ def make_data(rank: int, n: int, F: int, device):
 class Clocks:
     """nvidia-smi sampling during the timed region."""
 
-    def __init__(self, index: int):
+    def __init__(self, index: int, period_ms: int = 200):
         self.index = index
+        self.period = period_ms
         self.proc = None
         fd, self.path = tempfile.mkstemp(prefix="wgb_clocks_", suffix=".csv")
         os.close(fd)
 
     def __enter__(self):
+        if self.period <= 0:
+            return self
         try:
             self.f = open(self.path, "w")
             self.proc = subprocess.Popen(
@@ -98,7 +103,7 @@ class Clocks:
                  "--query-gpu=clocks.sm,clocks.max.sm,clocks_event_reasons.active,"
                  "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
                  "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap",
-                 "--format=csv,noheader,nounits", "-lms", "200"],
+                 "--format=csv,noheader,nounits", "-lms", str(self.period)],
                 stdout=self.f, stderr=subprocess.DEVNULL)
         except Exception:
             self.proc = None
@@ -317,15 +322,13 @@ def run_c5(args, world, rank, local):
     launches0 = _lib.LAUNCHES[0]
     fit_ms, pred_ms = [], []
     model = None
-    with Clocks(local) as clk:
+    with Clocks(local, args.clock_ms) as clk:
         for _ in range(args.steps):
             barrier()
             e0, e1, e2 = (torch.cuda.Event(enable_timing=True) for _ in range(3))
             e0.record()
             with contextlib.redirect_stdout(io.StringIO()):
                 model = WarpGBM(**params)
-                model._hist_events = []
-                model._comm_events = []
                 model.fit(X, y)
             e1.record()
             pred = model.predict(X)
@@ -334,6 +337,11 @@ def run_c5(args, world, rank, local):
             fit_ms.append(max_over_ranks(e0.elapsed_time(e1)))
             pred_ms.append(max_over_ranks(e1.elapsed_time(e2)))
     launches = _lib.LAUNCHES[0] - launches0
+    with contextlib.redirect_stdout(io.StringIO()):  # roofline fit, per-level events
+        model = WarpGBM(**params)
+        model._hist_events = []
+        model._comm_events = []
+        model.fit(X, y)
     hist_ms = sum(a.elapsed_time(b) for a, b in model._hist_events)
     comm_ms = sum(a.elapsed_time(b) for a, b in model._comm_events)
     hist_bytes = hist_algorithmic_bytes(model, n_total, F, 1, C5["num_bins"], world)
@@ -404,29 +412,41 @@ def main():
             WarpGBM(**params).fit(X, y)
     barrier()
     model = None
-    times, hist_ms, hist_bytes, comm_ms = [], 0.0, 0.0, 0.0
+    model = None
     launches0 = _lib.LAUNCHES[0]
-    with Clocks(local) as clk:
+    with Clocks(local, args.clock_ms) as clk:
         barrier()
         e0 = torch.cuda.Event(enable_timing=True)
         e1 = torch.cuda.Event(enable_timing=True)
         e0.record()
-        models = []
+        w0 = time.perf_counter()
         with contextlib.redirect_stdout(io.StringIO()):
             for _ in range(args.steps):
                 model = WarpGBM(**params)
-                model._hist_events = []
-                model._comm_events = []
                 model.fit(X, y)
-                models.append(model)
+        w1 = time.perf_counter()
         e1.record()
         barrier()
-    for model in models:  # host-side accounting, outside the timed region
-        hist_ms += sum(a.elapsed_time(b) for a, b in model._hist_events)
-        comm_ms += sum(a.elapsed_time(b) for a, b in model._comm_events)
-        hist_bytes += hist_algorithmic_bytes(model, model._n_global if world > 1 else n,
-                                             F, 1, CONFIG["num_bins"], world)
+    host_ms = (w1 - w0) * 1000.0 / args.steps
     launches = _lib.LAUNCHES[0] - launches0
+    # roofline: one more fit with CUDA events around every histogram level
+    # (and collective) on the launching stream; per-level events make it run
+    # with eager launches instead of the single-GPU tree graph
+    r0, r1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    barrier()
+    r0.record()
+    with contextlib.redirect_stdout(io.StringIO()):
+        model = WarpGBM(**params)
+        model._hist_events = []
+        model._comm_events = []
+        model.fit(X, y)
+    r1.record()
+    barrier()
+    eager_ms = r0.elapsed_time(r1)
+    hist_ms = sum(a.elapsed_time(b) for a, b in model._hist_events)
+    comm_ms = sum(a.elapsed_time(b) for a, b in model._comm_events)
+    hist_bytes = hist_algorithmic_bytes(model, model._n_global if world > 1 else n,
+                                        F, 1, CONFIG["num_bins"], world)
     t = e0.elapsed_time(e1) / args.steps
     tt = torch.tensor([t], device=dev)
     if world > 1:
@@ -435,7 +455,7 @@ def main():
     value = t / 1000.0 * 100.0 / args.trees
     peak, peak_kind = peaks()
     achieved = hist_bytes / (hist_ms / 1000.0) / 1e9 if hist_ms > 0 else None
-    nlaunch = len(model._hist_events) if model is not None else 0
+    nlaunch = len(model._hist_events)
 
     e2e = None
     if not args.no_e2e:
@@ -477,14 +497,18 @@ def main():
                          "achieved": round(achieved, 1) if achieved else None, "peak": peak,
                          "unit": "GB/s", "frac": round(achieved / peak, 4) if achieved else None,
                          "peak_kind": peak_kind,
-                         "traffic": round(HIST_TRAFFIC_PER_ALG_BYTE * hist_bytes / max(nlaunch * args.steps, 1))
+                         "traffic": round(HIST_TRAFFIC_PER_ALG_BYTE * hist_bytes / max(nlaunch, 1))
                          if hist_bytes else None,
                          "traffic_unit": "bytes per launch (ncu ratio 1.049 x algorithmic)",
-                         "launches_timed": nlaunch * args.steps,
-                         "avg_launch_ms": round(hist_ms / max(nlaunch * args.steps, 1), 4)},
+                         "launches_timed": nlaunch,
+                         "avg_launch_ms": round(hist_ms / max(nlaunch, 1), 4),
+                         "timed_on": "one extra fit with CUDA events around every histogram level"},
             "e2e": e2e,
-            "breakdown_rank0_ms_per_step": {"histogram_kernels": round(hist_ms / args.steps, 1),
-                                            "collectives": round(comm_ms / args.steps, 1)},
+            "breakdown_rank0_ms_per_step": {"histogram_kernels": round(hist_ms, 1),
+                                            "collectives": round(comm_ms, 1),
+                                            "roofline_fit": round(eager_ms, 1),
+                                            "host_wall_per_timed_fit": round(host_ms, 1),
+                                            "note": "from the roofline fit (eager launches)"},
             "gpu_launches": launches,
             "clocks": clk.summary(),
         }

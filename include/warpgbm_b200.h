@@ -126,6 +126,16 @@ int wgb_predict_forest(const int8_t *bin_indices, int64_t n, int64_t F,
 /* 2. level-wise engine                                                    */
 /* ---------------------------------------------------------------------- */
 
+/* Pre-binned int8 input in one pass (replaces the per-column copy of
+ * warpgbm/core.py:499-517): out [n][out_stride] = X (padding bytes 0),
+ * colmax[f] = max over rows of X[:, f] (the reference's pre-binned test is
+ * all(colmax < num_bins)), minmax[0] / minmax[1] = global min / max (bins
+ * outside [0, num_bins) take the checked histogram path).  With n == 0,
+ * colmax and minmax hold sentinels below / above every int8. */
+int wgb_prebinned_ingest(const int8_t *X, int64_t n, int32_t F, int64_t x_stride,
+                         int8_t *out, int64_t out_stride, int32_t *colmax,
+                         int32_t *minmax, void *stream);
+
 /* Binning of a row-major float32 matrix in one pass (replaces the per-column
  * loop of warpgbm/core.py:527-538 and core.py:902-915).  X is [n][F] with
  * row stride x_stride (elements); edges [F][num_bins-1]; out is int8

@@ -80,6 +80,31 @@ def test_bin_matrix_edge_lists(cuda, F, xs, B):
     assert (got[:, F:] == 0).all()
 
 
+@pytest.mark.parametrize("n,F", [(5000, 64), (3001, 37), (700, 130), (0, 9), (1, 1)])
+def test_prebinned_ingest(cuda, n, F):
+    """One-pass pre-binned copy: padded bins, per-column maxima (the reference's
+    pre-binned test, core.py:499-502) and global min / max."""
+    rng = np.random.default_rng(n + F)
+    X = rng.integers(-5, 40, (n, F)).astype(np.int8)
+    S = bins_stride(F)
+    out = torch.full((max(n, 1), S), 99, dtype=torch.int8, device=cuda)
+    colmax = torch.zeros(F, dtype=torch.int32, device=cuda)
+    minmax = torch.zeros(2, dtype=torch.int32, device=cuda)
+    Xd = torch.from_numpy(X).to(cuda)
+    _lib.call("wgb_prebinned_ingest", Xd.data_ptr() if n else 0, n, F, F, out.data_ptr(), S,
+              colmax.data_ptr(), minmax.data_ptr(), _st())
+    if n == 0:
+        assert (colmax.cpu().numpy() < -128).all()
+        mm = minmax.cpu().numpy()
+        assert mm[0] > 127 and mm[1] < -128
+        return
+    got = out.cpu().numpy()
+    assert np.array_equal(got[:, :F], X)
+    assert (got[:, F:] == 0).all()
+    assert np.array_equal(colmax.cpu().numpy(), X.max(axis=0).astype(np.int32))
+    assert list(minmax.cpu().numpy()) == [int(X.min()), int(X.max())]
+
+
 def test_torch_cuda_quantile_equals_oracle(cuda):
     """Pins the oracle's quantile restatement (FMA lerp, linspace formula) to
     torch.quantile on the B200 -- the op the reference calls at core.py:532."""

@@ -610,6 +610,29 @@ class WarpGBM(BaseEstimator, RegressorMixin):
             is_int = np.issubdtype(X_np.dtype, np.integer)
         if is_int and (fit or F == self.num_features):
             Xi = _to_dev(X_np, dev)
+            if Xi.dtype == torch.int8:
+                # one pass: padded copy, column maxima, global min / max
+                bins = torch.empty((n, S), dtype=torch.int8, device=dev)
+                colmax = torch.empty(F, dtype=torch.int32, device=dev)
+                minmax = torch.empty(2, dtype=torch.int32, device=dev)
+                _lib.call("wgb_prebinned_ingest", Xi.data_ptr(), n, F, F, bins.data_ptr(), S,
+                          colmax.data_ptr(), minmax.data_ptr(), torch.cuda.current_stream().cuda_stream)
+                mx = colmax.to(torch.int64)
+                if fit:
+                    self._comm.max_(mx)
+                if bool((mx < B).all().item()):
+                    print("Detected pre-binned integer input — skipping quantile binning." if fit
+                          else "Detected pre-binned input at predict-time — skipping binning.")
+                    if fit:
+                        self.bin_edges = torch.arange(1, B, dtype=torch.float32, device=dev).repeat(F, 1)
+                        mn = minmax[0:1].to(torch.int64)
+                        mxb = minmax[1:2].to(torch.int64)
+                        self._comm.max_(mxb)
+                        mn = -self._comm.max_(-mn)
+                        self._bins_regular = bool(mn.item() >= 0 and mxb.item() < B)
+                    return bins, True
+                del bins
+                return self._upload_float(Xi.to(torch.float32), fit)
             mx = torch.full((F,), -(2 ** 62), dtype=torch.int64, device=dev)
             if n:
                 mx = Xi.amax(dim=0).to(torch.int64)
@@ -636,6 +659,13 @@ class WarpGBM(BaseEstimator, RegressorMixin):
             Xd = Xi.to(torch.float32)
         else:
             Xd = _to_dev(X_np, dev, torch.float32)
+        return self._upload_float(Xd, fit)
+
+    def _upload_float(self, Xd, fit: bool):
+        """Quantile edges (at fit) and binning of a float32 device matrix."""
+        dev, B = self._dev, self.num_bins
+        n, F = Xd.shape
+        S = bins_stride(F)
         if fit:
             print("quantile binning.")
             self._bins_regular = True  # binner output is always in [0, B)
@@ -809,19 +839,21 @@ class WarpGBM(BaseEstimator, RegressorMixin):
             self._rec_decoded = 0
             self._rec_meta = []
             self._rec_events = []
+            self._graphs, self._graph_warm = {}, set()
             self._residuals = []
             if not resume:
                 self.feature_subsets_ = []
-            feats_all = torch.arange(F, dtype=torch.int32, device=dev)
+            subsets = self.colsample_bytree < 1.0
+            if not subsets:  # every tree uses all features in order
+                self._t["feats"].copy_(torch.arange(F, dtype=torch.int32, device=dev))
+                self._t["kpos"].copy_(torch.arange(F, dtype=torch.int32, device=dev))
             for i in range(start, self.n_estimators):
-                if self.colsample_bytree < 1.0:
+                if subsets:
                     feats = torch.randperm(F, device=dev, dtype=torch.int32)[:k]
                     comm.bcast_(feats)
-                else:
-                    feats = feats_all
-                self._t["feats"].copy_(feats)
-                self._t["kpos"].fill_(-1)
-                self._t["kpos"][feats.long()] = torch.arange(k, dtype=torch.int32, device=dev)
+                    self._t["feats"].copy_(feats)
+                    self._t["kpos"].fill_(-1)
+                    self._t["kpos"][feats.long()] = torch.arange(k, dtype=torch.int32, device=dev)
                 if classification:
                     grads = softmax(pred, dim=1)
                     grads[torch.arange(N, device=dev), Yl.long()] -= 1.0
@@ -847,9 +879,63 @@ class WarpGBM(BaseEstimator, RegressorMixin):
             self._release()
         return self
 
+    def _tree_launches(self, ws, st):
+        """Device work of one tree on a single GPU (what the tree graph holds)."""
+        p = ctypes_ptr(ws)
+        _lib.call("wgb_tree_reset", p, st())
+        _lib.call("wgb_tree_residual", p, st())
+        _lib.call("wgb_tree_quantize", p, st())
+        _lib.call("wgb_tree_root", p, st())
+        for d in range(self.max_depth):
+            _lib.call("wgb_level_hist", p, d, st())
+            _lib.call("wgb_level_split", p, d, st())
+            _lib.call("wgb_level_partition", p, d, st())
+        _lib.call("wgb_tree_finish", p, st())
+
+    def _capture_tree(self, ws, st, cls):
+        """CUDA graph of one tree's launches (sizes live on the device, so one
+        graph serves every tree of the fit); None if capture is refused."""
+        g = torch.cuda.CUDAGraph()
+        side = torch.cuda.Stream()
+        side.wait_stream(torch.cuda.current_stream())
+        n0 = _lib.LAUNCHES[0]
+        try:
+            with torch.cuda.stream(side):
+                g.capture_begin(capture_error_mode="thread_local")
+                try:
+                    self._tree_launches(ws, st)
+                finally:
+                    g.capture_end()
+        except Exception:
+            self._graphs = None  # eager launches from here on
+            return None
+        finally:
+            self._graph_launches = _lib.LAUNCHES[0] - n0
+            _lib.LAUNCHES[0] = n0
+            torch.cuda.current_stream().wait_stream(side)
+        self._graphs[cls] = g
+        return g
+
     def _grow_tree(self, ws, cls, st, i, c):
         comm = self._comm
         ws.cls = cls
+        graphs = getattr(self, "_graphs", None)
+        if (graphs is not None and not comm.on and getattr(self, "_hist_events", None) is None
+                and getattr(self, "_comm_events", None) is None
+                and not getattr(self, "_record_residuals", False)):
+            # single GPU: the first tree of each class runs eagerly (lazy
+            # one-time set-up), later ones replay a captured graph
+            g = graphs.get(cls)
+            if g is None and cls in self._graph_warm:
+                g = self._capture_tree(ws, st, cls)
+            if g is not None:
+                g.replay()
+                _lib.LAUNCHES[0] += self._graph_launches
+            else:
+                self._tree_launches(ws, st)
+                self._graph_warm.add(cls)
+            self._store_record(i, c)
+            return
         p = ctypes_ptr(ws)
         _lib.call("wgb_tree_reset", p, st())
         _lib.call("wgb_tree_residual", p, st())
@@ -889,6 +975,9 @@ class WarpGBM(BaseEstimator, RegressorMixin):
         _lib.call("wgb_tree_finish", p, st())
         if getattr(self, "_record_residuals", False):  # test hook: residual of every tree
             self._residuals.append(self._t["g"][: ws.N].cpu().numpy().copy())
+        self._store_record(i, c)
+
+    def _store_record(self, i, c):
         j = self._rec_done
         self._rec_nodes[j].copy_(self._t["nodes"], non_blocking=True)
         self._rec_gain[j, : self._t["era_gain"].numel()].copy_(self._t["era_gain"], non_blocking=True)
@@ -957,6 +1046,7 @@ class WarpGBM(BaseEstimator, RegressorMixin):
             self._rec_decoded = self._rec_done
 
     def _release(self):
+        self._graphs = None
         for name in ("_t", "_ws", "_keep", "_pred", "Y_gpu", "_eval_bins", "_eval_pred", "_Y_eval"):
             if hasattr(self, name):
                 delattr(self, name)

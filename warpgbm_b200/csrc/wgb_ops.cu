@@ -83,6 +83,57 @@ __global__ void __launch_bounds__(256) k_bin_matrix(const float *__restrict__ X,
     }
 }
 
+// Pre-binned int8 input (core.py:499-517), one pass: copy X [n][F] into the
+// padded bin matrix [n][S] (zeros past F), per-column maxima (the reference's
+// pre-binned test is max(X, axis=0) < num_bins) and the global minimum and
+// maximum (bins outside [0, B) need the checked histogram path).  CTA = 256
+// rows x 128 columns, lane l of a warp owns columns 4l..4l+3 of one row.
+__global__ void __launch_bounds__(256) k_prebinned(const int8_t *__restrict__ X, long long n, int F,
+                                                   long long xs, int8_t *__restrict__ out, long long os,
+                                                   int *__restrict__ colmax, int *__restrict__ minmax) {
+    const int tl = threadIdx.x & 31;
+    const int f = blockIdx.y * BIN_FT + 4 * tl;
+    const bool in_row = f < os;  // lanes past the row stay for the warp reductions below
+    const bool vec = (xs % 4 == 0) && (f + 4 <= F);
+    int cmax[4] = {INT_MIN, INT_MIN, INT_MIN, INT_MIN};
+    int gmin = INT_MAX, gmax = INT_MIN;
+    const long long r0 = (long long)blockIdx.x * BIN_ROWS;
+    for (int rr = threadIdx.x >> 5; in_row && rr < BIN_ROWS; rr += blockDim.x >> 5) {
+        const long long r = r0 + rr;
+        if (r >= n) break;
+        const int8_t *xr = X + r * xs;
+        uint32_t w;
+        if (vec) {
+            w = __ldg(reinterpret_cast<const uint32_t *>(xr + f));
+        } else {
+            w = 0;
+#pragma unroll
+            for (int j = 0; j < 4; ++j)
+                if (f + j < F) w |= (uint32_t)(uint8_t)__ldg(xr + f + j) << (8 * j);
+        }
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+            if (f + j < F) {
+                const int v = (int)(int8_t)(w >> (8 * j));
+                cmax[j] = max(cmax[j], v);
+                gmin = min(gmin, v);
+                gmax = max(gmax, v);
+            }
+        }
+        *reinterpret_cast<uint32_t *>(out + r * os + f) = w;
+    }
+#pragma unroll
+    for (int j = 0; j < 4; ++j)
+        if (f + j < F && cmax[j] != INT_MIN) atomicMax(colmax + f + j, cmax[j]);
+    gmin = warp_min(gmin);
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) gmax = max(gmax, __shfl_xor_sync(0xffffffffu, gmax, o));
+    if (tl == 0 && gmax != INT_MIN) {
+        atomicMin(minmax, gmin);
+        atomicMax(minmax + 1, gmax);
+    }
+}
+
 __global__ void k_bin_column(const float *__restrict__ X, long long n, const float *__restrict__ e,
                              int nb, int8_t *__restrict__ out) {
     long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x;
@@ -301,6 +352,23 @@ int wgb_bin_matrix(const float *X, int64_t n, int32_t F, int64_t x_stride, const
     WGB_CUDA(cudaFuncSetAttribute(k_bin_matrix, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
     k_bin_matrix<<<grid, 256, smem, as_stream(stream)>>>(X, n, F, x_stride, edges, nb, out, out_stride);
     WGB_LAUNCHED("k_bin_matrix");
+    return WGB_OK;
+}
+
+int wgb_prebinned_ingest(const int8_t *X, int64_t n, int32_t F, int64_t x_stride, int8_t *out,
+                         int64_t out_stride, int32_t *colmax, int32_t *minmax, void *stream) {
+    WGB_CHECK_ARG(n >= 0 && F >= 1 && x_stride >= F, "bad shape n=%lld F=%d", (long long)n, F);
+    WGB_CHECK_ARG(out_stride >= F && out_stride % 4 == 0, "out_stride must be >= F and a multiple of 4");
+    WGB_CHECK_ARG(colmax && minmax && (out || n == 0) && (X || n == 0), "NULL pointer");
+    cudaStream_t st = as_stream(stream);
+    // sentinels: 0x80808080 is below every int8, 0x7f7f7f7f above
+    WGB_CUDA(cudaMemsetAsync(colmax, 0x80, sizeof(int32_t) * F, st));
+    WGB_CUDA(cudaMemsetAsync(minmax, 0x7f, sizeof(int32_t), st));
+    WGB_CUDA(cudaMemsetAsync(minmax + 1, 0x80, sizeof(int32_t), st));
+    if (n == 0) return WGB_OK;
+    dim3 grid((unsigned)((n + BIN_ROWS - 1) / BIN_ROWS), (unsigned)((out_stride + BIN_FT - 1) / BIN_FT));
+    k_prebinned<<<grid, 256, 0, st>>>(X, n, F, x_stride, out, out_stride, colmax, minmax);
+    WGB_LAUNCHED("k_prebinned");
     return WGB_OK;
 }
 
