@@ -42,8 +42,8 @@ def test_bin_matrix_matches_oracle(cuda, n, F, B):
     assert (got[:, F:] == 0).all()
 
 
-@pytest.mark.parametrize("F,xs", [(64, 64), (61, 61), (40, 45)])
-@pytest.mark.parametrize("B", [2, 9, 32, 127])
+@pytest.mark.parametrize("F,xs", [(64, 64), (61, 61), (40, 45), (300, 300)])
+@pytest.mark.parametrize("B", [2, 4, 9, 16, 32, 64, 127])
 def test_bin_matrix_edge_lists(cuda, F, xs, B):
     """Binning against the oracle's leading-edge scan for edge lists of every
     shape: sorted, with ties, with infinities, unsorted, all-NaN, one NaN;

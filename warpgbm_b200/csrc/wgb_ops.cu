@@ -9,47 +9,43 @@ namespace wgb {
 // ====================================================================== //
 
 // Row-major float [n][F] -> int8 [n][out_stride] in one pass.  CTA = 256
-// rows x 128 features; lane l of a warp bins features 4l..4l+3 of one row.
-// Per element the reference scan (binner.cu:20-23) counts leading edges with
+// rows x 128 features; lane l of a warp bins features l, l+32, l+64, l+96 of
+// one row (four coalesced 128-byte loads, four 32-byte stores).  Per element
+// the reference scan (binner.cu:20-23) counts leading edges with
 // x >= edge, stopping at the first failure.  When a feature's edges are
 // non-decreasing (always true for quantile edges; all-NaN edges included,
 // where every comparison fails) that count is found by binary search; any
 // other edge list keeps the linear scan.  Edges sit in shared memory
-// feature-major with an odd stride ([128][nb | 1]).
+// edge-major ([b][128]), so the 32 lanes of a warp always read 32 distinct
+// banks, whatever edge each one is looking at.
 constexpr int BIN_FT = 128, BIN_ROWS = 256;
 
-__device__ __forceinline__ int bin_linear(float x, const float *e, int nb) {
-    int b = 0;
-    while (b < nb && x >= e[b]) ++b;
-    return b;
-}
-
+// NB > 0: num_bins - 1 == NB == 2^k - 1 at compile time (the search needs no
+// bounds test and unrolls); NB == 0: any num_bins.
+template <int NB>
 __global__ void __launch_bounds__(256) k_bin_matrix(const float *__restrict__ X, long long n, int F,
                                                     long long xs, const float *__restrict__ edges,
                                                     int nb, int8_t *__restrict__ out, long long os) {
-    extern __shared__ float s_e[];  // [BIN_FT][es]
+    extern __shared__ float s_e[];  // [nb][BIN_FT]
     __shared__ int s_mono[BIN_FT];
-    const int es = nb | 1;
     const int f0 = blockIdx.y * BIN_FT;
     for (int t = threadIdx.x; t < BIN_FT * nb; t += blockDim.x) {
         const int fl = t / nb, b = t - fl * nb;
         const int f = f0 + fl;
-        s_e[fl * es + b] = f < F ? edges[(long long)f * nb + b] : 0.0f;
+        s_e[b * BIN_FT + fl] = f < F ? edges[(long long)f * nb + b] : 0.0f;
     }
     __syncthreads();
     for (int fl = threadIdx.x; fl < BIN_FT; fl += blockDim.x) {
-        const float *e = s_e + fl * es;
         bool all_nan = true, mono = true;
-        for (int b = 0; b < nb; ++b) all_nan &= isnan(e[b]);
-        for (int b = 0; b + 1 < nb; ++b) mono &= e[b] <= e[b + 1];
+        for (int b = 0; b < nb; ++b) all_nan &= isnan(s_e[b * BIN_FT + fl]);
+        for (int b = 0; b + 1 < nb; ++b) mono &= s_e[b * BIN_FT + fl] <= s_e[(b + 1) * BIN_FT + fl];
         s_mono[fl] = all_nan || mono;
     }
     __syncthreads();
-    const int tl = threadIdx.x & 31;  // feature quad within the tile
-    const int f = f0 + 4 * tl;
-    if (f >= os) return;
-    const bool vec = (xs % 4 == 0) && (f + 4 <= F);
-    const bool mono = s_mono[4 * tl] && s_mono[4 * tl + 1] && s_mono[4 * tl + 2] && s_mono[4 * tl + 3];
+    const int tl = threadIdx.x & 31;
+    bool mono[4];
+#pragma unroll
+    for (int j = 0; j < 4; ++j) mono[j] = s_mono[tl + 32 * j];
     int top = 1;
     while (top * 2 <= nb) top *= 2;  // largest power of two <= nb
     const long long r0 = (long long)blockIdx.x * BIN_ROWS;
@@ -58,28 +54,33 @@ __global__ void __launch_bounds__(256) k_bin_matrix(const float *__restrict__ X,
         if (r >= n) break;
         const float *xr = X + r * xs;
         float v[4];
-        if (vec) {
-            const float4 x4 = __ldg(reinterpret_cast<const float4 *>(xr + f));
-            v[0] = x4.x; v[1] = x4.y; v[2] = x4.z; v[3] = x4.w;
-        } else {
-#pragma unroll
-            for (int j = 0; j < 4; ++j) v[j] = (f + j < F) ? __ldg(xr + f + j) : 0.0f;
-        }
-        uint32_t w = 0;
 #pragma unroll
         for (int j = 0; j < 4; ++j) {
-            const float *e = s_e + (4 * tl + j) * es;
-            int b;
-            if (mono) {
-                b = 0;
-                for (int step = top; step >= 1; step >>= 1)
-                    if (b + step <= nb && v[j] >= e[b + step - 1]) b += step;
-            } else {
-                b = bin_linear(v[j], e, nb);
-            }
-            if (f + j < F) w |= (uint32_t)(uint8_t)b << (8 * j);
+            const int f = f0 + tl + 32 * j;
+            v[j] = f < F ? __ldg(xr + f) : 0.0f;
         }
-        *reinterpret_cast<uint32_t *>(out + r * os + f) = w;
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+            const int f = f0 + tl + 32 * j;
+            if (f >= os) continue;
+            const float *e = s_e + tl + 32 * j;
+            int b = 0;
+            if (f < F) {
+                if (NB > 0 && mono[j]) {
+#pragma unroll
+                    for (int step = (NB + 1) / 2; step >= 1; step >>= 1) {
+                        const int c = b + step;  // <= NB for every path when NB = 2^k - 1
+                        b = v[j] >= e[(c - 1) * BIN_FT] ? c : b;
+                    }
+                } else if (mono[j]) {
+                    for (int step = top; step >= 1; step >>= 1)
+                        if (b + step <= nb && v[j] >= e[(b + step - 1) * BIN_FT]) b += step;
+                } else {
+                    while (b < nb && v[j] >= e[b * BIN_FT]) ++b;
+                }
+            }
+            out[r * os + f] = (int8_t)b;
+        }
     }
 }
 
@@ -347,11 +348,23 @@ int wgb_bin_matrix(const float *X, int64_t n, int32_t F, int64_t x_stride, const
     if (n == 0) return WGB_OK;
     WGB_CHECK_ARG(X && edges && out, "NULL pointer");
     const int nb = num_bins - 1;
-    size_t smem = (size_t)(nb | 1) * BIN_FT * sizeof(float);
+    size_t smem = (size_t)nb * BIN_FT * sizeof(float);
     dim3 grid((unsigned)((n + BIN_ROWS - 1) / BIN_ROWS), (unsigned)((out_stride + BIN_FT - 1) / BIN_FT));
-    WGB_CUDA(cudaFuncSetAttribute(k_bin_matrix, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
-    k_bin_matrix<<<grid, 256, smem, as_stream(stream)>>>(X, n, F, x_stride, edges, nb, out, out_stride);
-    WGB_LAUNCHED("k_bin_matrix");
+#define WGB_BIN_CASE(NB_)                                                                                  \
+    if (NB_ == 0 || nb == NB_) {                                                                          \
+        WGB_CUDA(cudaFuncSetAttribute(k_bin_matrix<NB_>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem)); \
+        k_bin_matrix<NB_><<<grid, 256, smem, as_stream(stream)>>>(X, n, F, x_stride, edges, nb, out, out_stride); \
+        WGB_LAUNCHED("k_bin_matrix");                                                                     \
+        return WGB_OK;                                                                                    \
+    }
+    WGB_BIN_CASE(31)
+    WGB_BIN_CASE(15)
+    WGB_BIN_CASE(63)
+    WGB_BIN_CASE(7)
+    WGB_BIN_CASE(3)
+    WGB_BIN_CASE(1)
+    WGB_BIN_CASE(0)
+#undef WGB_BIN_CASE
     return WGB_OK;
 }
 
