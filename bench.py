@@ -430,8 +430,8 @@ def main():
     host_ms = (w1 - w0) * 1000.0 / args.steps
     launches = _lib.LAUNCHES[0] - launches0
     # roofline: one more fit with CUDA events around every histogram level
-    # (and collective) on the launching stream; per-level events make it run
-    # with eager launches instead of the single-GPU tree graph
+    # (and collective) on the launching stream, so the timed fits above run
+    # without instrumentation
     r0, r1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     barrier()
     r0.record()
@@ -508,7 +508,7 @@ def main():
                                             "collectives": round(comm_ms, 1),
                                             "roofline_fit": round(eager_ms, 1),
                                             "host_wall_per_timed_fit": round(host_ms, 1),
-                                            "note": "from the roofline fit (eager launches)"},
+                                            "note": "from the roofline fit"},
             "gpu_launches": launches,
             "clocks": clk.summary(),
         }

@@ -134,34 +134,6 @@ def test_moderate_scale_bit_exact_and_deterministic(cuda):
     assert np.array_equal(p1, o.predict(X))
 
 
-@pytest.mark.parametrize("objective", ["regression", "multiclass"])
-def test_tree_graph_replay_equals_eager_launches(cuda, objective):
-    """On one GPU every tree after the first replays a captured CUDA graph;
-    a fit with per-level timing events runs eagerly.  Same trees, same
-    predictions, and the graph path really was taken."""
-    rng = np.random.default_rng(21)
-    n, F = 30_000, 24
-    X = rng.standard_normal((n, F)).astype(np.float32)
-    if objective == "regression":
-        y = (X[:, 0] - X[:, 1] * X[:, 2] + 0.2 * rng.standard_normal(n)).astype(np.float32)
-    else:
-        y = (X[:, 0] > 0).astype(np.int64) + (X[:, 3] > 0.5).astype(np.int64)
-    params = dict(objective=objective, num_bins=16, max_depth=5, n_estimators=6, learning_rate=0.3,
-                  colsample_bytree=0.7, random_state=1)
-    g = WarpGBM(**params)
-    g.fit(X, y)
-    assert g.__dict__.get("_graph_launches", 0) > 0
-    e = WarpGBM(**params)
-    e._hist_events = []
-    e.fit(X, y)
-    cl = objective != "regression"
-    assert _same(_flat(g, 5, cl), _flat(e, 5, cl))
-    if cl:
-        assert np.array_equal(g.predict_proba(X), e.predict_proba(X))
-    else:
-        assert np.array_equal(g.predict(X), e.predict(X))
-
-
 @pytest.mark.parametrize("D,n,F", [(10, 60_000, 40), (13, 40_000, 12)])
 def test_deep_trees_bit_exact(cuda, D, n, F):
     """BASELINE config 4's shape in miniature (pre-binned 0..31, depth 10) and a

@@ -123,7 +123,7 @@ def check(rc: int, what: str = "") -> None:
 # kernels each entry point launches (bench.py reports the count it saw)
 _KERNELS = {
     "wgb_tree_reset": 1, "wgb_tree_residual": 1, "wgb_tree_quantize": 1, "wgb_tree_root": 1,
-    "wgb_level_hist": 2, "wgb_level_split": 4, "wgb_level_partition": 4, "wgb_tree_finish": 1, "wgb_bins_feature_major": 1, "wgb_prebinned_ingest": 1,
+    "wgb_level_hist": 2, "wgb_level_split": 4, "wgb_level_partition": 3, "wgb_tree_finish": 1, "wgb_bins_feature_major": 1, "wgb_prebinned_ingest": 1,
     "wgb_bin_matrix": 1, "wgb_predict_packed": 1, "wgb_quantile_edges": 2, "wgb_compute_histogram3": 6, "wgb_compute_histogram3_noalloc": 6,
     "wgb_compute_split": 1, "wgb_custom_cuda_binner": 1, "wgb_predict_forest": 1,
 }

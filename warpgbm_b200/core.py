@@ -696,7 +696,7 @@ class WarpGBM(BaseEstimator, RegressorMixin):
         t["order1"] = torch.empty(max(N, 1), **i32)
         t["posnode0"] = torch.empty(max(N, 1), **i32)
         t["posnode1"] = torch.empty(max(N, 1), **i32)
-        t["flags"] = torch.empty(max(N, 1), dtype=torch.uint8, device=dev)
+        t["flags"] = torch.empty(max(N, 1) + 16, dtype=torch.uint8, device=dev)  # word reads past the end
         ntiles = max(1, (N + PART_TILE - 1) // PART_TILE)
         t["tile_cnt"] = torch.empty(ntiles, **i32)
         t["tile_off"] = torch.empty(ntiles + 1, **i32)
@@ -839,7 +839,6 @@ class WarpGBM(BaseEstimator, RegressorMixin):
             self._rec_decoded = 0
             self._rec_meta = []
             self._rec_events = []
-            self._graphs, self._graph_warm = {}, set()
             self._residuals = []
             if not resume:
                 self.feature_subsets_ = []
@@ -879,63 +878,9 @@ class WarpGBM(BaseEstimator, RegressorMixin):
             self._release()
         return self
 
-    def _tree_launches(self, ws, st):
-        """Device work of one tree on a single GPU (what the tree graph holds)."""
-        p = ctypes_ptr(ws)
-        _lib.call("wgb_tree_reset", p, st())
-        _lib.call("wgb_tree_residual", p, st())
-        _lib.call("wgb_tree_quantize", p, st())
-        _lib.call("wgb_tree_root", p, st())
-        for d in range(self.max_depth):
-            _lib.call("wgb_level_hist", p, d, st())
-            _lib.call("wgb_level_split", p, d, st())
-            _lib.call("wgb_level_partition", p, d, st())
-        _lib.call("wgb_tree_finish", p, st())
-
-    def _capture_tree(self, ws, st, cls):
-        """CUDA graph of one tree's launches (sizes live on the device, so one
-        graph serves every tree of the fit); None if capture is refused."""
-        g = torch.cuda.CUDAGraph()
-        side = torch.cuda.Stream()
-        side.wait_stream(torch.cuda.current_stream())
-        n0 = _lib.LAUNCHES[0]
-        try:
-            with torch.cuda.stream(side):
-                g.capture_begin(capture_error_mode="thread_local")
-                try:
-                    self._tree_launches(ws, st)
-                finally:
-                    g.capture_end()
-        except Exception:
-            self._graphs = None  # eager launches from here on
-            return None
-        finally:
-            self._graph_launches = _lib.LAUNCHES[0] - n0
-            _lib.LAUNCHES[0] = n0
-            torch.cuda.current_stream().wait_stream(side)
-        self._graphs[cls] = g
-        return g
-
     def _grow_tree(self, ws, cls, st, i, c):
         comm = self._comm
         ws.cls = cls
-        graphs = getattr(self, "_graphs", None)
-        if (graphs is not None and not comm.on and getattr(self, "_hist_events", None) is None
-                and getattr(self, "_comm_events", None) is None
-                and not getattr(self, "_record_residuals", False)):
-            # single GPU: the first tree of each class runs eagerly (lazy
-            # one-time set-up), later ones replay a captured graph
-            g = graphs.get(cls)
-            if g is None and cls in self._graph_warm:
-                g = self._capture_tree(ws, st, cls)
-            if g is not None:
-                g.replay()
-                _lib.LAUNCHES[0] += self._graph_launches
-            else:
-                self._tree_launches(ws, st)
-                self._graph_warm.add(cls)
-            self._store_record(i, c)
-            return
         p = ctypes_ptr(ws)
         _lib.call("wgb_tree_reset", p, st())
         _lib.call("wgb_tree_residual", p, st())
@@ -1046,7 +991,6 @@ class WarpGBM(BaseEstimator, RegressorMixin):
             self._rec_decoded = self._rec_done
 
     def _release(self):
-        self._graphs = None
         for name in ("_t", "_ws", "_keep", "_pred", "Y_gpu", "_eval_bins", "_eval_pred", "_Y_eval"):
             if hasattr(self, name):
                 delattr(self, name)

@@ -710,28 +710,21 @@ __global__ void __launch_bounds__(PART_THREADS) k_flags(
     }
 }
 
-// exclusive scan of tile counts (one block)
-__global__ void __launch_bounds__(1024) k_scan_tiles(const int *tile_cnt, int *tile_off, int ntiles) {
-    __shared__ int s_scan[33];
-    int base = 0;
-    for (int b0 = 0; b0 < ntiles; b0 += 1024) {
-        int i = b0 + threadIdx.x;
-        int v = i < ntiles ? tile_cnt[i] : 0;
-        int tot;
-        const int ex = block_scan_excl(v, s_scan, tot);
-        if (i < ntiles) tile_off[i] = base + ex;
-        base += tot;
-    }
-    if (threadIdx.x == 0) tile_off[ntiles] = base;  // total, for p == end
-}
-
 // lefts before position p (p may equal nact)
+// (flags are read as 32-bit words from the tile start, which is 2048-byte
+// aligned; the flag buffer is padded by 16 bytes past the last position)
 __device__ __forceinline__ int lefts_before(long long p, const uint8_t *flags, const int *tile_off,
                                             int lane) {
-    long long t = p / PART_TILE;
-    long long a = t * PART_TILE;
+    const long long t = p / PART_TILE, a = t * PART_TILE;
+    const int len = (int)(p - a);
+    const uint32_t *w = reinterpret_cast<const uint32_t *>(flags + a);
     int c = 0;
-    for (long long i = a + lane; i < p; i += 32) c += flags[i] == 1;
+    for (int i = lane; 4 * i < len; i += 32) {
+        uint32_t x = w[i];
+        const int rem = len - 4 * i;
+        if (rem < 4) x &= (1u << (8 * rem)) - 1u;     // bytes at or past p
+        c += __popc(__vcmpeq4(x, 0x01010101u)) >> 3;  // bytes equal to 1 (left)
+    }
     c = warp_sum(c);
     return tile_off[t] + c;
 }
@@ -740,8 +733,22 @@ __device__ __forceinline__ int lefts_before(long long p, const uint8_t *flags, c
 // next order; children's local segments; next level's active rows.
 __global__ void __launch_bounds__(1024) k_node_offsets(wgb_node *__restrict__ lvl, wgb_node *__restrict__ nxt,
                                                        const int *nn, int *nact, int d,
-                                                       const uint8_t *flags, const int *tile_off,
-                                                       int4 *part) {
+                                                       const uint8_t *flags, const int *tile_cnt,
+                                                       int *tile_off, int ntiles, int4 *part) {
+    __shared__ int s_scan[33];
+    {   // exclusive scan of the tiles' left counts (tile_off[ntiles] = total)
+        int base = 0;
+        for (int b0 = 0; b0 < ntiles; b0 += 1024) {
+            const int i = b0 + threadIdx.x;
+            const int v = i < ntiles ? tile_cnt[i] : 0;
+            int tot;
+            const int ex = block_scan_excl(v, s_scan, tot);
+            if (i < ntiles) tile_off[i] = base + ex;
+            base += tot;
+        }
+        if (threadIdx.x == 0) tile_off[ntiles] = base;
+        __syncthreads();
+    }
     const int nnd = nn[d];
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     for (int n = warp; n < nnd; n += 32) {
@@ -752,7 +759,6 @@ __global__ void __launch_bounds__(1024) k_node_offsets(wgb_node *__restrict__ lv
         if (lane == 0) part[n] = make_int4(a, 0, b - a, 0);
     }
     __syncthreads();
-    __shared__ int s_scan[33];
     int base = 0;
     for (int b0 = 0; b0 < nnd; b0 += 1024) {
         int i = b0 + threadIdx.x;
@@ -1049,11 +1055,9 @@ int wgb_level_partition(const wgb_ws *ws, int32_t d, void *stream) {
     k_flags<<<ntiles, PART_THREADS, 0, st>>>(lvl, ws->nact + d, ord, pn, ws->bins, ws->S, ws->bins_fm,
                                               (ws->N + 15) & ~15ll, ws->feats, ws->flags, ws->tile_cnt);
     WGB_LAUNCHED("k_flags");
-    k_scan_tiles<<<1, 1024, 0, st>>>(ws->tile_cnt, ws->tile_off, ntiles);
-    WGB_LAUNCHED("k_scan_tiles");
     int4 *part = reinterpret_cast<int4 *>(ws->part);
     k_node_offsets<<<1, 1024, 0, st>>>(lvl, level_nodes(ws, d + 1), ws->nn, ws->nact, d, ws->flags,
-                                       ws->tile_off, part);
+                                       ws->tile_cnt, ws->tile_off, ntiles, part);
     WGB_LAUNCHED("k_node_offsets");
     k_scatter<<<ntiles, PART_THREADS, 0, st>>>(lvl, ws->nact + d, ord, pn, ws->flags, ws->tile_off, part,
                                                 ws->order[d & 1], ws->posnode[d & 1], ws->pred, ws->K,

@@ -99,29 +99,40 @@ __global__ void __launch_bounds__(256) k_prebinned(const int8_t *__restrict__ X,
     int cmax[4] = {INT_MIN, INT_MIN, INT_MIN, INT_MIN};
     int gmin = INT_MAX, gmax = INT_MIN;
     const long long r0 = (long long)blockIdx.x * BIN_ROWS;
-    for (int rr = threadIdx.x >> 5; in_row && rr < BIN_ROWS; rr += blockDim.x >> 5) {
-        const long long r = r0 + rr;
-        if (r >= n) break;
-        const int8_t *xr = X + r * xs;
-        uint32_t w;
-        if (vec) {
-            w = __ldg(reinterpret_cast<const uint32_t *>(xr + f));
-        } else {
-            w = 0;
+    constexpr int RU = 8;  // rows in flight per warp
+    const int nw = blockDim.x >> 5;
+    for (int rr = threadIdx.x >> 5; in_row && rr < BIN_ROWS; rr += nw * RU) {
+        uint32_t w[RU];
 #pragma unroll
-            for (int j = 0; j < 4; ++j)
-                if (f + j < F) w |= (uint32_t)(uint8_t)__ldg(xr + f + j) << (8 * j);
-        }
+        for (int u = 0; u < RU; ++u) {
+            const long long r = r0 + rr + u * nw;
+            w[u] = 0;
+            if (rr + u * nw < BIN_ROWS && r < n) {
+                const int8_t *xr = X + r * xs;
+                if (vec) {
+                    w[u] = __ldg(reinterpret_cast<const uint32_t *>(xr + f));
+                } else {
 #pragma unroll
-        for (int j = 0; j < 4; ++j) {
-            if (f + j < F) {
-                const int v = (int)(int8_t)(w >> (8 * j));
-                cmax[j] = max(cmax[j], v);
-                gmin = min(gmin, v);
-                gmax = max(gmax, v);
+                    for (int j = 0; j < 4; ++j)
+                        if (f + j < F) w[u] |= (uint32_t)(uint8_t)__ldg(xr + f + j) << (8 * j);
+                }
             }
         }
-        *reinterpret_cast<uint32_t *>(out + r * os + f) = w;
+#pragma unroll
+        for (int u = 0; u < RU; ++u) {
+            const long long r = r0 + rr + u * nw;
+            if (rr + u * nw >= BIN_ROWS || r >= n) break;
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+                if (f + j < F) {
+                    const int v = (int)(int8_t)(w[u] >> (8 * j));
+                    cmax[j] = max(cmax[j], v);
+                    gmin = min(gmin, v);
+                    gmax = max(gmax, v);
+                }
+            }
+            *reinterpret_cast<uint32_t *>(out + r * os + f) = w[u];
+        }
     }
 #pragma unroll
     for (int j = 0; j < 4; ++j)
