@@ -460,37 +460,50 @@ __global__ void __launch_bounds__(SPLIT_THREADS) k_split(
     const wgb_node *__restrict__ lvl, const int *nn_d, const long long *__restrict__ hg,
     const long long *__restrict__ hc, long long slot_elems, int k, int E, int B, const int *shift,
     float mcw, float eps, float msg, float factor, int4 *cand, int nblk) {
+    // the block's 128 feature rows of one era are staged in shared memory as
+    // fp32 (G = float(sum q) * 2^-s, H = float(count)) with coalesced loads;
+    // each thread then scans its own row in bin order (the reference's
+    // sequential fp32 sums).  Odd row stride: conflict-free row reads.
+    extern __shared__ float s_split[];
     const int n = blockIdx.x / nblk, jb = blockIdx.x - n * nblk;  // node, feature block
     if (n >= *nn_d) return;
-    const int j = jb * SPLIT_THREADS + threadIdx.x;
+    const int j0 = jb * SPLIT_THREADS, j = j0 + threadIdx.x;
+    const int nj = min(SPLIT_THREADS, k - j0);
     const float inv = pow2f(-*shift);
-    const int B1 = B + 1, nb = B - 1;
+    const int B1 = B + 1, nb = B - 1, B1p = B1 | 1;
+    float *sG = s_split, *sH = s_split + SPLIT_THREADS * B1p;
     const long long slot = lvl[n].slot;
     Key best = key_none();
-    if (j < k) {
-        float cs[MULTI ? NB : 1];
-        int ds[MULTI ? NB : 1];
-        if (MULTI) {
+    float cs[MULTI ? NB : 1];
+    int ds[MULTI ? NB : 1];
+    if (MULTI) {
 #pragma unroll
-            for (int b = 0; b < (MULTI ? NB : 1); ++b) {
-                cs[b] = 0.0f;
-                ds[b] = 0;
-            }
+        for (int b = 0; b < (MULTI ? NB : 1); ++b) {
+            cs[b] = 0.0f;
+            ds[b] = 0;
         }
-        for (int e = 0; e < E; ++e) {
-            const long long off = slot * slot_elems + ((long long)e * k + j) * B1;
-            const long long *gp = hg + off;
-            const long long *cp = hc + off;
+    }
+    for (int e = 0; e < E; ++e) {
+        const long long base = slot * slot_elems + ((long long)e * k + j0) * B1;
+        __syncthreads();  // the previous era's rows are consumed
+        for (int t = threadIdx.x; t < nj * B1; t += SPLIT_THREADS) {
+            const int jl = t / B1, b = t - jl * B1;
+            sG[jl * B1p + b] = __fmul_rn(__ll2float_rn(__ldg(hg + base + t)), inv);
+            sH[jl * B1p + b] = __ll2float_rn(__ldg(hc + base + t));
+        }
+        __syncthreads();
+        if (j < k) {
+            const float *g = sG + threadIdx.x * B1p, *h = sH + threadIdx.x * B1p;
             float GT = 0.0f, HT = 0.0f;
             for (int b = 0; b < B; ++b) {
-                GT = __fadd_rn(GT, __fmul_rn(__ll2float_rn(__ldg(gp + b)), inv));
-                HT = __fadd_rn(HT, __ll2float_rn(__ldg(cp + b)));
+                GT = __fadd_rn(GT, g[b]);
+                HT = __fadd_rn(HT, h[b]);
             }
             float GL = 0.0f, HL = 0.0f;
 #pragma unroll 4
             for (int b = 0; b < nb; ++b) {
-                GL = __fadd_rn(GL, __fmul_rn(__ll2float_rn(__ldg(gp + b)), inv));
-                HL = __fadd_rn(HL, __ll2float_rn(__ldg(cp + b)));
+                GL = __fadd_rn(GL, g[b]);
+                HL = __fadd_rn(HL, h[b]);
                 SplitEval r = eval_split(GL, HL, GT, HT, mcw, eps);
                 if (MULTI) {
                     if (b < NB) {
@@ -503,14 +516,14 @@ __global__ void __launch_bounds__(SPLIT_THREADS) k_split(
                 }
             }
         }
-        if (MULTI) {
+    }
+    if (MULTI && j < k) {
 #pragma unroll
-            for (int b = 0; b < (MULTI ? NB : 1); ++b) {
-                if (b < nb) {
-                    float cr = __fmul_rn(cs[b], factor);
-                    Key kk{abs(ds[b]), cr > msg ? cr : -INFINITY, j * nb + b};
-                    if (key_better(kk, best)) best = kk;
-                }
+        for (int b = 0; b < (MULTI ? NB : 1); ++b) {
+            if (b < nb) {
+                float cr = __fmul_rn(cs[b], factor);
+                Key kk{abs(ds[b]), cr > msg ? cr : -INFINITY, j * nb + b};
+                if (key_better(kk, best)) best = kk;
             }
         }
     }
@@ -1007,15 +1020,20 @@ int wgb_level_split(const wgb_ws *ws, int32_t d, void *stream) {
 #define WGB_SPLIT_ARGS                                                                       \
     lvl, ws->nn + d, hg, hc, se, ws->k, ws->E, ws->B, ws->shift, ws->mcw, ws->eps, \
         ws->msg, ws->mean_factor, cand, nblk
+    const int split_smem = 2 * SPLIT_THREADS * ((ws->B + 1) | 1) * (int)sizeof(float);
+#define WGB_SPLIT_LAUNCH(NB_, MULTI_)                                                                      \
+    WGB_CUDA(cudaFuncSetAttribute(k_split<NB_, MULTI_>, cudaFuncAttributeMaxDynamicSharedMemorySize, split_smem)); \
+    k_split<NB_, MULTI_><<<g, SPLIT_THREADS, split_smem, st>>>(WGB_SPLIT_ARGS);
     if (ws->E == 1) {
-        k_split<1, false><<<g, SPLIT_THREADS, 0, st>>>(WGB_SPLIT_ARGS);
+        WGB_SPLIT_LAUNCH(1, false)
     } else if (nb <= 8) {
-        k_split<8, true><<<g, SPLIT_THREADS, 0, st>>>(WGB_SPLIT_ARGS);
+        WGB_SPLIT_LAUNCH(8, true)
     } else if (nb <= 32) {
-        k_split<32, true><<<g, SPLIT_THREADS, 0, st>>>(WGB_SPLIT_ARGS);
+        WGB_SPLIT_LAUNCH(32, true)
     } else {
-        k_split<128, true><<<g, SPLIT_THREADS, 0, st>>>(WGB_SPLIT_ARGS);
+        WGB_SPLIT_LAUNCH(128, true)
     }
+#undef WGB_SPLIT_LAUNCH
 #undef WGB_SPLIT_ARGS
     WGB_LAUNCHED("k_split");
     float *eg = ws->era_gain + (long long)((1 << d) - 1) * ws->E;
