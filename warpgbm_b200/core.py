@@ -35,7 +35,6 @@ from sklearn.preprocessing import LabelEncoder
 from . import _lib
 from .metrics import accuracy_torch, log_loss_torch, rmsle_torch, softmax
 
-HIST_FT = 128          # features per histogram tile (csrc/wgb_common.cuh)
 HIST_R = 1024          # rows per histogram chunk
 PART_TILE = 2048       # positions per partition tile
 SPLIT_THREADS = 128
@@ -43,11 +42,6 @@ SPLIT_THREADS = 128
 
 def _round_up(x, m):
     return (x + m - 1) // m * m
-
-
-def hist_ew_for(B: int) -> int:
-    """Eras per shared-memory window of the histogram kernel (<= 48 KB)."""
-    return max(1, min(8, (48 * 1024) // ((B + 1) * HIST_FT * 8)))
 
 
 def bins_stride(F: int) -> int:
