@@ -219,6 +219,9 @@ typedef struct wgb_ws {
     float *maxabs;           /* [1] max |g| (bit pattern compared as int)     */
     int32_t *shift;          /* [1] s                                         */
     int64_t *rootsum;        /* [1] sum of q over local rows                  */
+    void *part_hist;         /* per-chunk histogram words (8 bytes each), or  */
+    int64_t part_hist_elems; /*   NULL: wgb_hist_part_elems(S, F, B, chunk_cap) */
+                             /*   lets single-era levels skip global atomics  */
     /* sizes */
     int64_t N, S;
     int64_t N_global;
@@ -250,6 +253,9 @@ int wgb_tree_root(const wgb_ws *ws, void *stream);
  * *rootsum into the first spare cell of slot 0. */
 int wgb_level_hist(const wgb_ws *ws, int32_t d, void *stream);
 void wgb_built_slots(int32_t d, int32_t *first, int32_t *count);
+/* Elements (8 bytes each) of the per-chunk histogram buffer for `chunks`
+ * chunks of a matrix with row stride S, F features and B bins. */
+int64_t wgb_hist_part_elems(int64_t S, int32_t F, int32_t B, int64_t chunks);
 /* Level d: sibling = parent - built (in place), split search, per-era gains,
  * child totals, next level's node records. */
 int wgb_level_split(const wgb_ws *ws, int32_t d, void *stream);

@@ -45,7 +45,7 @@ class WgbWs(ctypes.Structure):
         ("chunks", _p), ("nchunks", _p),
         ("cand", _p), ("era_gain", _p),
         ("nodes", _p), ("nn", _p), ("nact", _p),
-        ("maxabs", _p), ("shift", _p), ("rootsum", _p),
+        ("maxabs", _p), ("shift", _p), ("rootsum", _p), ("part_hist", _p), ("part_hist_elems", _i64),
         ("N", _i64), ("S", _i64), ("N_global", _i64),
         ("F", _i32), ("k", _i32), ("E", _i32), ("B", _i32), ("D", _i32), ("K", _i32),
         ("cls", _i32),
@@ -77,6 +77,7 @@ _SIGS = {
     "wgb_level_split": ([_p, _i32, _p], _i32),
     "wgb_level_partition": ([_p, _i32, _p], _i32),
     "wgb_bins_feature_major": ([_p, _p, _p], _i32),
+    "wgb_hist_part_elems": ([_i64, _i32, _i32, _i64], _i64),
     "wgb_prebinned_ingest": ([_p, _i64, _i32, _i64, _p, _i64, _p, _p, _p], _i32),
     "wgb_tree_finish": ([_p, _p], _i32),
     "wgb_predict_packed": ([_p, _i64, _i64, _p, _p, _i32, _i32, _f32, _p, _p], _i32),

@@ -698,6 +698,13 @@ class WarpGBM(BaseEstimator, RegressorMixin):
         t["hg"] = torch.empty(nslots * P, dtype=torch.int64, device=dev)
         chunk_cap = (N + HIST_R - 1) // HIST_R + nslots
         t["chunks"] = torch.empty((max(chunk_cap, 1), 4), **i32)
+        # per-chunk histogram words: single-era levels store them and reduce per
+        # node instead of issuing global atomics from every chunk
+        part_elems = int(_lib.lib().wgb_hist_part_elems(S, F, B, chunk_cap)) if E == 1 else 0
+        if part_elems and part_elems * 8 < 0.2 * torch.cuda.mem_get_info(dev)[0]:
+            t["part_hist"] = torch.empty(part_elems * 2, dtype=torch.int32, device=dev)
+        else:
+            part_elems = 0
         ncand = (k + SPLIT_THREADS - 1) // SPLIT_THREADS
         t["cand"] = torch.empty((nslots, ncand, 4), **i32)
         t["era_gain"] = torch.zeros(((1 << D) - 1) * E, dtype=torch.float32, device=dev)
@@ -722,6 +729,8 @@ class WarpGBM(BaseEstimator, RegressorMixin):
             setattr(ws, name, t[name].data_ptr())
         ws.N, ws.S, ws.F, ws.k, ws.E, ws.B, ws.D, ws.K = N, S, F, k, E, B, D, K
         ws.chunk_cap, ws.ntiles, ws.ncand_blk = max(chunk_cap, 1), ntiles, ncand
+        ws.part_hist = t["part_hist"].data_ptr() if part_elems else None
+        ws.part_hist_elems = part_elems
         ws.hist_ew = 0  # automatic
         ws.regular = 1 if self._bins_regular else 0
         ws.mcw = float(np.float32(self.min_child_weight))

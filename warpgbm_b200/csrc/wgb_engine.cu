@@ -222,7 +222,8 @@ __global__ void __launch_bounds__(NT, MINB) k_hist(
     const int *__restrict__ q, const float *__restrict__ g, const int *shift,
     const int *__restrict__ era, const int *__restrict__ kpos, int k, int E, int B, int EW,
     const int4 *__restrict__ chunks, const int *nchunks, const wgb_node *__restrict__ lvl,
-    long long *__restrict__ hg, long long *__restrict__ hc, long long slot_elems, long long nrows) {
+    long long *__restrict__ hg, long long *__restrict__ hc, long long slot_elems, long long nrows,
+    uint2 *__restrict__ part) {
     constexpr int FT = 32 * FPL;             // features per tile
     constexpr int U = (FPL >= 16 || MINB > 1) ? 4 : 8;  // rows per pipeline step per warp
     constexpr int NW = NT / 32;
@@ -352,6 +353,13 @@ __global__ void __launch_bounds__(NT, MINB) k_hist(
             }
         }
         __syncthreads();
+        // one era and a partial buffer: store the chunk's raw words (coalesced,
+        // no atomics); k_hist_reduce sums the chunks of each node afterwards
+        if (!HAS_ERA && part) {
+            uint2 *dst = part + ((long long)c * gridDim.y + blockIdx.y) * (NSC * FT);
+            for (int wi = threadIdx.x; wi < NSC * FT; wi += NT) dst[wi] = make_uint2(sh32[wi], sh32[NSC * FT + wi]);
+            break;
+        }
         // flush bins 0..B of every feature (the trash slot is dropped),
         // walking the words in layout order (conflict-free reads)
         for (int ew = 0; ew < ew_n; ++ew) {
@@ -384,6 +392,63 @@ __global__ void __launch_bounds__(NT, MINB) k_hist(
     }
 }
 
+// Sums the per-chunk words k_hist stored for each node (one era): thread =
+// one cell of one feature tile over a segment of `seg` consecutive chunks;
+// chunks of one node are consecutive, so a thread adds its running total to
+// the node's int64 cell whenever the node changes -- one atomic per node and
+// segment instead of one per chunk.
+template <int FPL, int NSC>
+__global__ void __launch_bounds__(256) k_hist_reduce(const uint2 *__restrict__ part, const int4 *__restrict__ chunks,
+                                                     const int *nchunks, const wgb_node *__restrict__ lvl,
+                                                     const int *__restrict__ kpos, int F, int B, int seg,
+                                                     long long *__restrict__ hg, long long *__restrict__ hc,
+                                                     long long slot_elems) {
+    constexpr int FT = 32 * FPL, CELLS = NSC * FT;
+    const int nch = *nchunks;
+    const int c0 = blockIdx.z * seg;
+    const int wi = blockIdx.x * 256 + threadIdx.x;
+    if (c0 >= nch || wi >= CELLS) return;
+    const int jb = wi / (NSC * 64), rem = wi % (NSC * 64);
+    const int sl = rem >> 6, r2 = rem & 63;
+    if (sl > B) return;  // trash slot
+    const int jj = 2 * jb + (r2 >> 5), lj = r2 & 31;
+    const int f = blockIdx.y * FT + lj * FPL + jj;
+    const int kp = f < F ? kpos[f] : -1;
+    if (kp < 0) return;
+    const int B1 = B + 1;
+    const int c1 = min(nch, c0 + seg);
+    const int ntile = gridDim.y;
+    long long gs = 0, cn = 0;
+    int node = chunks[c0].x;
+    auto add = [&]() {
+        if (cn == 0) return;
+        const long long idx = (long long)lvl[node].slot * slot_elems + (long long)kp * B1 + sl;
+        atomicAdd(reinterpret_cast<unsigned long long *>(hg + idx), (unsigned long long)gs);
+        atomicAdd(reinterpret_cast<unsigned long long *>(hc + idx), (unsigned long long)cn);
+    };
+    for (int c = c0; c < c1; ++c) {
+        const int nd = chunks[c].x;
+        if (nd != node) {
+            add();
+            node = nd;
+            gs = 0;
+            cn = 0;
+        }
+        const uint2 v = part[((long long)c * ntile + blockIdx.y) * CELLS + wi];
+        cn += v.x >> 21;
+        gs += (long long)(int)v.y * 2048 + (long long)(v.x & 0x1FFFFFu);
+    }
+    add();
+}
+
+// Feature width per lane and bin-slot capacity of the histogram kernel
+// for a matrix (row stride S, F features, B bins); the same choice
+// launch_hist makes.
+static inline void hist_shape(long long S, int F, int B, int &fpl, int &nsc) {
+    fpl = (S % 8 == 0 && F > 128 && B <= 32) ? 8 : 4;
+    nsc = (B + 2 <= 8) ? 8 : (B + 2 <= 34 ? 34 : 130);
+}
+
 // Launch of the histogram kernel for one level: picks the feature width per
 // lane, the bin-slot capacity and the era window from the row alignment,
 // feature count, num_bins and era count.  Returns a cudaError_t.
@@ -392,11 +457,10 @@ static cudaError_t launch_hist(int grid_x, const int8_t *bins, long long S, int 
                                const int *kpos, int k, int E, int B, int EW, bool regular,
                                const int4 *chunks, const int *nchunks, const wgb_node *lvl,
                                long long *hg, long long *hc, long long slot_elems, long long nrows,
-                               cudaStream_t st) {
+                               cudaStream_t st, uint2 *part = nullptr) {
     const bool has_era = E > 1;
-    int fpl = 4;
-    if (S % 8 == 0 && F > 128 && B <= 32) fpl = 8;
-    const int nsc = (B + 2 <= 8) ? 8 : (B + 2 <= 34 ? 34 : 130);
+    int fpl, nsc;
+    hist_shape(S, F, B, fpl, nsc);
 #define WGB_HIST_CASE(FPL_, NT_, MINB_, NSC_, EWC_, ERA_, REG_)                                       \
     if (fpl == FPL_ && nsc == NSC_ && has_era == ERA_ && regular == REG_) {                            \
         auto fn = k_hist<FPL_, NT_, MINB_, NSC_, EWC_, ERA_, REG_>;                                    \
@@ -406,7 +470,13 @@ static cudaError_t launch_hist(int grid_x, const int8_t *bins, long long S, int 
         if (e != cudaSuccess) return e;                                                                \
         dim3 grid((unsigned)grid_x, (unsigned)((F + 32 * FPL_ - 1) / (32 * FPL_)));                    \
         fn<<<grid, NT_, smem, st>>>(bins, S, F, order, q, g, shift, era, kpos, k, E, B, ew, chunks,   \
-                                    nchunks, lvl, hg, hc, slot_elems, nrows);                          \
+                                    nchunks, lvl, hg, hc, slot_elems, nrows, part);                    \
+        e = cudaGetLastError();                                                                        \
+        if (e != cudaSuccess || !part || ERA_) return e;                                              \
+        const int seg = 32;                                                                            \
+        dim3 rg((unsigned)((NSC_ * 32 * FPL_ + 255) / 256), grid.y, (unsigned)((grid_x + seg - 1) / seg)); \
+        k_hist_reduce<FPL_, NSC_><<<rg, 256, 0, st>>>(part, chunks, nchunks, lvl, kpos, F, B, seg, hg, hc, \
+                                                      slot_elems);                                      \
         return cudaGetLastError();                                                                     \
     }
 #define WGB_HIST_REG(FPL_, NT_, MINB_, NSC_, EWC_, ERA_) \
@@ -963,6 +1033,13 @@ int wgb_tree_root(const wgb_ws *ws, void *stream) {
     return WGB_OK;
 }
 
+int64_t wgb_hist_part_elems(int64_t S, int32_t F, int32_t B, int64_t chunks) {
+    int fpl, nsc;
+    hist_shape(S, F, B, fpl, nsc);
+    const long long ft = 32ll * fpl;
+    return chunks * ((F + ft - 1) / ft) * nsc * ft;
+}
+
 int wgb_level_hist(const wgb_ws *ws, int32_t d, void *stream) {
     int rc = check_ws(ws);
     if (rc) return rc;
@@ -985,7 +1062,11 @@ int wgb_level_hist(const wgb_ws *ws, int32_t d, void *stream) {
     cudaError_t e = launch_hist((int)max_chunks, ws->bins, ws->S, ws->F, ord, ws->qg, nullptr, nullptr,
                                 ws->E > 1 ? ws->era : nullptr, ws->kpos, ws->k, ws->E, ws->B, ws->hist_ew,
                                 ws->regular != 0, reinterpret_cast<const int4 *>(ws->chunks), ws->nchunks,
-                                lvl, LL(ws->hg), LL(ws->hg) + nc, se, ws->N, st);
+                                lvl, LL(ws->hg), LL(ws->hg) + nc, se, ws->N, st,
+                                ws->E == 1 && ws->part_hist &&
+                                        ws->part_hist_elems >= wgb_hist_part_elems(ws->S, ws->F, ws->B, max_chunks)
+                                    ? reinterpret_cast<uint2 *>(ws->part_hist)
+                                    : nullptr);
     if (e != cudaSuccess) {
         set_error("k_hist launch failed: %s", cudaGetErrorString(e));
         return WGB_ERR_CUDA;
