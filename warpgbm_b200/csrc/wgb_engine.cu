@@ -426,17 +426,29 @@ __global__ void __launch_bounds__(256) k_hist_reduce(const uint2 *__restrict__ p
         atomicAdd(reinterpret_cast<unsigned long long *>(hg + idx), (unsigned long long)gs);
         atomicAdd(reinterpret_cast<unsigned long long *>(hc + idx), (unsigned long long)cn);
     };
-    for (int c = c0; c < c1; ++c) {
-        const int nd = chunks[c].x;
-        if (nd != node) {
-            add();
-            node = nd;
-            gs = 0;
-            cn = 0;
+    constexpr int UR = 8;  // chunk words in flight per thread
+    const uint2 *src = part + (long long)blockIdx.y * CELLS + wi;
+    const long long cstride = (long long)ntile * CELLS;
+    for (int cb = c0; cb < c1; cb += UR) {
+        uint2 v[UR];
+        int nd[UR];
+#pragma unroll
+        for (int u = 0; u < UR; ++u) {
+            const int c = cb + u;
+            v[u] = c < c1 ? src[c * cstride] : make_uint2(0u, 0u);
+            nd[u] = c < c1 ? chunks[c].x : node;
         }
-        const uint2 v = part[((long long)c * ntile + blockIdx.y) * CELLS + wi];
-        cn += v.x >> 21;
-        gs += (long long)(int)v.y * 2048 + (long long)(v.x & 0x1FFFFFu);
+#pragma unroll
+        for (int u = 0; u < UR; ++u) {
+            if (nd[u] != node) {
+                add();
+                node = nd[u];
+                gs = 0;
+                cn = 0;
+            }
+            cn += v[u].x >> 21;
+            gs += (long long)(int)v[u].y * 2048 + (long long)(v[u].x & 0x1FFFFFu);
+        }
     }
     add();
 }
@@ -473,7 +485,7 @@ static cudaError_t launch_hist(int grid_x, const int8_t *bins, long long S, int 
                                     nchunks, lvl, hg, hc, slot_elems, nrows, part);                    \
         e = cudaGetLastError();                                                                        \
         if (e != cudaSuccess || !part || ERA_) return e;                                              \
-        const int seg = 32;                                                                            \
+        const int seg = 16;                                                                            \
         dim3 rg((unsigned)((NSC_ * 32 * FPL_ + 255) / 256), grid.y, (unsigned)((grid_x + seg - 1) / seg)); \
         k_hist_reduce<FPL_, NSC_><<<rg, 256, 0, st>>>(part, chunks, nchunks, lvl, kpos, F, B, seg, hg, hc, \
                                                       slot_elems);                                      \
@@ -530,50 +542,37 @@ __global__ void __launch_bounds__(SPLIT_THREADS) k_split(
     const wgb_node *__restrict__ lvl, const int *nn_d, const long long *__restrict__ hg,
     const long long *__restrict__ hc, long long slot_elems, int k, int E, int B, const int *shift,
     float mcw, float eps, float msg, float factor, int4 *cand, int nblk) {
-    // the block's 128 feature rows of one era are staged in shared memory as
-    // fp32 (G = float(sum q) * 2^-s, H = float(count)) with coalesced loads;
-    // each thread then scans its own row in bin order (the reference's
-    // sequential fp32 sums).  Odd row stride: conflict-free row reads.
-    extern __shared__ float s_split[];
     const int n = blockIdx.x / nblk, jb = blockIdx.x - n * nblk;  // node, feature block
     if (n >= *nn_d) return;
-    const int j0 = jb * SPLIT_THREADS, j = j0 + threadIdx.x;
-    const int nj = min(SPLIT_THREADS, k - j0);
+    const int j = jb * SPLIT_THREADS + threadIdx.x;
     const float inv = pow2f(-*shift);
-    const int B1 = B + 1, nb = B - 1, B1p = B1 | 1;
-    float *sG = s_split, *sH = s_split + SPLIT_THREADS * B1p;
+    const int B1 = B + 1, nb = B - 1;
     const long long slot = lvl[n].slot;
     Key best = key_none();
-    float cs[MULTI ? NB : 1];
-    int ds[MULTI ? NB : 1];
-    if (MULTI) {
+    if (j < k) {
+        float cs[MULTI ? NB : 1];
+        int ds[MULTI ? NB : 1];
+        if (MULTI) {
 #pragma unroll
-        for (int b = 0; b < (MULTI ? NB : 1); ++b) {
-            cs[b] = 0.0f;
-            ds[b] = 0;
+            for (int b = 0; b < (MULTI ? NB : 1); ++b) {
+                cs[b] = 0.0f;
+                ds[b] = 0;
+            }
         }
-    }
-    for (int e = 0; e < E; ++e) {
-        const long long base = slot * slot_elems + ((long long)e * k + j0) * B1;
-        __syncthreads();  // the previous era's rows are consumed
-        for (int t = threadIdx.x; t < nj * B1; t += SPLIT_THREADS) {
-            const int jl = t / B1, b = t - jl * B1;
-            sG[jl * B1p + b] = __fmul_rn(__ll2float_rn(__ldg(hg + base + t)), inv);
-            sH[jl * B1p + b] = __ll2float_rn(__ldg(hc + base + t));
-        }
-        __syncthreads();
-        if (j < k) {
-            const float *g = sG + threadIdx.x * B1p, *h = sH + threadIdx.x * B1p;
+        for (int e = 0; e < E; ++e) {
+            const long long off = slot * slot_elems + ((long long)e * k + j) * B1;
+            const long long *gp = hg + off;
+            const long long *cp = hc + off;
             float GT = 0.0f, HT = 0.0f;
             for (int b = 0; b < B; ++b) {
-                GT = __fadd_rn(GT, g[b]);
-                HT = __fadd_rn(HT, h[b]);
+                GT = __fadd_rn(GT, __fmul_rn(__ll2float_rn(__ldg(gp + b)), inv));
+                HT = __fadd_rn(HT, __ll2float_rn(__ldg(cp + b)));
             }
             float GL = 0.0f, HL = 0.0f;
 #pragma unroll 4
             for (int b = 0; b < nb; ++b) {
-                GL = __fadd_rn(GL, g[b]);
-                HL = __fadd_rn(HL, h[b]);
+                GL = __fadd_rn(GL, __fmul_rn(__ll2float_rn(__ldg(gp + b)), inv));
+                HL = __fadd_rn(HL, __ll2float_rn(__ldg(cp + b)));
                 SplitEval r = eval_split(GL, HL, GT, HT, mcw, eps);
                 if (MULTI) {
                     if (b < NB) {
@@ -586,14 +585,14 @@ __global__ void __launch_bounds__(SPLIT_THREADS) k_split(
                 }
             }
         }
-    }
-    if (MULTI && j < k) {
+        if (MULTI) {
 #pragma unroll
-        for (int b = 0; b < (MULTI ? NB : 1); ++b) {
-            if (b < nb) {
-                float cr = __fmul_rn(cs[b], factor);
-                Key kk{abs(ds[b]), cr > msg ? cr : -INFINITY, j * nb + b};
-                if (key_better(kk, best)) best = kk;
+            for (int b = 0; b < (MULTI ? NB : 1); ++b) {
+                if (b < nb) {
+                    float cr = __fmul_rn(cs[b], factor);
+                    Key kk{abs(ds[b]), cr > msg ? cr : -INFINITY, j * nb + b};
+                    if (key_better(kk, best)) best = kk;
+                }
             }
         }
     }
@@ -1101,20 +1100,15 @@ int wgb_level_split(const wgb_ws *ws, int32_t d, void *stream) {
 #define WGB_SPLIT_ARGS                                                                       \
     lvl, ws->nn + d, hg, hc, se, ws->k, ws->E, ws->B, ws->shift, ws->mcw, ws->eps, \
         ws->msg, ws->mean_factor, cand, nblk
-    const int split_smem = 2 * SPLIT_THREADS * ((ws->B + 1) | 1) * (int)sizeof(float);
-#define WGB_SPLIT_LAUNCH(NB_, MULTI_)                                                                      \
-    WGB_CUDA(cudaFuncSetAttribute(k_split<NB_, MULTI_>, cudaFuncAttributeMaxDynamicSharedMemorySize, split_smem)); \
-    k_split<NB_, MULTI_><<<g, SPLIT_THREADS, split_smem, st>>>(WGB_SPLIT_ARGS);
     if (ws->E == 1) {
-        WGB_SPLIT_LAUNCH(1, false)
+        k_split<1, false><<<g, SPLIT_THREADS, 0, st>>>(WGB_SPLIT_ARGS);
     } else if (nb <= 8) {
-        WGB_SPLIT_LAUNCH(8, true)
+        k_split<8, true><<<g, SPLIT_THREADS, 0, st>>>(WGB_SPLIT_ARGS);
     } else if (nb <= 32) {
-        WGB_SPLIT_LAUNCH(32, true)
+        k_split<32, true><<<g, SPLIT_THREADS, 0, st>>>(WGB_SPLIT_ARGS);
     } else {
-        WGB_SPLIT_LAUNCH(128, true)
+        k_split<128, true><<<g, SPLIT_THREADS, 0, st>>>(WGB_SPLIT_ARGS);
     }
-#undef WGB_SPLIT_LAUNCH
 #undef WGB_SPLIT_ARGS
     WGB_LAUNCHED("k_split");
     float *eg = ws->era_gain + (long long)((1 << d) - 1) * ws->E;
