@@ -607,6 +607,90 @@ __global__ void __launch_bounds__(SPLIT_THREADS) k_split(
     }
 }
 
+template <int NB, bool MULTI>
+__global__ void __launch_bounds__(SPLIT_THREADS) k_split_staged(
+    const wgb_node *__restrict__ lvl, const int *nn_d, const long long *__restrict__ hg,
+    const long long *__restrict__ hc, long long slot_elems, int k, int E, int B, const int *shift,
+    float mcw, float eps, float msg, float factor, int4 *cand, int nblk) {
+    // k_split for levels with many nodes: the block's 128 feature rows of
+    // one era are staged in shared memory as fp32 (G = float(sum q) * 2^-s,
+    // H = float(count)) with coalesced loads; each thread then scans its own
+    // row in bin order (the reference's sequential fp32 sums).  Odd row
+    // stride: conflict-free row reads.
+    extern __shared__ float s_split[];
+    const int n = blockIdx.x / nblk, jb = blockIdx.x - n * nblk;  // node, feature block
+    if (n >= *nn_d) return;
+    const int j0 = jb * SPLIT_THREADS, j = j0 + threadIdx.x;
+    const int nj = min(SPLIT_THREADS, k - j0);
+    const float inv = pow2f(-*shift);
+    const int B1 = B + 1, nb = B - 1, B1p = B1 | 1;
+    float *sG = s_split, *sH = s_split + SPLIT_THREADS * B1p;
+    const long long slot = lvl[n].slot;
+    Key best = key_none();
+    float cs[MULTI ? NB : 1];
+    int ds[MULTI ? NB : 1];
+    if (MULTI) {
+#pragma unroll
+        for (int b = 0; b < (MULTI ? NB : 1); ++b) {
+            cs[b] = 0.0f;
+            ds[b] = 0;
+        }
+    }
+    for (int e = 0; e < E; ++e) {
+        const long long base = slot * slot_elems + ((long long)e * k + j0) * B1;
+        __syncthreads();  // the previous era's rows are consumed
+        for (int t = threadIdx.x; t < nj * B1; t += SPLIT_THREADS) {
+            const int jl = t / B1, b = t - jl * B1;
+            sG[jl * B1p + b] = __fmul_rn(__ll2float_rn(__ldg(hg + base + t)), inv);
+            sH[jl * B1p + b] = __ll2float_rn(__ldg(hc + base + t));
+        }
+        __syncthreads();
+        if (j < k) {
+            const float *g = sG + threadIdx.x * B1p, *h = sH + threadIdx.x * B1p;
+            float GT = 0.0f, HT = 0.0f;
+            for (int b = 0; b < B; ++b) {
+                GT = __fadd_rn(GT, g[b]);
+                HT = __fadd_rn(HT, h[b]);
+            }
+            float GL = 0.0f, HL = 0.0f;
+#pragma unroll 4
+            for (int b = 0; b < nb; ++b) {
+                GL = __fadd_rn(GL, g[b]);
+                HL = __fadd_rn(HL, h[b]);
+                SplitEval r = eval_split(GL, HL, GT, HT, mcw, eps);
+                if (MULTI) {
+                    if (b < NB) {
+                        cs[b] = __fadd_rn(cs[b], r.gain);
+                        ds[b] += (int)r.dir;
+                    }
+                } else {
+                    Key kk{0, r.gain > msg ? r.gain : -INFINITY, j * nb + b};
+                    if (key_better(kk, best)) best = kk;
+                }
+            }
+        }
+    }
+    if (MULTI && j < k) {
+#pragma unroll
+        for (int b = 0; b < (MULTI ? NB : 1); ++b) {
+            if (b < nb) {
+                float cr = __fmul_rn(cs[b], factor);
+                Key kk{abs(ds[b]), cr > msg ? cr : -INFINITY, j * nb + b};
+                if (key_better(kk, best)) best = kk;
+            }
+        }
+    }
+    best = warp_key_max(best);
+    __shared__ Key s_k[SPLIT_THREADS / 32];
+    if ((threadIdx.x & 31) == 0) s_k[threadIdx.x >> 5] = best;
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        for (int w = 1; w < SPLIT_THREADS / 32; ++w)
+            if (key_better(s_k[w], best)) best = s_k[w];
+        cand[(long long)n * nblk + jb] = make_int4(best.A, __float_as_int(best.c), best.idx, 0);
+    }
+}
+
 // Per node: final arg-max, per-era gain of the chosen split (importance,
 // core.py:624-627) and the exact left-child totals (bins <= bin plus the
 // negative-bin slot, which always goes left).
@@ -1100,15 +1184,28 @@ int wgb_level_split(const wgb_ws *ws, int32_t d, void *stream) {
 #define WGB_SPLIT_ARGS                                                                       \
     lvl, ws->nn + d, hg, hc, se, ws->k, ws->E, ws->B, ws->shift, ws->mcw, ws->eps, \
         ws->msg, ws->mean_factor, cand, nblk
-    if (ws->E == 1) {
-        k_split<1, false><<<g, SPLIT_THREADS, 0, st>>>(WGB_SPLIT_ARGS);
-    } else if (nb <= 8) {
-        k_split<8, true><<<g, SPLIT_THREADS, 0, st>>>(WGB_SPLIT_ARGS);
-    } else if (nb <= 32) {
-        k_split<32, true><<<g, SPLIT_THREADS, 0, st>>>(WGB_SPLIT_ARGS);
-    } else {
-        k_split<128, true><<<g, SPLIT_THREADS, 0, st>>>(WGB_SPLIT_ARGS);
+    // per-thread row reads while a level has few nodes; coalesced staging
+    // through shared memory once it has many (their histograms outgrow L2)
+    const bool staged = cap >= 64;
+    const int split_smem = staged ? 2 * SPLIT_THREADS * ((ws->B + 1) | 1) * (int)sizeof(float) : 0;
+#define WGB_SPLIT_LAUNCH(NB_, MULTI_)                                                                        \
+    if (staged) {                                                                                            \
+        WGB_CUDA(cudaFuncSetAttribute(k_split_staged<NB_, MULTI_>, cudaFuncAttributeMaxDynamicSharedMemorySize, \
+                                      split_smem));                                                          \
+        k_split_staged<NB_, MULTI_><<<g, SPLIT_THREADS, split_smem, st>>>(WGB_SPLIT_ARGS);                  \
+    } else {                                                                                                 \
+        k_split<NB_, MULTI_><<<g, SPLIT_THREADS, 0, st>>>(WGB_SPLIT_ARGS);                                  \
     }
+    if (ws->E == 1) {
+        WGB_SPLIT_LAUNCH(1, false)
+    } else if (nb <= 8) {
+        WGB_SPLIT_LAUNCH(8, true)
+    } else if (nb <= 32) {
+        WGB_SPLIT_LAUNCH(32, true)
+    } else {
+        WGB_SPLIT_LAUNCH(128, true)
+    }
+#undef WGB_SPLIT_LAUNCH
 #undef WGB_SPLIT_ARGS
     WGB_LAUNCHED("k_split");
     float *eg = ws->era_gain + (long long)((1 << d) - 1) * ws->E;
