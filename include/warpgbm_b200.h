@@ -77,7 +77,7 @@ int wgb_compute_histogram3(const int8_t *bin_indices, int64_t num_rows,
  * Same arguments and result as wgb_compute_histogram3; its scratch is a
  * fixed 64 MiB block inside the library (reserved on every GPU where the
  * library's kernels are loaded, until the process exits).  A call needs
- * num_eras*k*(num_bins+1)*16 + F_master*4 + ceil(n/1024)*16 + 96 bytes (each
+ * num_eras*k*(num_bins+1)*16 + F_master*4 + ceil(n/2048)*16 + 96 bytes (each
  * part rounded up to 256); larger calls return WGB_ERR_ARG.  Calls share the
  * block, so calls that may overlap on the GPU race; calls on one stream are
  * safe.  The first call on a device looks up the block's address and should

@@ -35,7 +35,7 @@ from sklearn.preprocessing import LabelEncoder
 from . import _lib
 from .metrics import accuracy_torch, log_loss_torch, rmsle_torch, softmax
 
-HIST_R = 1024          # rows per histogram chunk
+HIST_R = 2048          # rows per histogram chunk (csrc/wgb_common.cuh)
 PART_TILE = 2048       # positions per partition tile
 SPLIT_THREADS = 128
 

@@ -45,7 +45,15 @@ void set_error(const char *fmt, ...);
 inline cudaStream_t as_stream(void *s) { return reinterpret_cast<cudaStream_t>(s); }
 
 // ------------------------------------------------------------ constants --
-constexpr int HIST_R = 1024;        // rows per histogram chunk (cell packing needs <= 1024)
+constexpr int HIST_R = 2048;        // rows per histogram chunk (cell packing needs <= 2048)
+// Packing of a histogram cell into two 32-bit shared words for <= HIST_R rows:
+//   A += (1 << HIST_CNT_SHIFT) + (q & HIST_LO_MASK),  B += q >> HIST_LO_BITS
+// count = A >> HIST_CNT_SHIFT, sum q = B * 2^HIST_LO_BITS + (A & (2^HIST_CNT_SHIFT - 1)).
+// |q| <= 2^29 - 32 (fp32 residuals), so 2048 rows keep A below 2^32 and B in int32.
+constexpr int HIST_CNT_SHIFT = 20;
+constexpr int HIST_LO_BITS = 9;
+constexpr uint32_t HIST_LO_MASK = (1u << HIST_LO_BITS) - 1u;
+constexpr uint32_t HIST_A_SUM_MASK = (1u << HIST_CNT_SHIFT) - 1u;
 #define HIST_ERA_R(has_era) ((has_era) ? HIST_R : 1)
 constexpr int HIST_THREADS = 256;
 constexpr int SPLIT_THREADS = 128;  // features per split block
@@ -54,9 +62,9 @@ constexpr int PART_THREADS = 256;
 
 // --------------------------------------------------------- fixed point --
 // Residual quantisation: q = rint(g * 2^s), s = 29 - e where max|g| = m*2^e,
-// m in [0.5, 1).  |q| <= 2^29, so int64 totals hold 2^33 rows and the
-// histogram kernel's two 32-bit shared words per cell stay exact for
-// HIST_R rows.
+// m in [0.5, 1).  With fp32 residuals m <= 1 - 2^-24, so |q| <= 2^29 - 32:
+// int64 totals hold 2^33 rows and the histogram kernel's two 32-bit shared
+// words per cell stay exact for HIST_R rows.
 __host__ __device__ inline int quant_shift(float maxabs) {
     if (!(maxabs > 0.0f) || isinf(maxabs)) return 0;
     int e;

@@ -171,10 +171,10 @@ __global__ void __launch_bounds__(1024) k_chunk_plan(const wgb_node *__restrict_
 // tile (one FPL-byte load per row).  Every histogram cell is two 32-bit
 // shared words updated with native 32-bit reductions (64-bit shared atomics
 // are several times slower on sm_100):
-//     A  += (1 << 21) + (q & 0x7FF)       count (<= 1024) | low 11 bits of q
-//     Bw += q >> 11                       high bits of q (arithmetic shift)
-// so sum(q) = Bw * 2048 + (A & 0x1FFFFF) and count = A >> 21 exactly for up
-// to HIST_R = 1024 rows per chunk.
+//     A  += (1 << 20) + (q & 0x1FF)       count (<= 2048) | low 9 bits of q
+//     Bw += q >> 9                        high bits of q (arithmetic shift)
+// so sum(q) = Bw * 512 + (A & 0xFFFFF) and count = A >> 20 exactly for up
+// to HIST_R = 2048 rows per chunk (HIST_CNT_SHIFT / HIST_LO_BITS).
 // Shared layout of each word array: [era slot][j/2][bin slot 0..NSC-1][j%2][lane]
 // -- a bin slot is 256 bytes, so one byte-permute turns a bin into its byte
 // offset, the feature term is an immediate, and a warp's 32 reductions hit
@@ -341,8 +341,8 @@ __global__ void __launch_bounds__(NT, MINB) k_hist(
                     if (rec[u].x < 0) continue;
                     const uint32_t ra = sbase + (HAS_ERA ? (uint32_t)rec[u].z * (ESLOT * 4) : 0u);
                     const int qv = rec[u].y;
-                    hist_row<FPL, NSC, REGULAR>(w[u], ra, (1u << 21) + (uint32_t)(qv & 0x7FF),
-                                                (uint32_t)(qv >> 11), B);
+                    hist_row<FPL, NSC, REGULAR>(w[u], ra, (1u << HIST_CNT_SHIFT) + ((uint32_t)qv & HIST_LO_MASK),
+                                                (uint32_t)(qv >> HIST_LO_BITS), B);
                 }
 #pragma unroll
                 for (int u = 0; u < U; ++u) {
@@ -375,8 +375,8 @@ __global__ void __launch_bounds__(NT, MINB) k_hist(
                 if (kp < 0) continue;
                 const uint32_t a = Ae[wi];
                 if (a == 0u) continue;
-                const int cntv = (int)(a >> 21);
-                const long long gs = (long long)(int)Be[wi] * 2048 + (long long)(a & 0x1FFFFFu);
+                const int cntv = (int)(a >> HIST_CNT_SHIFT);
+                const long long gs = (long long)(int)Be[wi] * (1ll << HIST_LO_BITS) + (long long)(a & HIST_A_SUM_MASK);
                 const long long idx = ebase + (long long)kp * B1 + sl;
                 atomicAdd(reinterpret_cast<unsigned long long *>(hg + idx), (unsigned long long)gs);
                 atomicAdd(reinterpret_cast<unsigned long long *>(hc + idx), (unsigned long long)cntv);
@@ -446,8 +446,8 @@ __global__ void __launch_bounds__(256) k_hist_reduce(const uint2 *__restrict__ p
                 gs = 0;
                 cn = 0;
             }
-            cn += v[u].x >> 21;
-            gs += (long long)(int)v[u].y * 2048 + (long long)(v[u].x & 0x1FFFFFu);
+            cn += v[u].x >> HIST_CNT_SHIFT;
+            gs += (long long)(int)v[u].y * (1ll << HIST_LO_BITS) + (long long)(v[u].x & HIST_A_SUM_MASK);
         }
     }
     add();

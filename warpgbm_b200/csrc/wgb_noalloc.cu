@@ -11,7 +11,7 @@
 //   * the block is WGB_NOALLOC_SCRATCH_BYTES (64 MiB); every GPU on which the
 //     library's kernels are loaded keeps it reserved until the process exits;
 //   * a call needs num_eras * k * (num_bins + 1) * 16 bytes of histogram
-//     cells plus F_master * 4 + ceil(n / 1024) * 16 + 96 bytes, each part
+//     cells plus F_master * 4 + ceil(n / 2048) * 16 + 96 bytes, each part
 //     rounded up to 256 bytes; larger calls are rejected with WGB_ERR_ARG
 //     before any work is queued;
 //   * all calls share the block: two calls that can overlap on the GPU (on
