@@ -845,23 +845,56 @@ __global__ void __launch_bounds__(256) k_bins_fm(const int8_t *__restrict__ bins
 // one (rows of a node are ascending, so neighbouring positions read
 // neighbouring bytes), else from the row-major matrix.
 __global__ void __launch_bounds__(PART_THREADS) k_flags(
-    const wgb_node *__restrict__ lvl, const int *nact_d, const int *__restrict__ order,
+    const wgb_node *__restrict__ lvl, const int *nn_d, const int *nact_d, const int *__restrict__ order,
     const int *__restrict__ posnode, const int8_t *__restrict__ bins, long long S,
     const int8_t *__restrict__ bins_fm, long long NT,
     const int *__restrict__ feats, uint8_t *flags, int *tile_cnt) {
+    // (split feature or -1, split bin) of the level's nodes, cached once per CTA
+    constexpr int CACHE = 1024, IPT = PART_TILE / PART_THREADS;
+    __shared__ int2 s_nd[CACHE];
+    const int nnd = *nn_d;
+    for (int i = threadIdx.x; i < min(nnd, CACHE); i += PART_THREADS) {
+        const int fp = lvl[i].fpos;
+        s_nd[i] = make_int2(fp >= 0 ? feats[fp] : -1, lvl[i].bin);
+    }
+    __syncthreads();
     const int nact = *nact_d;
     const long long t0 = (long long)blockIdx.x * PART_TILE;
+    // positions t0 + tid + 256u: the loads of all IPT positions are issued
+    // before any of them is used
+    int nd[IPT], row[IPT];
+#pragma unroll
+    for (int u = 0; u < IPT; ++u) {
+        const long long p = t0 + threadIdx.x + (long long)u * PART_THREADS;
+        const bool ok = p < nact;
+        nd[u] = ok ? (posnode ? posnode[p] : 0) : -1;
+        row[u] = ok ? order[p] : 0;
+    }
+    int8_t bv[IPT];
+    int2 sp[IPT];
+#pragma unroll
+    for (int u = 0; u < IPT; ++u) {
+        sp[u] = make_int2(-1, 0);
+        if (nd[u] >= 0) {
+            if (nd[u] < CACHE) {
+                sp[u] = s_nd[nd[u]];
+            } else {
+                const int fp = lvl[nd[u]].fpos;
+                sp[u] = make_int2(fp >= 0 ? feats[fp] : -1, lvl[nd[u]].bin);
+            }
+        }
+        bv[u] = 0;
+        if (sp[u].x >= 0)
+            bv[u] = bins_fm ? bins_fm[(long long)sp[u].x * NT + row[u]] : bins[(long long)row[u] * S + sp[u].x];
+    }
     int cnt = 0;
-    for (int i = threadIdx.x; i < PART_TILE; i += PART_THREADS) {
-        long long p = t0 + i;
-        if (p >= nact) break;
-        int n = posnode ? posnode[p] : 0;
-        int fp = lvl[n].fpos;
+#pragma unroll
+    for (int u = 0; u < IPT; ++u) {
+        if (nd[u] < 0) continue;
+        const long long p = t0 + threadIdx.x + (long long)u * PART_THREADS;
         uint8_t fl = 2;
-        if (fp >= 0) {
-            const int row = order[p], feat = feats[fp];
-            const int b = bins_fm ? bins_fm[(long long)feat * NT + row] : bins[(long long)row * S + feat];
-            fl = b <= lvl[n].bin ? 1 : 0;
+        if (sp[u].x >= 0) {
+            fl = bv[u] <= sp[u].y ? 1 : 0;
             cnt += fl;
         }
         flags[p] = fl;
@@ -949,21 +982,59 @@ __global__ void __launch_bounds__(1024) k_node_offsets(wgb_node *__restrict__ lv
 
 // Scatter rows into the next level's order; finished rows get their leaf
 // update pred += lr * leaf (core.py:598-621).
+struct ScatterNode {
+    float leaf;
+    int lstart, child, px, py, pz;  // part[n]: lefts before the node, start of its children, left count
+};
+
 __global__ void __launch_bounds__(PART_THREADS) k_scatter(
-    const wgb_node *__restrict__ lvl, const int *nact_d, const int *__restrict__ order,
+    const wgb_node *__restrict__ lvl, const int *nn_d, const int *nact_d, const int *__restrict__ order,
     const int *__restrict__ posnode, const uint8_t *__restrict__ flags,
     const int *__restrict__ tile_off, const int4 *__restrict__ part, int *__restrict__ order_next,
     int *__restrict__ posnode_next, float *__restrict__ pred, int K, int cls, float lr, long long N) {
     constexpr int IPT = PART_TILE / PART_THREADS;  // 8 consecutive positions per thread
+    constexpr int CACHE = 512;                     // nodes whose records are cached per CTA
+    __shared__ ScatterNode s_nc[CACHE];
+    const int nnd = *nn_d;
+    for (int i = threadIdx.x; i < min(nnd, CACHE); i += PART_THREADS) {
+        const wgb_node &nd = lvl[i];
+        const int4 pr = nd.fpos >= 0 ? part[i] : make_int4(0, 0, 0, 0);
+        s_nc[i] = ScatterNode{nd.leaf, nd.lstart, nd.child, pr.x, pr.y, pr.z};
+    }
     const int nact = *nact_d;
     const long long p0 = (long long)blockIdx.x * PART_TILE + threadIdx.x * IPT;
+    const bool full = p0 + IPT <= nact;
     uint8_t f[IPT];
+    int nid[IPT], row[IPT];
+    if (full) {  // p0 is a multiple of 8: 8-byte flag and 32-byte index loads
+        const uint2 fw = *reinterpret_cast<const uint2 *>(flags + p0);
+#pragma unroll
+        for (int u = 0; u < IPT; ++u) f[u] = (uint8_t)(((u < 4 ? fw.x : fw.y) >> (8 * (u & 3))) & 0xFF);
+        const int4 *o4 = reinterpret_cast<const int4 *>(order + p0);
+        const int4 a = o4[0], b = o4[1];
+        row[0] = a.x; row[1] = a.y; row[2] = a.z; row[3] = a.w;
+        row[4] = b.x; row[5] = b.y; row[6] = b.z; row[7] = b.w;
+        if (posnode) {
+            const int4 *n4 = reinterpret_cast<const int4 *>(posnode + p0);
+            const int4 c = n4[0], d = n4[1];
+            nid[0] = c.x; nid[1] = c.y; nid[2] = c.z; nid[3] = c.w;
+            nid[4] = d.x; nid[5] = d.y; nid[6] = d.z; nid[7] = d.w;
+        } else {
+#pragma unroll
+            for (int u = 0; u < IPT; ++u) nid[u] = 0;
+        }
+    } else {
+#pragma unroll
+        for (int u = 0; u < IPT; ++u) {
+            const bool ok = p0 + u < nact;
+            f[u] = ok ? flags[p0 + u] : 3;
+            row[u] = ok ? order[p0 + u] : 0;
+            nid[u] = ok && posnode ? posnode[p0 + u] : 0;
+        }
+    }
     int c = 0;
 #pragma unroll
-    for (int u = 0; u < IPT; ++u) {
-        f[u] = (p0 + u < nact) ? flags[p0 + u] : 3;
-        c += f[u] == 1;
-    }
+    for (int u = 0; u < IPT; ++u) c += f[u] == 1;
     // block exclusive scan of c
     __shared__ int sw[PART_THREADS / 32];
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
@@ -974,34 +1045,38 @@ __global__ void __launch_bounds__(PART_THREADS) k_scatter(
         if (lane >= o) incl += t;
     }
     if (lane == 31) sw[warp] = incl;
-    __syncthreads();
+    __syncthreads();  // also publishes the node cache
     int wbase = 0;
     for (int w = 0; w < warp; ++w) wbase += sw[w];
     int lp = tile_off[blockIdx.x] + wbase + incl - c;
 #pragma unroll
     for (int u = 0; u < IPT; ++u) {
         if (f[u] == 3) break;
-        long long p = p0 + u;
-        int n = posnode ? posnode[p] : 0;
-        const wgb_node &nd = lvl[n];
-        int row = order[p];
+        const long long p = p0 + u;
+        const int n = nid[u];
+        ScatterNode nd;
+        if (n < CACHE) {
+            nd = s_nc[n];
+        } else {
+            const wgb_node &g = lvl[n];
+            const int4 pr = g.fpos >= 0 ? part[n] : make_int4(0, 0, 0, 0);
+            nd = ScatterNode{g.leaf, g.lstart, g.child, pr.x, pr.y, pr.z};
+        }
         if (f[u] == 2) {
-            float *pp = pred + (long long)row * K + cls;
+            float *pp = pred + (long long)row[u] * K + cls;
             *pp = __fadd_rn(*pp, __fmul_rn(lr, nd.leaf));
         } else {
-            int4 pr = part[n];
-            int lb = lp - pr.x;  // lefts before p inside the node
-            int np;
-            int child;
+            const int lb = lp - nd.px;  // lefts before p inside the node
+            int np, child;
             if (f[u] == 1) {
-                np = pr.y + lb;
+                np = nd.py + lb;
                 child = nd.child;
             } else {
-                np = pr.y + pr.z + (int)(p - nd.lstart) - lb;
+                np = nd.py + nd.pz + (int)(p - nd.lstart) - lb;
                 child = nd.child + 1;
             }
             if (np >= 0 && np < N) {  // always true for consistent offsets; guards memory
-                order_next[np] = row;
+                order_next[np] = row[u];
                 posnode_next[np] = child;
             }
             if (f[u] == 1) ++lp;
@@ -1242,14 +1317,14 @@ int wgb_level_partition(const wgb_ws *ws, int32_t d, void *stream) {
     WGB_CHECK_ARG(ntiles <= ws->ntiles, "tile buffer too small");
     const int *ord = level_order(ws, d);
     const int *pn = level_posnode(ws, d);
-    k_flags<<<ntiles, PART_THREADS, 0, st>>>(lvl, ws->nact + d, ord, pn, ws->bins, ws->S, ws->bins_fm,
+    k_flags<<<ntiles, PART_THREADS, 0, st>>>(lvl, ws->nn + d, ws->nact + d, ord, pn, ws->bins, ws->S, ws->bins_fm,
                                               (ws->N + 15) & ~15ll, ws->feats, ws->flags, ws->tile_cnt);
     WGB_LAUNCHED("k_flags");
     int4 *part = reinterpret_cast<int4 *>(ws->part);
     k_node_offsets<<<1, 1024, 0, st>>>(lvl, level_nodes(ws, d + 1), ws->nn, ws->nact, d, ws->flags,
                                        ws->tile_cnt, ws->tile_off, ntiles, part);
     WGB_LAUNCHED("k_node_offsets");
-    k_scatter<<<ntiles, PART_THREADS, 0, st>>>(lvl, ws->nact + d, ord, pn, ws->flags, ws->tile_off, part,
+    k_scatter<<<ntiles, PART_THREADS, 0, st>>>(lvl, ws->nn + d, ws->nact + d, ord, pn, ws->flags, ws->tile_off, part,
                                                 ws->order[d & 1], ws->posnode[d & 1], ws->pred, ws->K,
                                                 ws->cls, ws->lr, ws->N);
     WGB_LAUNCHED("k_scatter");
