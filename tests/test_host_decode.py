@@ -65,3 +65,32 @@ def test_vectorised_decode_matches_depth_first_walk(D, E, p):
         if len(sp_feat):
             np.add.at(imp, (slice(None), sp_feat), sp_gain.T)
         assert np.array_equal(imp, imp_ref)
+
+
+def test_forest_dicts_built_on_first_access_and_packing_without_them():
+    """fit() keeps compact pre-order arrays and a lazy marker; the nested-dict
+    forest (the reference's format) is built only when `forest` is read, and
+    the predict packing never needs it."""
+    from warpgbm_b200 import WarpGBM
+    rng = np.random.default_rng(3)
+    D, E, F = 4, 1, 12
+    feats = np.arange(F, dtype=np.int32)
+    m = WarpGBM(n_estimators=3, max_depth=D)
+    want, packs = [], []
+    for i in range(2):                                  # two trained trees, one untrained slot
+        nodes, gains = _records(rng, D, E, F, 0.8)
+        want.append(_walk(nodes, gains, feats, D, E, np.zeros((E, F), np.float32)))
+        comp = compact_tree(nodes, gains, feats, D, E)
+        m._compact[(i, 0)] = comp[:3]
+        m._lazy.add((i, 0))
+        packs.append(comp[0])
+    assert m._tree_slots() == [(0, 0), (1, 0)]
+    assert m.__dict__["_forest"][0] == {}              # not yet materialised
+    assert (0, 0) in m._lazy
+    f = m.forest
+    assert f[0] == want[0] and f[1] == want[1] and f[2] == {}
+    assert not m._lazy                                  # built once
+    nodes_all, offs = pack_trees([t for t in f if t])
+    assert np.array_equal(nodes_all, np.concatenate(packs))
+    m.forest = [{} for _ in range(3)]                   # assignment drops the compact arrays
+    assert m._compact == {} and m._tree_slots() == []
