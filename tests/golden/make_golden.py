@@ -1,7 +1,7 @@
 """Generate the golden fixtures in tests/golden/*.npz from the REFERENCE.
 
-Runs quantverse/warpgbm's own ``warpgbm/core.py`` (imported read-only from a
-checkout, default /root/reference) on the CPU: the compiled CUDA extension
+Runs quantverse/warpgbm's own ``warpgbm/core.py`` (imported read-only from the
+reference checkout given as the first argument, or $WGB_REFERENCE) on the CPU: the compiled CUDA extension
 ``warpgbm.cuda.node_kernel`` is replaced by ``_TorchKernels`` below, a torch
 restatement of the four kernels written independently of oracle/, and
 ``device="cuda"`` literals inside core.py are redirected to the CPU.  Every
@@ -288,4 +288,5 @@ def main(ref_root):
 
 
 if __name__ == "__main__":
-    main(sys.argv[1] if len(sys.argv) > 1 else "/root/reference")
+    main(sys.argv[1] if len(sys.argv) > 1
+         else os.environ.get("WGB_REFERENCE", os.path.join(os.sep, "root", "reference")))

@@ -74,8 +74,8 @@ def test_classification_bit_exact_trees(cuda, case):
     assert np.abs(pg.sum(axis=1) - 1).max() < 1e-5          # test_multiclass.py:76
     # vs the reference: its round-0 pure nodes split on fp32 rounding noise
     # (gain ~1e-5 against terms ~30), which any other summation order -- the
-    # reference's own atomics included -- resolves differently.  The
-    # north-star criterion is the final logloss within 1e-3.
+    # reference's own atomics included -- resolves differently.  The bar
+    # there is the final logloss within 1e-3.
     enc = m.label_encoder.transform(d["y"])
     ll = lambda p: -np.mean(np.log(np.clip(p[np.arange(len(enc)), enc], 1e-15, 1 - 1e-15)))  # noqa: E731
     assert abs(ll(pg) - ll(d["proba"])) < 1e-3

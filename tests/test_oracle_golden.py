@@ -58,7 +58,7 @@ def test_canonical_mode_within_tolerance_of_reference(case):
         assert np.abs(p - d["pred"]).max() <= 1e-5 * scale
         np.testing.assert_allclose(m.flat_forest()[..., 5], d["forest"][..., 5], rtol=1e-5, atol=1e-6)
     else:
-        # round 0 of the multiclass case holds pure nodes whose best "gain"
+        # the first boosting round of the multiclass case holds pure nodes whose best "gain"
         # is fp32 rounding noise (~1e-5 vs terms ~30); either arithmetic may
         # pick a different noise split there.  Probabilities stay close.
         p = m.predict_proba(Xp)
