@@ -56,9 +56,10 @@ def parse():
     ap.add_argument("--no-cpu", action="store_true", help="skip the cpu_baseline sample")
     ap.add_argument("--clock-ms", type=int, default=200,
                     help="nvidia-smi sampling period during the timed region (0: no sampling)")
-    ap.add_argument("--config", default="c2", choices=["c2", "c5"],
+    ap.add_argument("--config", default="c2", choices=["c1", "c2", "c3", "c4", "c5"],
                     help="c5: 20M x 500 pre-binned rows split over the GPUs (strong scaling), "
-                         "depth 10, 50 trees, then batch predict")
+                         "depth 10, 50 trees, then batch predict; c1 / c3 / c4: the other "
+                         "BASELINE configs on one GPU (one line each, not the headline)")
     return ap.parse_args()
 
 
@@ -373,6 +374,198 @@ def run_c5(args, world, rank, local):
         dist.destroy_process_group()
 
 
+def config_data(name: str, dev):
+    """Seeded synthetic inputs of BASELINE configs 1, 3 and 4 as host arrays
+    (the same arrays feed this build and the reference's kernels).  Config 4's
+    5.9 GB matrix is drawn on the GPU with a seeded torch generator and copied
+    to the host once."""
+    if name == "c1":
+        rng = np.random.default_rng(0)
+        n = 4096
+        X = rng.standard_normal((n, 16), dtype=np.float32)
+        y = (2 * X[:, 0] - X[:, 1] + 0.5 * X[:, 2] * X[:, 3] + rng.normal(0, 0.1, n)).astype(np.float32)
+        return dict(X=X, y=y, era=None, fit_kw={},
+                    params=dict(num_bins=32, max_depth=3, n_estimators=10, learning_rate=0.1, random_state=0),
+                    workload="config1: 4096 x 16 f32 regression, B=32, depth 3, 10 trees, lr 0.1")
+    if name == "c3":
+        rng = np.random.default_rng(0)
+        n, K = 10_000, 5
+        lab = np.repeat(np.arange(K), n // K)
+        rng.shuffle(lab)
+        centres = rng.normal(0.0, 2.0, (K, 30))
+        X = np.concatenate([centres[lab] + rng.standard_normal((n, 30)),
+                            rng.standard_normal((n, 20))], axis=1).astype(np.float32)
+        perm = rng.permutation(n)
+        tr, va = perm[:8000], perm[8000:]
+        return dict(X=X[tr], y=lab[tr], era=None,
+                    fit_kw=dict(X_eval=X[va], y_eval=lab[va], eval_every_n_trees=10,
+                                early_stopping_rounds=5, eval_metric="logloss"),
+                    params=dict(objective="multiclass", num_bins=32, max_depth=6, n_estimators=200,
+                                learning_rate=0.1),
+                    workload="config3: 8000 x 50 f32 train / 2000 eval, 5 classes, B=32, depth 6, "
+                             "200 rounds, lr 0.1, early stopping 5 on logloss every 10")
+    if name == "c4":
+        n, F, E = 2_500_000, 2376, 600
+        g = torch.Generator(device=dev)
+        g.manual_seed(4)
+        Xd = torch.randint(0, 5, (n, F), generator=g, device=dev, dtype=torch.int8)
+        era = (torch.arange(n, device=dev, dtype=torch.int64) * E // n).to(torch.int32)
+        rng = np.random.default_rng(4)
+        c = np.abs(rng.standard_normal((E, 50)))
+        c[:, :30] *= np.where(rng.random(30) < 0.5, -1.0, 1.0)       # 30 stable signs
+        c[:, 30:] *= np.where(rng.random((E, 20)) < 0.5, -1.0, 1.0)  # 20 flip per era
+        cd = torch.from_numpy(c.astype(np.float32)).to(dev)
+        el = era.long()
+        score = (Xd[:, :50].float() * cd[el]).sum(1) + 2.0 * torch.randn(n, generator=g, device=dev)
+        # per-era rank (eras are contiguous), quantised to {0, .25, .5, .75, 1}
+        s = score.double()
+        key = el.double() * 4.0 + (s - s.min()) / (s.max() - s.min() + 1e-30) * 2.0
+        pos = torch.empty(n, dtype=torch.int64, device=dev)
+        pos[torch.argsort(key)] = torch.arange(n, device=dev)
+        cnt = torch.bincount(el, minlength=E)
+        start = torch.cumsum(cnt, 0) - cnt
+        r = (pos - start[el]).double() / (cnt[el] - 1).double()
+        y = (torch.round(r * 4.0) / 4.0).float()
+        out = dict(X=Xd.cpu().numpy(), y=y.cpu().numpy(), era=era.cpu().numpy(), fit_kw={},
+                   params=dict(num_bins=5, max_depth=8, n_estimators=100, learning_rate=0.01,
+                               colsample_bytree=0.5, random_state=0),
+                   workload="config4: 2.5M x 2376 int8 in 0..4, 600 contiguous eras, DES, B=5, depth 8, "
+                            "100 trees, lr 0.01, colsample 0.5")
+        del Xd, score, s, key, pos
+        torch.cuda.empty_cache()
+        return out
+    raise ValueError(name)
+
+
+def run_config(args):
+    """--config c1 / c3 / c4 on one GPU: s per fit (and per 100 trees) of
+    this build from device tensors (`value`) and from numpy arrays (`e2e`);
+    config 1 also times the reference algorithm's full fit on the host cores
+    (oracle port); config 4 adds the histogram roofline.  Not the headline:
+    the driver's contract line is config 2."""
+    torch.cuda.set_device(0)
+    dev = torch.device("cuda", 0)
+    from warpgbm_b200 import WarpGBM, _lib
+    import contextlib
+    import io
+    d = config_data(args.config, dev)
+    params = d["params"]
+    trees = params["n_estimators"] if args.trees == CONFIG["n_estimators"] else args.trees
+    params = {**params, "n_estimators": trees}
+    X, y, era = d["X"], d["y"], d["era"]
+    cls = params.get("objective", "regression") != "regression"
+    Xd = torch.from_numpy(X).to(dev)
+    yd = torch.from_numpy(y).to(dev) if not cls else y   # labels go through the encoder on the host
+    erad = torch.from_numpy(era).to(dev) if era is not None else None
+
+    def fit(Xa, ya, ea):
+        with contextlib.redirect_stdout(io.StringIO()):
+            m = WarpGBM(**params)
+            m.fit(Xa, ya, era_id=ea, **d["fit_kw"])
+        return m
+
+    for _ in range(args.warmup):
+        fit(Xd, yd, erad)
+    torch.cuda.synchronize()
+    launches0 = _lib.LAUNCHES[0]
+    dev_ms, e2e_ms = [], []
+    m = None
+    with Clocks(0, args.clock_ms) as clk:
+        for _ in range(args.steps):
+            torch.cuda.synchronize()
+            a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            a.record()
+            m = fit(Xd, yd, erad)
+            b.record()
+            torch.cuda.synchronize()
+            dev_ms.append(a.elapsed_time(b))
+        launches = (_lib.LAUNCHES[0] - launches0) // max(args.steps, 1)
+        if not args.no_e2e:
+            for _ in range(args.steps):
+                torch.cuda.synchronize()
+                a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                a.record()
+                me = fit(X, y, era)
+                if cls:
+                    me.predict_proba(d["fit_kw"]["X_eval"])
+                b.record()
+                torch.cuda.synchronize()
+                e2e_ms.append(a.elapsed_time(b))
+    t = statistics.median(dev_ms)
+    grown = m._trees_trained
+    per100 = t / 1000.0 * 100.0 / max(grown, 1)
+    line = {"metric": f"train s per fit ({args.config})", "value": round(t / 1000.0, 4), "unit": "s/fit",
+            "s_per_100_trees": round(per100, 4), "trees_grown": grown,
+            "n_gpus": 1, "steps": args.steps, "warmup": args.warmup, "higher_is_better": False,
+            "data": f"synthetic ({args.config} generator, seeded)", "config": {"workload": d["workload"]},
+            "gpu_launches_per_fit": launches, "clocks": clk.summary()}
+    if e2e_ms:
+        line["e2e"] = {"value": round(statistics.median(e2e_ms) / 1000.0, 4), "unit": "s/fit",
+                       "h2d_bytes_per_step": int(X.nbytes + y.nbytes + (era.nbytes if era is not None else 0))}
+    if cls:
+        from warpgbm_b200.metrics import log_loss_torch
+        Xe, ye = d["fit_kw"]["X_eval"], d["fit_kw"]["y_eval"]
+        p = torch.from_numpy(m.predict_proba(Xe))
+        line["eval"] = {"logloss": round(float(log_loss_torch(torch.from_numpy(ye), p)), 5),
+                        "accuracy": round(float((m.predict(Xe) == ye).mean()), 4),
+                        "eval_points": len(m.eval_loss)}
+    if args.config == "c4":
+        with contextlib.redirect_stdout(io.StringIO()):
+            mr = WarpGBM(**params)
+            mr._hist_events = []
+            mr.fit(Xd, yd, era_id=erad)
+        hist_ms = sum(a.elapsed_time(b) for a, b in mr._hist_events)
+        k = max(1, int(params["colsample_bytree"] * X.shape[1]))
+        hb = hist_algorithmic_bytes(mr, X.shape[0], k, 600, params["num_bins"])
+        peak, peak_kind = peaks()
+        ach = hb / (hist_ms / 1000.0) / 1e9 if hist_ms > 0 else None
+        line["roofline"] = {"bound": "hbm", "kernel": "k_hist (era windows) per level",
+                            "achieved": round(ach, 1) if ach else None, "peak": peak, "unit": "GB/s",
+                            "frac": round(ach / peak, 4) if ach else None, "peak_kind": peak_kind,
+                            "histogram_ms_per_fit": round(hist_ms, 1)}
+    if args.config == "c1" and not args.no_cpu:
+        import oracle as O
+        op = {k: v for k, v in params.items() if k != "random_state"}
+        t0 = time.perf_counter()
+        O.OracleGBM(mode="reference", **op).fit(X, y)
+        line["cpu_baseline"] = {"value": round(time.perf_counter() - t0, 4), "unit": "s/fit",
+                                "cores": O.lib().orc_num_threads(), "kind": "port",
+                                "sample": "the full config-1 fit (oracle, reference mode)"}
+    print(json.dumps(line), flush=True)
+
+
+def run_reference_cuda_config(args):
+    """--impl reference-cuda --config c1 / c4: the reference's own kernels on
+    the same arrays as run_config.  Config 4 grows --trees trees (default 1:
+    the reference's era path takes seconds per tree) and scales to 100."""
+    torch.cuda.set_device(0)
+    from oracle.build_ref import load
+    from oracle.ref_cuda import RefCudaFit
+    ops = load()
+    d = config_data(args.config, torch.device("cuda", 0))
+    params = dict(d["params"])
+    params.pop("objective", None)
+    T = params["n_estimators"]
+    if args.config == "c4":
+        params["n_estimators"] = 1 if args.trees == CONFIG["n_estimators"] else args.trees
+    runs = []
+    for i in range(args.warmup + args.steps):
+        m = RefCudaFit(ops, **params).fit(d["X"], d["y"], era_id=d["era"])
+        if i >= args.warmup:
+            runs.append(m.timings)
+    ing = statistics.median(r["ingest_s"] for r in runs)
+    grow = statistics.median(r["grow_s"] for r in runs)
+    grown = params["n_estimators"]
+    line = {"metric": f"train s per fit ({args.config})", "impl": "reference-cuda",
+            "value": round(ing + grow * T / grown, 3), "unit": f"s/fit ({T} trees)",
+            "measured": {"ingest_binning_s": round(ing, 3), "growth_s": round(grow, 3), "trees": grown},
+            "n_gpus": 1, "steps": args.steps, "warmup": args.warmup, "higher_is_better": False,
+            "config": {"workload": d["workload"]},
+            "note": "reference kernels (compiled for sm_100a) under a restatement of the reference's fit "
+                    "loop, from numpy arrays" + ("" if grown == T else f"; growth scaled x{T / grown:g}")}
+    print(json.dumps(line), flush=True)
+
+
 def main():
     args = parse()
     world = int(os.environ.get("WORLD_SIZE", "1"))
@@ -382,7 +575,14 @@ def main():
         run_reference(args, rank)
         return
     if args.impl == "reference-cuda":
-        run_reference_cuda(args, rank)
+        if args.config in ("c1", "c4"):
+            run_reference_cuda_config(args)
+        else:
+            run_reference_cuda(args, rank)
+        return
+    if args.config in ("c1", "c3", "c4"):
+        if rank == 0:
+            run_config(args)
         return
     if args.config == "c5":
         run_c5(args, world, rank, local)
@@ -412,7 +612,6 @@ def main():
         for _ in range(args.warmup):
             WarpGBM(**params).fit(X, y)
     barrier()
-    model = None
     model = None
     launches0 = _lib.LAUNCHES[0]
     with Clocks(local, args.clock_ms) as clk:
