@@ -93,11 +93,13 @@ def test_eval_and_early_stopping_match_reference(cuda):
     assert np.abs(m.predict(d["X_pred"]) - d["pred"]).max() <= 1e-5 * np.abs(d["pred"]).max()
 
 
-def test_c4_like_era_des_prebinned_colsample(cuda):
-    """BASELINE config 3 in miniature: pre-binned {0..4}, many sorted eras,
-    colsample 0.5, DES on."""
+@pytest.mark.parametrize("F", [100, 264])
+def test_c4_like_era_des_prebinned_colsample(cuda, F):
+    """BASELINE config 4 in miniature: pre-binned {0..4}, many sorted eras,
+    colsample 0.5, DES on; 100 features take the 4-features-per-lane
+    histogram, 264 the 8-per-lane one (as the full config does)."""
     rng = np.random.default_rng(3)
-    n, F, E = 60000, 100, 60
+    n, E = 60000, 60
     X = rng.integers(0, 5, (n, F)).astype(np.int8)
     era = np.repeat(np.arange(E), n // E).astype(np.int32)
     c = rng.standard_normal((E, 10))

@@ -152,6 +152,11 @@ def test_compute_split_bit_exact(cuda, E, k, B):
     (50000, 300, 200, 1, 32, True),
     (20000, 61, 61, 3, 10, False),      # unaligned rows (F % 4 != 0), unsorted eras
     (30000, 40, 20, 37, 5, True),
+    # 8 features per lane (row stride % 8 == 0, > 128 features) with eras:
+    # 8 era slots of 8 bin slots, 2 era slots of 34, unsorted eras
+    (40000, 264, 150, 7, 5, True),
+    (20000, 264, 200, 4, 32, True),
+    (20000, 136, 136, 3, 10, False),
     (777, 8, 8, 1, 2, True),
     (0, 8, 8, 1, 4, True),
 ])
