@@ -209,7 +209,10 @@ typedef struct wgb_ws {
     int32_t *chunks;         /* [chunk_cap][4] = node, p0, p1, -              */
     int32_t *nchunks;        /* [1]                                           */
     /* split search */
-    int32_t *cand;           /* [2^(D-1)][ceil(k/128)][4] partial arg-max    */
+    int32_t *cand;           /* [2^(D-1)][ncand_blk][4] partial arg-max:     */
+                             /*   ncand_blk >= ceil(k/128) required; with    */
+                             /*   >= ceil(k/32) eras take the era-parallel   */
+                             /*   search (same result, faster)               */
     float *era_gain;         /* [2^D - 1][E] per-era gain of chosen split     */
     /* nodes and level sizes */
     wgb_node *nodes;         /* [2^(D+1) - 1]                                 */

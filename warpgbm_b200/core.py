@@ -37,7 +37,7 @@ from .metrics import accuracy_torch, log_loss_torch, rmsle_torch, softmax
 
 HIST_R = 2048          # rows per histogram chunk (csrc/wgb_common.cuh)
 PART_TILE = 2048       # positions per partition tile
-SPLIT_THREADS = 128
+SPLIT_ERA_FEATURES = 32  # features per era split block (csrc/wgb_engine.cu)
 
 
 def _round_up(x, m):
@@ -705,7 +705,9 @@ class WarpGBM(BaseEstimator, RegressorMixin):
             t["part_hist"] = torch.empty(part_elems * 2, dtype=torch.int32, device=dev)
         else:
             part_elems = 0
-        ncand = (k + SPLIT_THREADS - 1) // SPLIT_THREADS
+        # per-node partial arg-max: blocks of 32 features (the era split
+        # search; the single-era search uses ceil(k/128) of them)
+        ncand = (k + SPLIT_ERA_FEATURES - 1) // SPLIT_ERA_FEATURES
         t["cand"] = torch.empty((nslots, ncand, 4), **i32)
         t["era_gain"] = torch.zeros(((1 << D) - 1) * E, dtype=torch.float32, device=dev)
         t["nodes"] = torch.zeros(((1 << (D + 1)) - 1) * 64, dtype=torch.uint8, device=dev)

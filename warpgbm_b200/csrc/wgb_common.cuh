@@ -165,6 +165,16 @@ __device__ __forceinline__ int block_min(int v, int *scratch /* >= 33 ints */) {
     return r;
 }
 
+// First index in a[0, n) (ascending) whose value is >= v; n if none.
+__device__ __forceinline__ int lower_bound_int(const int *a, int n, int v) {
+    int lo = 0, hi = n;
+    while (lo < hi) {
+        const int mid = (lo + hi) >> 1;
+        if (a[mid] < v) lo = mid + 1; else hi = mid;
+    }
+    return lo;
+}
+
 // Exclusive prefix sum over the block (blockDim.x a multiple of 32, at most
 // 1024); `total` receives the block's sum.  Every thread calls it.
 __device__ __forceinline__ int block_scan_excl(int v, int *scratch /* >= 33 ints */, int &total) {

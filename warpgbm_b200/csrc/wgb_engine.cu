@@ -279,17 +279,30 @@ __global__ void __launch_bounds__(NT, MINB) k_hist(
     const int8_t *tile = bins + f0 + FPL * lane;
 
     int e_lo = 0;
+    bool era_sorted = false;
     if (HAS_ERA) {
         int m = INT_MAX;
         for (int i = threadIdx.x; i < cnt; i += NT) m = min(m, s_era[i]);
         e_lo = block_min(m, s_red);
         if (e_lo == INT_MAX) return;  // no valid row (uniform)
+        // the engine's node rows are era-sorted: each window is then one
+        // contiguous run of the chunk (the drop-in entry may pass any order)
+        int uns = 0;
+        for (int i = threadIdx.x; i + 1 < cnt; i += NT) uns |= s_era[i] > s_era[i + 1];
+        era_sorted = !__syncthreads_or(uns);
     }
     for (;;) {
+        // rows [i_lo, i_hi) of the chunk and era slots [0, nsl) of this window
+        int i_lo = 0, i_hi = cnt, nsl = ew_n;
+        if (HAS_ERA && era_sorted) {
+            i_lo = lower_bound_int(s_era, cnt, e_lo);           // e_lo is some row's era
+            i_hi = lower_bound_int(s_era, cnt, e_lo + ew_n);    // > i_lo
+            nsl = s_era[i_hi - 1] - e_lo + 1;                  // in [1, ew_n]
+        }
         {
             uint4 *z = reinterpret_cast<uint4 *>(sh32);
             const uint4 zero = make_uint4(0u, 0u, 0u, 0u);
-            for (int t = threadIdx.x; t < (ew_n * ESLOT) / 4; t += NT) z[t] = zero;
+            for (int t = threadIdx.x; t < (nsl * ESLOT) / 4; t += NT) z[t] = zero;
         }
         __syncthreads();
         if (lane_live) {
@@ -301,7 +314,7 @@ __global__ void __launch_bounds__(NT, MINB) k_hist(
 #pragma unroll
                 for (int u = 0; u < U; ++u) {
                     const int i = i0 + NW * u;
-                    const int2 rq = i < cnt ? s_rec[i] : make_int2(-1, 0);
+                    const int2 rq = i < i_hi ? s_rec[i] : make_int2(-1, 0);
                     int4 r4 = make_int4(rq.x, rq.y, 0, 0);
                     if (HAS_ERA && r4.x >= 0) {
                         const int e = s_era[i] - e_lo;
@@ -332,10 +345,10 @@ __global__ void __launch_bounds__(NT, MINB) k_hist(
                     }
                 }
             };
-            fetch(warp, rec, w);
-            for (int i0 = warp; i0 < cnt; i0 += NW * U) {
+            fetch(i_lo + warp, rec, w);
+            for (int i0 = i_lo + warp; i0 < i_hi; i0 += NW * U) {
                 const int i1 = i0 + NW * U;
-                if (i1 < cnt) fetch(i1, recn, wn);
+                if (i1 < i_hi) fetch(i1, recn, wn);
 #pragma unroll
                 for (int u = 0; u < U; ++u) {
                     if (rec[u].x < 0) continue;
@@ -361,11 +374,11 @@ __global__ void __launch_bounds__(NT, MINB) k_hist(
             break;
         }
         // flush bins 0..B of every feature (the trash slot is dropped),
-        // walking the words in layout order (conflict-free reads)
-        for (int ew = 0; ew < ew_n; ++ew) {
-            const uint32_t *Ae = sh32 + ew * ESLOT;
-            const uint32_t *Be = Ae + NSC * FT;
-            const long long ebase = slot * slot_elems + (long long)(e_lo + ew) * k * B1;
+        // walking the words in layout order (conflict-free reads); a word's
+        // cell index is decoded once for all era slots of the window
+        {
+            const long long estride = (long long)k * B1;
+            const long long wbase = slot * slot_elems + (long long)e_lo * estride;
             for (int wi = threadIdx.x; wi < NSC * FT; wi += NT) {
                 const int jb = wi / (NSC * 64), rem = wi % (NSC * 64);
                 const int sl = rem >> 6, r2 = rem & 63;
@@ -373,13 +386,17 @@ __global__ void __launch_bounds__(NT, MINB) k_hist(
                 const int jj = 2 * jb + (r2 >> 5), lj = r2 & 31;
                 const int kp = s_kp[jj * 32 + lj];
                 if (kp < 0) continue;
-                const uint32_t a = Ae[wi];
-                if (a == 0u) continue;
-                const int cntv = (int)(a >> HIST_CNT_SHIFT);
-                const long long gs = (long long)(int)Be[wi] * (1ll << HIST_LO_BITS) + (long long)(a & HIST_A_SUM_MASK);
-                const long long idx = ebase + (long long)kp * B1 + sl;
-                atomicAdd(reinterpret_cast<unsigned long long *>(hg + idx), (unsigned long long)gs);
-                atomicAdd(reinterpret_cast<unsigned long long *>(hc + idx), (unsigned long long)cntv);
+                const long long cidx = wbase + (long long)kp * B1 + sl;
+                for (int ew = 0; ew < nsl; ++ew) {
+                    const uint32_t a = sh32[ew * ESLOT + wi];
+                    if (a == 0u) continue;
+                    const uint32_t bw = sh32[ew * ESLOT + NSC * FT + wi];
+                    const int cntv = (int)(a >> HIST_CNT_SHIFT);
+                    const long long gs = (long long)(int)bw * (1ll << HIST_LO_BITS) + (long long)(a & HIST_A_SUM_MASK);
+                    const long long idx = cidx + (long long)ew * estride;
+                    atomicAdd(reinterpret_cast<unsigned long long *>(hg + idx), (unsigned long long)gs);
+                    atomicAdd(reinterpret_cast<unsigned long long *>(hc + idx), (unsigned long long)cntv);
+                }
             }
         }
         if (!HAS_ERA) break;
@@ -689,6 +706,115 @@ __global__ void __launch_bounds__(SPLIT_THREADS) k_split_staged(
             if (key_better(s_k[w], best)) best = s_k[w];
         cand[(long long)n * nblk + jb] = make_int4(best.A, __float_as_int(best.c), best.idx, 0);
     }
+}
+
+// Era split search (E > 1, B - 1 <= NB <= 32) with the eras spread over
+// warps: block = one node x 32 features, eras in batches of 8, one warp per
+// era.  Phase 1: a warp stages its era's 32 feature rows in shared memory
+// with coalesced loads (G = float(sum q) * 2^-s, H = float(count); odd row
+// stride, conflict-free), then lane f scans feature f's bins with the
+// reference arithmetic (as k_split) and leaves the era's B-1 gains and
+// directions in shared memory.  Phase 2: thread = (bin, feature) items add
+// the batch's gains in era order to a running fp32 sum -- the sequential
+// era sum of k_split, bit for bit -- and the directions to an integer
+// agreement.  Block arg-max -> cand[node][blk] (ceil(k/32) blocks).
+constexpr int SPLIT_ERA_FB = 32;  // features per block
+constexpr int SPLIT_ERA_EB = 8;   // eras per batch (= warps)
+
+template <int NB>
+__global__ void __launch_bounds__(256) k_split_eras(
+    const wgb_node *__restrict__ lvl, const int *nn_d, const long long *__restrict__ hg,
+    const long long *__restrict__ hc, long long slot_elems, int k, int E, int B, const int *shift,
+    float mcw, float eps, float msg, float factor, int4 *cand, int nblk) {
+    constexpr int FB = SPLIT_ERA_FB, EB = SPLIT_ERA_EB;
+    constexpr int IPT = (FB * NB + 255) / 256;  // phase-2 items per thread
+    extern __shared__ float s_era_split[];      // [EB][2][FB][B1p] rows, [EB][NB][FB] gains, dirs
+    const int n = blockIdx.x / nblk, jb = blockIdx.x - n * nblk;  // node, feature block
+    if (n >= *nn_d) return;
+    const int j0 = jb * FB;
+    const int nf = min(FB, k - j0);
+    const int B1 = B + 1, nb = B - 1, B1p = B1 | 1;
+    const float inv = pow2f(-*shift);
+    const long long slot = lvl[n].slot;
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    float *stg = s_era_split + warp * 2 * FB * B1p;
+    float *sg = s_era_split + EB * 2 * FB * B1p;
+    signed char *sd = reinterpret_cast<signed char *>(sg + EB * NB * FB);
+    float cs[IPT];
+    int ds[IPT];
+#pragma unroll
+    for (int t = 0; t < IPT; ++t) {
+        cs[t] = 0.0f;
+        ds[t] = 0;
+    }
+    for (int e0 = 0; e0 < E; e0 += EB) {
+        const int e = e0 + warp;
+        if (e < E) {
+            const long long base = slot * slot_elems + ((long long)e * k + j0) * B1;
+            for (int t = lane; t < nf * B1; t += 32) {
+                const int f = t / B1, b = t - f * B1;
+                stg[f * B1p + b] = __fmul_rn(__ll2float_rn(__ldg(hg + base + t)), inv);
+                stg[(FB + f) * B1p + b] = __ll2float_rn(__ldg(hc + base + t));
+            }
+            __syncwarp();
+            if (lane < nf) {
+                const float *g = stg + lane * B1p, *h = stg + (FB + lane) * B1p;
+                float GT = 0.0f, HT = 0.0f;
+                for (int b = 0; b < B; ++b) {
+                    GT = __fadd_rn(GT, g[b]);
+                    HT = __fadd_rn(HT, h[b]);
+                }
+                float GL = 0.0f, HL = 0.0f;
+                for (int b = 0; b < nb; ++b) {
+                    GL = __fadd_rn(GL, g[b]);
+                    HL = __fadd_rn(HL, h[b]);
+                    const SplitEval r = eval_split(GL, HL, GT, HT, mcw, eps);
+                    sg[(warp * NB + b) * FB + lane] = r.gain;
+                    sd[(warp * NB + b) * FB + lane] = (signed char)r.dir;
+                }
+            }
+        }
+        __syncthreads();
+        const int ne = min(EB, E - e0);
+#pragma unroll
+        for (int t = 0; t < IPT; ++t) {
+            const int it = threadIdx.x + 256 * t;
+            const int b = it / FB, f = it - b * FB;
+            if (b < nb && f < nf) {
+                for (int w = 0; w < ne; ++w) {
+                    cs[t] = __fadd_rn(cs[t], sg[(w * NB + b) * FB + f]);
+                    ds[t] += sd[(w * NB + b) * FB + f];
+                }
+            }
+        }
+        __syncthreads();  // the batch's gains are consumed before the next batch writes them
+    }
+    Key best = key_none();
+#pragma unroll
+    for (int t = 0; t < IPT; ++t) {
+        const int it = threadIdx.x + 256 * t;
+        const int b = it / FB, f = it - b * FB;
+        if (b < nb && f < nf) {
+            const float cr = __fmul_rn(cs[t], factor);
+            const Key kk{abs(ds[t]), cr > msg ? cr : -INFINITY, (j0 + f) * nb + b};
+            if (key_better(kk, best)) best = kk;
+        }
+    }
+    best = warp_key_max(best);
+    __shared__ Key s_k[8];
+    if (lane == 0) s_k[warp] = best;
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        for (int w = 1; w < 8; ++w)
+            if (key_better(s_k[w], best)) best = s_k[w];
+        cand[(long long)n * nblk + jb] = make_int4(best.A, __float_as_int(best.c), best.idx, 0);
+    }
+}
+
+static inline size_t split_eras_smem(int B, int NB) {
+    const int B1p = (B + 1) | 1;
+    return (size_t)SPLIT_ERA_EB * 2 * SPLIT_ERA_FB * B1p * sizeof(float) +
+           (size_t)SPLIT_ERA_EB * NB * SPLIT_ERA_FB * (sizeof(float) + 1);
 }
 
 // Per node: final arg-max, per-era gain of the chosen split (importance,
@@ -1246,9 +1372,14 @@ int wgb_level_split(const wgb_ws *ws, int32_t d, void *stream) {
         k_root_total<<<1, 1, 0, st>>>(ws->nodes, hg + 2 * nc, ws->shift);
         WGB_LAUNCHED("k_root_total");
     } else {
-        int bx = (int)((nc + 255) / 256);
-        if (bx > 64) bx = 64;
-        k_subtract<<<(unsigned)bx * (cap / 2), 256, 0, st>>>(lvl, ws->nn + d, hg, hc, se, nc, bx);
+        // blocks per pair: about 8 blocks per SM over all pairs of the level,
+        // at most one per 256 cells (a few pairs of large era histograms
+        // would otherwise leave most SMs idle)
+        const long long per_cell = (nc + 255) / 256;
+        long long bx = (148 * 8 + cap / 2 - 1) / (cap / 2);
+        if (bx < 64) bx = 64;
+        if (bx > per_cell) bx = per_cell;
+        k_subtract<<<(unsigned)(bx * (cap / 2)), 256, 0, st>>>(lvl, ws->nn + d, hg, hc, se, nc, (int)bx);
         WGB_LAUNCHED("k_subtract");
     }
     const int nblk = (ws->k + SPLIT_THREADS - 1) / SPLIT_THREADS;
@@ -1271,7 +1402,24 @@ int wgb_level_split(const wgb_ws *ws, int32_t d, void *stream) {
     } else {                                                                                                 \
         k_split<NB_, MULTI_><<<g, SPLIT_THREADS, 0, st>>>(WGB_SPLIT_ARGS);                                  \
     }
-    if (ws->E == 1) {
+    // eras: the era-parallel search when the candidate buffer holds
+    // ceil(k/32) blocks per node (otherwise the per-thread scans above)
+    const int nblk_e = (ws->k + SPLIT_ERA_FB - 1) / SPLIT_ERA_FB;
+    const bool era_split = ws->E > 1 && nb <= 32 && nblk_e <= ws->ncand_blk;
+    int nblk_used = nblk;
+    if (era_split) {
+        nblk_used = nblk_e;
+        const unsigned ge = (unsigned)nblk_e * (unsigned)cap;
+#define WGB_SPLIT_ERAS(NB_)                                                                                   \
+    {                                                                                                         \
+        const size_t sm = split_eras_smem(ws->B, NB_);                                                        \
+        WGB_CUDA(cudaFuncSetAttribute(k_split_eras<NB_>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm)); \
+        k_split_eras<NB_><<<ge, 256, sm, st>>>(lvl, ws->nn + d, hg, hc, se, ws->k, ws->E, ws->B, ws->shift,   \
+                                               ws->mcw, ws->eps, ws->msg, ws->mean_factor, cand, nblk_e);     \
+    }
+        if (nb <= 8) WGB_SPLIT_ERAS(8) else WGB_SPLIT_ERAS(32)
+#undef WGB_SPLIT_ERAS
+    } else if (ws->E == 1) {
         WGB_SPLIT_LAUNCH(1, false)
     } else if (nb <= 8) {
         WGB_SPLIT_LAUNCH(8, true)
@@ -1285,7 +1433,7 @@ int wgb_level_split(const wgb_ws *ws, int32_t d, void *stream) {
     WGB_LAUNCHED("k_split");
     float *eg = ws->era_gain + (long long)((1 << d) - 1) * ws->E;
     k_split_final<<<cap, 256, 0, st>>>(lvl, ws->nn + d, hg, hc, se, ws->k, ws->E, ws->B,
-                                       ws->shift, ws->mcw, ws->eps, cand, nblk, eg);
+                                       ws->shift, ws->mcw, ws->eps, cand, nblk_used, eg);
     WGB_LAUNCHED("k_split_final");
     k_plan_next<<<1, 1024, 0, st>>>(lvl, level_nodes(ws, d + 1), ws->nn, d, ws->shift);
     WGB_LAUNCHED("k_plan_next");
