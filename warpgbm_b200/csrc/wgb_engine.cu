@@ -516,8 +516,9 @@ static cudaError_t launch_hist(int grid_x, const int8_t *bins, long long S, int 
     WGB_HIST_REG(4, 256, 1, 34, 1, false)
     WGB_HIST_REG(4, 256, 1, 8, 1, false)
     WGB_HIST_REG(4, 256, 1, 130, 1, false)
-    // eras: several era slots per window
-    WGB_HIST_REG(8, 512, 1, 8, 8, true)
+    // eras: several era slots per window; up to 8 bins, 4 slots keep two
+    // CTAs per SM (one CTA's window barriers overlap the other's updates)
+    WGB_HIST_REG(8, 512, 2, 8, 4, true)
     WGB_HIST_REG(8, 512, 1, 34, 2, true)
     WGB_HIST_REG(4, 256, 1, 8, 8, true)
     WGB_HIST_REG(4, 256, 1, 34, 4, true)
