@@ -516,7 +516,7 @@ def run_config(args):
             mr.fit(Xd, yd, era_id=erad)
         hist_ms = sum(a.elapsed_time(b) for a, b in mr._hist_events)
         k = max(1, int(params["colsample_bytree"] * X.shape[1]))
-        hb = hist_algorithmic_bytes(mr, X.shape[0], k, 600, params["num_bins"])
+        hb = hist_algorithmic_bytes(mr, X.shape[0], k, mr.num_eras, params["num_bins"])
         peak, peak_kind = peaks()
         ach = hb / (hist_ms / 1000.0) / 1e9 if hist_ms > 0 else None
         line["roofline"] = {"bound": "hbm", "kernel": "k_hist (era windows) per level",
