@@ -119,6 +119,24 @@ def test_c4_like_era_des_prebinned_colsample(cuda, F):
     assert np.array_equal(m.predict(X), o.predict(X))
 
 
+@pytest.mark.parametrize("B", [33, 64])
+def test_era_des_many_bins_bit_exact(cuda, B):
+    """Eras with 32 split points (the era-parallel split search's largest)
+    and with 63 (the per-thread era scan), float input binned on the GPU."""
+    rng = np.random.default_rng(B)
+    n, F, E = 24_000, 30, 12
+    X = rng.standard_normal((n, F)).astype(np.float32)
+    era = rng.integers(0, E, n).astype(np.int32)
+    sign = np.where(era % 3 == 0, -1.0, 1.0)
+    y = (X[:, 0] + sign * X[:, 1] + 0.5 * rng.standard_normal(n)).astype(np.float32)
+    params = dict(num_bins=B, max_depth=4, n_estimators=3, learning_rate=0.1, min_child_weight=5)
+    m = WarpGBM(**params).fit(X, y, era_id=era)
+    o = _oracle_for(m, params, X, y, era)
+    assert _same(_flat(m, 4), o.flat_forest())
+    assert np.array_equal(m.per_era_feature_importance_, o.per_era_feature_importance_)
+    assert np.array_equal(m.predict(X), o.predict(X))
+
+
 def test_moderate_scale_bit_exact_and_deterministic(cuda):
     rng = np.random.default_rng(9)
     n, F = 200_000, 256
