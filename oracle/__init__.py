@@ -211,6 +211,71 @@ def cuda_mean_factor(E: int, k: int, nb: int) -> np.float32:
     return np.float32(np.float32(k * nb) / np.float32(E * k * nb))
 
 
+def cuda_era_mean(x: np.ndarray, num_sms: int = 148, max_threads_per_sm: int = 2048) -> np.ndarray:
+    """Mean over axis 0 of a contiguous fp32 ``[E, ...]`` array in the order
+    in which torch's CUDA reduction adds (the reference's
+    ``per_era_gain.mean(dim=0)``, core.py:581-582), restated from the
+    published ``ATen/native/cuda/Reduce.cuh`` of torch 2.11:
+
+    * launch shape (``setReduceConfig`` / ``set_block_dimension``): outputs
+      are vectorised by ``vec`` = the largest of 4, 2, 1 dividing the output
+      count M; ``mnt = 512 / vec`` threads; block width and height are the
+      powers of two ``bw = min(p2(M/vec), 32)``, ``bh = min(p2(E), mnt/bw)``,
+      ``bw = min(p2(M/vec), mnt/bh)`` (``p2`` = largest power of two <= n,
+      capped at ``mnt``); the eras are split over the ``bh`` rows of the
+      block when ``E >= min(16 bh, 256)``;
+    * per thread (``thread_reduce_impl``): four accumulators, the t-th era
+      of a thread going to accumulator ``t % 4``, each summed in era order
+      from 0, then ``((a0 + a1) + a2) + a3``;
+    * across the block rows (``block_y_reduce``): a halving tree,
+      ``r[y] += r[y + off]`` for off = bh/2, ..., 1;
+    * ``* factor`` with ``factor = float(M) / float(E * M)``.
+
+    Launches that would also split the eras across thread blocks (a global
+    reduction; at least 256 eras per block row) are not restated and raise.
+    ``num_sms`` / ``max_threads_per_sm`` (a B200: 148, 2048) only decide
+    that case."""
+    x = np.ascontiguousarray(x, np.float32)
+    E = x.shape[0]
+    M = x.size // E
+    if E < 2 or M < 2:
+        raise NotImplementedError("a trivial dimension changes the reduction's layout")
+    flat = x.reshape(E, M)
+    vec = 4
+    while M % vec:
+        vec //= 2
+    dim0 = M // vec
+    mnt = 512 // vec
+
+    def p2(n):
+        return mnt if n >= mnt else 1 << (int(n).bit_length() - 1)
+
+    bw = min(p2(dim0), 32)
+    bh = min(p2(E), mnt // bw)
+    bw = min(p2(dim0), mnt // bh)
+    split = E >= min(bh * 16, 256)
+    if split:
+        vpt = -(-E // bh)
+        grid = -(-dim0 // bw)
+        target = num_sms * (max_threads_per_sm // (bw * bh))
+        if vpt >= 256 and grid <= target:
+            ctas = max(min(-(-target // grid), -(-vpt // 16)), -(-vpt // 256))
+            if ctas > 1:
+                raise NotImplementedError("eras split across thread blocks (global reduction)")
+    Y = bh if split else 1
+    acc = np.zeros((Y, 4, M), np.float32)
+    for e in range(E):
+        y, t = e % Y, e // Y
+        acc[y, t % 4] = acc[y, t % 4] + flat[e]
+    r = ((acc[:, 0] + acc[:, 1]) + acc[:, 2]) + acc[:, 3]
+    off = Y // 2
+    while off > 0:
+        r[:off] = r[:off] + r[off:2 * off]
+        off //= 2
+    factor = np.float32(np.float32(M) / np.float32(E * M))
+    return (r[0] * factor).astype(np.float32).reshape(x.shape[1:])
+
+
 def des_pick(gain, d, msg, mean_mode):
     """core.py:577-594: flat index of the chosen [k, B-1] cell, or -1."""
     gain = _c(gain, np.float32)

@@ -153,7 +153,7 @@ def test_compute_split_bit_exact(cuda, E, k, B):
     (20000, 61, 61, 3, 10, False),      # unaligned rows (F % 4 != 0), unsorted eras
     (30000, 40, 20, 37, 5, True),
     # 8 features per lane (row stride % 8 == 0, > 128 features) with eras:
-    # 8 era slots of 8 bin slots, 2 era slots of 34, unsorted eras
+    # 4 era slots of 8 bin slots, 2 era slots of 34, unsorted eras
     (40000, 264, 150, 7, 5, True),
     (20000, 264, 200, 4, 32, True),
     (20000, 136, 136, 3, 10, False),
@@ -273,3 +273,18 @@ def test_quantile_edges_kernel_equals_torch_quantile(cuda, B):
     got = _quantile_columns(Xd, q, chunk_elems=20_000 * 8).cpu().numpy()
     ref = torch.quantile(Xd, q, dim=0).T.cpu().numpy()
     assert np.array_equal(got, ref, equal_nan=True)
+
+
+@pytest.mark.parametrize("E,k,nb", [(3, 40, 4), (30, 40, 4), (60, 50, 4), (100, 300, 9), (600, 1188, 4),
+                                    (600, 128, 4), (12, 30, 32), (200, 7, 3), (64, 2, 2), (40, 16, 4)])
+def test_oracle_era_mean_order_equals_torch_cuda_mean(cuda, E, k, nb):
+    """The oracle's restatement of the order in which torch's CUDA mean adds
+    the eras (the reference's DES criterion, core.py:581-582) against torch
+    on this GPU, bit for bit."""
+    import torch
+    g = torch.Generator(device=cuda)
+    g.manual_seed(E * 1000 + k + nb)
+    x = torch.randn((E, k, nb), generator=g, device=cuda) * 10.0
+    want = x.mean(dim=0).cpu().numpy()
+    got = O.cuda_era_mean(x.cpu().numpy())
+    assert np.array_equal(got.view(np.int32), want.view(np.int32))
