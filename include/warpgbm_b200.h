@@ -210,9 +210,9 @@ typedef struct wgb_ws {
     int32_t *nchunks;        /* [1]                                           */
     /* split search */
     int32_t *cand;           /* [2^(D-1)][ncand_blk][4] partial arg-max:     */
-                             /*   ncand_blk >= ceil(k/128) required; with    */
-                             /*   >= ceil(k/32) eras take the era-parallel   */
-                             /*   search (same result, faster)               */
+                             /*   ncand_blk >= ceil(k/128) with one era;     */
+                             /*   with eras >= ceil(k/32) (num_bins <= 33)   */
+                             /*   or ceil(k/8) (num_bins > 33)               */
     float *era_gain;         /* [2^D - 1][E] per-era gain of chosen split     */
     /* nodes and level sizes */
     wgb_node *nodes;         /* [2^(D+1) - 1]                                 */
@@ -225,6 +225,11 @@ typedef struct wgb_ws {
     void *part_hist;         /* per-chunk histogram words (8 bytes each), or  */
     int64_t part_hist_elems; /*   NULL: wgb_hist_part_elems(S, F, B, chunk_cap) */
                              /*   lets single-era levels skip global atomics  */
+    /* era criterion (E > 1): the plan of wgb_era_mean_plan(E, k*(B-1), ...) */
+    const int32_t *era_sched; /* [E] eras in the order the criterion adds them */
+    const uint8_t *era_ops;  /* [era_nops] accumulator program                */
+    float *crit_out;         /* optional [k][B-1]: criterion of node 0 of each */
+                             /*   level (inspection), or NULL                  */
     /* sizes */
     int64_t N, S;
     int64_t N_global;
@@ -233,6 +238,7 @@ typedef struct wgb_ws {
     int32_t chunk_cap, ntiles, ncand_blk;
     int32_t hist_ew;         /* max eras per shared-memory window (0 = auto)  */
     int32_t regular;         /* 1 if every bin is known to lie in [0, B)      */
+    int32_t era_nops, era_depth; /* program length and stack depth of the plan */
     /* hyper-parameters (fp32 as the reference passes them) */
     float mcw, eps, msg, lr, mean_factor;
 } wgb_ws;
@@ -260,8 +266,28 @@ void wgb_built_slots(int32_t d, int32_t *first, int32_t *count);
  * chunks of a matrix with row stride S, F features and B bins. */
 int64_t wgb_hist_part_elems(int64_t S, int32_t F, int32_t B, int64_t chunks);
 /* Level d: sibling = parent - built (in place), split search, per-era gains,
- * child totals, next level's node records. */
+ * child totals, next level's node records.  With eras the criterion is
+ * torch's CUDA per_era_gain.mean(dim=0) (warpgbm/core.py:581-582) bit for
+ * bit: the eras are added in the order of ws->era_sched / ws->era_ops. */
 int wgb_level_split(const wgb_ws *ws, int32_t d, void *stream);
+
+/* Plan of the order in which torch's CUDA mean(dim=0) of a contiguous fp32
+ * [E][M] tensor adds its E rows (ATen's reduce kernel: rows spread over the
+ * block's rows and over blocks, four accumulators per thread, fixed
+ * combining trees; the launch shape depends on E, M, the SM count and the
+ * threads per SM -- num_sms / max_threads_per_sm <= 0 take the current
+ * device's).  Replaces the ordering of warpgbm/core.py:581-582's
+ * per_era_gain.mean(dim=0) and per_era_direction.mean(dim=0) with M =
+ * k*(num_bins-1).  Writes sched[E] (eras in the order they are first added)
+ * and ops[] (0: push the accumulator and restart it at 0; 1: accumulator +=
+ * popped value; 2: accumulator += next scheduled era); *depth = stack depth.
+ * Returns the program length (write nothing with ops == NULL to size it;
+ * ops_cap must hold it), or a negative status.  M == 1 (a single candidate)
+ * is reduced by torch along another path; the plan is then a sequential
+ * sum. */
+int64_t wgb_era_mean_plan(int32_t E, int64_t M, int32_t num_sms,
+                          int32_t max_threads_per_sm, int32_t *sched,
+                          uint8_t *ops, int64_t ops_cap, int32_t *depth);
 /* Feature-major copy of ws->bins into out ([F][NT], NT = N rounded up to a
  * multiple of 16, 16-byte aligned): the partition reads one feature of many
  * rows, which this layout makes contiguous.  Set ws->bins_fm = out after. */

@@ -15,15 +15,16 @@ Two modes:
 ``mode="reference"``
     fp32 histogram sums in sample order, fp32 sibling subtraction
     (core.py:636-643), leaf = torch mean of the residuals (core.py:599),
-    era means as torch's CPU ``mean`` (sum / E).  Pinned against fixtures
-    produced by the reference's own ``core.py`` (tests/golden).
+    era means as torch's CUDA ``mean`` adds them (cuda_era_mean: the
+    reference runs on CUDA).  Pinned against fixtures produced by the
+    reference's own ``core.py`` (tests/golden).
 
 ``mode="canonical"``
     What the CUDA product computes, so that it can be compared bit for bit:
     residuals quantised per tree to ``q = rint(g * 2^s)`` with
     ``s = 29 - frexp_exponent(max|g|)``; histograms are exact int64 sums;
     leaf = ``float(sum_q) * 2^-s * (1 / float(n))`` in fp32; era means as
-    torch's CUDA ``mean`` (sum times ``factor``); base prediction from an
+    torch's CUDA ``mean`` adds them (cuda_era_mean); base prediction from an
     exact fixed-point sum of y.
 """
 from __future__ import annotations
@@ -211,36 +212,12 @@ def cuda_mean_factor(E: int, k: int, nb: int) -> np.float32:
     return np.float32(np.float32(k * nb) / np.float32(E * k * nb))
 
 
-def cuda_era_mean(x: np.ndarray, num_sms: int = 148, max_threads_per_sm: int = 2048) -> np.ndarray:
-    """Mean over axis 0 of a contiguous fp32 ``[E, ...]`` array in the order
-    in which torch's CUDA reduction adds (the reference's
-    ``per_era_gain.mean(dim=0)``, core.py:581-582), restated from the
-    published ``ATen/native/cuda/Reduce.cuh`` of torch 2.11:
-
-    * launch shape (``setReduceConfig`` / ``set_block_dimension``): outputs
-      are vectorised by ``vec`` = the largest of 4, 2, 1 dividing the output
-      count M; ``mnt = 512 / vec`` threads; block width and height are the
-      powers of two ``bw = min(p2(M/vec), 32)``, ``bh = min(p2(E), mnt/bw)``,
-      ``bw = min(p2(M/vec), mnt/bh)`` (``p2`` = largest power of two <= n,
-      capped at ``mnt``); the eras are split over the ``bh`` rows of the
-      block when ``E >= min(16 bh, 256)``;
-    * per thread (``thread_reduce_impl``): four accumulators, the t-th era
-      of a thread going to accumulator ``t % 4``, each summed in era order
-      from 0, then ``((a0 + a1) + a2) + a3``;
-    * across the block rows (``block_y_reduce``): a halving tree,
-      ``r[y] += r[y + off]`` for off = bh/2, ..., 1;
-    * ``* factor`` with ``factor = float(M) / float(E * M)``.
-
-    Launches that would also split the eras across thread blocks (a global
-    reduction; at least 256 eras per block row) are not restated and raise.
-    ``num_sms`` / ``max_threads_per_sm`` (a B200: 148, 2048) only decide
-    that case."""
-    x = np.ascontiguousarray(x, np.float32)
-    E = x.shape[0]
-    M = x.size // E
-    if E < 2 or M < 2:
-        raise NotImplementedError("a trivial dimension changes the reduction's layout")
-    flat = x.reshape(E, M)
+def _cuda_mean_layout(E: int, M: int, num_sms: int, max_threads_per_sm: int):
+    """(rows, ctas) of torch's CUDA reduce kernel for the mean over axis 0 of
+    a contiguous fp32 [E, M] array (ATen/native/cuda/Reduce.cuh of torch
+    2.11, ``setReduceConfig`` / ``set_block_dimension``): the eras are spread
+    over ``rows`` block rows and ``ctas`` thread blocks (both 1 when a thread
+    sums its output alone)."""
     vec = 4
     while M % vec:
         vec //= 2
@@ -253,37 +230,105 @@ def cuda_era_mean(x: np.ndarray, num_sms: int = 148, max_threads_per_sm: int = 2
     bw = min(p2(dim0), 32)
     bh = min(p2(E), mnt // bw)
     bw = min(p2(dim0), mnt // bh)
-    split = E >= min(bh * 16, 256)
-    if split:
-        vpt = -(-E // bh)
-        grid = -(-dim0 // bw)
-        target = num_sms * (max_threads_per_sm // (bw * bh))
-        if vpt >= 256 and grid <= target:
-            ctas = max(min(-(-target // grid), -(-vpt // 16)), -(-vpt // 256))
-            if ctas > 1:
-                raise NotImplementedError("eras split across thread blocks (global reduction)")
-    Y = bh if split else 1
-    acc = np.zeros((Y, 4, M), np.float32)
+    if not E >= min(bh * 16, 256):
+        return 1, 1
+    vpt = -(-E // bh)
+    grid = -(-dim0 // bw)
+    target = num_sms * (max_threads_per_sm // (bw * bh))
+    ctas = 1
+    if vpt >= 256 and grid <= target:
+        ctas = max(min(-(-target // grid), -(-vpt // 16)), -(-vpt // 256))
+    return bh, max(ctas, 1)
+
+
+def cuda_era_mean(x: np.ndarray, num_sms: int = 148, max_threads_per_sm: int = 2048) -> np.ndarray:
+    """Mean over axis 0 of a contiguous fp32 ``[E, ...]`` array in the order
+    in which torch's CUDA reduction adds (the reference's
+    ``per_era_gain.mean(dim=0)``, core.py:581-582), restated from the
+    published ``ATen/native/cuda/Reduce.cuh`` of torch 2.11:
+
+    * launch shape (``setReduceConfig`` / ``set_block_dimension``): outputs
+      are vectorised by ``vec`` = the largest of 4, 2, 1 dividing the output
+      count M; ``mnt = 512 / vec`` threads; block width and height are the
+      powers of two ``bw = min(p2(M/vec), 32)``, ``bh = min(p2(E), mnt/bw)``,
+      ``bw = min(p2(M/vec), mnt/bh)`` (``p2`` = largest power of two <= n,
+      capped at ``mnt``); the eras are split over the ``bh`` rows of the
+      block when ``E >= min(16 bh, 256)``, and also over ``ctas`` thread
+      blocks when a row would still sum 256 eras or more and the output grid
+      is small (``ctas = max(min(ceil(target / grid), ceil(vpt / 16)),
+      ceil(vpt / 256))``, ``vpt = ceil(E / bh)``, ``target`` = SMs x blocks
+      per SM);
+    * per thread (``thread_reduce_impl``): thread (row y, block c) takes the
+      eras e = y + bh*c (mod bh*ctas); its t-th era goes to accumulator
+      ``t % 4``, each summed in era order from 0, then ``((a0 + a1) + a2) +
+      a3``;
+    * across the block rows (``block_y_reduce``): a halving tree,
+      ``r[y] += r[y + off]`` for off = bh/2, ..., 1;
+    * across blocks (``global_reduce``): row y of the last block adds the
+      block results c = y, y + bh, ... in order from 0, then the halving
+      tree again;
+    * ``* factor`` with ``factor = float(M) / float(E * M)``.
+
+    ``num_sms`` / ``max_threads_per_sm`` (a B200: 148, 2048) only decide the
+    number of blocks.  A single output (M == 1) is reduced along another
+    path (vectorised loads of the contiguous eras, warp shuffles), which is
+    not restated: it raises."""
+    x = np.ascontiguousarray(x, np.float32)
+    E = x.shape[0]
+    M = x.size // E
+    if E < 1 or M < 2:
+        raise NotImplementedError("a single output is reduced along another path")
+    flat = x.reshape(E, M)
+    Y, C = _cuda_mean_layout(E, M, num_sms, max_threads_per_sm)
+    L = Y * C
+    acc = np.zeros((L, 4, M), np.float32)
     for e in range(E):
-        y, t = e % Y, e // Y
-        acc[y, t % 4] = acc[y, t % 4] + flat[e]
+        lane, t = e % L, e // L
+        acc[lane, t % 4] = acc[lane, t % 4] + flat[e]
     r = ((acc[:, 0] + acc[:, 1]) + acc[:, 2]) + acc[:, 3]
-    off = Y // 2
-    while off > 0:
-        r[:off] = r[:off] + r[off:2 * off]
-        off //= 2
+    v = r.reshape(C, Y, M)                     # lane y + Y*c -> [c, y]
+
+    def halve(a):                              # block_y_reduce over axis -2
+        off = a.shape[-2] // 2
+        while off > 0:
+            a[..., :off, :] = a[..., :off, :] + a[..., off:2 * off, :]
+            off //= 2
+        return a[..., 0, :]
+
+    vc = halve(v)                              # [C, M]
+    if C > 1:
+        u = np.zeros((Y, M), np.float32)
+        for c in range(C):
+            u[c % Y] = u[c % Y] + vc[c]
+        res = halve(u)
+    else:
+        res = vc[0]
     factor = np.float32(np.float32(M) / np.float32(E * M))
-    return (r[0] * factor).astype(np.float32).reshape(x.shape[1:])
+    return (res * factor).astype(np.float32).reshape(x.shape[1:])
 
 
 def des_pick(gain, d, msg, mean_mode):
-    """core.py:577-594: flat index of the chosen [k, B-1] cell, or -1."""
+    """core.py:577-594: flat index of the chosen [k, B-1] cell, or -1.
+
+    mean_mode 1: the era means as torch's CUDA ``mean(dim=0)`` computes them
+    (cuda_era_mean; the reference runs on CUDA); mean_mode 0: a sequential
+    era sum divided by E (torch's CPU mean for the few eras of the golden
+    fixtures).  The agreement |mean dir| is exact in any order (sums of
+    -1/0/1 in fp32), times the same factor."""
     gain = _c(gain, np.float32)
     d = _c(d, np.float32)
     E, k, nb = gain.shape
-    factor = cuda_mean_factor(E, k, nb) if mean_mode == 1 else np.float32(1.0)
-    return int(lib().orc_des_pick(_ptr(gain), _ptr(d), E, k, nb + 1,
-                                  float(np.float32(msg)), mean_mode, float(factor)))
+    if E == 1 or mean_mode == 0 or k * nb < 2:
+        factor = cuda_mean_factor(E, k, nb) if mean_mode == 1 else np.float32(1.0)
+        return int(lib().orc_des_pick(_ptr(gain), _ptr(d), E, k, nb + 1,
+                                      float(np.float32(msg)), mean_mode, float(factor)))
+    crit = cuda_era_mean(gain).reshape(-1)
+    factor = cuda_mean_factor(E, k, nb)
+    agree = np.abs(d.reshape(E, -1).sum(axis=0, dtype=np.float64).astype(np.float32) * factor)
+    mask = (agree == agree.max()) & (crit > np.float32(msg))
+    if not mask.any():
+        return -1
+    return int(np.argmax(np.where(mask, crit, np.float32(-np.inf))))
 
 
 def predict_flat(bins, forest, lr, out):
@@ -426,7 +471,7 @@ class OracleGBM:
         else:
             G, H = dequant(hist[0], hist[1], self.qshift)
         gain, d = split(G, H, self.min_child_weight, self.L2_reg)
-        idx = des_pick(gain, d, self.min_split_gain, 0 if self.mode == "reference" else 1)
+        idx = des_pick(gain, d, self.min_split_gain, 1)
         return idx, gain
 
     def _leaf(self, rows):

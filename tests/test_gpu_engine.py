@@ -119,6 +119,27 @@ def test_c4_like_era_des_prebinned_colsample(cuda, F):
     assert np.array_equal(m.predict(X), o.predict(X))
 
 
+@pytest.mark.parametrize("E,n,F", [(600, 120_000, 64), (2100, 210_000, 32)])
+def test_many_era_des_bit_exact(cuda, E, n, F):
+    """Hundreds and thousands of eras: the criterion is torch's CUDA era mean
+    (core.py:581-582), whose order spreads the eras over block rows (600)
+    and over several blocks (2100); trees against the oracle that restates
+    that order."""
+    rng = np.random.default_rng(E)
+    X = rng.integers(0, 5, (n, F)).astype(np.int8)
+    era = np.repeat(np.arange(E), n // E).astype(np.int32)
+    c = rng.standard_normal((E, 8))
+    c[:, :5] = np.abs(c[:, :5])
+    y = ((X[:, :8] * c[era]).sum(1) + rng.standard_normal(n)).astype(np.float32)
+    params = dict(num_bins=5, max_depth=5, n_estimators=3, learning_rate=0.01,
+                  colsample_bytree=0.5, random_state=0, min_child_weight=5)
+    m = WarpGBM(**params).fit(X, y, era_id=era)
+    o = _oracle_for(m, params, X, y, era)
+    assert _same(_flat(m, 5), o.flat_forest())
+    assert np.array_equal(m.per_era_feature_importance_, o.per_era_feature_importance_)
+    assert np.array_equal(m.predict(X), o.predict(X))
+
+
 @pytest.mark.parametrize("B", [33, 64])
 def test_era_des_many_bins_bit_exact(cuda, B):
     """Eras with 32 split points (the era-parallel split search's largest)

@@ -46,11 +46,12 @@ class WgbWs(ctypes.Structure):
         ("cand", _p), ("era_gain", _p),
         ("nodes", _p), ("nn", _p), ("nact", _p),
         ("maxabs", _p), ("shift", _p), ("rootsum", _p), ("part_hist", _p), ("part_hist_elems", _i64),
+        ("era_sched", _p), ("era_ops", _p), ("crit_out", _p),
         ("N", _i64), ("S", _i64), ("N_global", _i64),
         ("F", _i32), ("k", _i32), ("E", _i32), ("B", _i32), ("D", _i32), ("K", _i32),
         ("cls", _i32),
         ("chunk_cap", _i32), ("ntiles", _i32), ("ncand_blk", _i32),
-        ("hist_ew", _i32), ("regular", _i32),
+        ("hist_ew", _i32), ("regular", _i32), ("era_nops", _i32), ("era_depth", _i32),
         ("mcw", _f32), ("eps", _f32), ("msg", _f32), ("lr", _f32), ("mean_factor", _f32),
     ]
 
@@ -75,6 +76,7 @@ _SIGS = {
     "wgb_level_hist": ([_p, _i32, _p], _i32),
     "wgb_built_slots": ([_i32, ctypes.POINTER(_i32), ctypes.POINTER(_i32)], None),
     "wgb_level_split": ([_p, _i32, _p], _i32),
+    "wgb_era_mean_plan": ([_i32, _i64, _i32, _i32, _p, _p, _i64, ctypes.POINTER(_i32)], _i64),
     "wgb_level_partition": ([_p, _i32, _p], _i32),
     "wgb_bins_feature_major": ([_p, _p, _p], _i32),
     "wgb_hist_part_elems": ([_i64, _i32, _i32, _i64], _i64),
@@ -134,6 +136,22 @@ LAUNCHES = [0]
 def call(name: str, *args) -> None:
     check(getattr(lib(), name)(*args), name)
     LAUNCHES[0] += _KERNELS.get(name, 0)
+
+
+def era_mean_plan(E: int, M: int, num_sms: int = 0, max_threads_per_sm: int = 0):
+    """(sched int32 [E], ops uint8 [n], depth) of wgb_era_mean_plan."""
+    import numpy as np
+    depth = _i32()
+    n = lib().wgb_era_mean_plan(E, M, num_sms, max_threads_per_sm, None, None, 0, ctypes.byref(depth))
+    if n < 0:
+        check(-n, "wgb_era_mean_plan")
+    sched = np.empty(E, np.int32)
+    ops = np.empty(max(n, 1), np.uint8)
+    n2 = lib().wgb_era_mean_plan(E, M, num_sms, max_threads_per_sm, sched.ctypes.data, ops.ctypes.data, n,
+                                 ctypes.byref(depth))
+    if n2 != n:
+        raise WgbError(f"wgb_era_mean_plan returned {n2}, expected {n}")
+    return sched, ops[:n], depth.value
 
 
 def built_slots(d: int):

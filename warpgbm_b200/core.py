@@ -37,7 +37,9 @@ from .metrics import accuracy_torch, log_loss_torch, rmsle_torch, softmax
 
 HIST_R = 2048          # rows per histogram chunk (csrc/wgb_common.cuh)
 PART_TILE = 2048       # positions per partition tile
-SPLIT_ERA_FEATURES = 32  # features per era split block (csrc/wgb_engine.cu)
+def split_era_features(B: int) -> int:
+    """Features per block of the era split search (csrc/wgb_engine.cu)."""
+    return 32 if B - 1 <= 32 else 8
 
 
 def _round_up(x, m):
@@ -705,10 +707,19 @@ class WarpGBM(BaseEstimator, RegressorMixin):
             t["part_hist"] = torch.empty(part_elems * 2, dtype=torch.int32, device=dev)
         else:
             part_elems = 0
-        # per-node partial arg-max: blocks of 32 features (the era split
-        # search; the single-era search uses ceil(k/128) of them)
-        ncand = (k + SPLIT_ERA_FEATURES - 1) // SPLIT_ERA_FEATURES
+        # per-node partial arg-max: blocks of 128 features with one era, of
+        # 32 (or 8 for num_bins > 33) with eras
+        fb = 128 if E == 1 else split_era_features(B)
+        ncand = (k + fb - 1) // fb
         t["cand"] = torch.empty((nslots, ncand, 4), **i32)
+        if E > 1:
+            # order in which the reference's per_era_gain.mean(dim=0) adds the
+            # eras on this device (core.py:581-582)
+            props = torch.cuda.get_device_properties(dev)
+            sched, ops, depth = _lib.era_mean_plan(E, k * (B - 1), props.multi_processor_count,
+                                                   props.max_threads_per_multi_processor)
+            t["era_sched"] = torch.from_numpy(sched).to(dev)
+            t["era_ops"] = torch.from_numpy(ops).to(dev)
         t["era_gain"] = torch.zeros(((1 << D) - 1) * E, dtype=torch.float32, device=dev)
         t["nodes"] = torch.zeros(((1 << (D + 1)) - 1) * 64, dtype=torch.uint8, device=dev)
         t["nn"] = torch.zeros(D + 1, **i32)
@@ -740,6 +751,9 @@ class WarpGBM(BaseEstimator, RegressorMixin):
         ws.msg = float(np.float32(self.min_split_gain))
         ws.lr = float(np.float32(self.learning_rate))
         ws.mean_factor = cuda_mean_factor(E, k, B - 1)
+        if E > 1:
+            ws.era_sched, ws.era_ops = t["era_sched"].data_ptr(), t["era_ops"].data_ptr()
+            ws.era_nops, ws.era_depth = int(t["era_ops"].numel()), depth
         self._ws = ws
         return ws
 

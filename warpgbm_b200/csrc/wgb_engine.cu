@@ -16,6 +16,7 @@
 //
 // No host synchronisation happens inside a tree: level sizes live on the
 // device and every grid is sized by a host-known upper bound.
+#include <algorithm>
 #include <cstdarg>
 #include <cstdio>
 
@@ -551,15 +552,13 @@ __global__ void k_subtract(const wgb_node *__restrict__ lvl, const int *nn_d, lo
 // split search                                                           //
 // ====================================================================== //
 
-// One thread = (node, feature position j): every era's bin scan with the
-// reference arithmetic; E == 1 takes gain as the criterion, E > 1 the
-// sequential fp32 era sum times `factor` (torch's CUDA mean) and the
-// agreement |sum dir| (core.py:581-583).  Block arg-max -> cand[node][blk].
-template <int NB, bool MULTI>
+// One thread = (node, feature position j): the bin scan of a single-era
+// histogram with the reference arithmetic (best_split_kernel.cu:25-53),
+// criterion = gain (core.py:577-579).  Block arg-max -> cand[node][blk].
 __global__ void __launch_bounds__(SPLIT_THREADS) k_split(
     const wgb_node *__restrict__ lvl, const int *nn_d, const long long *__restrict__ hg,
-    const long long *__restrict__ hc, long long slot_elems, int k, int E, int B, const int *shift,
-    float mcw, float eps, float msg, float factor, int4 *cand, int nblk) {
+    const long long *__restrict__ hc, long long slot_elems, int k, int B, const int *shift,
+    float mcw, float eps, float msg, int4 *cand, int nblk, float *crit_out) {
     const int n = blockIdx.x / nblk, jb = blockIdx.x - n * nblk;  // node, feature block
     if (n >= *nn_d) return;
     const int j = jb * SPLIT_THREADS + threadIdx.x;
@@ -568,50 +567,23 @@ __global__ void __launch_bounds__(SPLIT_THREADS) k_split(
     const long long slot = lvl[n].slot;
     Key best = key_none();
     if (j < k) {
-        float cs[MULTI ? NB : 1];
-        int ds[MULTI ? NB : 1];
-        if (MULTI) {
-#pragma unroll
-            for (int b = 0; b < (MULTI ? NB : 1); ++b) {
-                cs[b] = 0.0f;
-                ds[b] = 0;
-            }
+        const long long off = slot * slot_elems + (long long)j * B1;
+        const long long *gp = hg + off;
+        const long long *cp = hc + off;
+        float GT = 0.0f, HT = 0.0f;
+        for (int b = 0; b < B; ++b) {
+            GT = __fadd_rn(GT, __fmul_rn(__ll2float_rn(__ldg(gp + b)), inv));
+            HT = __fadd_rn(HT, __ll2float_rn(__ldg(cp + b)));
         }
-        for (int e = 0; e < E; ++e) {
-            const long long off = slot * slot_elems + ((long long)e * k + j) * B1;
-            const long long *gp = hg + off;
-            const long long *cp = hc + off;
-            float GT = 0.0f, HT = 0.0f;
-            for (int b = 0; b < B; ++b) {
-                GT = __fadd_rn(GT, __fmul_rn(__ll2float_rn(__ldg(gp + b)), inv));
-                HT = __fadd_rn(HT, __ll2float_rn(__ldg(cp + b)));
-            }
-            float GL = 0.0f, HL = 0.0f;
+        float GL = 0.0f, HL = 0.0f;
 #pragma unroll 4
-            for (int b = 0; b < nb; ++b) {
-                GL = __fadd_rn(GL, __fmul_rn(__ll2float_rn(__ldg(gp + b)), inv));
-                HL = __fadd_rn(HL, __ll2float_rn(__ldg(cp + b)));
-                SplitEval r = eval_split(GL, HL, GT, HT, mcw, eps);
-                if (MULTI) {
-                    if (b < NB) {
-                        cs[b] = __fadd_rn(cs[b], r.gain);
-                        ds[b] += (int)r.dir;
-                    }
-                } else {
-                    Key kk{0, r.gain > msg ? r.gain : -INFINITY, j * nb + b};
-                    if (key_better(kk, best)) best = kk;
-                }
-            }
-        }
-        if (MULTI) {
-#pragma unroll
-            for (int b = 0; b < (MULTI ? NB : 1); ++b) {
-                if (b < nb) {
-                    float cr = __fmul_rn(cs[b], factor);
-                    Key kk{abs(ds[b]), cr > msg ? cr : -INFINITY, j * nb + b};
-                    if (key_better(kk, best)) best = kk;
-                }
-            }
+        for (int b = 0; b < nb; ++b) {
+            GL = __fadd_rn(GL, __fmul_rn(__ll2float_rn(__ldg(gp + b)), inv));
+            HL = __fadd_rn(HL, __ll2float_rn(__ldg(cp + b)));
+            SplitEval r = eval_split(GL, HL, GT, HT, mcw, eps);
+            if (crit_out && n == 0) crit_out[j * nb + b] = r.gain;
+            Key kk{0, r.gain > msg ? r.gain : -INFINITY, j * nb + b};
+            if (key_better(kk, best)) best = kk;
         }
     }
     best = warp_key_max(best);
@@ -625,16 +597,15 @@ __global__ void __launch_bounds__(SPLIT_THREADS) k_split(
     }
 }
 
-template <int NB, bool MULTI>
+// k_split for levels with many nodes: the block's 128 feature rows are
+// staged in shared memory as fp32 (G = float(sum q) * 2^-s, H =
+// float(count)) with coalesced loads; each thread then scans its own row in
+// bin order (the reference's sequential fp32 sums).  Odd row stride:
+// conflict-free row reads.
 __global__ void __launch_bounds__(SPLIT_THREADS) k_split_staged(
     const wgb_node *__restrict__ lvl, const int *nn_d, const long long *__restrict__ hg,
-    const long long *__restrict__ hc, long long slot_elems, int k, int E, int B, const int *shift,
-    float mcw, float eps, float msg, float factor, int4 *cand, int nblk) {
-    // k_split for levels with many nodes: the block's 128 feature rows of
-    // one era are staged in shared memory as fp32 (G = float(sum q) * 2^-s,
-    // H = float(count)) with coalesced loads; each thread then scans its own
-    // row in bin order (the reference's sequential fp32 sums).  Odd row
-    // stride: conflict-free row reads.
+    const long long *__restrict__ hc, long long slot_elems, int k, int B, const int *shift,
+    float mcw, float eps, float msg, int4 *cand, int nblk, float *crit_out) {
     extern __shared__ float s_split[];
     const int n = blockIdx.x / nblk, jb = blockIdx.x - n * nblk;  // node, feature block
     if (n >= *nn_d) return;
@@ -645,57 +616,29 @@ __global__ void __launch_bounds__(SPLIT_THREADS) k_split_staged(
     float *sG = s_split, *sH = s_split + SPLIT_THREADS * B1p;
     const long long slot = lvl[n].slot;
     Key best = key_none();
-    float cs[MULTI ? NB : 1];
-    int ds[MULTI ? NB : 1];
-    if (MULTI) {
-#pragma unroll
-        for (int b = 0; b < (MULTI ? NB : 1); ++b) {
-            cs[b] = 0.0f;
-            ds[b] = 0;
-        }
+    const long long base = slot * slot_elems + (long long)j0 * B1;
+    for (int t = threadIdx.x; t < nj * B1; t += SPLIT_THREADS) {
+        const int jl = t / B1, b = t - jl * B1;
+        sG[jl * B1p + b] = __fmul_rn(__ll2float_rn(__ldg(hg + base + t)), inv);
+        sH[jl * B1p + b] = __ll2float_rn(__ldg(hc + base + t));
     }
-    for (int e = 0; e < E; ++e) {
-        const long long base = slot * slot_elems + ((long long)e * k + j0) * B1;
-        __syncthreads();  // the previous era's rows are consumed
-        for (int t = threadIdx.x; t < nj * B1; t += SPLIT_THREADS) {
-            const int jl = t / B1, b = t - jl * B1;
-            sG[jl * B1p + b] = __fmul_rn(__ll2float_rn(__ldg(hg + base + t)), inv);
-            sH[jl * B1p + b] = __ll2float_rn(__ldg(hc + base + t));
+    __syncthreads();
+    if (j < k) {
+        const float *g = sG + threadIdx.x * B1p, *h = sH + threadIdx.x * B1p;
+        float GT = 0.0f, HT = 0.0f;
+        for (int b = 0; b < B; ++b) {
+            GT = __fadd_rn(GT, g[b]);
+            HT = __fadd_rn(HT, h[b]);
         }
-        __syncthreads();
-        if (j < k) {
-            const float *g = sG + threadIdx.x * B1p, *h = sH + threadIdx.x * B1p;
-            float GT = 0.0f, HT = 0.0f;
-            for (int b = 0; b < B; ++b) {
-                GT = __fadd_rn(GT, g[b]);
-                HT = __fadd_rn(HT, h[b]);
-            }
-            float GL = 0.0f, HL = 0.0f;
+        float GL = 0.0f, HL = 0.0f;
 #pragma unroll 4
-            for (int b = 0; b < nb; ++b) {
-                GL = __fadd_rn(GL, g[b]);
-                HL = __fadd_rn(HL, h[b]);
-                SplitEval r = eval_split(GL, HL, GT, HT, mcw, eps);
-                if (MULTI) {
-                    if (b < NB) {
-                        cs[b] = __fadd_rn(cs[b], r.gain);
-                        ds[b] += (int)r.dir;
-                    }
-                } else {
-                    Key kk{0, r.gain > msg ? r.gain : -INFINITY, j * nb + b};
-                    if (key_better(kk, best)) best = kk;
-                }
-            }
-        }
-    }
-    if (MULTI && j < k) {
-#pragma unroll
-        for (int b = 0; b < (MULTI ? NB : 1); ++b) {
-            if (b < nb) {
-                float cr = __fmul_rn(cs[b], factor);
-                Key kk{abs(ds[b]), cr > msg ? cr : -INFINITY, j * nb + b};
-                if (key_better(kk, best)) best = kk;
-            }
+        for (int b = 0; b < nb; ++b) {
+            GL = __fadd_rn(GL, g[b]);
+            HL = __fadd_rn(HL, h[b]);
+            SplitEval r = eval_split(GL, HL, GT, HT, mcw, eps);
+            if (crit_out && n == 0) crit_out[j * nb + b] = r.gain;
+            Key kk{0, r.gain > msg ? r.gain : -INFINITY, j * nb + b};
+            if (key_better(kk, best)) best = kk;
         }
     }
     best = warp_key_max(best);
@@ -709,27 +652,159 @@ __global__ void __launch_bounds__(SPLIT_THREADS) k_split_staged(
     }
 }
 
-// Era split search (E > 1, B - 1 <= NB <= 32) with the eras spread over
-// warps: block = one node x 32 features, eras in batches of 8, one warp per
-// era.  Phase 1: a warp stages its era's 32 feature rows in shared memory
-// with coalesced loads (G = float(sum q) * 2^-s, H = float(count); odd row
-// stride, conflict-free), then lane f scans feature f's bins with the
-// reference arithmetic (as k_split) and leaves the era's B-1 gains and
-// directions in shared memory.  Phase 2: thread = (bin, feature) items add
-// the batch's gains in era order to a running fp32 sum -- the sequential
-// era sum of k_split, bit for bit -- and the directions to an integer
-// agreement.  Block arg-max -> cand[node][blk] (ceil(k/32) blocks).
-constexpr int SPLIT_ERA_FB = 32;  // features per block
+// ---------------------------------------------------------------------- //
+// Era criterion in the order of torch's CUDA mean                         //
+// ---------------------------------------------------------------------- //
+//
+// The reference's DES criterion is per_era_gain.mean(dim=0) on CUDA
+// (core.py:581-582).  torch's reduce kernel (ATen/native/cuda/Reduce.cuh)
+// does not add the eras one after another: depending on E and on the output
+// count M = k*(B-1) it spreads them over the rows of a block and over
+// several blocks, gives each thread four accumulators, and combines the
+// partial sums by fixed trees.  fp32 addition is not associative, so the
+// criterion is reproduced bit for bit only by adding in that order.  The
+// host turns the launch shape into a plan: a schedule of the eras in the
+// order they are first needed and a program for a small accumulator stack
+// per output cell:
+//     ERA_PUSH0  push the running accumulator, start a new one at 0
+//     ERA_ADD2   accumulator = popped value + accumulator
+//     ERA_ADD    accumulator += gain of the next scheduled era
+// which k_split_eras runs for every (feature, bin) cell of its block.
+enum : uint8_t { ERA_PUSH0 = 0, ERA_ADD2 = 1, ERA_ADD = 2 };
+
+// Launch shape of torch's reduce kernel for mean(dim=0) of a contiguous fp32
+// [E, M] tensor (setReduceConfig / set_block_dimension, torch 2.11): the eras
+// go to `rows` block rows and `ctas` blocks.
+static void era_mean_layout(int E, long long M, int num_sms, int max_threads_per_sm, int &rows, int &ctas) {
+    int vec = 4;
+    while (M % vec) vec >>= 1;
+    const long long dim0 = M / vec;
+    const int mnt = 512 / vec;
+    auto p2 = [mnt](long long n) {
+        if (n >= mnt) return mnt;
+        int p = 1;
+        while ((long long)p * 2 <= n) p *= 2;
+        return p;
+    };
+    int bw = std::min(p2(dim0), 32);
+    const int bh = std::min(p2(E), mnt / bw);
+    bw = std::min(p2(dim0), mnt / bh);
+    rows = 1;
+    ctas = 1;
+    if (!(E >= std::min(bh * 16, 256))) return;  // each thread sums whole outputs
+    rows = bh;
+    const long long vpt = (E + bh - 1) / bh;
+    const long long grid = (dim0 + bw - 1) / bw;
+    const long long target = (long long)num_sms * (max_threads_per_sm / (bw * bh));
+    if (vpt >= 256 && grid <= target) {
+        const long long c1 = (target + grid - 1) / grid, c2 = (vpt + 15) / 16, c3 = (vpt + 255) / 256;
+        const long long c = std::max(std::min(c1, c2), c3);
+        if (c > 1) ctas = (int)c;
+    }
+}
+
+struct EraPlanWriter {
+    int32_t *sched;
+    uint8_t *ops;
+    long long cap, n = 0, ns = 0;
+    int sp = 0, depth = 0;
+    void op(uint8_t o) {
+        if (ops && n < cap) ops[n] = o;
+        ++n;
+        if (o == ERA_PUSH0) depth = std::max(depth, ++sp);
+        if (o == ERA_ADD2) --sp;
+    }
+    void era(int e) {
+        if (sched) sched[ns] = e;
+        ++ns;
+        op(ERA_ADD);
+    }
+};
+
+// thread_reduce_impl of one thread: its t-th era (e = lane + L*t) goes to
+// accumulator t % 4; the result is ((a0 + a1) + a2) + a3.
+static void era_plan_lane(EraPlanWriter &w, int E, int lane, int L) {
+    for (int a = 0; a < 4; ++a) {
+        w.op(ERA_PUSH0);
+        for (long long e = lane + (long long)L * a; e < E; e += 4ll * L) w.era((int)e);
+        if (a) w.op(ERA_ADD2);
+    }
+}
+
+// block_y_reduce's halving tree (r[y] += r[y + off], off = count/2 .. 1)
+// over the values leaf(first + stride*i), i < count (a power of two): the
+// result is tree(even positions) + tree(odd positions) of that list, so
+// leaf y meets leaf y + count/2 first.
+template <class Leaf>
+static void era_plan_tree(EraPlanWriter &w, int first, int stride, int count, Leaf &&leaf) {
+    if (count == 1) {
+        leaf(first);
+        return;
+    }
+    era_plan_tree(w, first, stride * 2, count / 2, leaf);
+    era_plan_tree(w, first + stride, stride * 2, count / 2, leaf);
+    w.op(ERA_ADD2);
+}
+
+// The whole plan: per block c the tree over its rows' lanes y + rows*c;
+// with several blocks, row y of the last one adds the block results
+// c = y, y + rows, ... in order from 0 (global_reduce), then the tree again.
+static void era_plan(EraPlanWriter &w, int E, int rows, int ctas) {
+    const int L = rows * ctas;
+    auto block = [&](int c) {
+        era_plan_tree(w, 0, 1, rows, [&](int y) { era_plan_lane(w, E, y + rows * c, L); });
+    };
+    if (ctas == 1) {
+        block(0);
+        return;
+    }
+    era_plan_tree(w, 0, 1, rows, [&](int y) {
+        w.op(ERA_PUSH0);
+        for (int c = y; c < ctas; c += rows) {
+            block(c);
+            w.op(ERA_ADD2);
+        }
+    });
+}
+
+// Era split search (E > 1) with the eras spread over warps: block = one
+// node x FB features, eras in batches of EB taken in the plan's schedule
+// order, one warp per era.  Phase 1: a warp stages its era's FB feature
+// rows in shared memory with coalesced loads (G = float(sum q) * 2^-s,
+// H = float(count); odd row stride, conflict-free), then lane f scans
+// feature f's bins with the reference arithmetic and leaves the era's B-1
+// gains and directions in shared memory.  Phase 2: thread = (bin, feature)
+// cells run the plan's program over the batch -- the criterion is then
+// torch's CUDA mean bit for bit -- and add the directions to an integer
+// agreement (exact in any order).  Block arg-max -> cand[node][blk]
+// (ceil(k/FB) blocks).
 constexpr int SPLIT_ERA_EB = 8;   // eras per batch (= warps)
+
+template <int NB>
+struct EraSplitShape {
+    static constexpr int FB = NB <= 32 ? 32 : 8;      // features per block
+    static constexpr int IPT = (FB * NB + 255) / 256;  // cells per thread
+};
+
+static inline int split_era_fb(int B) { return B - 1 <= 32 ? 32 : 8; }
+
+static inline size_t split_eras_smem(int B, int NB, int FB, int depth) {
+    const int B1p = (B + 1) | 1;
+    const int ipt = (FB * NB + 255) / 256;
+    return (size_t)SPLIT_ERA_EB * 2 * FB * B1p * sizeof(float) +      // staged rows
+           (size_t)SPLIT_ERA_EB * NB * FB * sizeof(float) +           // gains
+           (size_t)depth * ipt * 256 * sizeof(float) +                // accumulator stacks
+           (size_t)SPLIT_ERA_EB * NB * FB;                            // directions
+}
 
 template <int NB>
 __global__ void __launch_bounds__(256) k_split_eras(
     const wgb_node *__restrict__ lvl, const int *nn_d, const long long *__restrict__ hg,
     const long long *__restrict__ hc, long long slot_elems, int k, int E, int B, const int *shift,
-    float mcw, float eps, float msg, float factor, int4 *cand, int nblk) {
-    constexpr int FB = SPLIT_ERA_FB, EB = SPLIT_ERA_EB;
-    constexpr int IPT = (FB * NB + 255) / 256;  // phase-2 items per thread
-    extern __shared__ float s_era_split[];      // [EB][2][FB][B1p] rows, [EB][NB][FB] gains, dirs
+    float mcw, float eps, float msg, float factor, const int *__restrict__ sched,
+    const uint8_t *__restrict__ ops, int nops, int depth, int4 *cand, int nblk, float *crit_out) {
+    constexpr int FB = EraSplitShape<NB>::FB, IPT = EraSplitShape<NB>::IPT, EB = SPLIT_ERA_EB;
+    extern __shared__ float s_era_split[];
     const int n = blockIdx.x / nblk, jb = blockIdx.x - n * nblk;  // node, feature block
     if (n >= *nn_d) return;
     const int j0 = jb * FB;
@@ -740,17 +815,34 @@ __global__ void __launch_bounds__(256) k_split_eras(
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     float *stg = s_era_split + warp * 2 * FB * B1p;
     float *sg = s_era_split + EB * 2 * FB * B1p;
-    signed char *sd = reinterpret_cast<signed char *>(sg + EB * NB * FB);
-    float cs[IPT];
+    float *stk = sg + EB * NB * FB;
+    signed char *sd = reinterpret_cast<signed char *>(stk + depth * IPT * 256);
+    float acc[IPT];
     int ds[IPT];
 #pragma unroll
     for (int t = 0; t < IPT; ++t) {
-        cs[t] = 0.0f;
+        acc[t] = 0.0f;
         ds[t] = 0;
     }
+    int pc = 0, sp = 0;  // program counter and stack depth (uniform over the block)
+    auto step = [&](uint8_t op) {
+        if (op == ERA_PUSH0) {
+#pragma unroll
+            for (int t = 0; t < IPT; ++t) {
+                stk[(sp * IPT + t) * 256 + threadIdx.x] = acc[t];
+                acc[t] = 0.0f;
+            }
+            ++sp;
+        } else {  // ERA_ADD2
+            --sp;
+#pragma unroll
+            for (int t = 0; t < IPT; ++t) acc[t] = __fadd_rn(stk[(sp * IPT + t) * 256 + threadIdx.x], acc[t]);
+        }
+    };
     for (int e0 = 0; e0 < E; e0 += EB) {
-        const int e = e0 + warp;
-        if (e < E) {
+        const int ne = min(EB, E - e0);
+        if (warp < ne) {
+            const int e = sched[e0 + warp];
             const long long base = slot * slot_elems + ((long long)e * k + j0) * B1;
             for (int t = lane; t < nf * B1; t += 32) {
                 const int f = t / B1, b = t - f * B1;
@@ -776,27 +868,27 @@ __global__ void __launch_bounds__(256) k_split_eras(
             }
         }
         __syncthreads();
-        const int ne = min(EB, E - e0);
+        for (int w = 0; w < ne; ++w) {
+            uint8_t op;
+            while (pc < nops && (op = __ldg(ops + pc++)) != ERA_ADD) step(op);
 #pragma unroll
-        for (int t = 0; t < IPT; ++t) {
-            const int it = threadIdx.x + 256 * t;
-            const int b = it / FB, f = it - b * FB;
-            if (b < nb && f < nf) {
-                for (int w = 0; w < ne; ++w) {
-                    cs[t] = __fadd_rn(cs[t], sg[(w * NB + b) * FB + f]);
-                    ds[t] += sd[(w * NB + b) * FB + f];
-                }
+            for (int t = 0; t < IPT; ++t) {
+                const int it = threadIdx.x + 256 * t;  // it / FB < NB by construction
+                acc[t] = __fadd_rn(acc[t], sg[(w * NB) * FB + it]);
+                ds[t] += sd[(w * NB) * FB + it];
             }
         }
         __syncthreads();  // the batch's gains are consumed before the next batch writes them
     }
+    while (pc < nops) step(__ldg(ops + pc++));
     Key best = key_none();
 #pragma unroll
     for (int t = 0; t < IPT; ++t) {
         const int it = threadIdx.x + 256 * t;
         const int b = it / FB, f = it - b * FB;
         if (b < nb && f < nf) {
-            const float cr = __fmul_rn(cs[t], factor);
+            const float cr = __fmul_rn(acc[t], factor);
+            if (crit_out && n == 0) crit_out[(j0 + f) * nb + b] = cr;
             const Key kk{abs(ds[t]), cr > msg ? cr : -INFINITY, (j0 + f) * nb + b};
             if (key_better(kk, best)) best = kk;
         }
@@ -810,12 +902,6 @@ __global__ void __launch_bounds__(256) k_split_eras(
             if (key_better(s_k[w], best)) best = s_k[w];
         cand[(long long)n * nblk + jb] = make_int4(best.A, __float_as_int(best.c), best.idx, 0);
     }
-}
-
-static inline size_t split_eras_smem(int B, int NB) {
-    const int B1p = (B + 1) | 1;
-    return (size_t)SPLIT_ERA_EB * 2 * SPLIT_ERA_FB * B1p * sizeof(float) +
-           (size_t)SPLIT_ERA_EB * NB * SPLIT_ERA_FB * (sizeof(float) + 1);
 }
 
 // Per node: final arg-max, per-era gain of the chosen split (importance,
@@ -1271,6 +1357,37 @@ void wgb_built_slots(int32_t d, int32_t *first, int32_t *count) {
     }
 }
 
+int64_t wgb_era_mean_plan(int32_t E, int64_t M, int32_t num_sms, int32_t max_threads_per_sm,
+                          int32_t *sched, uint8_t *ops, int64_t ops_cap, int32_t *depth) {
+    if (E < 1 || M < 1) {
+        set_error("E and M must be >= 1");
+        return -WGB_ERR_ARG;
+    }
+    if (num_sms <= 0 || max_threads_per_sm <= 0) {
+        int dev = 0;
+        if (cudaGetDevice(&dev) != cudaSuccess ||
+            cudaDeviceGetAttribute(&num_sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess ||
+            cudaDeviceGetAttribute(&max_threads_per_sm, cudaDevAttrMaxThreadsPerMultiProcessor, dev) != cudaSuccess) {
+            set_error("no device to take the SM count from; pass num_sms and max_threads_per_sm");
+            return -WGB_ERR_CUDA;
+        }
+    }
+    EraPlanWriter w{sched, ops, ops ? ops_cap : 0};
+    if (M == 1) {
+        // a single output is reduced along another path of torch (contiguous
+        // eras, vectorised loads, warp shuffles) that is not restated here:
+        // sequential sum (only the test crit > min_split_gain reads it)
+        w.op(ERA_PUSH0);
+        for (int e = 0; e < E; ++e) w.era(e);
+    } else {
+        int rows, ctas;
+        era_mean_layout(E, M, num_sms, max_threads_per_sm, rows, ctas);
+        era_plan(w, E, rows, ctas);
+    }
+    if (depth) *depth = w.depth;
+    return w.n;
+}
+
 static int check_ws(const wgb_ws *ws) {
     WGB_CHECK_ARG(ws != nullptr, "workspace is NULL");
     WGB_CHECK_ARG(ws->B >= 2 && ws->B <= 127, "num_bins must be in [2, 127], got %d", ws->B);
@@ -1383,58 +1500,52 @@ int wgb_level_split(const wgb_ws *ws, int32_t d, void *stream) {
         k_subtract<<<(unsigned)(bx * (cap / 2)), 256, 0, st>>>(lvl, ws->nn + d, hg, hc, se, nc, (int)bx);
         WGB_LAUNCHED("k_subtract");
     }
-    const int nblk = (ws->k + SPLIT_THREADS - 1) / SPLIT_THREADS;
-    WGB_CHECK_ARG(nblk <= ws->ncand_blk, "candidate buffer too small");
-    const unsigned g = (unsigned)nblk * (unsigned)cap;  // node-major blocks
     const int nb = ws->B - 1;
     int4 *cand = reinterpret_cast<int4 *>(ws->cand);
-#define WGB_SPLIT_ARGS                                                                       \
-    lvl, ws->nn + d, hg, hc, se, ws->k, ws->E, ws->B, ws->shift, ws->mcw, ws->eps, \
-        ws->msg, ws->mean_factor, cand, nblk
-    // per-thread row reads while a level has few nodes; coalesced staging
-    // through shared memory once it has many (their histograms outgrow L2)
-    const bool staged = cap >= 64;
-    const int split_smem = staged ? 2 * SPLIT_THREADS * ((ws->B + 1) | 1) * (int)sizeof(float) : 0;
-#define WGB_SPLIT_LAUNCH(NB_, MULTI_)                                                                        \
-    if (staged) {                                                                                            \
-        WGB_CUDA(cudaFuncSetAttribute(k_split_staged<NB_, MULTI_>, cudaFuncAttributeMaxDynamicSharedMemorySize, \
-                                      split_smem));                                                          \
-        k_split_staged<NB_, MULTI_><<<g, SPLIT_THREADS, split_smem, st>>>(WGB_SPLIT_ARGS);                  \
-    } else {                                                                                                 \
-        k_split<NB_, MULTI_><<<g, SPLIT_THREADS, 0, st>>>(WGB_SPLIT_ARGS);                                  \
-    }
-    // eras: the era-parallel search when the candidate buffer holds
-    // ceil(k/32) blocks per node (otherwise the per-thread scans above)
-    const int nblk_e = (ws->k + SPLIT_ERA_FB - 1) / SPLIT_ERA_FB;
-    const bool era_split = ws->E > 1 && nb <= 32 && nblk_e <= ws->ncand_blk;
-    int nblk_used = nblk;
-    if (era_split) {
-        nblk_used = nblk_e;
-        const unsigned ge = (unsigned)nblk_e * (unsigned)cap;
-#define WGB_SPLIT_ERAS(NB_)                                                                                   \
-    {                                                                                                         \
-        const size_t sm = split_eras_smem(ws->B, NB_);                                                        \
-        WGB_CUDA(cudaFuncSetAttribute(k_split_eras<NB_>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm)); \
-        k_split_eras<NB_><<<ge, 256, sm, st>>>(lvl, ws->nn + d, hg, hc, se, ws->k, ws->E, ws->B, ws->shift,   \
-                                               ws->mcw, ws->eps, ws->msg, ws->mean_factor, cand, nblk_e);     \
-    }
-        if (nb <= 8) WGB_SPLIT_ERAS(8) else WGB_SPLIT_ERAS(32)
-#undef WGB_SPLIT_ERAS
-    } else if (ws->E == 1) {
-        WGB_SPLIT_LAUNCH(1, false)
-    } else if (nb <= 8) {
-        WGB_SPLIT_LAUNCH(8, true)
-    } else if (nb <= 32) {
-        WGB_SPLIT_LAUNCH(32, true)
+    int nblk;
+    if (ws->E == 1) {
+        nblk = (ws->k + SPLIT_THREADS - 1) / SPLIT_THREADS;
+        WGB_CHECK_ARG(nblk <= ws->ncand_blk, "candidate buffer too small: %d blocks per node needed", nblk);
+        const unsigned g = (unsigned)nblk * (unsigned)cap;  // node-major blocks
+        // per-thread row reads while a level has few nodes; coalesced staging
+        // through shared memory once it has many (their histograms outgrow L2)
+        if (cap >= 64) {
+            const int sm = 2 * SPLIT_THREADS * ((ws->B + 1) | 1) * (int)sizeof(float);
+            WGB_CUDA(cudaFuncSetAttribute(k_split_staged, cudaFuncAttributeMaxDynamicSharedMemorySize, sm));
+            k_split_staged<<<g, SPLIT_THREADS, sm, st>>>(lvl, ws->nn + d, hg, hc, se, ws->k, ws->B, ws->shift,
+                                                         ws->mcw, ws->eps, ws->msg, cand, nblk, ws->crit_out);
+        } else {
+            k_split<<<g, SPLIT_THREADS, 0, st>>>(lvl, ws->nn + d, hg, hc, se, ws->k, ws->B, ws->shift, ws->mcw,
+                                                 ws->eps, ws->msg, cand, nblk, ws->crit_out);
+        }
+        WGB_LAUNCHED("k_split");
     } else {
-        WGB_SPLIT_LAUNCH(128, true)
+        WGB_CHECK_ARG(ws->era_sched && ws->era_ops && ws->era_nops >= ws->E && ws->era_depth >= 1,
+                      "levels with eras need the criterion plan of wgb_era_mean_plan in the workspace");
+        const int fb = split_era_fb(ws->B);
+        nblk = (ws->k + fb - 1) / fb;
+        WGB_CHECK_ARG(nblk <= ws->ncand_blk, "candidate buffer too small: %d blocks per node needed", nblk);
+        const unsigned g = (unsigned)nblk * (unsigned)cap;
+        int dev = 0, smem_max = 0;
+        WGB_CUDA(cudaGetDevice(&dev));
+        WGB_CUDA(cudaDeviceGetAttribute(&smem_max, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev));
+#define WGB_SPLIT_ERAS(NB_)                                                                                    \
+    {                                                                                                          \
+        const size_t sm = split_eras_smem(ws->B, NB_, EraSplitShape<NB_>::FB, ws->era_depth);                  \
+        WGB_CHECK_ARG(sm <= (size_t)smem_max, "era criterion plan too deep (%d) for shared memory", ws->era_depth); \
+        WGB_CUDA(cudaFuncSetAttribute(k_split_eras<NB_>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm)); \
+        k_split_eras<NB_><<<g, 256, sm, st>>>(lvl, ws->nn + d, hg, hc, se, ws->k, ws->E, ws->B, ws->shift,       \
+                                              ws->mcw, ws->eps, ws->msg, ws->mean_factor, ws->era_sched,        \
+                                              ws->era_ops, ws->era_nops, ws->era_depth, cand, nblk,             \
+                                              ws->crit_out);                                                    \
     }
-#undef WGB_SPLIT_LAUNCH
-#undef WGB_SPLIT_ARGS
-    WGB_LAUNCHED("k_split");
+        if (nb <= 8) WGB_SPLIT_ERAS(8) else if (nb <= 32) WGB_SPLIT_ERAS(32) else WGB_SPLIT_ERAS(128)
+#undef WGB_SPLIT_ERAS
+        WGB_LAUNCHED("k_split_eras");
+    }
     float *eg = ws->era_gain + (long long)((1 << d) - 1) * ws->E;
     k_split_final<<<cap, 256, 0, st>>>(lvl, ws->nn + d, hg, hc, se, ws->k, ws->E, ws->B,
-                                       ws->shift, ws->mcw, ws->eps, cand, nblk_used, eg);
+                                       ws->shift, ws->mcw, ws->eps, cand, nblk, eg);
     WGB_LAUNCHED("k_split_final");
     k_plan_next<<<1, 1024, 0, st>>>(lvl, level_nodes(ws, d + 1), ws->nn, d, ws->shift);
     WGB_LAUNCHED("k_plan_next");
