@@ -9,8 +9,8 @@ the built module travels to the GPU box with the tree).  The reference's own
 build system is not used: torch.utils.cpp_extension compiles the same five
 files directly.
 
-    python -m oracle.build_ref            # build (needs the reference checkout)
-    from oracle.build_ref import load     # import the built module (no sources needed)
+    python -m oracle.build_ref /path/to/reference   # build (or set WGB_REFERENCE)
+    from oracle.build_ref import load                # import the built module (no sources needed)
 """
 from __future__ import annotations
 
@@ -22,7 +22,6 @@ import os
 HERE = os.path.dirname(os.path.abspath(__file__))
 OUT = os.path.join(HERE, "_ref")
 NAME = "wgb_ref_node_kernel"
-REF_SRC = os.path.join(os.sep, "root", "reference", "warpgbm", "cuda")
 SOURCES = ["histogram_kernel.cu", "best_split_kernel.cu", "binner.cu", "predict.cu", "node_kernel.cpp"]
 
 
@@ -31,12 +30,15 @@ def built_path():
     return hits[0] if hits else None
 
 
-def build(force: bool = False):
-    """Compile the reference extension into oracle/_ref/; returns the .so path,
-    or None when the reference checkout is absent (the GPU box)."""
-    if not os.path.isdir(REF_SRC):
+def build(ref_root=None, force: bool = False):
+    """Compile the reference extension of the checkout at ref_root (or
+    $WGB_REFERENCE) into oracle/_ref/; returns the .so path.  Without a
+    checkout (the GPU box) the prebuilt module is returned, or None."""
+    ref_root = ref_root or os.environ.get("WGB_REFERENCE")
+    src_dir = os.path.join(ref_root, "warpgbm", "cuda") if ref_root else None
+    if not src_dir or not os.path.isdir(src_dir):
         return built_path()
-    srcs = [os.path.join(REF_SRC, s) for s in SOURCES]
+    srcs = [os.path.join(src_dir, s) for s in SOURCES]
     so = built_path()
     if so and not force and all(os.path.getmtime(so) >= os.path.getmtime(s) for s in srcs):
         return so
@@ -64,4 +66,5 @@ def load():
 
 
 if __name__ == "__main__":
-    print(build(force=True))
+    import sys
+    print(build(sys.argv[1] if len(sys.argv) > 1 else None, force=True))

@@ -288,5 +288,7 @@ def main(ref_root):
 
 
 if __name__ == "__main__":
-    main(sys.argv[1] if len(sys.argv) > 1
-         else os.environ.get("WGB_REFERENCE", os.path.join(os.sep, "root", "reference")))
+    root = sys.argv[1] if len(sys.argv) > 1 else os.environ.get("WGB_REFERENCE")
+    if not root:
+        sys.exit("usage: make_golden.py /path/to/reference  (or set WGB_REFERENCE)")
+    main(root)

@@ -142,8 +142,8 @@ def test_many_era_des_bit_exact(cuda, E, n, F):
 
 @pytest.mark.parametrize("B", [33, 64])
 def test_era_des_many_bins_bit_exact(cuda, B):
-    """Eras with 32 split points (the era-parallel split search's largest)
-    and with 63 (the per-thread era scan), float input binned on the GPU."""
+    """Eras with 32 split points (32 features per era split block) and with
+    63 (8 features per block), float input binned on the GPU."""
     rng = np.random.default_rng(B)
     n, F, E = 24_000, 30, 12
     X = rng.standard_normal((n, F)).astype(np.float32)
@@ -241,3 +241,26 @@ def test_fit_from_device_tensors_equals_numpy(cuda):
     b = WarpGBM(n_estimators=4, max_depth=4, num_bins=32).fit(torch.from_numpy(X).to(cuda),
                                                                torch.from_numpy(y).to(cuda))
     assert _same(_flat(a, 4), _flat(b, 4))
+
+
+def test_inference_uses_the_trained_features_only(cuda):
+    """core.py:902-915 bins columns 0..num_features-1: extra columns are
+    ignored (float and integer input), missing ones raise IndexError."""
+    rng = np.random.default_rng(12)
+    X = rng.standard_normal((4000, 10)).astype(np.float32)
+    y = (X[:, 0] - X[:, 3] + 0.1 * rng.standard_normal(4000)).astype(np.float32)
+    m = WarpGBM(n_estimators=5, max_depth=3, num_bins=16).fit(X, y)
+    want = m.predict(X)
+    wide = np.concatenate([X, rng.standard_normal((4000, 7)).astype(np.float32) * 100], axis=1)
+    assert np.array_equal(m.predict(wide), want)
+    assert np.array_equal(m.predict(torch.from_numpy(wide).to(cuda)), want)
+    with pytest.raises(IndexError):
+        m.predict(X[:, :9])
+    # integer input whose column count differs from the model's is binned
+    # with the edges, like the reference (no pre-binned shortcut)
+    Xi = rng.integers(0, 16, (4000, 10)).astype(np.int8)
+    mi = WarpGBM(n_estimators=3, max_depth=3, num_bins=16).fit(Xi, y)
+    wide_i = np.concatenate([Xi, np.zeros((4000, 2), np.int8)], axis=1)
+    assert np.array_equal(mi.predict(wide_i), mi.predict(Xi.astype(np.float32)))
+    with pytest.raises(IndexError):
+        mi.predict(Xi[:, :4])

@@ -599,12 +599,22 @@ class WarpGBM(BaseEstimator, RegressorMixin):
         dev = self._dev
         B = self.num_bins
         n, F = X_np.shape
-        S = bins_stride(F)
         if torch.is_tensor(X_np):
             is_int = not X_np.is_floating_point()
         else:
             is_int = np.issubdtype(X_np.dtype, np.integer)
-        if is_int and (fit or F == self.num_features):
+        prebinned_ok = fit or F == self.num_features
+        if not fit and F != self.num_features:
+            # core.py:902-915 bins columns 0..num_features-1 of the input with
+            # the stored edges: extra columns are ignored, missing ones raise
+            # numpy's IndexError
+            nf = self.num_features
+            if F < nf:
+                raise IndexError(f"index {F} is out of bounds for axis 1 with size {F}")
+            X_np = X_np[:, :nf]
+            F = nf
+        S = bins_stride(F)
+        if is_int and prebinned_ok:
             Xi = _to_dev(X_np, dev)
             if Xi.dtype == torch.int8:
                 # one pass: padded copy, column maxima, global min / max
@@ -667,6 +677,8 @@ class WarpGBM(BaseEstimator, RegressorMixin):
             self._bins_regular = True  # binner output is always in [0, B)
             q = torch.linspace(0, 1, B + 1, device=dev, dtype=torch.float32)[1:-1]
             self.bin_edges = sharded_quantile_edges(Xd, q, self._comm)
+        if self.bin_edges.shape[0] < F:
+            raise ValueError(f"{F} columns to bin with edges of {self.bin_edges.shape[0]} features")
         bins = torch.empty((n, S), dtype=torch.int8, device=dev)
         _lib.call("wgb_bin_matrix", Xd.data_ptr(), n, F, F, self.bin_edges.data_ptr(), B,
                   bins.data_ptr(), S, torch.cuda.current_stream().cuda_stream)

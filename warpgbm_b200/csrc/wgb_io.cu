@@ -122,11 +122,30 @@ extern "C" int wgb_h2d(void *dst, const void *src, int64_t bytes, void *stream) 
                 cudaFreeHost(g_stage.buf[i]);
                 g_stage.buf[i] = nullptr;
             }
+            g_stage.device = -1;
+        }
+        // everything is created into locals and kept only once all of it
+        // exists: a failure part way frees what was made and leaves the
+        // staging unset, so the next call starts clean
+        void *buf[Staging::NBUF] = {nullptr, nullptr, nullptr};
+        cudaEvent_t ev[Staging::NBUF] = {nullptr, nullptr, nullptr};
+        cudaError_t e = cudaSuccess;
+        for (int i = 0; i < Staging::NBUF && e == cudaSuccess; ++i) {
+            e = cudaHostAlloc(&buf[i], Staging::CHUNK, cudaHostAllocDefault);
+            if (e == cudaSuccess) e = cudaEventCreateWithFlags(&ev[i], cudaEventDisableTiming);
+            if (e == cudaSuccess) e = cudaEventRecord(ev[i], st);
+        }
+        if (e != cudaSuccess) {
+            for (int i = 0; i < Staging::NBUF; ++i) {
+                if (ev[i]) cudaEventDestroy(ev[i]);
+                if (buf[i]) cudaFreeHost(buf[i]);
+            }
+            set_error("pinned staging setup failed: %s", cudaGetErrorString(e));
+            return WGB_ERR_CUDA;
         }
         for (int i = 0; i < Staging::NBUF; ++i) {
-            WGB_CUDA(cudaHostAlloc(&g_stage.buf[i], Staging::CHUNK, cudaHostAllocDefault));
-            WGB_CUDA(cudaEventCreateWithFlags(&g_stage.ev[i], cudaEventDisableTiming));
-            WGB_CUDA(cudaEventRecord(g_stage.ev[i], st));
+            g_stage.buf[i] = buf[i];
+            g_stage.ev[i] = ev[i];
         }
         g_stage.device = dev;
     }
