@@ -314,6 +314,21 @@ int wgb_predict_packed(const int8_t *bins, int64_t n, int64_t S,
                        int32_t T, int32_t K, float lr, float *out,
                        void *stream);
 
+/* Forest prediction with trees of depth D <= 12 laid out as complete binary
+ * trees (the fast path of warpgbm/cuda/predict.cu:5-45's traversal).  Tree t
+ * is 2^(D+1) uint32 words at heap + t*2^(D+1) (heap 16-byte aligned): word i
+ * < 2^D - 1 is heap slot i (children 2i+1, 2i+2) = (feature & 0xFFFF) |
+ * (uint8 split bin << 16), a row going left iff its int8 bin <= the split
+ * bin; the value of the leaf reached at depth-D slot h is word h + 1.  A
+ * leaf at depth d < D is a chain of pass-through slots (feature 0, bin 127)
+ * to its leftmost depth-D descendant, which holds its value.
+ * out[i*K + t%K] += lr * leaf_t(i), trees in order t = 0..T-1 (fp32, the
+ * same sums as wgb_predict_packed).  Rows are staged in shared memory when
+ * at least 64 of them fit, else read from global memory (any width). */
+int wgb_predict_heap(const int8_t *bins, int64_t n, int64_t S,
+                     const uint32_t *heap, int32_t T, int32_t K, int32_t D,
+                     float lr, float *out, void *stream);
+
 #ifdef __cplusplus
 }
 #endif

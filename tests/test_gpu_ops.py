@@ -288,3 +288,48 @@ def test_oracle_era_mean_order_equals_torch_cuda_mean(cuda, E, k, nb):
     want = x.mean(dim=0).cpu().numpy()
     got = O.cuda_era_mean(x.cpu().numpy())
     assert np.array_equal(got.view(np.int32), want.view(np.int32))
+
+
+@pytest.mark.parametrize("F,D,objective", [(50, 4, "multiclass"), (7000, 3, "regression"),
+                                           (300, 10, "regression"), (40, 13, "regression")])
+def test_heap_and_packed_predictors_agree_with_oracle(cuda, F, D, objective):
+    """wgb_predict_heap (complete-tree layout, depth <= 12) and
+    wgb_predict_packed (pre-order, any depth), with rows staged in shared
+    memory and -- for rows too wide to stage (7000 features) -- read from
+    global memory, against the oracle's flattened-forest predict
+    (predict.cu:17-44 semantics, tree order)."""
+    from warpgbm_b200 import WarpGBM
+    from warpgbm_b200.core import heap_forest
+    rng = np.random.default_rng(F + D)
+    n = 3000
+    X = rng.standard_normal((n, F)).astype(np.float32)
+    if objective == "multiclass":
+        y = (X[:, 0] > 0).astype(int) + (X[:, F - 1] > 0.5).astype(int)
+    else:
+        y = (X[:, 0] - X[:, F - 1] + 0.1 * rng.standard_normal(n)).astype(np.float32)
+    m = WarpGBM(objective=objective, n_estimators=6, max_depth=D, num_bins=16, min_child_weight=2).fit(X, y)
+    bins = m.bin_inference_data(X)
+    nodes, offs_d, offs, heap = m._ensure_packed()
+    K = m.num_classes if objective == "multiclass" else 1
+    T = len(offs) - 1
+    st = torch.cuda.current_stream().cuda_stream
+    out_p = torch.zeros((n, K), dtype=torch.float32, device=cuda)
+    _lib.call("wgb_predict_packed", bins.data_ptr(), n, bins.shape[1], nodes.data_ptr(), offs_d.data_ptr(),
+              T, K, float(np.float32(0.1)), out_p.data_ptr(), st)
+    bins_h = bins[:, :F].cpu().numpy()
+    parts = [nodes.cpu().numpy().reshape(-1, 2)[offs[t]:offs[t + 1]] for t in range(T)]
+    flat = m._flat_trees()
+    for c in range(K):
+        want = np.zeros(n, np.float32)
+        O.predict_flat(bins_h, np.stack([O.flatten_tree(t, 2 ** (D + 1)) for t in flat[c::K]]),
+                       np.float32(0.1), want)
+        assert np.array_equal(out_p[:, c].cpu().numpy(), want)
+    if D <= 12:
+        H = heap_forest(parts, D)
+        Hd = torch.from_numpy(H.reshape(-1).view(np.int32)).to(cuda)
+        out_h = torch.zeros((n, K), dtype=torch.float32, device=cuda)
+        _lib.call("wgb_predict_heap", bins.data_ptr(), n, bins.shape[1], Hd.data_ptr(), T, K, D,
+                  float(np.float32(0.1)), out_h.data_ptr(), st)
+        assert torch.equal(out_h, out_p)
+    else:
+        assert heap is None

@@ -94,3 +94,51 @@ def test_forest_dicts_built_on_first_access_and_packing_without_them():
     assert np.array_equal(nodes_all, np.concatenate(packs))
     m.forest = [{} for _ in range(3)]                   # assignment drops the compact arrays
     assert m._compact == {} and m._tree_slots() == []
+
+
+def _predict_dict(tree, row):
+    while "leaf_value" not in tree:
+        tree = tree["left"] if row[tree["feature"]] <= tree["bin"] else tree["right"]
+    return np.float32(tree["leaf_value"])
+
+
+def _predict_heap(H, D, row):
+    node = 0
+    for _ in range(D):
+        w = int(H[node])
+        f, sb = w & 0xFFFF, np.int8(np.uint8((w >> 16) & 0xFF))
+        node = 2 * node + 1 + (1 if row[f] > sb else 0)
+    return np.uint32(H[node + 1]).view(np.float32)
+
+
+@pytest.mark.parametrize("D,p", [(1, 1.0), (3, 0.6), (6, 0.9), (10, 0.97), (12, 0.5), (5, 0.0)])
+def test_heap_layout_walks_like_the_dict_trees(D, p):
+    """heap_forest (the wgb_predict_heap layout: complete binary trees,
+    early leaves as pass-through chains) reaches the same leaf as the
+    nested-dict tree for every row, negative int8 bins included."""
+    from warpgbm_b200.core import heap_forest
+    rng = np.random.default_rng(D * 10 + int(p * 10))
+    F = 40
+    trees = []
+    for t in range(4):
+        nodes, gains = _records(rng, D, 1, F, p)
+        feats = rng.permutation(F).astype(np.int32)
+        packed, leaf, samples, *_ = compact_tree(nodes, gains, feats, D, 1)
+        trees.append((packed, tree_dict(packed, leaf, samples)))
+    H = heap_forest([pk for pk, _ in trees], D)
+    assert H.shape == (4, 2 << D)
+    rows = rng.integers(-5, 32, (300, F)).astype(np.int8)
+    for t, (_, tree) in enumerate(trees):
+        for row in rows:
+            assert _predict_heap(H[t], D, row) == _predict_dict(tree, row)
+
+
+def test_heap_layout_rejects_what_it_cannot_hold():
+    from warpgbm_b200.core import heap_forest
+    deep, _ = pack_trees([{"feature": 1, "bin": 0, "left": {"leaf_value": 1.0, "samples": 1},
+                           "right": {"feature": 2, "bin": 3, "left": {"leaf_value": 2.0, "samples": 1},
+                                     "right": {"leaf_value": 3.0, "samples": 1}}}])
+    assert heap_forest([deep], 1) is None                 # deeper than D
+    wide, _ = pack_trees([{"feature": 70000, "bin": 0, "left": {"leaf_value": 1.0, "samples": 1},
+                           "right": {"leaf_value": 2.0, "samples": 1}}])
+    assert heap_forest([wide], 3) is None                 # feature index beyond 16 bits

@@ -10,8 +10,9 @@ in libwgb_b200.so (include/warpgbm_b200.h):
 * trees: level-wise, without host synchronisation inside a tree --
   histogram of every node of a level in one launch, split search, on-device
   partition and leaf updates;
-* prediction: ``wgb_predict_packed``, all trees (and all classes) in one
-  launch, summed in tree order.
+* prediction: ``wgb_predict_heap`` (trees as complete binary trees in
+  shared memory, depth <= 12) or ``wgb_predict_packed``, all trees (and all
+  classes) in one launch, summed in tree order.
 
 Histograms are exact integer sums of residuals quantised per tree to a
 power-of-two grid (q = rint(g * 2^s), s = 29 - exponent(max|g|)), so every
@@ -354,6 +355,54 @@ def compact_tree(nodes, gains, feats, D, E):
         sp_pre = sp_feat = np.zeros(0, np.int64)
         sp_gain = np.zeros((0, E), np.float32)
     return packed, leaf, samples, sp_pre, sp_feat, sp_gain
+
+
+HEAP_DMAX = 12          # deepest forest the heap predictor takes (csrc/wgb_ops.cu)
+HEAP_PASS = 127 << 16   # pass-through slot: feature 0, split bin 127 (every row goes left)
+
+
+def heap_forest(parts, D):
+    """Pre-order packed trees (pack_trees / compact_tree format) -> the heap
+    layout of wgb_predict_heap: uint32 [T, 2^(D+1)], slot i's children
+    2i+1 / 2i+2, internal slot = feature | split bin << 16, the value of the
+    leaf reached at depth-D slot h in word h + 1, leaves above depth D as
+    pass-through chains to their leftmost depth-D descendant.  Built level
+    by level over all trees at once.  Returns None if a tree is deeper than
+    D or uses a feature index >= 2^16."""
+    T = len(parts)
+    W = 2 << D
+    H = np.zeros((T, W), np.uint32)
+    H[:, : (1 << D) - 1] = HEAP_PASS
+    if T == 0:
+        return H
+    sizes = np.array([len(p) for p in parts], np.int64)
+    offs = np.zeros(T + 1, np.int64)
+    offs[1:] = np.cumsum(sizes)
+    allp = np.concatenate(parts).astype(np.int64)
+    tid = np.arange(T, dtype=np.int64)
+    slot = np.zeros(T, np.int64)
+    pid = offs[:-1].copy()
+    for d in range(D + 1):
+        if tid.size == 0:
+            break
+        feat, w = allp[pid, 0], allp[pid, 1]
+        leaf = feat < 0
+        if leaf.any():
+            # value at the leftmost depth-D descendant of this slot (word h + 1)
+            h = (slot[leaf] + 1) * (1 << (D - d)) - 1
+            H[tid[leaf], h + 1] = (w[leaf] & 0xFFFFFFFF).astype(np.uint32)
+        inner = ~leaf
+        if not inner.any():
+            break
+        if d == D or int(feat[inner].max()) >= (1 << 16):
+            return None
+        ti, si, fi, wi = tid[inner], slot[inner], feat[inner], w[inner]
+        H[ti, si] = (fi | ((wi & 0xFF) << 16)).astype(np.uint32)
+        left, right = pid[inner] + 1, offs[ti] + (wi >> 8)
+        tid = np.concatenate([ti, ti])
+        slot = np.concatenate([2 * si + 1, 2 * si + 2])
+        pid = np.concatenate([left, right])
+    return H
 
 
 def tree_dict(packed, leaf, samples):
@@ -1141,21 +1190,28 @@ class WarpGBM(BaseEstimator, RegressorMixin):
                 offs[1:] = np.cumsum([len(p) for p in parts])
             nodes = np.concatenate(parts) if parts else np.zeros((0, 2), np.int32)
             dev = getattr(self, "_dev", torch.device("cuda", torch.cuda.current_device()))
+            heap = heap_forest(parts, self.max_depth) if self.max_depth <= HEAP_DMAX else None
             self._packed = (torch.from_numpy(nodes.reshape(-1)).to(dev),
-                            torch.from_numpy(offs).to(dev), offs)
+                            torch.from_numpy(offs).to(dev), offs,
+                            torch.from_numpy(heap.reshape(-1).view(np.int32)).to(dev) if heap is not None else None)
         return self._packed
 
     def _predict_into(self, bins, out, r0, r1):
         """out[:, class] += lr * leaf for the trees of rounds [r0, r1)."""
-        nodes, offs_d, offs = self._ensure_packed()
+        nodes, offs_d, offs, heap = self._ensure_packed()
         K = out.shape[1]
         t0, t1 = r0 * K, min(r1 * K, len(offs) - 1)
         if t1 <= t0:
             return
-        _lib.call("wgb_predict_packed", bins.data_ptr(), bins.shape[0], bins.shape[1],
-                  nodes.data_ptr(), offs_d[t0:].data_ptr(), t1 - t0, K,
-                  float(np.float32(self.learning_rate)), out.data_ptr(),
-                  torch.cuda.current_stream().cuda_stream)
+        lr = float(np.float32(self.learning_rate))
+        st = torch.cuda.current_stream().cuda_stream
+        if heap is not None:
+            W = 2 << self.max_depth
+            _lib.call("wgb_predict_heap", bins.data_ptr(), bins.shape[0], bins.shape[1],
+                      heap.data_ptr() + 4 * t0 * W, t1 - t0, K, self.max_depth, lr, out.data_ptr(), st)
+        else:
+            _lib.call("wgb_predict_packed", bins.data_ptr(), bins.shape[0], bins.shape[1],
+                      nodes.data_ptr(), offs_d[t0:].data_ptr(), t1 - t0, K, lr, out.data_ptr(), st)
 
     def _init_proba_logits(self, n):
         """core.py:1001-1007: the prior of class k is 1/K (sic), computed on the host."""

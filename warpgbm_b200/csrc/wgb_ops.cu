@@ -162,12 +162,15 @@ __global__ void k_bin_column(const float *__restrict__ X, long long n, const flo
 
 // Packed forest: node = int2; internal {feature >= 0, bin | right << 8}
 // (left child = node + 1, pre-order), leaf {-1, float bits of value}.
-// One thread per row; the CTA stages its rows' bins in shared memory
-// (row stride S + 4 bytes: the same feature of consecutive rows falls in
-// consecutive banks).  Trees are walked PG at a time (independent chains for
-// latency hiding) and their leaves added strictly in tree order.
+// One thread per row.  STAGED: the CTA stages its rows' bins in shared
+// memory (row stride S + 4 bytes: the same feature of consecutive rows falls
+// in consecutive banks); otherwise rows are read from global memory (rows
+// too wide to stage).  Trees are walked PRED_G at a time (independent chains
+// for latency hiding) and their leaves added strictly in tree order.  Any
+// depth; the heap predictor below is the fast path for depth <= 12.
 constexpr int PRED_ROWS = 128, PRED_G = 4;
 
+template <bool STAGED>
 __global__ void __launch_bounds__(PRED_ROWS) k_predict_packed(
     const int8_t *__restrict__ bins, long long n, long long S, const int2 *__restrict__ nodes,
     const int *__restrict__ tree_off, int T, int K, float lr, float *__restrict__ out) {
@@ -176,14 +179,16 @@ __global__ void __launch_bounds__(PRED_ROWS) k_predict_packed(
     const int RP = blockDim.x;        // rows per CTA (<= PRED_ROWS, fewer for wide rows)
     const long long r0 = (long long)blockIdx.x * RP;
     const int nrows = (int)min((long long)RP, n - r0);
-    for (int t = threadIdx.x; t < nrows * (SW - 1); t += RP) {
-        int rr = t / (SW - 1), w = t - rr * (SW - 1);
-        s_rows[rr * SW + w] = __ldg(reinterpret_cast<const uint32_t *>(bins + (r0 + rr) * S) + w);
+    if (STAGED) {
+        for (int t = threadIdx.x; t < nrows * (SW - 1); t += RP) {
+            int rr = t / (SW - 1), w = t - rr * (SW - 1);
+            s_rows[rr * SW + w] = __ldg(reinterpret_cast<const uint32_t *>(bins + (r0 + rr) * S) + w);
+        }
+        __syncthreads();
     }
-    __syncthreads();
     if (threadIdx.x >= nrows) return;
-    const uint8_t *myrow = reinterpret_cast<const uint8_t *>(s_rows + threadIdx.x * SW);
     const long long row = r0 + threadIdx.x;
+    const int8_t *myrow = STAGED ? reinterpret_cast<const int8_t *>(s_rows + threadIdx.x * SW) : bins + row * S;
     for (int c = 0; c < K; ++c) {
         float acc = out[row * K + c];
         for (int t0 = c; t0 < T; t0 += K * PRED_G) {
@@ -216,7 +221,7 @@ __global__ void __launch_bounds__(PRED_ROWS) k_predict_packed(
                         live[u] = false;
                         continue;
                     }
-                    int b = (int)(int8_t)myrow[nd.x];
+                    int b = (int)(STAGED ? myrow[nd.x] : __ldg(myrow + nd.x));
                     int nxt = (b <= (nd.y & 0xff)) ? node[u] + 1 : (nd.y >> 8);
                     // pre-order ids only grow; anything else is a malformed tree
                     if (nxt <= node[u] || nxt >= lim[u]) {
@@ -234,6 +239,110 @@ __global__ void __launch_bounds__(PRED_ROWS) k_predict_packed(
         }
         out[row * K + c] = acc;
     }
+}
+
+// Heap forest (depth D <= HEAP_DMAX): tree t is 2^(D+1) 32-bit words at
+// heap + t * 2^(D+1): words [0, 2^D - 1) are the internal slots of a
+// complete binary tree in heap order (children of slot i: 2i+1, 2i+2), each
+// (feature & 0xFFFF) | (uint8 split bin << 16); word 2^D - 1 is unused;
+// the leaf value of depth-D slot h (2^D - 1 <= h < 2^(D+1) - 1) is word
+// h + 1, so words [2^D, 2^(D+1)) hold the leaves.  A leaf at depth
+// d < D becomes a chain of pass-through slots {feature 0, bin 127} (every
+// int8 bin is <= 127, so rows go left) ending at its leftmost depth-D
+// descendant, which holds its value.  Every walk is then exactly D steps
+// with no data-dependent trip count.
+//
+// One thread per row.  A CTA stages its R rows' bins in shared memory
+// (STAGED; else rows are read from global memory) and streams the forest
+// through two shared-memory buffers of G trees each with cp.async: group
+// g + 1 is copied while every thread walks its row through the trees of
+// group g, four trees at a time, adding leaves strictly in tree order
+// (class of tree t = t % K).
+constexpr int HEAP_DMAX = 12;
+constexpr int HEAP_THREADS = 256, HEAP_CH = 4;
+
+__device__ __forceinline__ void cp_async16(void *smem, const void *gmem) {
+    const uint32_t sa = (uint32_t)__cvta_generic_to_shared(smem);
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(sa), "l"(gmem) : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+template <int N>
+__device__ __forceinline__ void cp_async_wait() { asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory"); }
+
+template <bool STAGED>
+__global__ void __launch_bounds__(HEAP_THREADS) k_predict_heap(
+    const int8_t *__restrict__ bins, long long n, long long S, const uint32_t *__restrict__ heap, int T, int K,
+    int D, int G, float lr, float *__restrict__ out) {
+    extern __shared__ __align__(16) uint32_t s_heap[];
+    const int TW = 2 << D;                 // words per tree
+    uint32_t *tb = s_heap;                 // [2][G * TW]
+    uint32_t *rows = s_heap + 2 * G * TW;  // [R][SW]
+    const int SW = (int)(S / 4) + 1;
+    const int R = blockDim.x;
+    const long long r0 = (long long)blockIdx.x * R;
+    const int nrows = (int)min((long long)R, n - r0);
+    auto prefetch = [&](int g) {
+        const int t0 = g * G, nt = min(G, T - t0);
+        const uint4 *src = reinterpret_cast<const uint4 *>(heap + (long long)t0 * TW);
+        uint4 *dst = reinterpret_cast<uint4 *>(tb + (g & 1) * G * TW);
+        for (int i = threadIdx.x; i < nt * TW / 4; i += R) cp_async16(dst + i, src + i);
+        cp_async_commit();
+    };
+    const int ngroups = (T + G - 1) / G;
+    prefetch(0);
+    if (STAGED) {
+        for (int t = threadIdx.x; t < nrows * (SW - 1); t += R) {
+            const int rr = t / (SW - 1), w = t - rr * (SW - 1);
+            rows[rr * SW + w] = __ldg(reinterpret_cast<const uint32_t *>(bins + (r0 + rr) * S) + w);
+        }
+    }
+    const bool live = threadIdx.x < nrows;
+    const long long row = r0 + threadIdx.x;
+    const int8_t *myrow = STAGED ? reinterpret_cast<const int8_t *>(rows + threadIdx.x * SW)
+                                 : bins + (live ? row : 0) * S;
+    float acc = (live && K == 1) ? out[row] : 0.0f;
+    for (int g = 0; g < ngroups; ++g) {
+        if (g + 1 < ngroups) {
+            prefetch(g + 1);
+            cp_async_wait<1>();
+        } else {
+            cp_async_wait<0>();
+        }
+        __syncthreads();  // group g (and, first time, the rows) visible to every thread
+        if (live) {
+            const uint32_t *grp = tb + (g & 1) * G * TW;
+            const int t0 = g * G, nt = min(G, T - t0);
+            for (int u0 = 0; u0 < nt; u0 += HEAP_CH) {
+                int node[HEAP_CH];
+#pragma unroll
+                for (int u = 0; u < HEAP_CH; ++u) node[u] = 0;
+                for (int d = 0; d < D; ++d) {
+#pragma unroll
+                    for (int u = 0; u < HEAP_CH; ++u) {
+                        const uint32_t w = grp[min(u0 + u, nt - 1) * TW + node[u]];
+                        const int f = (int)(w & 0xFFFFu);
+                        const int sb = (int)(int8_t)(w >> 16);
+                        const int b = (int)(f < S ? (STAGED ? myrow[f] : __ldg(myrow + f)) : 0);
+                        node[u] = 2 * node[u] + 1 + (b > sb ? 1 : 0);
+                    }
+                }
+#pragma unroll
+                for (int u = 0; u < HEAP_CH; ++u) {
+                    if (u0 + u >= nt) break;
+                    const float v = __uint_as_float(grp[(u0 + u) * TW + node[u] + 1]);
+                    const int t = t0 + u0 + u;
+                    if (K == 1) {
+                        acc = __fadd_rn(acc, __fmul_rn(lr, v));
+                    } else {
+                        float *o = out + row * K + (t % K);
+                        *o = __fadd_rn(*o, __fmul_rn(lr, v));
+                    }
+                }
+            }
+        }
+        __syncthreads();  // group g's buffer is read before group g + 2 overwrites it
+    }
+    if (live && K == 1) out[row] = acc;
 }
 
 // The reference's flattened format (core.py:1215-1252): [T][max_nodes][6].
@@ -407,21 +516,58 @@ int wgb_custom_cuda_binner(const float *X, int64_t n, const float *bin_edges, in
     return WGB_OK;
 }
 
+// rows per CTA of the staged predictors: the largest multiple of 32 (at
+// most `cap`) whose rows fit `budget` bytes; 0 = rows too wide to stage
+static int staged_rows(long long S, int cap, size_t budget) {
+    int r = cap;
+    while (r >= 64 && (size_t)r * (size_t)(S + 4) > budget) r -= 32;
+    return (size_t)r * (size_t)(S + 4) <= budget && r >= 64 ? r : 0;
+}
+
 int wgb_predict_packed(const int8_t *bins, int64_t n, int64_t S, const int32_t *nodes,
                        const int32_t *tree_off, int32_t T, int32_t K, float lr, float *out,
                        void *stream) {
     WGB_CHECK_ARG(n >= 0 && S >= 4 && S % 4 == 0, "bad bins shape (stride must be a multiple of 4)");
     WGB_CHECK_ARG(T >= 0 && K >= 1, "bad forest shape");
     if (n == 0 || T == 0) return WGB_OK;
-    // rows per CTA: up to PRED_ROWS, fewer (multiple of 32) when rows are wide
-    int rp = PRED_ROWS;
-    while (rp > 32 && (size_t)rp * (S + 4) > 200 * 1024) rp -= 32;
-    size_t smem = (size_t)rp * (S + 4);
-    WGB_CHECK_ARG(smem <= 200 * 1024, "rows too wide for the staged predictor (S=%lld)", (long long)S);
-    WGB_CUDA(cudaFuncSetAttribute(k_predict_packed, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
-    k_predict_packed<<<(unsigned)((n + rp - 1) / rp), rp, smem, as_stream(stream)>>>(
-        bins, n, S, reinterpret_cast<const int2 *>(nodes), tree_off, T, K, lr, out);
+    const int rp = staged_rows(S, PRED_ROWS, 160 * 1024);
+    if (rp) {
+        const size_t smem = (size_t)rp * (S + 4);
+        WGB_CUDA(cudaFuncSetAttribute(k_predict_packed<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+        k_predict_packed<true><<<(unsigned)((n + rp - 1) / rp), rp, smem, as_stream(stream)>>>(
+            bins, n, S, reinterpret_cast<const int2 *>(nodes), tree_off, T, K, lr, out);
+    } else {
+        k_predict_packed<false><<<(unsigned)((n + PRED_ROWS - 1) / PRED_ROWS), PRED_ROWS, 0, as_stream(stream)>>>(
+            bins, n, S, reinterpret_cast<const int2 *>(nodes), tree_off, T, K, lr, out);
+    }
     WGB_LAUNCHED("k_predict_packed");
+    return WGB_OK;
+}
+
+int wgb_predict_heap(const int8_t *bins, int64_t n, int64_t S, const uint32_t *heap, int32_t T, int32_t K,
+                     int32_t D, float lr, float *out, void *stream) {
+    WGB_CHECK_ARG(n >= 0 && S >= 4 && S % 4 == 0, "bad bins shape (stride must be a multiple of 4)");
+    WGB_CHECK_ARG(T >= 0 && K >= 1, "bad forest shape");
+    WGB_CHECK_ARG(D >= 1 && D <= HEAP_DMAX, "heap forests hold depth 1..%d, got %d", HEAP_DMAX, D);
+    WGB_CHECK_ARG((reinterpret_cast<uintptr_t>(heap) & 15) == 0, "heap must be 16-byte aligned");
+    if (n == 0 || T == 0) return WGB_OK;
+    const size_t tree_bytes = (size_t)8 << D;  // 2^(D+1) words
+    // trees per buffer: up to 16, within 64 KB for both buffers together
+    int G = (int)std::min<size_t>(16, std::max<size_t>(1, (64 * 1024) / (2 * tree_bytes)));
+    if (G > T) G = T;
+    const size_t tsm = 2 * (size_t)G * tree_bytes;
+    const int R = staged_rows(S, HEAP_THREADS, 220 * 1024 - tsm);
+    cudaStream_t st = as_stream(stream);
+    if (R) {
+        const size_t smem = tsm + (size_t)R * (S + 4);
+        WGB_CUDA(cudaFuncSetAttribute(k_predict_heap<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+        k_predict_heap<true><<<(unsigned)((n + R - 1) / R), R, smem, st>>>(bins, n, S, heap, T, K, D, G, lr, out);
+    } else {
+        WGB_CUDA(cudaFuncSetAttribute(k_predict_heap<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)tsm));
+        k_predict_heap<false><<<(unsigned)((n + HEAP_THREADS - 1) / HEAP_THREADS), HEAP_THREADS, tsm, st>>>(
+            bins, n, S, heap, T, K, D, G, lr, out);
+    }
+    WGB_LAUNCHED("k_predict_heap");
     return WGB_OK;
 }
 
