@@ -52,6 +52,8 @@ def parse():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference", "reference-cuda"])
     ap.add_argument("--rows", type=int, default=CONFIG["n"])
     ap.add_argument("--trees", type=int, default=CONFIG["n_estimators"])
+    ap.add_argument("--features", type=int, default=None,
+                    help="config 4 only: fewer features (a reduced case for profiling)")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu", action="store_true", help="skip the cpu_baseline sample")
     ap.add_argument("--clock-ms", type=int, default=200,
@@ -72,17 +74,21 @@ def peaks():
         return 6650.0, "fallback"
 
 
-def make_data(rank: int, n: int, F: int, device):
-    """Config 2 synthetic regression, seeded per rank (rank r = shard r)."""
-    g = torch.Generator(device=device)
-    g.manual_seed(1234 + rank)
-    X = torch.randn((n, F), generator=g, device=device, dtype=torch.float32)
-    gw = torch.Generator(device=device)
-    gw.manual_seed(99)  # the same weights on every rank
-    w = torch.randn(20, generator=gw, device=device)
-    noise = torch.randn(n, generator=g, device=device) * 0.5
-    y = X[:, :20] @ w + 0.3 * torch.sin(X[:, 20:30]).sum(1) + noise
-    return X, y.contiguous()
+DATA_DESC = ("synthetic (config 2 generator: numpy default_rng, SeedSequence(0) child rank+1 for the "
+             "rank's rows, child 0 for the weights; the same arrays in both arms)")
+
+
+def make_data(rank: int, n: int, F: int):
+    """Config 2 synthetic regression on the host (numpy, seeded): rank r
+    draws shard r; the 20 weights are shared by every rank.  Both arms of
+    the bench use these arrays."""
+    kids = np.random.SeedSequence(0).spawn(rank + 2)
+    w = np.random.default_rng(kids[0]).standard_normal(20)
+    rng = np.random.default_rng(kids[rank + 1])
+    X = rng.standard_normal((n, F), dtype=np.float32)
+    noise = rng.normal(0.0, 0.5, n)
+    y = (X[:, :20].astype(np.float64) @ w + 0.3 * np.sin(X[:, 20:30].astype(np.float64)).sum(1) + noise)
+    return X, y.astype(np.float32)
 
 
 class Clocks:
@@ -172,69 +178,108 @@ def hist_algorithmic_bytes(model, n_total: int, k: int, E: int, B: int, world: i
     return total
 
 
-def cpu_sample(Xh: np.ndarray, yh: np.ndarray, bins_h: np.ndarray, edges_h: np.ndarray, trees: int):
-    """Reference algorithm on the host cores (all threads): quantile edges of
-    every column and the binning pass, then one full tree on the full 1M x 1K
-    matrix (fp32 histograms, reference mode), scaled to sec/100 trees."""
+CPU_SAMPLE_COLS = 100   # columns binned per CPU sample (scaled to all F)
+
+
+def cpu_sample(Xh: np.ndarray, yh: np.ndarray, bins_h: np.ndarray):
+    """One bounded sample of the reference algorithm on the host cores (the
+    CPU oracle port, reference mode, all threads): exact quantile edges and
+    binning of CPU_SAMPLE_COLS columns, scaled to all F columns, plus one
+    full tree on the full matrix (fp32 histograms), extrapolated to a
+    100-tree fit.  Returns (record, measured seconds of the sample)."""
     import oracle as O
     threads = O.lib().orc_num_threads()
-    F = Xh.shape[1]
+    n, F = Xh.shape
+    cols = min(CPU_SAMPLE_COLS, F)
+    Xs = np.ascontiguousarray(Xh[:, :cols])
     q = O.linspace_q(CONFIG["num_bins"])
-    t0 = time.perf_counter()
-    O.quantile_edges_matrix(Xh, q)
-    O.bin_matrix(Xh, edges_h)
-    bin_time = time.perf_counter() - t0
+    w0 = time.perf_counter()
+    edges = O.quantile_edges_matrix(Xs, q)
+    O.bin_matrix(Xs, edges)
+    bin_time = (time.perf_counter() - w0) * F / cols
     m = O.OracleGBM(mode="reference", num_bins=CONFIG["num_bins"], max_depth=CONFIG["max_depth"],
                     learning_rate=CONFIG["learning_rate"], n_estimators=1)
     m.num_samples, m.num_features = bins_h.shape
-    m.bins, m.era, m.E = bins_h, np.zeros(bins_h.shape[0], np.int32), 1
+    m.bins, m.era, m.E = bins_h, np.zeros(n, np.int32), 1
     m.imp = np.zeros((1, F), np.float32)
     m.base_prediction = float(np.float32(yh.mean()))
-    m.pred = np.zeros((bins_h.shape[0], 1), np.float32) + np.float32(m.base_prediction)
+    m.pred = np.zeros((n, 1), np.float32) + np.float32(m.base_prediction)
     t0 = time.perf_counter()
     m._tree(yh - m.pred[:, 0], 0, np.arange(F, dtype=np.int32))
     tree_time = time.perf_counter() - t0
-    total = bin_time + tree_time * trees
-    value = total * 100.0 / trees
-    return {"value": round(value, 3), "unit": "s/100 trees", "cores": threads, "kind": "port",
-            "sample": f"quantile edges + binning of all {F} columns, then 1 tree of "
-                      f"{Xh.shape[0]} x {F}, depth {CONFIG['max_depth']} scaled x{trees}; "
-                      f"measured {bin_time:.2f} s binning, {tree_time:.2f} s/tree"}
+    sample_s = time.perf_counter() - w0
+    value = bin_time + tree_time * 100
+    return ({"value": round(value, 3), "unit": "s/100 trees", "cores": threads, "kind": "port",
+             "sample": f"quantile edges + binning of {cols} of {F} columns (x{F / cols:g}) and one full "
+                       f"tree of {n} x {F}, depth {CONFIG['max_depth']} (x100); measured "
+                       f"{bin_time * cols / F:.2f} s binning, {tree_time:.2f} s/tree",
+             "extrapolated": f"binning x{F / cols:g}, trees x100"}, sample_s)
+
+
+def reference_cuda_record(Xh: np.ndarray, yh: np.ndarray, trees: int):
+    """The reference's own CUDA kernels (warpgbm/cuda/*.cu compiled
+    unchanged for sm_100a into oracle/_ref/) under a restatement of its
+    regression fit loop (oracle/ref_cuda.py), growing all `trees` trees of
+    config 2 from the numpy arrays, like the reference's fit."""
+    try:
+        from oracle.build_ref import load
+        from oracle.ref_cuda import RefCudaFit
+        ops = load()
+    except Exception as e:  # the module is built where the reference checkout exists
+        return {"unavailable": f"reference CUDA build not loadable: {e}"}
+    if not torch.cuda.is_available():
+        return {"unavailable": "no CUDA device"}
+    params = dict(num_bins=CONFIG["num_bins"], max_depth=CONFIG["max_depth"],
+                  learning_rate=CONFIG["learning_rate"])
+    RefCudaFit(ops, n_estimators=2, **params).fit(Xh[:100_000], yh[:100_000])  # warm-up
+    m = RefCudaFit(ops, n_estimators=trees, **params).fit(Xh, yh)
+    t = m.timings
+    total = t["ingest_s"] + t["grow_s"]
+    return {"value": round(total * 100.0 / trees, 3), "unit": "s/100 trees", "trees_grown": trees,
+            "ingest_binning_s": round(t["ingest_s"], 3), "growth_s": round(t["grow_s"], 3),
+            "extrapolated": trees != 100,
+            "kind": "the reference's own CUDA kernels (compiled from its sources for sm_100a) under a "
+                    "restatement of its fit loop, from numpy X, y; one fit after a warm-up",
+            "device": torch.cuda.get_device_name(0)}
 
 
 def run_reference(args, rank):
-    """--impl reference: the reference algorithm (oracle port) on the host."""
+    """--impl reference: the reference algorithm on the host cores (CPU
+    oracle port, bounded samples of config 2, extrapolated), and the
+    reference's own CUDA build growing the full 100-tree fit on the GPU
+    (reference_cuda)."""
     if rank != 0:
         return
-    rng = np.random.default_rng(0)
-    n, F = args.rows, CONFIG["F"]
-    Xh = rng.standard_normal((n, F), dtype=np.float32)
-    w = rng.standard_normal(20)
-    yh = (Xh[:, :20] @ w + 0.3 * np.sin(Xh[:, 20:30]).sum(1) + rng.normal(0, 0.5, n)).astype(np.float32)
     import oracle as O
-    q = O.linspace_q(CONFIG["num_bins"])
-    # bins for the sample tree from edges of a 50k-row subsample (untimed;
-    # the timed sample recomputes exact edges of every column)
-    sub = Xh[:: max(1, n // 50_000)]
-    edges = np.stack([O.quantile_edges(sub[:, f], q) for f in range(F)])
+    n, F = args.rows, CONFIG["F"]
+    Xh, yh = make_data(0, n, F)
+    # bins for the sample trees: the oracle's exact binning of every column (untimed setup)
+    edges = O.quantile_edges_matrix(Xh, O.linspace_q(CONFIG["num_bins"]))
     bins = O.bin_matrix(Xh, edges)
-    samples = []
+    recs, step_s = [], []
     for i in range(args.warmup + args.steps):
-        r = cpu_sample(Xh, yh, bins, edges, args.trees)
+        r, dt = cpu_sample(Xh, yh, bins)
         if i >= args.warmup:
-            samples.append(r)
-    v = statistics.median(s["value"] for s in samples)
-    last = samples[-1]
+            recs.append(r)
+            step_s.append(dt)
+    v = statistics.median(r["value"] for r in recs)
     line = {"metric": "train sec/100 trees @1M×1K", "value": v, "unit": "s/100 trees",
             "impl": "reference", "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
-            "ms_per_step": v * 1000.0, "higher_is_better": False, "scaling": "weak",
-            "vs_baseline": None, "dtype": "f32", "data": "synthetic (config 2 generator, numpy seed 0)",
-            "config": {"workload": "config2: 1M x 1000 f32 regression, B=32, depth 5, 100 trees, lr 0.01",
-                       "rows_per_rank": n},
-            "cpu_baseline": {**last, "value": v},
-            "e2e": {"value": v, "unit": "s/100 trees", "h2d_bytes_per_step": 0,
-                    "d2h_bytes_per_step": 0}}
+            "ms_per_step": round(statistics.median(step_s) * 1000.0, 1), "higher_is_better": False,
+            "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": DATA_DESC,
+            "config": config_c2(n, args.trees, args.gpus),
+            "extrapolated": recs[-1]["extrapolated"] + " (ms_per_step is the measured sample)",
+            "cpu_baseline": {**recs[-1], "value": v},
+            "e2e": {"value": v, "unit": "s/100 trees", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+            "reference_cuda": reference_cuda_record(Xh, yh, args.trees)}
     print(json.dumps(line), flush=True)
+
+
+def config_c2(n, trees, world):
+    return {"workload": "config2: 1M x 1000 f32 regression, B=32, depth 5, 100 trees, lr 0.01",
+            "rows_per_rank": n, "features": CONFIG["F"], "trees": trees,
+            "parallelism": f"row-shard dp{world}",
+            "l2": "inputs > L2 (X 4 GB, bins 1 GB); no flush needed"}
 
 
 def run_reference_cuda(args, rank):
@@ -246,11 +291,8 @@ def run_reference_cuda(args, rank):
     from oracle.build_ref import load
     from oracle.ref_cuda import RefCudaFit
     ops = load()
-    rng = np.random.default_rng(0)
     n, F = args.rows, CONFIG["F"]
-    Xh = rng.standard_normal((n, F), dtype=np.float32)
-    w = rng.standard_normal(20)
-    yh = (Xh[:, :20] @ w + 0.3 * np.sin(Xh[:, 20:30]).sum(1) + rng.normal(0, 0.5, n)).astype(np.float32)
+    Xh, yh = make_data(0, n, F)
     params = dict(num_bins=CONFIG["num_bins"], max_depth=CONFIG["max_depth"],
                   learning_rate=CONFIG["learning_rate"], n_estimators=args.trees)
     runs = []
@@ -263,9 +305,8 @@ def run_reference_cuda(args, rank):
     line = {"metric": "train sec/100 trees @1M×1K", "value": round(v, 3), "unit": "s/100 trees",
             "impl": "reference-cuda", "n_gpus": 1, "steps": args.steps, "warmup": args.warmup,
             "ms_per_step": round(statistics.median(total) * 1000.0, 1), "higher_is_better": False,
-            "dtype": "f32", "data": "synthetic (config 2 generator, numpy seed 0)",
-            "config": {"workload": "config2: 1M x 1000 f32 regression, B=32, depth 5, lr 0.01",
-                       "rows": n, "trees": args.trees},
+            "dtype": "f32", "data": DATA_DESC,
+            "config": config_c2(n, args.trees, 1),
             "breakdown": {"ingest_binning_s": round(statistics.median(r["ingest_s"] for r in runs), 3),
                           "growth_s_per_100_trees": round(statistics.median(r["grow_s"] for r in runs)
                                                           * 100.0 / args.trees, 3)},
@@ -374,7 +415,7 @@ def run_c5(args, world, rank, local):
         dist.destroy_process_group()
 
 
-def config_data(name: str, dev):
+def config_data(name: str, dev, rows=None, features=None):
     """Seeded synthetic inputs of BASELINE configs 1, 3 and 4 as host arrays
     (the same arrays feed this build and the reference's kernels).  Config 4's
     5.9 GB matrix is drawn on the GPU with a seeded torch generator and copied
@@ -405,7 +446,7 @@ def config_data(name: str, dev):
                     workload="config3: 8000 x 50 f32 train / 2000 eval, 5 classes, B=32, depth 6, "
                              "200 rounds, lr 0.1, early stopping 5 on logloss every 10")
     if name == "c4":
-        n, F, E = 2_500_000, 2376, 600
+        n, F, E = rows or 2_500_000, features or 2376, 600
         g = torch.Generator(device=dev)
         g.manual_seed(4)
         Xd = torch.randint(0, 5, (n, F), generator=g, device=dev, dtype=torch.int8)
@@ -429,12 +470,18 @@ def config_data(name: str, dev):
         out = dict(X=Xd.cpu().numpy(), y=y.cpu().numpy(), era=era.cpu().numpy(), fit_kw={},
                    params=dict(num_bins=5, max_depth=8, n_estimators=100, learning_rate=0.01,
                                colsample_bytree=0.5, random_state=0),
-                   workload="config4: 2.5M x 2376 int8 in 0..4, 600 contiguous eras, DES, B=5, depth 8, "
-                            "100 trees, lr 0.01, colsample 0.5")
+                   workload=f"config4: {n / 1e6:g}M x {F} int8 in 0..4, 600 contiguous eras, DES, B=5, "
+                            "depth 8, 100 trees, lr 0.01, colsample 0.5"
+                            + ("" if (n, F) == (2_500_000, 2376) else " (reduced case)"))
         del Xd, score, s, key, pos
         torch.cuda.empty_cache()
         return out
     raise ValueError(name)
+
+
+def _reduced(args):
+    """(rows, features) of a reduced config-4 case (profiling), or Nones."""
+    return (None if args.rows == CONFIG["n"] else args.rows), args.features
 
 
 def run_config(args):
@@ -448,7 +495,7 @@ def run_config(args):
     from warpgbm_b200 import WarpGBM, _lib
     import contextlib
     import io
-    d = config_data(args.config, dev)
+    d = config_data(args.config, dev, *_reduced(args))
     params = d["params"]
     trees = params["n_estimators"] if args.trees == CONFIG["n_estimators"] else args.trees
     params = {**params, "n_estimators": trees}
@@ -542,7 +589,7 @@ def run_reference_cuda_config(args):
     from oracle.build_ref import load
     from oracle.ref_cuda import RefCudaFit
     ops = load()
-    d = config_data(args.config, torch.device("cuda", 0))
+    d = config_data(args.config, torch.device("cuda", 0), *_reduced(args))
     params = dict(d["params"])
     params.pop("objective", None)
     T = params["n_estimators"]
@@ -595,7 +642,8 @@ def main():
         dist.init_process_group("nccl", timeout=timedelta(seconds=300), device_id=dev)
     from warpgbm_b200 import WarpGBM, _lib
     n, F = args.rows, CONFIG["F"]
-    X, y = make_data(rank, n, F, dev)
+    Xh, yh = make_data(rank, n, F)
+    X, y = torch.from_numpy(Xh).to(dev), torch.from_numpy(yh).to(dev)
     params = dict(num_bins=CONFIG["num_bins"], max_depth=CONFIG["max_depth"],
                   n_estimators=args.trees, learning_rate=CONFIG["learning_rate"],
                   distributed=world > 1)
@@ -659,8 +707,6 @@ def main():
 
     e2e = None
     if not args.no_e2e:
-        Xh = X.cpu().numpy()
-        yh = y.cpu().numpy()
         with contextlib.redirect_stdout(io.StringIO()):
             WarpGBM(**{**params, "n_estimators": 1}).fit(Xh, yh)  # untimed: pinned staging setup
         barrier()
@@ -687,12 +733,9 @@ def main():
             "metric": "train sec/100 trees @1M×1K", "value": round(value, 4), "unit": "s/100 trees",
             "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
             "ms_per_step": round(t, 3), "higher_is_better": False, "scaling": "weak",
-            "vs_baseline": None, "dtype": "f32 (int64 fixed-point histograms)",
-            "data": "synthetic (config 2 generator, torch seed 1234+rank)",
-            "config": {"workload": "config2: 1M x 1000 f32 regression, B=32, depth 5, 100 trees, lr 0.01",
-                       "rows_per_rank": n, "features": F, "trees": args.trees,
-                       "parallelism": f"row-shard dp{world}",
-                       "l2": "inputs > L2 (X 4 GB, bins 1 GB); no flush needed"},
+            "vs_baseline": None, "dtype": "f32",
+            "data": DATA_DESC,
+            "config": config_c2(n, args.trees, world),
             "roofline": {"bound": "hbm", "kernel": "k_hist (wgb_level_hist)",
                          "achieved": round(achieved, 1) if achieved else None, "peak": peak,
                          "unit": "GB/s", "frac": round(achieved / peak, 4) if achieved else None,
@@ -715,12 +758,10 @@ def main():
         if world == 1 and not args.no_cpu:
             # CPU leg on the same matrix; the bins it grows the sample tree on
             # are the model's own (identical to the oracle's binning)
-            Xh = X.cpu().numpy()
-            yh = y.cpu().numpy()
             with contextlib.redirect_stdout(io.StringIO()):
                 bd = model.bin_inference_data(X)
-            bins_h = bd[:, :F].cpu().numpy()
-            line["cpu_baseline"] = cpu_sample(Xh, yh, bins_h, model.bin_edges.cpu().numpy(), args.trees)
+            bins_h = np.ascontiguousarray(bd[:, :F].cpu().numpy())
+            line["cpu_baseline"] = cpu_sample(Xh, yh, bins_h)[0]
         print(json.dumps(line), flush=True)
     if world > 1:
         dist.barrier()
