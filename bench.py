@@ -388,6 +388,21 @@ def run_c5(args, world, rank, local):
     hist_ms = sum(a.elapsed_time(b) for a, b in model._hist_events)
     comm_ms = sum(a.elapsed_time(b) for a, b in model._comm_events)
     hist_bytes = hist_algorithmic_bytes(model, n_total, F, 1, C5["num_bins"], world)
+    # the predict kernel alone (bins resident, forest packed): algorithmic
+    # bytes n * (F bin bytes + 4 output bytes) per launch
+    with contextlib.redirect_stdout(io.StringIO()):
+        pbins = model.bin_inference_data(X)
+    model.predict_binned(pbins)
+    pk = []
+    for _ in range(3):
+        k0, k1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        k0.record()
+        model.predict_binned(pbins)
+        k1.record()
+        torch.cuda.synchronize()
+        pk.append(k0.elapsed_time(k1))
+    pred_kernel_ms = statistics.median(pk)
+    del pbins
     peak, peak_kind = peaks()
     achieved = hist_bytes / (hist_ms / 1000.0) / 1e9 if hist_ms > 0 else None
     if rank == 0:
@@ -401,7 +416,10 @@ def run_c5(args, world, rank, local):
                            "rows_total": n_total, "rows_per_rank": n, "trees": trees,
                            "parallelism": f"row-shard dp{world}"},
                 "predict": {"value": round(statistics.median(pred_ms) / 1000.0, 4), "unit": "s",
-                            "rows_per_rank": n, "trees": trees},
+                            "rows_per_rank": n, "trees": trees,
+                            "note": "model.predict(X): ingest of the int8 rows, forest packing, kernel, copy out",
+                            "kernel_ms": round(pred_kernel_ms, 3),
+                            "kernel_gbs": round(n * (F + 4) / (pred_kernel_ms / 1000.0) / 1e9, 1)},
                 "breakdown_rank0_ms": {"histogram_kernels": round(hist_ms, 1), "collectives": round(comm_ms, 1),
                                        "fit": round(fit_ms[-1], 1)},
                 "roofline": {"bound": "hbm", "kernel": "k_hist (wgb_level_hist)",

@@ -210,7 +210,7 @@ typedef struct wgb_ws {
     int32_t *nchunks;        /* [1]                                           */
     /* split search */
     int32_t *cand;           /* [2^(D-1)][ncand_blk][4] partial arg-max:     */
-                             /*   ncand_blk >= ceil(k/128) with one era;     */
+                             /*   ncand_blk >= ceil(k/8) with one era;       */
                              /*   with eras >= ceil(k/32) (num_bins <= 33)   */
                              /*   or ceil(k/8) (num_bins > 33)               */
     float *era_gain;         /* [2^D - 1][E] per-era gain of chosen split     */

@@ -38,6 +38,9 @@ from .metrics import accuracy_torch, log_loss_torch, rmsle_torch, softmax
 
 HIST_R = 2048          # rows per histogram chunk (csrc/wgb_common.cuh)
 PART_TILE = 2048       # positions per partition tile
+SPLIT_WARPS = 8           # features per single-era split block (csrc/wgb_common.cuh)
+
+
 def split_era_features(B: int) -> int:
     """Features per block of the era split search (csrc/wgb_engine.cu)."""
     return 32 if B - 1 <= 32 else 8
@@ -768,9 +771,9 @@ class WarpGBM(BaseEstimator, RegressorMixin):
             t["part_hist"] = torch.empty(part_elems * 2, dtype=torch.int32, device=dev)
         else:
             part_elems = 0
-        # per-node partial arg-max: blocks of 128 features with one era, of
+        # per-node partial arg-max: blocks of 8 features with one era, of
         # 32 (or 8 for num_bins > 33) with eras
-        fb = 128 if E == 1 else split_era_features(B)
+        fb = SPLIT_WARPS if E == 1 else split_era_features(B)
         ncand = (k + fb - 1) // fb
         t["cand"] = torch.empty((nslots, ncand, 4), **i32)
         if E > 1:

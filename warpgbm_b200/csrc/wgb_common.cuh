@@ -56,7 +56,7 @@ constexpr uint32_t HIST_LO_MASK = (1u << HIST_LO_BITS) - 1u;
 constexpr uint32_t HIST_A_SUM_MASK = (1u << HIST_CNT_SHIFT) - 1u;
 #define HIST_ERA_R(has_era) ((has_era) ? HIST_R : 1)
 constexpr int HIST_THREADS = 256;
-constexpr int SPLIT_THREADS = 128;  // features per split block
+constexpr int SPLIT_WARPS = 8;     // features per single-era split block (one warp each)
 constexpr int PART_TILE = 2048;     // positions per partition tile
 constexpr int PART_THREADS = 256;
 

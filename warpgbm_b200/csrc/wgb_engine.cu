@@ -552,101 +552,64 @@ __global__ void k_subtract(const wgb_node *__restrict__ lvl, const int *nn_d, lo
 // split search                                                           //
 // ====================================================================== //
 
-// One thread = (node, feature position j): the bin scan of a single-era
-// histogram with the reference arithmetic (best_split_kernel.cu:25-53),
-// criterion = gain (core.py:577-579).  Block arg-max -> cand[node][blk].
-__global__ void __launch_bounds__(SPLIT_THREADS) k_split(
+// Single-era split search (criterion = gain, core.py:577-579): one warp =
+// (node, feature position j), SPLIT_WARPS features per block.  The warp
+// stages the feature's B bins in shared memory (G = float(sum q) * 2^-s,
+// H = float(count)); every lane then forms the reference's sequential fp32
+// sums (totals over all B bins, prefix over b < B-1, best_split_kernel.cu:
+// 25-53) from the staged values -- the additions stay in bin order, so the
+// sums are the reference's bit for bit -- and evaluates the split points
+// b = lane, lane + 32, ...  (one gain per lane instead of B-1 per thread:
+// a level with one node still fills the GPU).  Block arg-max ->
+// cand[node][blk].
+template <int NBW>  // split points per lane: ceil((B-1) / 32)
+__global__ void __launch_bounds__(SPLIT_WARPS * 32) k_split(
     const wgb_node *__restrict__ lvl, const int *nn_d, const long long *__restrict__ hg,
     const long long *__restrict__ hc, long long slot_elems, int k, int B, const int *shift,
     float mcw, float eps, float msg, int4 *cand, int nblk, float *crit_out) {
+    __shared__ float sG[SPLIT_WARPS][32 * NBW + 1], sH[SPLIT_WARPS][32 * NBW + 1];
+    __shared__ Key s_k[SPLIT_WARPS];
     const int n = blockIdx.x / nblk, jb = blockIdx.x - n * nblk;  // node, feature block
     if (n >= *nn_d) return;
-    const int j = jb * SPLIT_THREADS + threadIdx.x;
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const int j = jb * SPLIT_WARPS + warp;
     const float inv = pow2f(-*shift);
-    const int B1 = B + 1, nb = B - 1;
-    const long long slot = lvl[n].slot;
+    const int nb = B - 1;
     Key best = key_none();
     if (j < k) {
-        const long long off = slot * slot_elems + (long long)j * B1;
-        const long long *gp = hg + off;
-        const long long *cp = hc + off;
-        float GT = 0.0f, HT = 0.0f;
-        for (int b = 0; b < B; ++b) {
-            GT = __fadd_rn(GT, __fmul_rn(__ll2float_rn(__ldg(gp + b)), inv));
-            HT = __fadd_rn(HT, __ll2float_rn(__ldg(cp + b)));
+        const long long off = lvl[n].slot * slot_elems + (long long)j * (B + 1);
+        for (int b = lane; b < B; b += 32) {
+            sG[warp][b] = __fmul_rn(__ll2float_rn(__ldg(hg + off + b)), inv);
+            sH[warp][b] = __ll2float_rn(__ldg(hc + off + b));
         }
-        float GL = 0.0f, HL = 0.0f;
-#pragma unroll 4
-        for (int b = 0; b < nb; ++b) {
-            GL = __fadd_rn(GL, __fmul_rn(__ll2float_rn(__ldg(gp + b)), inv));
-            HL = __fadd_rn(HL, __ll2float_rn(__ldg(cp + b)));
-            SplitEval r = eval_split(GL, HL, GT, HT, mcw, eps);
-            if (crit_out && n == 0) crit_out[j * nb + b] = r.gain;
-            Key kk{0, r.gain > msg ? r.gain : -INFINITY, j * nb + b};
-            if (key_better(kk, best)) best = kk;
-        }
-    }
-    best = warp_key_max(best);
-    __shared__ Key s_k[SPLIT_THREADS / 32];
-    if ((threadIdx.x & 31) == 0) s_k[threadIdx.x >> 5] = best;
-    __syncthreads();
-    if (threadIdx.x == 0) {
-        for (int w = 1; w < SPLIT_THREADS / 32; ++w)
-            if (key_better(s_k[w], best)) best = s_k[w];
-        cand[(long long)n * nblk + jb] = make_int4(best.A, __float_as_int(best.c), best.idx, 0);
-    }
-}
-
-// k_split for levels with many nodes: the block's 128 feature rows are
-// staged in shared memory as fp32 (G = float(sum q) * 2^-s, H =
-// float(count)) with coalesced loads; each thread then scans its own row in
-// bin order (the reference's sequential fp32 sums).  Odd row stride:
-// conflict-free row reads.
-__global__ void __launch_bounds__(SPLIT_THREADS) k_split_staged(
-    const wgb_node *__restrict__ lvl, const int *nn_d, const long long *__restrict__ hg,
-    const long long *__restrict__ hc, long long slot_elems, int k, int B, const int *shift,
-    float mcw, float eps, float msg, int4 *cand, int nblk, float *crit_out) {
-    extern __shared__ float s_split[];
-    const int n = blockIdx.x / nblk, jb = blockIdx.x - n * nblk;  // node, feature block
-    if (n >= *nn_d) return;
-    const int j0 = jb * SPLIT_THREADS, j = j0 + threadIdx.x;
-    const int nj = min(SPLIT_THREADS, k - j0);
-    const float inv = pow2f(-*shift);
-    const int B1 = B + 1, nb = B - 1, B1p = B1 | 1;
-    float *sG = s_split, *sH = s_split + SPLIT_THREADS * B1p;
-    const long long slot = lvl[n].slot;
-    Key best = key_none();
-    const long long base = slot * slot_elems + (long long)j0 * B1;
-    for (int t = threadIdx.x; t < nj * B1; t += SPLIT_THREADS) {
-        const int jl = t / B1, b = t - jl * B1;
-        sG[jl * B1p + b] = __fmul_rn(__ll2float_rn(__ldg(hg + base + t)), inv);
-        sH[jl * B1p + b] = __ll2float_rn(__ldg(hc + base + t));
-    }
-    __syncthreads();
-    if (j < k) {
-        const float *g = sG + threadIdx.x * B1p, *h = sH + threadIdx.x * B1p;
+        __syncwarp();
+        const float *g = sG[warp], *h = sH[warp];
         float GT = 0.0f, HT = 0.0f;
         for (int b = 0; b < B; ++b) {
             GT = __fadd_rn(GT, g[b]);
             HT = __fadd_rn(HT, h[b]);
         }
         float GL = 0.0f, HL = 0.0f;
-#pragma unroll 4
-        for (int b = 0; b < nb; ++b) {
-            GL = __fadd_rn(GL, g[b]);
-            HL = __fadd_rn(HL, h[b]);
-            SplitEval r = eval_split(GL, HL, GT, HT, mcw, eps);
-            if (crit_out && n == 0) crit_out[j * nb + b] = r.gain;
-            Key kk{0, r.gain > msg ? r.gain : -INFINITY, j * nb + b};
+        int b = 0;
+#pragma unroll
+        for (int i = 0; i < NBW; ++i) {
+            const int bi = lane + 32 * i;  // this lane's i-th split point
+            if (bi >= nb) break;
+            for (; b <= bi; ++b) {
+                GL = __fadd_rn(GL, g[b]);
+                HL = __fadd_rn(HL, h[b]);
+            }
+            const SplitEval r = eval_split(GL, HL, GT, HT, mcw, eps);
+            if (crit_out && n == 0) crit_out[j * nb + bi] = r.gain;
+            const Key kk{0, r.gain > msg ? r.gain : -INFINITY, j * nb + bi};
             if (key_better(kk, best)) best = kk;
         }
     }
     best = warp_key_max(best);
-    __shared__ Key s_k[SPLIT_THREADS / 32];
-    if ((threadIdx.x & 31) == 0) s_k[threadIdx.x >> 5] = best;
+    if (lane == 0) s_k[warp] = best;
     __syncthreads();
     if (threadIdx.x == 0) {
-        for (int w = 1; w < SPLIT_THREADS / 32; ++w)
+        for (int w = 1; w < SPLIT_WARPS; ++w)
             if (key_better(s_k[w], best)) best = s_k[w];
         cand[(long long)n * nblk + jb] = make_int4(best.A, __float_as_int(best.c), best.idx, 0);
     }
@@ -913,18 +876,25 @@ __global__ void __launch_bounds__(256) k_split_final(
     float mcw, float eps, const int4 *__restrict__ cand, int nblk, float *era_gain) {
     const int n = blockIdx.x;
     if (n >= *nn_d) return;
-    __shared__ Key s_best;
+    __shared__ Key s_best, s_kw[8];
     __shared__ long long s_c[8], s_g[8];
-    if (threadIdx.x == 0) {
+    {   // arg-max over the node's candidate blocks, all threads
         Key best = key_none();
-        for (int b = 0; b < nblk; ++b) {
-            int4 v = cand[(long long)n * nblk + b];
-            Key kk{v.x, __int_as_float(v.y), v.z};
+        for (int b = threadIdx.x; b < nblk; b += blockDim.x) {
+            const int4 v = cand[(long long)n * nblk + b];
+            const Key kk{v.x, __int_as_float(v.y), v.z};
             if (key_better(kk, best)) best = kk;
         }
-        s_best = best;
+        best = warp_key_max(best);
+        if ((threadIdx.x & 31) == 0) s_kw[threadIdx.x >> 5] = best;
+        __syncthreads();
+        if (threadIdx.x == 0) {
+            for (int w = 1; w < (int)(blockDim.x >> 5); ++w)
+                if (key_better(s_kw[w], best)) best = s_kw[w];
+            s_best = best;
+        }
+        __syncthreads();
     }
-    __syncthreads();
     const Key best = s_best;
     wgb_node &nd = lvl[n];
     if (!(best.c > -INFINITY)) {
@@ -1504,20 +1474,14 @@ int wgb_level_split(const wgb_ws *ws, int32_t d, void *stream) {
     int4 *cand = reinterpret_cast<int4 *>(ws->cand);
     int nblk;
     if (ws->E == 1) {
-        nblk = (ws->k + SPLIT_THREADS - 1) / SPLIT_THREADS;
+        nblk = (ws->k + SPLIT_WARPS - 1) / SPLIT_WARPS;
         WGB_CHECK_ARG(nblk <= ws->ncand_blk, "candidate buffer too small: %d blocks per node needed", nblk);
         const unsigned g = (unsigned)nblk * (unsigned)cap;  // node-major blocks
-        // per-thread row reads while a level has few nodes; coalesced staging
-        // through shared memory once it has many (their histograms outgrow L2)
-        if (cap >= 64) {
-            const int sm = 2 * SPLIT_THREADS * ((ws->B + 1) | 1) * (int)sizeof(float);
-            WGB_CUDA(cudaFuncSetAttribute(k_split_staged, cudaFuncAttributeMaxDynamicSharedMemorySize, sm));
-            k_split_staged<<<g, SPLIT_THREADS, sm, st>>>(lvl, ws->nn + d, hg, hc, se, ws->k, ws->B, ws->shift,
-                                                         ws->mcw, ws->eps, ws->msg, cand, nblk, ws->crit_out);
-        } else {
-            k_split<<<g, SPLIT_THREADS, 0, st>>>(lvl, ws->nn + d, hg, hc, se, ws->k, ws->B, ws->shift, ws->mcw,
-                                                 ws->eps, ws->msg, cand, nblk, ws->crit_out);
-        }
+#define WGB_SPLIT_W(NBW_)                                                                                  \
+    k_split<NBW_><<<g, SPLIT_WARPS * 32, 0, st>>>(lvl, ws->nn + d, hg, hc, se, ws->k, ws->B, ws->shift,   \
+                                                ws->mcw, ws->eps, ws->msg, cand, nblk, ws->crit_out)
+        if (nb <= 32) WGB_SPLIT_W(1); else if (nb <= 64) WGB_SPLIT_W(2); else WGB_SPLIT_W(4);
+#undef WGB_SPLIT_W
         WGB_LAUNCHED("k_split");
     } else {
         WGB_CHECK_ARG(ws->era_sched && ws->era_ops && ws->era_nops >= ws->E && ws->era_depth >= 1,

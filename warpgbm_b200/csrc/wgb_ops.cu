@@ -252,14 +252,16 @@ __global__ void __launch_bounds__(PRED_ROWS) k_predict_packed(
 // descendant, which holds its value.  Every walk is then exactly D steps
 // with no data-dependent trip count.
 //
-// One thread per row.  A CTA stages its R rows' bins in shared memory
-// (STAGED; else rows are read from global memory) and streams the forest
-// through two shared-memory buffers of G trees each with cp.async: group
-// g + 1 is copied while every thread walks its row through the trees of
-// group g, four trees at a time, adding leaves strictly in tree order
-// (class of tree t = t % K).
+// One thread per row, two CTAs per SM.  A CTA stages its R rows' bins in
+// shared memory with 16-byte cp.async copies (STAGED: row stride a multiple
+// of 16 and at least 64 rows fit; else rows are read from global memory) and
+// streams the forest through two shared-memory buffers of G trees each:
+// group g + 1 is copied while every thread walks its row through the trees
+// of group g, four trees at a time, adding leaves strictly in tree order
+// (class of tree t = t % K).  While one CTA of an SM waits for its rows,
+// the other walks trees.
 constexpr int HEAP_DMAX = 12;
-constexpr int HEAP_THREADS = 256, HEAP_CH = 4;
+constexpr int HEAP_THREADS = 192, HEAP_CH = 4;
 
 __device__ __forceinline__ void cp_async16(void *smem, const void *gmem) {
     const uint32_t sa = (uint32_t)__cvta_generic_to_shared(smem);
@@ -270,14 +272,14 @@ template <int N>
 __device__ __forceinline__ void cp_async_wait() { asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory"); }
 
 template <bool STAGED>
-__global__ void __launch_bounds__(HEAP_THREADS) k_predict_heap(
+__global__ void __launch_bounds__(HEAP_THREADS, 2) k_predict_heap(
     const int8_t *__restrict__ bins, long long n, long long S, const uint32_t *__restrict__ heap, int T, int K,
     int D, int G, float lr, float *__restrict__ out) {
     extern __shared__ __align__(16) uint32_t s_heap[];
     const int TW = 2 << D;                 // words per tree
     uint32_t *tb = s_heap;                 // [2][G * TW]
-    uint32_t *rows = s_heap + 2 * G * TW;  // [R][SW]
-    const int SW = (int)(S / 4) + 1;
+    uint8_t *rows = reinterpret_cast<uint8_t *>(s_heap + 2 * G * TW);  // [R][RS]
+    const int RS = (int)S + 16;            // staged row stride: 16-byte aligned, shifts banks by 4 per row
     const int R = blockDim.x;
     const long long r0 = (long long)blockIdx.x * R;
     const int nrows = (int)min((long long)R, n - r0);
@@ -286,24 +288,26 @@ __global__ void __launch_bounds__(HEAP_THREADS) k_predict_heap(
         const uint4 *src = reinterpret_cast<const uint4 *>(heap + (long long)t0 * TW);
         uint4 *dst = reinterpret_cast<uint4 *>(tb + (g & 1) * G * TW);
         for (int i = threadIdx.x; i < nt * TW / 4; i += R) cp_async16(dst + i, src + i);
-        cp_async_commit();
     };
     const int ngroups = (T + G - 1) / G;
-    prefetch(0);
-    if (STAGED) {
-        for (int t = threadIdx.x; t < nrows * (SW - 1); t += R) {
-            const int rr = t / (SW - 1), w = t - rr * (SW - 1);
-            rows[rr * SW + w] = __ldg(reinterpret_cast<const uint32_t *>(bins + (r0 + rr) * S) + w);
+    if (STAGED) {  // the CTA's rows, 16 bytes per copy, all in flight at once
+        const int v16 = (int)(S / 16);
+        for (int t = threadIdx.x; t < nrows * v16; t += R) {
+            const int rr = t / v16, c = t - rr * v16;
+            cp_async16(rows + (size_t)rr * RS + 16 * c, bins + (r0 + rr) * S + 16 * c);
         }
     }
+    prefetch(0);
+    cp_async_commit();  // group: rows + trees of group 0
     const bool live = threadIdx.x < nrows;
     const long long row = r0 + threadIdx.x;
-    const int8_t *myrow = STAGED ? reinterpret_cast<const int8_t *>(rows + threadIdx.x * SW)
+    const int8_t *myrow = STAGED ? reinterpret_cast<const int8_t *>(rows + (size_t)threadIdx.x * RS)
                                  : bins + (live ? row : 0) * S;
     float acc = (live && K == 1) ? out[row] : 0.0f;
     for (int g = 0; g < ngroups; ++g) {
         if (g + 1 < ngroups) {
             prefetch(g + 1);
+            cp_async_commit();
             cp_async_wait<1>();
         } else {
             cp_async_wait<0>();
@@ -313,13 +317,17 @@ __global__ void __launch_bounds__(HEAP_THREADS) k_predict_heap(
             const uint32_t *grp = tb + (g & 1) * G * TW;
             const int t0 = g * G, nt = min(G, T - t0);
             for (int u0 = 0; u0 < nt; u0 += HEAP_CH) {
+                const uint32_t *tr[HEAP_CH];
                 int node[HEAP_CH];
 #pragma unroll
-                for (int u = 0; u < HEAP_CH; ++u) node[u] = 0;
+                for (int u = 0; u < HEAP_CH; ++u) {
+                    tr[u] = grp + min(u0 + u, nt - 1) * TW;
+                    node[u] = 0;
+                }
                 for (int d = 0; d < D; ++d) {
 #pragma unroll
                     for (int u = 0; u < HEAP_CH; ++u) {
-                        const uint32_t w = grp[min(u0 + u, nt - 1) * TW + node[u]];
+                        const uint32_t w = tr[u][node[u]];
                         const int f = (int)(w & 0xFFFFu);
                         const int sb = (int)(int8_t)(w >> 16);
                         const int b = (int)(f < S ? (STAGED ? myrow[f] : __ldg(myrow + f)) : 0);
@@ -329,7 +337,7 @@ __global__ void __launch_bounds__(HEAP_THREADS) k_predict_heap(
 #pragma unroll
                 for (int u = 0; u < HEAP_CH; ++u) {
                     if (u0 + u >= nt) break;
-                    const float v = __uint_as_float(grp[(u0 + u) * TW + node[u] + 1]);
+                    const float v = __uint_as_float(tr[u][node[u] + 1]);
                     const int t = t0 + u0 + u;
                     if (K == 1) {
                         acc = __fadd_rn(acc, __fmul_rn(lr, v));
@@ -552,14 +560,22 @@ int wgb_predict_heap(const int8_t *bins, int64_t n, int64_t S, const uint32_t *h
     WGB_CHECK_ARG((reinterpret_cast<uintptr_t>(heap) & 15) == 0, "heap must be 16-byte aligned");
     if (n == 0 || T == 0) return WGB_OK;
     const size_t tree_bytes = (size_t)8 << D;  // 2^(D+1) words
-    // trees per buffer: up to 16, within 64 KB for both buffers together
-    int G = (int)std::min<size_t>(16, std::max<size_t>(1, (64 * 1024) / (2 * tree_bytes)));
+    // two CTAs per SM (one stages its rows while the other walks trees):
+    // each gets up to 110 KB -- trees per buffer up to 8 within 32 KB for
+    // both buffers together, the rest for its rows
+    int G = (int)std::min<size_t>(8, std::max<size_t>(1, (32 * 1024) / (2 * tree_bytes)));
     if (G > T) G = T;
     const size_t tsm = 2 * (size_t)G * tree_bytes;
-    const int R = staged_rows(S, HEAP_THREADS, 220 * 1024 - tsm);
+    const size_t budget = tsm < 110 * 1024 ? 110 * 1024 - tsm : 0;
+    int R = 0;
+    if (S % 16 == 0) {
+        R = HEAP_THREADS;
+        while (R >= 64 && (size_t)R * (size_t)(S + 16) > budget) R -= 32;
+        if (R < 64 || (size_t)R * (size_t)(S + 16) > budget) R = 0;
+    }
     cudaStream_t st = as_stream(stream);
     if (R) {
-        const size_t smem = tsm + (size_t)R * (S + 4);
+        const size_t smem = tsm + (size_t)R * (S + 16);
         WGB_CUDA(cudaFuncSetAttribute(k_predict_heap<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
         k_predict_heap<true><<<(unsigned)((n + R - 1) / R), R, smem, st>>>(bins, n, S, heap, T, K, D, G, lr, out);
     } else {
