@@ -222,6 +222,8 @@ typedef struct wgb_ws {
     float *maxabs;           /* [1] max |g| (bit pattern compared as int)     */
     int32_t *shift;          /* [1] s                                         */
     int64_t *rootsum;        /* [1] sum of q over local rows                  */
+    int32_t *sync;           /* [4] zero-initialised counters of the fused    */
+                             /*   per-level kernels (left at zero by them)    */
     void *part_hist;         /* per-chunk histogram words (8 bytes each), or  */
     int64_t part_hist_elems; /*   NULL: wgb_hist_part_elems(S, F, B, chunk_cap) */
                              /*   lets single-era levels skip global atomics  */
@@ -254,8 +256,9 @@ int wgb_tree_quantize(const wgb_ws *ws, void *stream);
 /* Root record (its sum and leaf are set at level 0's split) and level
  * counters. */
 int wgb_tree_root(const wgb_ws *ws, void *stream);
-/* Level d: chunk plan, zero of the built slots, histogram build of the
- * built nodes from local rows.  Built slots of level d are the contiguous
+/* Level d: zero of the built slots, histogram build of the built nodes
+ * from local rows (level 0 plans its chunk list here; level d > 0 uses the
+ * list that wgb_level_partition(d - 1) planned).  Built slots of level d are the contiguous
  * range returned by wgb_built_slots; one int64 SUM all-reduce over ranks of
  * hg[first*P, (first+count)*P), P = 2*E*k*(B+1) + 2, covers sums, counts
  * and (level 0) the root's sum of q, which wgb_level_hist copies from
@@ -265,8 +268,9 @@ void wgb_built_slots(int32_t d, int32_t *first, int32_t *count);
 /* Elements (8 bytes each) of the per-chunk histogram buffer for `chunks`
  * chunks of a matrix with row stride S, F features and B bins. */
 int64_t wgb_hist_part_elems(int64_t S, int32_t F, int32_t B, int64_t chunks);
-/* Level d: sibling = parent - built (in place), split search, per-era gains,
- * child totals, next level's node records.  With eras the criterion is
+/* Level d: sibling = parent - built (in place, fused into the split
+ * search), split search, per-era gains, child totals, next level's node
+ * records.  With eras the criterion is
  * torch's CUDA per_era_gain.mean(dim=0) (warpgbm/core.py:581-582) bit for
  * bit: the eras are added in the order of ws->era_sched / ws->era_ops. */
 int wgb_level_split(const wgb_ws *ws, int32_t d, void *stream);
@@ -293,9 +297,12 @@ int64_t wgb_era_mean_plan(int32_t E, int64_t M, int32_t num_sms,
  * rows, which this layout makes contiguous.  Set ws->bins_fm = out after. */
 int wgb_bins_feature_major(const wgb_ws *ws, int8_t *out, void *stream);
 /* Level d: stable partition of local rows into the next level's order; rows
- * of nodes that became leaves get pred[:, cls] += lr * leaf. */
+ * of nodes that became leaves get pred[:, cls] += lr * leaf; then the next
+ * level's histogram chunk list.  At d = D - 1 every row gets its leaf
+ * update (the children are the last level). */
 int wgb_level_partition(const wgb_ws *ws, int32_t d, void *stream);
-/* Level D: every remaining row gets its leaf update. */
+/* Tree end: nothing left to launch (the last level's leaf updates happen in
+ * wgb_level_partition(D - 1)); validates the workspace. */
 int wgb_tree_finish(const wgb_ws *ws, void *stream);
 
 /* Host -> device copy of `bytes` from pageable host memory, pipelined

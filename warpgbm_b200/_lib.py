@@ -45,7 +45,7 @@ class WgbWs(ctypes.Structure):
         ("chunks", _p), ("nchunks", _p),
         ("cand", _p), ("era_gain", _p),
         ("nodes", _p), ("nn", _p), ("nact", _p),
-        ("maxabs", _p), ("shift", _p), ("rootsum", _p), ("part_hist", _p), ("part_hist_elems", _i64),
+        ("maxabs", _p), ("shift", _p), ("rootsum", _p), ("sync", _p), ("part_hist", _p), ("part_hist_elems", _i64),
         ("era_sched", _p), ("era_ops", _p), ("crit_out", _p),
         ("N", _i64), ("S", _i64), ("N_global", _i64),
         ("F", _i32), ("k", _i32), ("E", _i32), ("B", _i32), ("D", _i32), ("K", _i32),
@@ -127,7 +127,7 @@ def check(rc: int, what: str = "") -> None:
 # kernels each entry point launches (bench.py reports the count it saw)
 _KERNELS = {
     "wgb_tree_reset": 1, "wgb_tree_residual": 1, "wgb_tree_quantize": 1, "wgb_tree_root": 1,
-    "wgb_level_hist": 2, "wgb_level_split": 4, "wgb_level_partition": 3, "wgb_tree_finish": 1, "wgb_bins_feature_major": 1, "wgb_prebinned_ingest": 1,
+    "wgb_level_hist": 2, "wgb_level_split": 2, "wgb_level_partition": 3, "wgb_tree_finish": 0, "wgb_bins_feature_major": 1, "wgb_prebinned_ingest": 1,
     "wgb_bin_matrix": 1, "wgb_predict_packed": 1, "wgb_predict_heap": 1, "wgb_quantile_edges": 2, "wgb_compute_histogram3": 6, "wgb_compute_histogram3_noalloc": 6,
     "wgb_compute_split": 1, "wgb_custom_cuda_binner": 1, "wgb_predict_forest": 1,
 }

@@ -792,6 +792,7 @@ class WarpGBM(BaseEstimator, RegressorMixin):
         t["shift"] = torch.zeros(1, **i32)
         t["maxabs"] = torch.zeros(1, dtype=torch.float32, device=dev)
         t["rootsum"] = torch.zeros(1, dtype=torch.int64, device=dev)
+        t["sync"] = torch.zeros(4, dtype=torch.int32, device=dev)
         t["g"] = torch.empty(max(N, 1), dtype=torch.float32, device=dev)
         t["qg"] = torch.empty(max(N, 1), **i32)
         t["feats"] = torch.empty(k, **i32)
@@ -801,7 +802,7 @@ class WarpGBM(BaseEstimator, RegressorMixin):
         ws.order[0], ws.order[1] = t["order0"].data_ptr(), t["order1"].data_ptr()
         ws.posnode[0], ws.posnode[1] = t["posnode0"].data_ptr(), t["posnode1"].data_ptr()
         for name in ("flags", "tile_cnt", "tile_off", "part", "hg", "chunks", "cand",
-                     "era_gain", "nodes", "rootsum", "g", "qg", "feats", "kpos", "nn", "nact",
+                     "era_gain", "nodes", "rootsum", "sync", "g", "qg", "feats", "kpos", "nn", "nact",
                      "nchunks", "shift", "maxabs"):
             setattr(ws, name, t[name].data_ptr())
         ws.N, ws.S, ws.F, ws.k, ws.E, ws.B, ws.D, ws.K = N, S, F, k, E, B, D, K

@@ -126,15 +126,13 @@ __global__ void k_root_total(wgb_node *nodes, const long long *root_cell, const 
 // histogram build                                                        //
 // ====================================================================== //
 
-// Chunk list of level d: every built node's local rows cut into HIST_R-row
-// pieces.  One block.
-__global__ void __launch_bounds__(1024) k_chunk_plan(const wgb_node *__restrict__ lvl,
-                                                     const int *nn_d, int4 *chunks,
-                                                     int *nchunks, int cap) {
+// Chunk list of a level: every built node's local rows cut into HIST_R-row
+// pieces, by one block of 1024 threads.  The level's records come from
+// earlier launches or from this block (visible after its barrier).
+__device__ void plan_chunks(const wgb_node *__restrict__ lvl, int nnd, int4 *chunks, int *nchunks, int cap) {
     __shared__ int s_cnt[1024];
     __shared__ int s_off[1025];
     __shared__ int s_scan[33];
-    int nnd = *nn_d;
     int base = 0;
     for (int b0 = 0; b0 < nnd; b0 += 1024) {
         int i = b0 + threadIdx.x;
@@ -165,6 +163,12 @@ __global__ void __launch_bounds__(1024) k_chunk_plan(const wgb_node *__restrict_
         base = hi;
     }
     if (threadIdx.x == 0) *nchunks = min(base, cap);
+}
+
+// Chunk list of level 0 (later levels are planned by k_node_offsets).
+__global__ void __launch_bounds__(1024) k_chunk_plan(const wgb_node *__restrict__ lvl, const int *nn_d,
+                                                     int4 *chunks, int *nchunks, int cap) {
+    plan_chunks(lvl, *nn_d, chunks, nchunks, cap);
 }
 
 // One CTA = one chunk (<= HIST_R rows of one node) x one tile of 32*FPL
@@ -529,25 +533,6 @@ static cudaError_t launch_hist(int grid_x, const int8_t *bins, long long S, int 
     return cudaErrorInvalidValue;
 }
 
-// sibling = parent - built, in place of the parent's slot (the sibling
-// inherits it).  Block b works on pair b / bpp (bpp blocks per pair).
-__global__ void k_subtract(const wgb_node *__restrict__ lvl, const int *nn_d, long long *hg, long long *hc,
-                           long long slot_elems, long long ncell, int bpp) {
-    const int p = blockIdx.x / bpp, bx = blockIdx.x - p * bpp;
-    if (2 * p + 1 >= *nn_d) return;
-    const wgb_node &a = lvl[2 * p], &b = lvl[2 * p + 1];
-    long long sb = a.built ? b.slot : a.slot;  // sibling (= parent) slot
-    long long bb = a.built ? a.slot : b.slot;  // built slot
-    long long *gs = hg + sb * slot_elems;
-    const long long *gb = hg + bb * slot_elems;
-    long long *cs = hc + sb * slot_elems;
-    const long long *cb = hc + bb * slot_elems;
-    for (long long i = bx * (long long)blockDim.x + threadIdx.x; i < ncell; i += (long long)bpp * blockDim.x) {
-        gs[i] -= gb[i];
-        cs[i] -= cb[i];
-    }
-}
-
 // ====================================================================== //
 // split search                                                           //
 // ====================================================================== //
@@ -560,12 +545,14 @@ __global__ void k_subtract(const wgb_node *__restrict__ lvl, const int *nn_d, lo
 // 25-53) from the staged values -- the additions stay in bin order, so the
 // sums are the reference's bit for bit -- and evaluates the split points
 // b = lane, lane + 32, ...  (one gain per lane instead of B-1 per thread:
-// a level with one node still fills the GPU).  Block arg-max ->
+// a level with one node still fills the GPU).  A node whose histogram was
+// not built (the larger child, core.py:636-643) first becomes parent -
+// built sibling, written back in place of the parent.  Block arg-max ->
 // cand[node][blk].
 template <int NBW>  // split points per lane: ceil((B-1) / 32)
 __global__ void __launch_bounds__(SPLIT_WARPS * 32) k_split(
-    const wgb_node *__restrict__ lvl, const int *nn_d, const long long *__restrict__ hg,
-    const long long *__restrict__ hc, long long slot_elems, int k, int B, const int *shift,
+    const wgb_node *__restrict__ lvl, const int *nn_d, long long *hg, long long *hc, long long slot_elems,
+    int k, int B, const int *shift,
     float mcw, float eps, float msg, int4 *cand, int nblk, float *crit_out) {
     __shared__ float sG[SPLIT_WARPS][32 * NBW + 1], sH[SPLIT_WARPS][32 * NBW + 1];
     __shared__ Key s_k[SPLIT_WARPS];
@@ -577,10 +564,27 @@ __global__ void __launch_bounds__(SPLIT_WARPS * 32) k_split(
     const int nb = B - 1;
     Key best = key_none();
     if (j < k) {
-        const long long off = lvl[n].slot * slot_elems + (long long)j * (B + 1);
-        for (int b = lane; b < B; b += 32) {
-            sG[warp][b] = __fmul_rn(__ll2float_rn(__ldg(hg + off + b)), inv);
-            sH[warp][b] = __ll2float_rn(__ldg(hc + off + b));
+        const wgb_node &nd = lvl[n];
+        const long long off = nd.slot * slot_elems + (long long)j * (B + 1);
+        if (nd.built) {
+            for (int b = lane; b < B; b += 32) {
+                sG[warp][b] = __fmul_rn(__ll2float_rn(hg[off + b]), inv);
+                sH[warp][b] = __ll2float_rn(hc[off + b]);
+            }
+        } else {
+            // sibling = parent - built sibling, in place of the parent (whose
+            // slot it inherits), for all B+1 cells; exact in integers
+            const long long boff = lvl[n ^ 1].slot * slot_elems + (long long)j * (B + 1);
+            for (int b = lane; b <= B; b += 32) {
+                const long long gv = hg[off + b] - hg[boff + b];
+                const long long cv = hc[off + b] - hc[boff + b];
+                hg[off + b] = gv;
+                hc[off + b] = cv;
+                if (b < B) {
+                    sG[warp][b] = __fmul_rn(__ll2float_rn(gv), inv);
+                    sH[warp][b] = __ll2float_rn(cv);
+                }
+            }
         }
         __syncwarp();
         const float *g = sG[warp], *h = sH[warp];
@@ -762,8 +766,8 @@ static inline size_t split_eras_smem(int B, int NB, int FB, int depth) {
 
 template <int NB>
 __global__ void __launch_bounds__(256) k_split_eras(
-    const wgb_node *__restrict__ lvl, const int *nn_d, const long long *__restrict__ hg,
-    const long long *__restrict__ hc, long long slot_elems, int k, int E, int B, const int *shift,
+    const wgb_node *__restrict__ lvl, const int *nn_d, long long *hg, long long *hc, long long slot_elems,
+    int k, int E, int B, const int *shift,
     float mcw, float eps, float msg, float factor, const int *__restrict__ sched,
     const uint8_t *__restrict__ ops, int nops, int depth, int4 *cand, int nblk, float *crit_out) {
     constexpr int FB = EraSplitShape<NB>::FB, IPT = EraSplitShape<NB>::IPT, EB = SPLIT_ERA_EB;
@@ -775,6 +779,8 @@ __global__ void __launch_bounds__(256) k_split_eras(
     const int B1 = B + 1, nb = B - 1, B1p = B1 | 1;
     const float inv = pow2f(-*shift);
     const long long slot = lvl[n].slot;
+    const bool built = lvl[n].built != 0;
+    const long long bslot = built ? slot : lvl[n ^ 1].slot;  // built sibling of an unbuilt node
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     float *stg = s_era_split + warp * 2 * FB * B1p;
     float *sg = s_era_split + EB * 2 * FB * B1p;
@@ -807,10 +813,18 @@ __global__ void __launch_bounds__(256) k_split_eras(
         if (warp < ne) {
             const int e = sched[e0 + warp];
             const long long base = slot * slot_elems + ((long long)e * k + j0) * B1;
+            const long long bbase = bslot * slot_elems + ((long long)e * k + j0) * B1;
             for (int t = lane; t < nf * B1; t += 32) {
                 const int f = t / B1, b = t - f * B1;
-                stg[f * B1p + b] = __fmul_rn(__ll2float_rn(__ldg(hg + base + t)), inv);
-                stg[(FB + f) * B1p + b] = __ll2float_rn(__ldg(hc + base + t));
+                long long gv = hg[base + t], cv = hc[base + t];
+                if (!built) {  // sibling = parent - built sibling, written back in place
+                    gv -= hg[bbase + t];
+                    cv -= hc[bbase + t];
+                    hg[base + t] = gv;
+                    hc[base + t] = cv;
+                }
+                stg[f * B1p + b] = __fmul_rn(__ll2float_rn(gv), inv);
+                stg[(FB + f) * B1p + b] = __ll2float_rn(cv);
             }
             __syncwarp();
             if (lane < nf) {
@@ -867,117 +881,37 @@ __global__ void __launch_bounds__(256) k_split_eras(
     }
 }
 
-// Per node: final arg-max, per-era gain of the chosen split (importance,
-// core.py:624-627) and the exact left-child totals (bins <= bin plus the
-// negative-bin slot, which always goes left).
-__global__ void __launch_bounds__(256) k_split_final(
-    wgb_node *__restrict__ lvl, const int *nn_d, const long long *__restrict__ hg,
-    const long long *__restrict__ hc, long long slot_elems, int k, int E, int B, const int *shift,
-    float mcw, float eps, const int4 *__restrict__ cand, int nblk, float *era_gain) {
-    const int n = blockIdx.x;
-    if (n >= *nn_d) return;
-    __shared__ Key s_best, s_kw[8];
-    __shared__ long long s_c[8], s_g[8];
-    {   // arg-max over the node's candidate blocks, all threads
-        Key best = key_none();
-        for (int b = threadIdx.x; b < nblk; b += blockDim.x) {
-            const int4 v = cand[(long long)n * nblk + b];
-            const Key kk{v.x, __int_as_float(v.y), v.z};
-            if (key_better(kk, best)) best = kk;
-        }
-        best = warp_key_max(best);
-        if ((threadIdx.x & 31) == 0) s_kw[threadIdx.x >> 5] = best;
-        __syncthreads();
-        if (threadIdx.x == 0) {
-            for (int w = 1; w < (int)(blockDim.x >> 5); ++w)
-                if (key_better(s_kw[w], best)) best = s_kw[w];
-            s_best = best;
-        }
-        __syncthreads();
-    }
-    const Key best = s_best;
-    wgb_node &nd = lvl[n];
-    if (!(best.c > -INFINITY)) {
-        if (threadIdx.x == 0) {
-            nd.fpos = -1;
-            nd.lsumq = 0;
-            nd.lcount = 0;
-        }
-        return;
-    }
-    const int nb = B - 1, B1 = B + 1;
-    const int fpos = best.idx / nb, bin = best.idx - fpos * nb;
-    const float inv = pow2f(-*shift);
-    const long long slot = nd.slot;
-    long long lc = 0, ls = 0;
-    for (int e = threadIdx.x; e < E; e += blockDim.x) {
-        const long long off = slot * slot_elems + ((long long)e * k + fpos) * B1;
-        const long long *gp = hg + off;
-        const long long *cp = hc + off;
-        float GT = 0.0f, HT = 0.0f, GL = 0.0f, HL = 0.0f;
-        for (int b = 0; b < B; ++b) {
-            float gv = __fmul_rn(__ll2float_rn(gp[b]), inv);
-            float hv = __ll2float_rn(cp[b]);
-            GT = __fadd_rn(GT, gv);
-            HT = __fadd_rn(HT, hv);
-            if (b <= bin) {
-                GL = __fadd_rn(GL, gv);
-                HL = __fadd_rn(HL, hv);
-                lc += cp[b];
-                ls += gp[b];
-            }
-        }
-        lc += cp[B];
-        ls += gp[B];
-        era_gain[(long long)n * E + e] = eval_split(GL, HL, GT, HT, mcw, eps).gain;
-    }
-    lc = warp_sum(lc);
-    ls = warp_sum(ls);
-    if ((threadIdx.x & 31) == 0) {
-        s_c[threadIdx.x >> 5] = lc;
-        s_g[threadIdx.x >> 5] = ls;
-    }
-    __syncthreads();
-    if (threadIdx.x == 0) {
-        for (int w = 1; w < (int)(blockDim.x >> 5); ++w) {
-            lc += s_c[w];
-            ls += s_g[w];
-        }
-        nd.fpos = fpos;
-        nd.bin = bin;
-        nd.lcount = lc;
-        nd.lsumq = ls;
-    }
-}
-
-// Next level's node records (one block): children of splitting nodes in
+// Next level's node records, by one block: children of splitting nodes in
 // node order, smaller child built (left on ties, core.py:636), the built
-// child in a fresh slot 2^d + r, the sibling in the parent's slot.
-__global__ void __launch_bounds__(1024) k_plan_next(wgb_node *__restrict__ lvl, wgb_node *__restrict__ nxt,
-                                                    int *nn, int d, const int *shift) {
-    __shared__ int s_scan[33];
-    const int nnd = nn[d];
-    const float inv = pow2f(-*shift);
+// child in a fresh slot 2^d + r, the sibling in the parent's slot.  The
+// level's records were written by other blocks of the same launch: they are
+// read through L2 (ld.global.cg).
+__device__ void plan_next_level(wgb_node *__restrict__ lvl, wgb_node *__restrict__ nxt, int *nn, int d,
+                                float inv, int *s_scan) {
+    const int nnd = __ldcg(nn + d);
     int base = 0;
-    for (int b0 = 0; b0 < nnd; b0 += 1024) {
-        int i = b0 + threadIdx.x;
-        int f = (i < nnd && lvl[i].fpos >= 0) ? 1 : 0;
+    for (int b0 = 0; b0 < nnd; b0 += blockDim.x) {
+        const int i = b0 + threadIdx.x;
+        const int fp = i < nnd ? __ldcg(&lvl[i].fpos) : -1;
+        const int f = fp >= 0 ? 1 : 0;
         int tot;
-        int r = base + block_scan_excl(f, s_scan, tot);
+        const int r = base + block_scan_excl(f, s_scan, tot);
         if (f) {
             wgb_node &p = lvl[i];
             p.child = 2 * r;
-            long long cl = p.lcount, cr = p.count - p.lcount;
-            long long sl = p.lsumq, sr = p.sumq - p.lsumq;
-            int builtL = cl <= cr;
-            int fresh = (1 << d) + r;
+            const long long cl = __ldcg(&p.lcount), cnt = __ldcg(&p.count);
+            const long long sl = __ldcg(&p.lsumq), sm = __ldcg(&p.sumq);
+            const long long cr = cnt - cl, sr = sm - sl;
+            const int pslot = __ldcg(&p.slot);
+            const int builtL = cl <= cr;
+            const int fresh = (1 << d) + r;
             wgb_node L, R;
             L.sumq = sl; L.count = cl; R.sumq = sr; R.count = cr;
             L.lsumq = R.lsumq = 0; L.lcount = R.lcount = 0;
             L.lstart = R.lstart = 0; L.lcnt = R.lcnt = 0;
             L.built = builtL; R.built = !builtL;
-            L.slot = builtL ? fresh : p.slot;
-            R.slot = builtL ? p.slot : fresh;
+            L.slot = builtL ? fresh : pslot;
+            R.slot = builtL ? pslot : fresh;
             L.fpos = R.fpos = -1; L.bin = R.bin = 0; L.child = R.child = -1;
             L.leaf = canon_leaf(sl, cl, inv);
             R.leaf = canon_leaf(sr, cr, inv);
@@ -989,6 +923,105 @@ __global__ void __launch_bounds__(1024) k_plan_next(wgb_node *__restrict__ lvl, 
         base += tot;
     }
     if (threadIdx.x == 0) nn[d + 1] = 2 * base;
+}
+
+// Per node: final arg-max, per-era gain of the chosen split (importance,
+// core.py:624-627) and the exact left-child totals (bins <= bin plus the
+// negative-bin slot, which always goes left).  The last block of the launch
+// to finish then plans the next level (plan_next_level); `done` is a
+// zero-initialised counter that this block returns to zero.
+__global__ void __launch_bounds__(256) k_split_final(
+    wgb_node *__restrict__ lvl, wgb_node *__restrict__ nxt, int *nn, int d, const long long *__restrict__ hg,
+    const long long *__restrict__ hc, long long slot_elems, int k, int E, int B, const int *shift,
+    float mcw, float eps, const int4 *__restrict__ cand, int nblk, float *era_gain, int *done) {
+    const int n = blockIdx.x;
+    __shared__ Key s_best, s_kw[8];
+    __shared__ long long s_c[8], s_g[8];
+    __shared__ int s_scan[33];
+    __shared__ bool s_last;
+    const float inv = pow2f(-*shift);
+    if (n < nn[d]) {
+        {   // arg-max over the node's candidate blocks, all threads
+            Key best = key_none();
+            for (int b = threadIdx.x; b < nblk; b += blockDim.x) {
+                const int4 v = cand[(long long)n * nblk + b];
+                const Key kk{v.x, __int_as_float(v.y), v.z};
+                if (key_better(kk, best)) best = kk;
+            }
+            best = warp_key_max(best);
+            if ((threadIdx.x & 31) == 0) s_kw[threadIdx.x >> 5] = best;
+            __syncthreads();
+            if (threadIdx.x == 0) {
+                for (int w = 1; w < (int)(blockDim.x >> 5); ++w)
+                    if (key_better(s_kw[w], best)) best = s_kw[w];
+                s_best = best;
+            }
+            __syncthreads();
+        }
+        const Key best = s_best;
+        wgb_node &nd = lvl[n];
+        if (!(best.c > -INFINITY)) {
+            if (threadIdx.x == 0) {
+                nd.fpos = -1;
+                nd.lsumq = 0;
+                nd.lcount = 0;
+            }
+        } else {
+            const int nb = B - 1, B1 = B + 1;
+            const int fpos = best.idx / nb, bin = best.idx - fpos * nb;
+            const long long slot = nd.slot;
+            long long lc = 0, ls = 0;
+            for (int e = threadIdx.x; e < E; e += blockDim.x) {
+                const long long off = slot * slot_elems + ((long long)e * k + fpos) * B1;
+                const long long *gp = hg + off;
+                const long long *cp = hc + off;
+                float GT = 0.0f, HT = 0.0f, GL = 0.0f, HL = 0.0f;
+                for (int b = 0; b < B; ++b) {
+                    float gv = __fmul_rn(__ll2float_rn(gp[b]), inv);
+                    float hv = __ll2float_rn(cp[b]);
+                    GT = __fadd_rn(GT, gv);
+                    HT = __fadd_rn(HT, hv);
+                    if (b <= bin) {
+                        GL = __fadd_rn(GL, gv);
+                        HL = __fadd_rn(HL, hv);
+                        lc += cp[b];
+                        ls += gp[b];
+                    }
+                }
+                lc += cp[B];
+                ls += gp[B];
+                era_gain[(long long)n * E + e] = eval_split(GL, HL, GT, HT, mcw, eps).gain;
+            }
+            lc = warp_sum(lc);
+            ls = warp_sum(ls);
+            if ((threadIdx.x & 31) == 0) {
+                s_c[threadIdx.x >> 5] = lc;
+                s_g[threadIdx.x >> 5] = ls;
+            }
+            __syncthreads();
+            if (threadIdx.x == 0) {
+                for (int w = 1; w < (int)(blockDim.x >> 5); ++w) {
+                    lc += s_c[w];
+                    ls += s_g[w];
+                }
+                nd.fpos = fpos;
+                nd.bin = bin;
+                nd.lcount = lc;
+                nd.lsumq = ls;
+            }
+        }
+    }
+    // the last block to get here plans the next level
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        __threadfence();
+        s_last = atomicAdd(done, 1) == (int)gridDim.x - 1;
+    }
+    __syncthreads();
+    if (!s_last) return;
+    __threadfence();
+    plan_next_level(lvl, nxt, nn, d, inv, s_scan);
+    if (threadIdx.x == 0) *done = 0;
 }
 
 // ====================================================================== //
@@ -1112,11 +1145,13 @@ __device__ __forceinline__ int lefts_before(long long p, const uint8_t *flags, c
 }
 
 // Per splitting node: local left count and the start of its children in the
-// next order; children's local segments; next level's active rows.
+// next order; children's local segments; next level's active rows; then the
+// next level's histogram chunk list.
 __global__ void __launch_bounds__(1024) k_node_offsets(wgb_node *__restrict__ lvl, wgb_node *__restrict__ nxt,
                                                        const int *nn, int *nact, int d,
                                                        const uint8_t *flags, const int *tile_cnt,
-                                                       int *tile_off, int ntiles, int4 *part) {
+                                                       int *tile_off, int ntiles, int4 *part, int4 *chunks,
+                                                       int *nchunks, int chunk_cap) {
     __shared__ int s_scan[33];
     {   // exclusive scan of the tiles' left counts (tile_off[ntiles] = total)
         int base = 0;
@@ -1161,10 +1196,17 @@ __global__ void __launch_bounds__(1024) k_node_offsets(wgb_node *__restrict__ lv
         base += tot;
     }
     if (threadIdx.x == 0) nact[d + 1] = base;
+    // the next level's histogram chunk list (chunks == NULL at the last level)
+    if (chunks) {
+        __syncthreads();
+        plan_chunks(nxt, nn[d + 1], chunks, nchunks, chunk_cap);
+    }
 }
 
 // Scatter rows into the next level's order; finished rows get their leaf
-// update pred += lr * leaf (core.py:598-621).
+// update pred += lr * leaf (core.py:598-621).  At the tree's last split
+// level (`last` = the next level's records, all leaves) every row gets its
+// leaf update instead of a place in the next order.
 struct ScatterNode {
     float leaf;
     int lstart, child, px, py, pz;  // part[n]: lefts before the node, start of its children, left count
@@ -1174,7 +1216,8 @@ __global__ void __launch_bounds__(PART_THREADS) k_scatter(
     const wgb_node *__restrict__ lvl, const int *nn_d, const int *nact_d, const int *__restrict__ order,
     const int *__restrict__ posnode, const uint8_t *__restrict__ flags,
     const int *__restrict__ tile_off, const int4 *__restrict__ part, int *__restrict__ order_next,
-    int *__restrict__ posnode_next, float *__restrict__ pred, int K, int cls, float lr, long long N) {
+    int *__restrict__ posnode_next, float *__restrict__ pred, int K, int cls, float lr, long long N,
+    const wgb_node *__restrict__ last) {
     constexpr int IPT = PART_TILE / PART_THREADS;  // 8 consecutive positions per thread
     constexpr int CACHE = 512;                     // nodes whose records are cached per CTA
     __shared__ ScatterNode s_nc[CACHE];
@@ -1258,25 +1301,15 @@ __global__ void __launch_bounds__(PART_THREADS) k_scatter(
                 np = nd.py + nd.pz + (int)(p - nd.lstart) - lb;
                 child = nd.child + 1;
             }
-            if (np >= 0 && np < N) {  // always true for consistent offsets; guards memory
+            if (last) {  // the children are the tree's last level: their leaf updates
+                float *pp = pred + (long long)row[u] * K + cls;
+                *pp = __fadd_rn(*pp, __fmul_rn(lr, last[child].leaf));
+            } else if (np >= 0 && np < N) {  // always true for consistent offsets; guards memory
                 order_next[np] = row[u];
                 posnode_next[np] = child;
             }
             if (f[u] == 1) ++lp;
         }
-    }
-}
-
-__global__ void k_finish(const wgb_node *__restrict__ lvl, const int *nact_d, const int *__restrict__ order,
-                         const int *__restrict__ posnode, float *__restrict__ pred, int K, int cls,
-                         float lr) {
-    const int nact = *nact_d;
-    for (long long p = blockIdx.x * (long long)blockDim.x + threadIdx.x; p < nact;
-         p += (long long)gridDim.x * blockDim.x) {
-        int n = posnode ? posnode[p] : 0;
-        int row = order[p];
-        float *pp = pred + (long long)row * K + cls;
-        *pp = __fadd_rn(*pp, __fmul_rn(lr, lvl[n].leaf));
     }
 }
 
@@ -1424,9 +1457,11 @@ int wgb_level_hist(const wgb_ws *ws, int32_t d, void *stream) {
     if (d == 0)  // this rank's root sum rides along with the level-0 reduction
         WGB_CUDA(cudaMemcpyAsync(ws->hg + 2 * nc, ws->rootsum, sizeof(int64_t), cudaMemcpyDeviceToDevice, st));
     wgb_node *lvl = level_nodes(ws, d);
-    k_chunk_plan<<<1, 1024, 0, st>>>(lvl, ws->nn + d, reinterpret_cast<int4 *>(ws->chunks),
-                                     ws->nchunks, ws->chunk_cap);
-    WGB_LAUNCHED("k_chunk_plan");
+    if (d == 0) {  // later levels' chunk lists are planned by the previous level's partition
+        k_chunk_plan<<<1, 1024, 0, st>>>(lvl, ws->nn + d, reinterpret_cast<int4 *>(ws->chunks),
+                                         ws->nchunks, ws->chunk_cap);
+        WGB_LAUNCHED("k_chunk_plan");
+    }
     if (ws->N == 0) return WGB_OK;
     long long max_chunks = (ws->N + HIST_R - 1) / HIST_R + count;
     if (max_chunks > ws->chunk_cap) max_chunks = ws->chunk_cap;
@@ -1459,17 +1494,9 @@ int wgb_level_split(const wgb_ws *ws, int32_t d, void *stream) {
     if (d == 0) {
         k_root_total<<<1, 1, 0, st>>>(ws->nodes, hg + 2 * nc, ws->shift);
         WGB_LAUNCHED("k_root_total");
-    } else {
-        // blocks per pair: about 8 blocks per SM over all pairs of the level,
-        // at most one per 256 cells (a few pairs of large era histograms
-        // would otherwise leave most SMs idle)
-        const long long per_cell = (nc + 255) / 256;
-        long long bx = (148 * 8 + cap / 2 - 1) / (cap / 2);
-        if (bx < 64) bx = 64;
-        if (bx > per_cell) bx = per_cell;
-        k_subtract<<<(unsigned)(bx * (cap / 2)), 256, 0, st>>>(lvl, ws->nn + d, hg, hc, se, nc, (int)bx);
-        WGB_LAUNCHED("k_subtract");
     }
+    // (from level 1 on, the split kernels first turn each unbuilt node's
+    // parent histogram into parent - built sibling)
     const int nb = ws->B - 1;
     int4 *cand = reinterpret_cast<int4 *>(ws->cand);
     int nblk;
@@ -1508,11 +1535,10 @@ int wgb_level_split(const wgb_ws *ws, int32_t d, void *stream) {
         WGB_LAUNCHED("k_split_eras");
     }
     float *eg = ws->era_gain + (long long)((1 << d) - 1) * ws->E;
-    k_split_final<<<cap, 256, 0, st>>>(lvl, ws->nn + d, hg, hc, se, ws->k, ws->E, ws->B,
-                                       ws->shift, ws->mcw, ws->eps, cand, nblk, eg);
+    WGB_CHECK_ARG(ws->sync != nullptr, "workspace needs its sync counters");
+    k_split_final<<<cap, 256, 0, st>>>(lvl, level_nodes(ws, d + 1), ws->nn, d, hg, hc, se, ws->k, ws->E, ws->B,
+                                       ws->shift, ws->mcw, ws->eps, cand, nblk, eg, ws->sync);
     WGB_LAUNCHED("k_split_final");
-    k_plan_next<<<1, 1024, 0, st>>>(lvl, level_nodes(ws, d + 1), ws->nn, d, ws->shift);
-    WGB_LAUNCHED("k_plan_next");
     return WGB_OK;
 }
 
@@ -1545,26 +1571,23 @@ int wgb_level_partition(const wgb_ws *ws, int32_t d, void *stream) {
                                               (ws->N + 15) & ~15ll, ws->feats, ws->flags, ws->tile_cnt);
     WGB_LAUNCHED("k_flags");
     int4 *part = reinterpret_cast<int4 *>(ws->part);
+    const bool last = d == ws->D - 1;
     k_node_offsets<<<1, 1024, 0, st>>>(lvl, level_nodes(ws, d + 1), ws->nn, ws->nact, d, ws->flags,
-                                       ws->tile_cnt, ws->tile_off, ntiles, part);
+                                       ws->tile_cnt, ws->tile_off, ntiles, part,
+                                       last ? nullptr : reinterpret_cast<int4 *>(ws->chunks), ws->nchunks,
+                                       ws->chunk_cap);
     WGB_LAUNCHED("k_node_offsets");
     k_scatter<<<ntiles, PART_THREADS, 0, st>>>(lvl, ws->nn + d, ws->nact + d, ord, pn, ws->flags, ws->tile_off, part,
                                                 ws->order[d & 1], ws->posnode[d & 1], ws->pred, ws->K,
-                                                ws->cls, ws->lr, ws->N);
+                                                ws->cls, ws->lr, ws->N, last ? level_nodes(ws, d + 1) : nullptr);
     WGB_LAUNCHED("k_scatter");
     return WGB_OK;
 }
 
 int wgb_tree_finish(const wgb_ws *ws, void *stream) {
-    int rc = check_ws(ws);
-    if (rc) return rc;
-    if (ws->N == 0) return WGB_OK;
-    const int D = ws->D;
-    k_finish<<<grid_for(ws->N, 256), 256, 0, as_stream(stream)>>>(
-        level_nodes(ws, D), ws->nact + D, level_order(ws, D), level_posnode(ws, D), ws->pred, ws->K,
-        ws->cls, ws->lr);
-    WGB_LAUNCHED("k_finish");
-    return WGB_OK;
+    // the last level's leaf updates happen in wgb_level_partition(D - 1)
+    (void)stream;
+    return check_ws(ws);
 }
 
 }  // extern "C"
