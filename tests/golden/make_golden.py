@@ -10,8 +10,10 @@ remapping, DES rule, argmax, partition, leaf means, importance, flattening,
 multiclass softmax) runs unchanged, so the fixtures pin the oracle's host
 logic to the reference's.
 
-Usage:  python tests/golden/make_golden.py [/path/to/reference]
-The fixtures are committed; the GPU box never needs the reference.
+Usage:  python tests/golden/make_golden.py [/path/to/reference] [--models]
+(--models writes only the two model pickles saved by the reference's own
+save_model).  The fixtures are committed; the GPU box never needs the
+reference.
 """
 from __future__ import annotations
 
@@ -159,7 +161,8 @@ def load_reference(ref_root):
     return core, proxy
 
 
-def run_case(core, proxy, name, X, y, era, params, fit_kw=None, X_pred=None):
+def run_case(core, proxy, name, X, y, era, params, fit_kw=None, X_pred=None, save_model=None,
+             write_npz=True):
     proxy.perms.clear()
     captured = {}
 
@@ -173,6 +176,10 @@ def run_case(core, proxy, name, X, y, era, params, fit_kw=None, X_pred=None):
 
     m = Recorder(device="cpu", **params)
     m.fit(X, y, era_id=era, **(fit_kw or {}))
+    if save_model:  # the reference's own save_model (core.py:1103-1153)
+        m.save_model(os.path.join(HERE, save_model))
+    if not write_npz:
+        return
     mx = 2 ** (m.max_depth + 1)
     if m.objective == "regression":
         flat = np.stack([m.flatten_tree(t, mx).numpy() for t in m.forest if t])
@@ -202,6 +209,30 @@ def run_case(core, proxy, name, X, y, era, params, fit_kw=None, X_pred=None):
     path = os.path.join(HERE, f"{name}.npz")
     np.savez_compressed(path, **res)
     print(f"wrote {path}: trees={flat.shape[0]} nodes/tree<={mx}")
+
+
+def models(ref_root):
+    """Pickles written by the reference's save_model (its tree dicts hold 0-d
+    tensors in "feature" and the edges as a tensor): the C1 regression and
+    the multiclass case, for the load-compatibility test."""
+    core, proxy = load_reference(ref_root)
+    torch.manual_seed(0)
+    rng = np.random.default_rng(0)
+    X = rng.standard_normal((4096, 16)).astype(np.float32)
+    y = (2 * X[:, 0] - X[:, 1] + 0.5 * X[:, 2] * X[:, 3]
+         + rng.normal(0, 0.1, 4096)).astype(np.float32)
+    run_case(core, proxy, "c1_regression", X, y, None,
+             dict(num_bins=32, max_depth=3, n_estimators=10, learning_rate=0.1, random_state=0),
+             save_model="ref_model_c1.pkl", write_npz=False)
+    rng = np.random.default_rng(3)
+    n, F, K = 600, 8, 3
+    lab = rng.integers(0, K, n)
+    cent = rng.normal(0, 2, (K, F))
+    X = (cent[lab] + rng.standard_normal((n, F))).astype(np.float32)
+    run_case(core, proxy, "multiclass", X, lab.astype(np.int64), None,
+             dict(objective="multiclass", num_bins=16, max_depth=3, n_estimators=4,
+                  learning_rate=0.3, min_child_weight=5, random_state=3),
+             save_model="ref_model_multiclass.pkl", write_npz=False)
 
 
 def main(ref_root):
@@ -288,7 +319,12 @@ def main(ref_root):
 
 
 if __name__ == "__main__":
-    root = sys.argv[1] if len(sys.argv) > 1 else os.environ.get("WGB_REFERENCE")
+    args = [a for a in sys.argv[1:] if not a.startswith("--")]
+    root = args[0] if args else os.environ.get("WGB_REFERENCE")
     if not root:
-        sys.exit("usage: make_golden.py /path/to/reference  (or set WGB_REFERENCE)")
-    main(root)
+        sys.exit("usage: make_golden.py /path/to/reference [--models]  (or set WGB_REFERENCE)")
+    if "--models" in sys.argv:
+        models(root)
+    else:
+        main(root)
+        models(root)

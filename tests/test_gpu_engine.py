@@ -264,3 +264,27 @@ def test_inference_uses_the_trained_features_only(cuda):
     assert np.array_equal(mi.predict(wide_i), mi.predict(Xi.astype(np.float32)))
     with pytest.raises(IndexError):
         mi.predict(Xi[:, :4])
+
+
+@pytest.mark.parametrize("case,pkl", [("c1_regression", "ref_model_c1.pkl"),
+                                      ("multiclass", "ref_model_multiclass.pkl")])
+def test_loads_models_saved_by_the_reference(cuda, case, pkl):
+    """A pickle written by the reference's own save_model (core.py:1103-1153;
+    tree dicts with 0-d tensors as features, edges as a tensor) loads and
+    predicts like the reference run that saved it; warm start continues it."""
+    import os
+    from conftest import GOLDEN
+    d, params = load_golden(case)
+    m = WarpGBM().load_model(os.path.join(GOLDEN, pkl))
+    if case == "c1_regression":
+        p = m.predict(d["X"])
+        assert np.abs(p - d["pred"]).max() <= 1e-5 * np.abs(d["pred"]).max()
+        m.warm_start = True
+        m.n_estimators = 14
+        m.fit(d["X"], d["y"])
+        assert m._trees_trained == 14 and len([t for t in m.forest if t]) == 14
+        assert np.mean((m.predict(d["X"]) - d["y"]) ** 2) < np.mean((p - d["y"]) ** 2)
+    else:
+        pr = m.predict_proba(d["X"])
+        assert np.abs(pr - d["proba"]).max() < 1e-5
+        assert np.array_equal(m.predict(d["X"]), d["labels"])
