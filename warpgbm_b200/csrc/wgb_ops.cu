@@ -257,11 +257,11 @@ __global__ void __launch_bounds__(PRED_ROWS) k_predict_packed(
 // of 16 and at least 64 rows fit; else rows are read from global memory) and
 // streams the forest through two shared-memory buffers of G trees each:
 // group g + 1 is copied while every thread walks its row through the trees
-// of group g, four trees at a time, adding leaves strictly in tree order
+// of group g, up to four trees at a time, adding leaves strictly in tree order
 // (class of tree t = t % K).  While one CTA of an SM waits for its rows,
 // the other walks trees.
 constexpr int HEAP_DMAX = 12;
-constexpr int HEAP_THREADS = 192, HEAP_CH = 4;
+constexpr int HEAP_THREADS = 192;
 
 __device__ __forceinline__ void cp_async16(void *smem, const void *gmem) {
     const uint32_t sa = (uint32_t)__cvta_generic_to_shared(smem);
@@ -271,7 +271,7 @@ __device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commi
 template <int N>
 __device__ __forceinline__ void cp_async_wait() { asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory"); }
 
-template <bool STAGED>
+template <bool STAGED, int CH>  // CH: trees walked at once per thread (<= trees per buffer)
 __global__ void __launch_bounds__(HEAP_THREADS, 2) k_predict_heap(
     const int8_t *__restrict__ bins, long long n, long long S, const uint32_t *__restrict__ heap, int T, int K,
     int D, int G, float lr, float *__restrict__ out) {
@@ -280,6 +280,7 @@ __global__ void __launch_bounds__(HEAP_THREADS, 2) k_predict_heap(
     uint32_t *tb = s_heap;                 // [2][G * TW]
     uint8_t *rows = reinterpret_cast<uint8_t *>(s_heap + 2 * G * TW);  // [R][RS]
     const int RS = (int)S + 16;            // staged row stride: 16-byte aligned, shifts banks by 4 per row
+    const int Smax = (int)S - 1;
     const int R = blockDim.x;
     const long long r0 = (long long)blockIdx.x * R;
     const int nrows = (int)min((long long)R, n - r0);
@@ -316,26 +317,26 @@ __global__ void __launch_bounds__(HEAP_THREADS, 2) k_predict_heap(
         if (live) {
             const uint32_t *grp = tb + (g & 1) * G * TW;
             const int t0 = g * G, nt = min(G, T - t0);
-            for (int u0 = 0; u0 < nt; u0 += HEAP_CH) {
-                const uint32_t *tr[HEAP_CH];
-                int node[HEAP_CH];
+            for (int u0 = 0; u0 < nt; u0 += CH) {
+                const uint32_t *tr[CH];
+                int node[CH];
 #pragma unroll
-                for (int u = 0; u < HEAP_CH; ++u) {
+                for (int u = 0; u < CH; ++u) {
                     tr[u] = grp + min(u0 + u, nt - 1) * TW;
                     node[u] = 0;
                 }
                 for (int d = 0; d < D; ++d) {
 #pragma unroll
-                    for (int u = 0; u < HEAP_CH; ++u) {
+                    for (int u = 0; u < CH; ++u) {
                         const uint32_t w = tr[u][node[u]];
-                        const int f = (int)(w & 0xFFFFu);
+                        const int f = min((int)(w & 0xFFFFu), Smax);  // a feature past the row reads its last byte
                         const int sb = (int)(int8_t)(w >> 16);
-                        const int b = (int)(f < S ? (STAGED ? myrow[f] : __ldg(myrow + f)) : 0);
+                        const int b = (int)(STAGED ? myrow[f] : __ldg(myrow + f));
                         node[u] = 2 * node[u] + 1 + (b > sb ? 1 : 0);
                     }
                 }
 #pragma unroll
-                for (int u = 0; u < HEAP_CH; ++u) {
+                for (int u = 0; u < CH; ++u) {
                     if (u0 + u >= nt) break;
                     const float v = __uint_as_float(tr[u][node[u] + 1]);
                     const int t = t0 + u0 + u;
@@ -574,15 +575,27 @@ int wgb_predict_heap(const int8_t *bins, int64_t n, int64_t S, const uint32_t *h
         if (R < 64 || (size_t)R * (size_t)(S + 16) > budget) R = 0;
     }
     cudaStream_t st = as_stream(stream);
-    if (R) {
-        const size_t smem = tsm + (size_t)R * (S + 16);
-        WGB_CUDA(cudaFuncSetAttribute(k_predict_heap<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
-        k_predict_heap<true><<<(unsigned)((n + R - 1) / R), R, smem, st>>>(bins, n, S, heap, T, K, D, G, lr, out);
-    } else {
-        WGB_CUDA(cudaFuncSetAttribute(k_predict_heap<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)tsm));
-        k_predict_heap<false><<<(unsigned)((n + HEAP_THREADS - 1) / HEAP_THREADS), HEAP_THREADS, tsm, st>>>(
-            bins, n, S, heap, T, K, D, G, lr, out);
+#define WGB_HEAP_LAUNCH(CH_)                                                                                 \
+    if (R) {                                                                                                 \
+        const size_t smem = tsm + (size_t)R * (S + 16);                                                      \
+        WGB_CUDA(cudaFuncSetAttribute(k_predict_heap<true, CH_>, cudaFuncAttributeMaxDynamicSharedMemorySize, \
+                                      (int)smem));                                                          \
+        k_predict_heap<true, CH_><<<(unsigned)((n + R - 1) / R), R, smem, st>>>(bins, n, S, heap, T, K, D, G, lr, \
+                                                                               out);                          \
+    } else {                                                                                                 \
+        WGB_CUDA(cudaFuncSetAttribute(k_predict_heap<false, CH_>, cudaFuncAttributeMaxDynamicSharedMemorySize, \
+                                      (int)tsm));                                                           \
+        k_predict_heap<false, CH_><<<(unsigned)((n + HEAP_THREADS - 1) / HEAP_THREADS), HEAP_THREADS, tsm, st>>>( \
+            bins, n, S, heap, T, K, D, G, lr, out);                                                          \
     }
+    if (G >= 4) {
+        WGB_HEAP_LAUNCH(4)
+    } else if (G >= 2) {
+        WGB_HEAP_LAUNCH(2)
+    } else {
+        WGB_HEAP_LAUNCH(1)
+    }
+#undef WGB_HEAP_LAUNCH
     WGB_LAUNCHED("k_predict_heap");
     return WGB_OK;
 }
