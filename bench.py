@@ -55,6 +55,7 @@ def parse():
     ap.add_argument("--features", type=int, default=None,
                     help="config 4 only: fewer features (a reduced case for profiling)")
     ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--no-c5", action="store_true", help="skip the config-5 strong-scaling sub-record")
     ap.add_argument("--no-cpu", action="store_true", help="skip the cpu_baseline sample")
     ap.add_argument("--clock-ms", type=int, default=200,
                     help="nvidia-smi sampling period during the timed region (0: no sampling)")
@@ -319,18 +320,32 @@ C5 = dict(n=20_000_000, F=500, num_bins=32, max_depth=10, n_estimators=50, learn
 
 
 def run_c5(args, world, rank, local):
-    """BASELINE config 5: 20M x 500 pre-binned int8 (uniform 0..31) split over
-    the ranks (strong scaling), y = sum_{j<25} w_j x_j/31 + N(0, 0.2^2),
-    depth 10, 50 trees, lr 0.05; then predict every row.  Rows are generated
-    on each rank's GPU (seeded by rank); the fit is timed with X in HBM."""
+    """--config c5: the config-5 line on its own (see c5_measure)."""
     import torch.distributed as dist
     from datetime import timedelta
     torch.cuda.set_device(local)
     dev = torch.device("cuda", local)
     if world > 1:
         dist.init_process_group("nccl", timeout=timedelta(seconds=300), device_id=dev)
+    line = c5_measure(args, world, rank, local, dev, args.steps, args.warmup, args.clock_ms,
+                      None if args.rows == CONFIG["n"] else args.rows,
+                      None if args.trees == CONFIG["n_estimators"] else args.trees)
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+def c5_measure(args, world, rank, local, dev, steps, warmup, clock_ms, rows=None, trees=None):
+    """BASELINE config 5: 20M x 500 pre-binned int8 (uniform 0..31) split over
+    the ranks (strong scaling), y = sum_{j<25} w_j x_j/31 + N(0, 0.2^2),
+    depth 10, 50 trees, lr 0.05; then predict every row.  Rows are generated
+    on each rank's GPU (seeded by rank); the fit is timed with X in HBM.
+    Every rank takes the same collective steps; rank 0 gets the line."""
+    import torch.distributed as dist
     from warpgbm_b200 import WarpGBM, _lib
-    n_total = C5["n"] if args.rows == CONFIG["n"] else args.rows
+    n_total = rows or C5["n"]
     cut = [n_total * r // world for r in range(world + 1)]
     n = cut[rank + 1] - cut[rank]
     F = C5["F"]
@@ -341,7 +356,7 @@ def run_c5(args, world, rank, local):
     gw.manual_seed(77)
     w = torch.randn(25, generator=gw, device=dev)
     y = (X[:, :25].float() / 31.0) @ w + 0.2 * torch.randn(n, generator=g, device=dev)
-    trees = args.trees if args.trees != CONFIG["n_estimators"] else C5["n_estimators"]
+    trees = trees or C5["n_estimators"]
     params = dict(num_bins=C5["num_bins"], max_depth=C5["max_depth"], n_estimators=trees,
                   learning_rate=C5["learning_rate"], distributed=world > 1)
 
@@ -359,14 +374,14 @@ def run_c5(args, world, rank, local):
     import contextlib
     import io
     with contextlib.redirect_stdout(io.StringIO()):
-        for _ in range(args.warmup):
+        for _ in range(warmup):
             WarpGBM(**params).fit(X, y)
     barrier()
     launches0 = _lib.LAUNCHES[0]
     fit_ms, pred_ms = [], []
     model = None
-    with Clocks(local, args.clock_ms) as clk:
-        for _ in range(args.steps):
+    with Clocks(local, clock_ms) as clk:
+        for _ in range(steps):
             barrier()
             e0, e1, e2 = (torch.cuda.Event(enable_timing=True) for _ in range(3))
             e0.record()
@@ -405,10 +420,11 @@ def run_c5(args, world, rank, local):
     del pbins
     peak, peak_kind = peaks()
     achieved = hist_bytes / (hist_ms / 1000.0) / 1e9 if hist_ms > 0 else None
+    line = None
     if rank == 0:
         t = statistics.median(fit_ms)
         line = {"metric": "train sec/50 trees @20M×500 pre-binned (config 5)", "value": round(t / 1000.0, 4),
-                "unit": "s/50 trees", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+                "unit": "s/50 trees", "n_gpus": world, "steps": steps, "warmup": warmup,
                 "ms_per_step": round(t, 3), "higher_is_better": False, "scaling": "strong",
                 "dtype": "int8 bins, int64 fixed-point histograms",
                 "data": "synthetic (config 5 generator, torch seed 5000+rank)",
@@ -427,10 +443,9 @@ def run_c5(args, world, rank, local):
                              "unit": "GB/s", "frac": round(achieved / peak, 4) if achieved else None,
                              "peak_kind": peak_kind},
                 "gpu_launches": launches, "clocks": clk.summary()}
-        print(json.dumps(line), flush=True)
-    if world > 1:
-        dist.barrier()
-        dist.destroy_process_group()
+    del X, y, model
+    torch.cuda.empty_cache()
+    return line
 
 
 def config_data(name: str, dev, rows=None, features=None):
@@ -773,12 +788,26 @@ def main():
             "gpu_launches": launches,
             "clocks": clk.summary(),
         }
-        if world == 1 and not args.no_cpu:
-            # CPU leg on the same matrix; the bins it grows the sample tree on
-            # are the model's own (identical to the oracle's binning)
-            with contextlib.redirect_stdout(io.StringIO()):
-                bd = model.bin_inference_data(X)
-            bins_h = np.ascontiguousarray(bd[:, :F].cpu().numpy())
+    bins_h = None
+    if rank == 0 and world == 1 and not args.no_cpu:
+        # the CPU leg grows its sample tree on the model's own bins
+        # (identical to the oracle's binning of the same matrix)
+        with contextlib.redirect_stdout(io.StringIO()):
+            bd = model.bin_inference_data(X)
+        bins_h = np.ascontiguousarray(bd[:, :F].cpu().numpy())
+        del bd
+    if not args.no_c5:
+        # BASELINE config 5 (20M rows split over the ranks, strong scaling):
+        # the north star's multi-GPU target is set on it
+        del X, y, model
+        torch.cuda.empty_cache()
+        c5 = c5_measure(args, world, rank, local, dev, steps=2, warmup=1, clock_ms=0)
+        if rank == 0:
+            line["config5_strong"] = {k: c5[k] for k in ("metric", "value", "unit", "n_gpus", "steps", "warmup",
+                                                         "ms_per_step", "scaling", "config", "breakdown_rank0_ms",
+                                                         "roofline", "predict")}
+    if rank == 0:
+        if bins_h is not None:
             line["cpu_baseline"] = cpu_sample(Xh, yh, bins_h)[0]
         print(json.dumps(line), flush=True)
     if world > 1:
