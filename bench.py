@@ -399,9 +399,12 @@ def c5_measure(args, world, rank, local, dev, steps, warmup, clock_ms, rows=None
         model = WarpGBM(**params)
         model._hist_events = []
         model._comm_events = []
+        model._split_events = []
         model.fit(X, y)
     hist_ms = sum(a.elapsed_time(b) for a, b in model._hist_events)
     comm_ms = sum(a.elapsed_time(b) for a, b in model._comm_events)
+    split_ms = sum(a.elapsed_time(b) for a, b, _ in model._split_events)
+    part_ms = sum(b.elapsed_time(c) for _, b, c in model._split_events)
     hist_bytes = hist_algorithmic_bytes(model, n_total, F, 1, C5["num_bins"], world)
     # the predict kernel alone (bins resident, forest packed): algorithmic
     # bytes n * (F bin bytes + 4 output bytes) per launch
@@ -437,6 +440,7 @@ def c5_measure(args, world, rank, local, dev, steps, warmup, clock_ms, rows=None
                             "kernel_ms": round(pred_kernel_ms, 3),
                             "kernel_gbs": round(n * (F + 4) / (pred_kernel_ms / 1000.0) / 1e9, 1)},
                 "breakdown_rank0_ms": {"histogram_kernels": round(hist_ms, 1), "collectives": round(comm_ms, 1),
+                                       "split_kernels": round(split_ms, 1), "partition_kernels": round(part_ms, 1),
                                        "fit": round(fit_ms[-1], 1)},
                 "roofline": {"bound": "hbm", "kernel": "k_hist (wgb_level_hist)",
                              "achieved": round(achieved, 1) if achieved else None, "peak": peak,
@@ -720,12 +724,15 @@ def main():
         model = WarpGBM(**params)
         model._hist_events = []
         model._comm_events = []
+        model._split_events = []
         model.fit(X, y)
     r1.record()
     barrier()
     eager_ms = r0.elapsed_time(r1)
     hist_ms = sum(a.elapsed_time(b) for a, b in model._hist_events)
     comm_ms = sum(a.elapsed_time(b) for a, b in model._comm_events)
+    split_ms = sum(a.elapsed_time(b) for a, b, _ in model._split_events)
+    part_ms = sum(b.elapsed_time(c) for _, b, c in model._split_events)
     hist_bytes = hist_algorithmic_bytes(model, model._n_global if world > 1 else n,
                                         F, 1, CONFIG["num_bins"], world)
     t = e0.elapsed_time(e1) / args.steps
@@ -782,6 +789,8 @@ def main():
             "e2e": e2e,
             "breakdown_rank0_ms_per_step": {"histogram_kernels": round(hist_ms, 1),
                                             "collectives": round(comm_ms, 1),
+                                            "split_kernels": round(split_ms, 1),
+                                            "partition_kernels": round(part_ms, 1),
                                             "roofline_fit": round(eager_ms, 1),
                                             "host_wall_per_timed_fit": round(host_ms, 1),
                                             "note": "from the roofline fit"},

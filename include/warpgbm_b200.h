@@ -167,7 +167,8 @@ typedef struct wgb_node {
     int32_t lstart;  /* local rows: positions [lstart, lstart+lcnt) of the  */
     int32_t lcnt;    /*   level's row order                                 */
     int32_t slot;    /* histogram slot                                      */
-    int32_t built;   /* 1: histogram built from rows; 0: parent - sibling   */
+    int32_t built;   /* bit 0: histogram built from rows (else parent -     */
+                     /*   sibling); bits 8..: the node's tree in the batch  */
     int32_t fpos;    /* chosen split: position in the tree's feature subset,
                         -1 = leaf                                           */
     int32_t bin;     /* chosen threshold bin (go left iff bin <= this)      */
@@ -178,50 +179,54 @@ typedef struct wgb_node {
 /* Device workspace of one fit on one rank.  The host allocates every buffer
  * and fills the pointers; sizes in comments.  N = local rows, S = bins row
  * stride, F = features, k = features per tree, E = eras, B = num_bins,
- * D = max_depth, K = output columns (1, or classes).  Per-level node arrays
- * are packed: level d occupies nodes[(1<<d)-1 .. (1<<(d+1))-2]. */
+ * D = max_depth, K = output columns (1, or classes), T = ntree = trees grown
+ * together (1; or K for a multiclass round: tree t updates output column
+ * cls + t).  Per-level node arrays are packed: level d occupies
+ * nodes[T((1<<d)-1) .. T((1<<(d+1))-1) - 1]; tree t's root is node t of
+ * level 0, and its rows are the level-0 positions [tN, (t+1)N). */
 typedef struct wgb_ws {
     /* data (fixed for the fit) */
     const int8_t *bins;      /* [N][S]                                       */
     const int8_t *bins_fm;   /* [F][NT] feature-major copy, NT = N rounded up */
                              /*   to 16 (wgb_bins_feature_major), or NULL     */
     const int32_t *era;      /* [N] dense era id per row, or NULL if E == 1   */
-    const int32_t *root_order; /* [N] row ids sorted by era (stable)          */
+    const int32_t *root_order; /* [T][N] row ids sorted by era (stable), the  */
+                             /*   same order repeated for every tree         */
     const float *y;          /* [N] regression target (NULL: g given)        */
     float *pred;             /* [N][K] running prediction                    */
-    float *g;                /* [N] residual of the current tree             */
-    int32_t *qg;             /* [N] quantised residual                        */
+    float *g;                /* [T][N] residual of the current trees         */
+    int32_t *qg;             /* [T][N] quantised residual                     */
     /* per tree */
     const int32_t *feats;    /* [k] physical feature of each position         */
     int32_t *kpos;           /* [F] position of each physical feature or -1   */
     /* row order per level (ping-pong) */
-    int32_t *order[2];       /* [N]                                           */
-    int32_t *posnode[2];     /* [N] node index (within level) per position    */
-    uint8_t *flags;          /* [N]                                           */
+    int32_t *order[2];       /* [T*N]                                         */
+    int32_t *posnode[2];     /* [T*N] node index (within level) per position  */
+    uint8_t *flags;          /* [T*N + 16]                                    */
     int32_t *tile_cnt;       /* [ntiles]                                      */
     int32_t *tile_off;       /* [ntiles]                                      */
-    int32_t *part;           /* [2^D][4] per-node partition scratch           */
+    int32_t *part;           /* [T 2^D][4] per-node partition scratch         */
     /* histograms */
-    int64_t *hg;             /* histogram pool, 2^(D-1) slots of           */
+    int64_t *hg;             /* histogram pool, T 2^(D-1) slots of         */
                              /*   2*E*k*(B+1) + 2 int64: [E][k][B+1] sums of */
                              /*   q, [E][k][B+1] counts, root sum, spare     */
     /* chunk work list of the histogram build */
     int32_t *chunks;         /* [chunk_cap][4] = node, p0, p1, -              */
     int32_t *nchunks;        /* [1]                                           */
     /* split search */
-    int32_t *cand;           /* [2^(D-1)][ncand_blk][4] partial arg-max:     */
+    int32_t *cand;           /* [T 2^(D-1)][ncand_blk][4] partial arg-max:   */
                              /*   ncand_blk >= ceil(k/8) with one era;       */
                              /*   with eras >= ceil(k/32) (num_bins <= 33)   */
                              /*   or ceil(k/8) (num_bins > 33)               */
-    float *era_gain;         /* [2^D - 1][E] per-era gain of chosen split     */
+    float *era_gain;         /* [T (2^D - 1)][E] per-era gain of chosen split */
     /* nodes and level sizes */
-    wgb_node *nodes;         /* [2^(D+1) - 1]                                 */
-    int32_t *nn;             /* [D+1] nodes per level                         */
-    int32_t *nact;           /* [D+1] local rows per level                    */
-    /* scalars of the current tree */
-    float *maxabs;           /* [1] max |g| (bit pattern compared as int)     */
-    int32_t *shift;          /* [1] s                                         */
-    int64_t *rootsum;        /* [1] sum of q over local rows                  */
+    wgb_node *nodes;         /* [T (2^(D+1) - 1)]                             */
+    int32_t *nn;             /* [D+1] nodes per level (all trees)             */
+    int32_t *nact;           /* [D+1] local positions per level (all trees)   */
+    /* scalars of the current trees */
+    float *maxabs;           /* [T] max |g| (bit pattern compared as int)     */
+    int32_t *shift;          /* [T] s                                         */
+    int64_t *rootsum;        /* [T] sum of q over local rows                  */
     int32_t *sync;           /* [4] zero-initialised counters of the fused    */
                              /*   per-level kernels (left at zero by them)    */
     void *part_hist;         /* per-chunk histogram words (8 bytes each), or  */
@@ -236,11 +241,12 @@ typedef struct wgb_ws {
     int64_t N, S;
     int64_t N_global;
     int32_t F, k, E, B, D, K;
-    int32_t cls;             /* output column updated by this tree            */
+    int32_t cls;             /* output column updated by tree 0 of the batch  */
     int32_t chunk_cap, ntiles, ncand_blk;
     int32_t hist_ew;         /* max eras per shared-memory window (0 = auto)  */
     int32_t regular;         /* 1 if every bin is known to lie in [0, B)      */
     int32_t era_nops, era_depth; /* program length and stack depth of the plan */
+    int32_t ntree;           /* T, trees grown together (0 is taken as 1)     */
     /* hyper-parameters (fp32 as the reference passes them) */
     float mcw, eps, msg, lr, mean_factor;
 } wgb_ws;
@@ -258,13 +264,16 @@ int wgb_tree_quantize(const wgb_ws *ws, void *stream);
 int wgb_tree_root(const wgb_ws *ws, void *stream);
 /* Level d: zero of the built slots, histogram build of the built nodes
  * from local rows (level 0 plans its chunk list here; level d > 0 uses the
- * list that wgb_level_partition(d - 1) planned).  Built slots of level d are the contiguous
- * range returned by wgb_built_slots; one int64 SUM all-reduce over ranks of
- * hg[first*P, (first+count)*P), P = 2*E*k*(B+1) + 2, covers sums, counts
- * and (level 0) the root's sum of q, which wgb_level_hist copies from
- * *rootsum into the first spare cell of slot 0. */
+ * list that wgb_level_partition(d - 1) planned).  Built slots of level d are
+ * the contiguous range returned by wgb_level_slots; one int64 SUM all-reduce
+ * over ranks of hg[first*P, (first+count)*P), P = 2*E*k*(B+1) + 2, covers
+ * sums, counts and (level 0) the roots' sums of q, which wgb_level_hist
+ * copies from rootsum[t] into the first spare cell of slot t. */
 int wgb_level_hist(const wgb_ws *ws, int32_t d, void *stream);
+/* Built slots of level d for one tree at a time (ntree = 1). */
 void wgb_built_slots(int32_t d, int32_t *first, int32_t *count);
+/* Built slots of level d of the workspace's batch of ntree trees. */
+void wgb_level_slots(const wgb_ws *ws, int32_t d, int32_t *first, int32_t *count);
 /* Elements (8 bytes each) of the per-chunk histogram buffer for `chunks`
  * chunks of a matrix with row stride S, F features and B bins. */
 int64_t wgb_hist_part_elems(int64_t S, int32_t F, int32_t B, int64_t chunks);

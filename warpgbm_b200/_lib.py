@@ -51,7 +51,7 @@ class WgbWs(ctypes.Structure):
         ("F", _i32), ("k", _i32), ("E", _i32), ("B", _i32), ("D", _i32), ("K", _i32),
         ("cls", _i32),
         ("chunk_cap", _i32), ("ntiles", _i32), ("ncand_blk", _i32),
-        ("hist_ew", _i32), ("regular", _i32), ("era_nops", _i32), ("era_depth", _i32),
+        ("hist_ew", _i32), ("regular", _i32), ("era_nops", _i32), ("era_depth", _i32), ("ntree", _i32),
         ("mcw", _f32), ("eps", _f32), ("msg", _f32), ("lr", _f32), ("mean_factor", _f32),
     ]
 
@@ -75,6 +75,7 @@ _SIGS = {
     "wgb_tree_root": ([_p, _p], _i32),
     "wgb_level_hist": ([_p, _i32, _p], _i32),
     "wgb_built_slots": ([_i32, ctypes.POINTER(_i32), ctypes.POINTER(_i32)], None),
+    "wgb_level_slots": ([_p, _i32, ctypes.POINTER(_i32), ctypes.POINTER(_i32)], None),
     "wgb_level_split": ([_p, _i32, _p], _i32),
     "wgb_era_mean_plan": ([_i32, _i64, _i32, _i32, _p, _p, _i64, ctypes.POINTER(_i32)], _i64),
     "wgb_level_partition": ([_p, _i32, _p], _i32),
@@ -155,7 +156,12 @@ def era_mean_plan(E: int, M: int, num_sms: int = 0, max_threads_per_sm: int = 0)
     return sched, ops[:n], depth.value
 
 
-def built_slots(d: int):
+def built_slots(d: int, ws_ptr=None):
+    """(first, count) of level d's built histogram slots (of the workspace's
+    batch of trees when ws_ptr is given)."""
     a, b = _i32(), _i32()
-    lib().wgb_built_slots(d, ctypes.byref(a), ctypes.byref(b))
+    if ws_ptr is None:
+        lib().wgb_built_slots(d, ctypes.byref(a), ctypes.byref(b))
+    else:
+        lib().wgb_level_slots(ws_ptr, d, ctypes.byref(a), ctypes.byref(b))
     return a.value, b.value

@@ -287,17 +287,19 @@ def pack_trees(trees) -> (np.ndarray, np.ndarray):
     return arr, np.array(offs, np.int32)
 
 
-def compact_tree(nodes, gains, feats, D, E):
+def compact_tree(nodes, gains, feats, D, E, ntree=1, root=0):
     """One tree's level-packed node records -> pre-order arrays, vectorised
-    per level (no per-node Python).  Returns (packed [n,2] int32 in the
+    per level (no per-node Python).  `nodes` holds a batch of `ntree` trees
+    grown together (level d = ntree << d records; tree t's root is node t of
+    level 0); `root` picks the tree.  Returns (packed [n,2] int32 in the
     wgb_predict_packed format, leaf values [n] f32, samples [n] int64,
     split pre-order ids, split global features, split per-era gains [s, E]).
     Only nodes reachable from the root are real (the record buffer keeps
     stale entries of earlier trees)."""
     fpos_all = nodes["fpos"].astype(np.int64)
     child_all = nodes["child"].astype(np.int64)
-    base = [(1 << d) - 1 for d in range(D + 1)]
-    real = [np.zeros(1, np.int64)]                       # level-local ids of real nodes
+    base = [ntree * ((1 << d) - 1) for d in range(D + 1)]
+    real = [np.full(1, root, np.int64)]                  # level-local ids of real nodes
     split = []                                           # per level: bool mask over real
     for d in range(D + 1):
         r = real[d]
@@ -314,12 +316,12 @@ def compact_tree(nodes, gains, feats, D, E):
         if d < D and split[d].any():
             c = child_all[base[d] + r[split[d]]]
             sz[split[d]] += size[d + 1][c] + size[d + 1][c + 1]
-        full = np.zeros((1 << d), np.int64)
+        full = np.zeros((ntree << d), np.int64)
         full[r] = sz
         size[d] = full
-    n = int(size[0][0])
+    n = int(size[0][root])
     pre = [None] * (D + 1)
-    pre[0] = np.zeros(1, np.int64)
+    pre[0] = np.zeros(ntree, np.int64)
     packed = np.zeros((n, 2), np.int32)
     leaf = np.zeros(n, np.float32)
     samples = np.zeros(n, np.int64)
@@ -336,7 +338,7 @@ def compact_tree(nodes, gains, feats, D, E):
         leaf[pr[lf]] = nodes["leaf"][g[lf]]
         samples[pr[lf]] = nodes["count"][g[lf]]
         if d < D:
-            nxt = np.zeros((1 << (d + 1)), np.int64)
+            nxt = np.zeros((ntree << (d + 1)), np.int64)
             if split[d].any():
                 ps, gs = pr[split[d]], g[split[d]]
                 c = child_all[gs]
@@ -736,11 +738,15 @@ class WarpGBM(BaseEstimator, RegressorMixin):
                   bins.data_ptr(), S, torch.cuda.current_stream().cuda_stream)
         return bins, False
 
-    def _alloc_ws(self, N, F, k, E, K):
+    def _alloc_ws(self, N, F, k, E, K, ntree=1):
+        """Device workspace for growing `ntree` trees together (one per class
+        in a multiclass round: a level's node set spans the batch)."""
         dev = self._dev
         B, D = self.num_bins, self.max_depth
         S = bins_stride(F)
-        nslots = 1 << (D - 1)
+        T = ntree
+        NP = T * N                      # level-0 positions: tree t's rows at [tN, (t+1)N)
+        nslots = T << (D - 1)
         se = E * k * (B + 1)
         P = 2 * se + 2                  # int64 per slot: sums, counts, root sum, spare
         hist_bytes = nslots * P * 8
@@ -752,17 +758,17 @@ class WarpGBM(BaseEstimator, RegressorMixin):
                 f"only {free / 2**30:.1f} GiB free -- reduce max_depth or features")
         i32 = dict(dtype=torch.int32, device=dev)
         t = {}
-        t["order0"] = torch.empty(max(N, 1), **i32)
-        t["order1"] = torch.empty(max(N, 1), **i32)
-        t["posnode0"] = torch.empty(max(N, 1), **i32)
-        t["posnode1"] = torch.empty(max(N, 1), **i32)
-        t["flags"] = torch.empty(max(N, 1) + 16, dtype=torch.uint8, device=dev)  # word reads past the end
-        ntiles = max(1, (N + PART_TILE - 1) // PART_TILE)
+        t["order0"] = torch.empty(max(NP, 1), **i32)
+        t["order1"] = torch.empty(max(NP, 1), **i32)
+        t["posnode0"] = torch.empty(max(NP, 1), **i32)
+        t["posnode1"] = torch.empty(max(NP, 1), **i32)
+        t["flags"] = torch.empty(max(NP, 1) + 16, dtype=torch.uint8, device=dev)  # word reads past the end
+        ntiles = max(1, (NP + PART_TILE - 1) // PART_TILE)
         t["tile_cnt"] = torch.empty(ntiles, **i32)
         t["tile_off"] = torch.empty(ntiles + 1, **i32)
         t["part"] = torch.empty((max(nslots, 1), 4), **i32)
         t["hg"] = torch.empty(nslots * P, dtype=torch.int64, device=dev)
-        chunk_cap = (N + HIST_R - 1) // HIST_R + nslots
+        chunk_cap = (NP + HIST_R - 1) // HIST_R + nslots
         t["chunks"] = torch.empty((max(chunk_cap, 1), 4), **i32)
         # per-chunk histogram words: single-era levels store them and reduce per
         # node instead of issuing global atomics from every chunk
@@ -784,17 +790,17 @@ class WarpGBM(BaseEstimator, RegressorMixin):
                                                    props.max_threads_per_multi_processor)
             t["era_sched"] = torch.from_numpy(sched).to(dev)
             t["era_ops"] = torch.from_numpy(ops).to(dev)
-        t["era_gain"] = torch.zeros(((1 << D) - 1) * E, dtype=torch.float32, device=dev)
-        t["nodes"] = torch.zeros(((1 << (D + 1)) - 1) * 64, dtype=torch.uint8, device=dev)
+        t["era_gain"] = torch.zeros(T * ((1 << D) - 1) * E, dtype=torch.float32, device=dev)
+        t["nodes"] = torch.zeros(T * ((1 << (D + 1)) - 1) * 64, dtype=torch.uint8, device=dev)
         t["nn"] = torch.zeros(D + 1, **i32)
         t["nact"] = torch.zeros(D + 1, **i32)
         t["nchunks"] = torch.zeros(1, **i32)
-        t["shift"] = torch.zeros(1, **i32)
-        t["maxabs"] = torch.zeros(1, dtype=torch.float32, device=dev)
-        t["rootsum"] = torch.zeros(1, dtype=torch.int64, device=dev)
+        t["shift"] = torch.zeros(T, **i32)
+        t["maxabs"] = torch.zeros(T, dtype=torch.float32, device=dev)
+        t["rootsum"] = torch.zeros(T, dtype=torch.int64, device=dev)
         t["sync"] = torch.zeros(4, dtype=torch.int32, device=dev)
-        t["g"] = torch.empty(max(N, 1), dtype=torch.float32, device=dev)
-        t["qg"] = torch.empty(max(N, 1), **i32)
+        t["g"] = torch.empty(max(NP, 1), dtype=torch.float32, device=dev)
+        t["qg"] = torch.empty(max(NP, 1), **i32)
         t["feats"] = torch.empty(k, **i32)
         t["kpos"] = torch.empty(F, **i32)
         self._t = t
@@ -810,6 +816,7 @@ class WarpGBM(BaseEstimator, RegressorMixin):
         ws.part_hist = t["part_hist"].data_ptr() if part_elems else None
         ws.part_hist_elems = part_elems
         ws.hist_ew = 0  # automatic
+        ws.ntree = T
         ws.regular = 1 if self._bins_regular else 0
         ws.mcw = float(np.float32(self.min_child_weight))
         ws.eps = float(np.float32(self.L2_reg))
@@ -841,7 +848,12 @@ class WarpGBM(BaseEstimator, RegressorMixin):
                 root_order = torch.sort(era_dense, stable=True).indices.to(torch.int32)
             else:
                 root_order = torch.arange(N, dtype=torch.int32, device=dev)
-            ws = self._alloc_ws(N, F, k, E, K)
+            # a multiclass round grows its K class trees together (one level
+            # launch sequence over the K trees' nodes)
+            ntree = K if classification else 1
+            if ntree > 1:
+                root_order = root_order.repeat(ntree)
+            ws = self._alloc_ws(N, F, k, E, K, ntree)
             ws.bins, ws.root_order = bins.data_ptr(), root_order.data_ptr()
             ws.era = era_dense.data_ptr() if E > 1 else None
             ws.N_global = self._n_global
@@ -913,9 +925,9 @@ class WarpGBM(BaseEstimator, RegressorMixin):
             if self.objective == "regression" and len(self.forest) < self.n_estimators:
                 self.forest.extend([{} for _ in range(self.n_estimators - len(self.forest))])
             D = self.max_depth
-            rec_nodes = ((1 << (D + 1)) - 1) * 64
-            rec_gain = ((1 << D) - 1) * E
-            T_new = (self.n_estimators - start) * K
+            rec_nodes = ntree * ((1 << (D + 1)) - 1) * 64
+            rec_gain = ntree * ((1 << D) - 1) * E
+            T_new = self.n_estimators - start      # one record per grow call (a round's K trees)
             self._rec_nodes = torch.empty((T_new, rec_nodes), dtype=torch.uint8, pin_memory=True)
             self._rec_gain = torch.empty((T_new, max(rec_gain, 1)), dtype=torch.float32, pin_memory=True)
             self._rec_feats = torch.empty((T_new, k), dtype=torch.int32, pin_memory=True)
@@ -938,11 +950,11 @@ class WarpGBM(BaseEstimator, RegressorMixin):
                     self._t["kpos"].fill_(-1)
                     self._t["kpos"][feats.long()] = torch.arange(k, dtype=torch.int32, device=dev)
                 if classification:
+                    # core.py:782: residual of class c = -(softmax(F) - onehot)[:, c]
                     grads = softmax(pred, dim=1)
                     grads[torch.arange(N, device=dev), Yl.long()] -= 1.0
-                    for c in range(K):
-                        self._t["g"].copy_(-grads[:, c])
-                        self._grow_tree(ws, c, st, i, c)
+                    self._t["g"][: K * N].view(K, N).copy_(grads.t().neg())
+                    self._grow_tree(ws, 0, st, i, None)
                     self._trees_trained = i + 1
                     self._eval_classification(i)
                 else:
@@ -963,6 +975,8 @@ class WarpGBM(BaseEstimator, RegressorMixin):
         return self
 
     def _grow_tree(self, ws, cls, st, i, c):
+        """Grow one tree (c = its class index) or, with c None, the batch of
+        ws.ntree trees of round i (one per class)."""
         comm = self._comm
         ws.cls = cls
         p = ctypes_ptr(ws)
@@ -980,6 +994,7 @@ class WarpGBM(BaseEstimator, RegressorMixin):
         _lib.call("wgb_tree_quantize", p, st())
         _lib.call("wgb_tree_root", p, st())
         P = 2 * ws.E * ws.k * (ws.B + 1) + 2
+        wsp = ctypes_ptr(ws)
         timer = getattr(self, "_hist_events", None)
         for d in range(self.max_depth):
             if timer is not None:
@@ -991,7 +1006,7 @@ class WarpGBM(BaseEstimator, RegressorMixin):
                 ev1.record()
                 timer.append((ev0, ev1))
             if comm.on:
-                first, count = _lib.built_slots(d)
+                first, count = _lib.built_slots(d, wsp)
                 if ctimer is not None:
                     c0, c1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
                     c0.record()
@@ -999,11 +1014,21 @@ class WarpGBM(BaseEstimator, RegressorMixin):
                 if ctimer is not None:
                     c1.record()
                     ctimer.append((c0, c1))
+            stimer = getattr(self, "_split_events", None)  # bench hook: split / partition device time
+            if stimer is not None:
+                s0, s1, s2 = (torch.cuda.Event(enable_timing=True) for _ in range(3))
+                s0.record()
             _lib.call("wgb_level_split", p, d, st())
+            if stimer is not None:
+                s1.record()
             _lib.call("wgb_level_partition", p, d, st())
+            if stimer is not None:
+                s2.record()
+                stimer.append((s0, s1, s2))
         _lib.call("wgb_tree_finish", p, st())
         if getattr(self, "_record_residuals", False):  # test hook: residual of every tree
-            self._residuals.append(self._t["g"][: ws.N].cpu().numpy().copy())
+            g = self._t["g"][: ws.ntree * ws.N].view(ws.ntree, ws.N).cpu().numpy()
+            self._residuals.extend(g[t].copy() for t in range(ws.ntree))
         self._store_record(i, c)
 
     def _store_record(self, i, c):
@@ -1021,15 +1046,15 @@ class WarpGBM(BaseEstimator, RegressorMixin):
     # ------------------------------------------------------------------
     # tree records -> reference dict trees, importance (core.py:623-658)
     # ------------------------------------------------------------------
-    def _decode_tree(self, j):
-        """Record j -> compact pre-order arrays; per-era importance of its
-        splits accumulated in pre-order (core.py:624-627 adds them while
-        growing depth first, left before right)."""
+    def _decode_tree(self, j, t=0, ntree=1):
+        """Tree t of record j -> compact pre-order arrays; per-era importance
+        of its splits accumulated in pre-order (core.py:624-627 adds them
+        while growing depth first, left before right)."""
         D, E = self.max_depth, self.num_eras
         nodes = self._rec_nodes[j].numpy().view(_lib.NODE_DTYPE)
-        gains = self._rec_gain[j].numpy()[: ((1 << D) - 1) * E]
+        gains = self._rec_gain[j].numpy()[: ntree * ((1 << D) - 1) * E]
         feats = self._rec_feats[j].numpy()
-        packed, leaf, samples, sp_pre, sp_feat, sp_gain = compact_tree(nodes, gains, feats, D, E)
+        packed, leaf, samples, sp_pre, sp_feat, sp_gain = compact_tree(nodes, gains, feats, D, E, ntree, t)
         if len(sp_feat):
             np.add.at(self.per_era_feature_importance_, (slice(None), sp_feat), sp_gain.T)
         return packed, leaf, samples
@@ -1051,11 +1076,12 @@ class WarpGBM(BaseEstimator, RegressorMixin):
         self._rec_decoded = self._rec_done
 
     def _store_tree(self, j, classification):
+        """Record j -> its tree (c an index) or its round's K class trees
+        (c None, a batch grown together), decoded in class order."""
         i, c = self._rec_meta[j]
-        compact = self._decode_tree(j)
         if not hasattr(self, "feature_subsets_"):
             self.feature_subsets_ = []
-        if c == 0:
+        if c in (0, None):
             while len(self.feature_subsets_) <= i:
                 self.feature_subsets_.append(None)
             self.feature_subsets_[i] = self._rec_feats[j].numpy().copy()
@@ -1063,8 +1089,11 @@ class WarpGBM(BaseEstimator, RegressorMixin):
         if classification:
             while len(f) <= i:
                 f.append([None] * self.num_classes)
-        self._compact[(i, c)] = compact
-        self._lazy.add((i, c))
+        classes = [c] if c is not None else list(range(self.num_classes))
+        for cc in classes:
+            compact = self._decode_tree(j, 0 if c is not None else cc, 1 if c is not None else len(classes))
+            self._compact[(i, cc)] = compact
+            self._lazy.add((i, cc))
         self._packed = None
 
     def _sync_records(self, classification):

@@ -75,6 +75,12 @@ __host__ __device__ inline int quant_shift(float maxabs) {
     return s;
 }
 
+// wgb_node.built: bit 0 = histogram built from rows, bits 8.. = the node's
+// tree within the batch of trees grown together (its class offset)
+__host__ __device__ inline int node_flags(bool built, int tree) { return (tree << 8) | (built ? 1 : 0); }
+__host__ __device__ inline bool node_built(int flags) { return (flags & 1) != 0; }
+__host__ __device__ inline int node_tree(int flags) { return flags >> 8; }
+
 // 2^s as float for s in [-126, 127]
 __device__ __forceinline__ float pow2f(int s) { return __int_as_float((127 + s) << 23); }
 

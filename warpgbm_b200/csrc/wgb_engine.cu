@@ -38,20 +38,26 @@ void set_error(const char *fmt, ...) {
 // tree start                                                             //
 // ====================================================================== //
 
-__global__ void k_reset(float *maxabs, long long *rootsum) {
-    *maxabs = 0.0f;
-    *rootsum = 0;
+__global__ void k_reset(float *maxabs, long long *rootsum, int ntree) {
+    for (int t = threadIdx.x; t < ntree; t += blockDim.x) {
+        maxabs[t] = 0.0f;
+        rootsum[t] = 0;
+    }
 }
 
-// g = y - pred[:, cls] (regression, core.py:719) and max |g|.
+// Tree t = blockIdx.y of the batch: g[t][i] = y - pred[:, cls + t]
+// (regression, core.py:719; y == NULL: g is given, e.g. the softmax
+// residuals of a multiclass round, core.py:782) and max |g| of the tree.
 __global__ void k_residual(const float *__restrict__ y, const float *__restrict__ pred, int K,
                            int cls, float *__restrict__ g, long long n, float *maxabs) {
+    const int t = blockIdx.y;
+    g += (long long)t * n;
     float m = 0.0f;
     for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < n;
          i += (long long)gridDim.x * blockDim.x) {
         float v;
         if (y) {
-            v = __fsub_rn(y[i], pred[i * K + cls]);
+            v = __fsub_rn(y[i], pred[i * K + cls + t]);
             g[i] = v;
         } else {
             v = g[i];
@@ -66,14 +72,18 @@ __global__ void k_residual(const float *__restrict__ y, const float *__restrict_
     if (threadIdx.x == 0) {
         for (int i = 1; i < (blockDim.x >> 5); ++i) m = fmaxf(m, sm[i]);
         // non-negative floats order like their bit patterns
-        atomicMax(reinterpret_cast<int *>(maxabs), __float_as_int(m));
+        atomicMax(reinterpret_cast<int *>(maxabs + t), __float_as_int(m));
     }
 }
 
+// Tree t = blockIdx.y: q = rint(g * 2^s) with the tree's own shift, sum of q.
 __global__ void k_quantize(const float *__restrict__ g, int *__restrict__ qg, long long n,
                            const float *maxabs, int *shift_out, long long *rootsum) {
-    int s = quant_shift(*maxabs);
-    if (blockIdx.x == 0 && threadIdx.x == 0) *shift_out = s;
+    const int t = blockIdx.y;
+    g += (long long)t * n;
+    qg += (long long)t * n;
+    const int s = quant_shift(maxabs[t]);
+    if (blockIdx.x == 0 && threadIdx.x == 0) shift_out[t] = s;
     float sc = pow2f(s);
     long long acc = 0;
     for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < n;
@@ -88,38 +98,54 @@ __global__ void k_quantize(const float *__restrict__ g, int *__restrict__ qg, lo
     __syncthreads();
     if (threadIdx.x == 0) {
         for (int i = 1; i < (blockDim.x >> 5); ++i) acc += sm[i];
-        atomicAdd(reinterpret_cast<unsigned long long *>(rootsum), (unsigned long long)acc);
+        atomicAdd(reinterpret_cast<unsigned long long *>(rootsum + t), (unsigned long long)acc);
     }
 }
 
-// Root record; its sum of q and leaf are filled by k_root_total once the
-// level-0 histograms (which carry the root sum) are complete on every rank.
+// Root records of the batch's trees (root t = node t of level 0, slot t,
+// local positions [t*N, (t+1)*N)); their sums of q and leaves are filled by
+// k_root_total once the level-0 histograms (which carry the root sums) are
+// complete on every rank.
 __global__ void k_root(wgb_node *nodes, int *nn, int *nact, int D, long long n_local,
-                       long long n_global) {
-    wgb_node r;
-    r.sumq = 0;
-    r.count = n_global;
-    r.lsumq = 0;
-    r.lcount = 0;
-    r.lstart = 0;
-    r.lcnt = (int)n_local;
-    r.slot = 0;
-    r.built = 1;
-    r.fpos = -1;
-    r.bin = 0;
-    r.child = -1;
-    r.leaf = 0.0f;
-    nodes[0] = r;
-    for (int d = 0; d <= D; ++d) {
-        nn[d] = d == 0 ? 1 : 0;
-        nact[d] = d == 0 ? (int)n_local : 0;
+                       long long n_global, int ntree) {
+    for (int t = threadIdx.x; t < ntree; t += blockDim.x) {
+        wgb_node r;
+        r.sumq = 0;
+        r.count = n_global;
+        r.lsumq = 0;
+        r.lcount = 0;
+        r.lstart = (int)(t * n_local);
+        r.lcnt = (int)n_local;
+        r.slot = t;
+        r.built = node_flags(true, t);
+        r.fpos = -1;
+        r.bin = 0;
+        r.child = -1;
+        r.leaf = 0.0f;
+        nodes[t] = r;
+    }
+    if (threadIdx.x == 0) {
+        for (int d = 0; d <= D; ++d) {
+            nn[d] = d == 0 ? ntree : 0;
+            nact[d] = d == 0 ? (int)(ntree * n_local) : 0;
+        }
     }
 }
 
-__global__ void k_root_total(wgb_node *nodes, const long long *root_cell, const int *shift) {
-    wgb_node &r = nodes[0];
-    r.sumq = *root_cell;
-    r.leaf = canon_leaf(r.sumq, r.count, pow2f(-*shift));
+// Copies each tree's local root sum into its root slot's first spare cell,
+// so that the level-0 reduction carries it.
+__global__ void k_root_cells(long long *hg, const long long *rootsum, long long slot_elems, long long nc,
+                             int ntree) {
+    for (int t = threadIdx.x; t < ntree; t += blockDim.x) hg[t * slot_elems + 2 * nc] = rootsum[t];
+}
+
+__global__ void k_root_total(wgb_node *nodes, const long long *hg, long long slot_elems, long long nc,
+                             const int *shift, int ntree) {
+    for (int t = threadIdx.x; t < ntree; t += blockDim.x) {
+        wgb_node &r = nodes[t];
+        r.sumq = hg[t * slot_elems + 2 * nc];
+        r.leaf = canon_leaf(r.sumq, r.count, pow2f(-shift[t]));
+    }
 }
 
 // ====================================================================== //
@@ -137,7 +163,7 @@ __device__ void plan_chunks(const wgb_node *__restrict__ lvl, int nnd, int4 *chu
     for (int b0 = 0; b0 < nnd; b0 += 1024) {
         int i = b0 + threadIdx.x;
         int c = 0;
-        if (i < nnd && lvl[i].built) c = (lvl[i].lcnt + HIST_R - 1) / HIST_R;
+        if (i < nnd && node_built(lvl[i].built)) c = (lvl[i].lcnt + HIST_R - 1) / HIST_R;
         s_cnt[threadIdx.x] = c;
         int tot;
         const int ex = block_scan_excl(c, s_scan, tot);
@@ -255,6 +281,7 @@ __global__ void __launch_bounds__(NT, MINB) k_hist(
     const int4 ch = chunks[c];
     const int cnt = ch.z - ch.y;
     const long long slot = lvl[ch.x].slot;
+    if (q) q += (long long)node_tree(lvl[ch.x].built) * nrows;  // the node's tree's residuals
     float sc = 0.0f;
     if (!q) sc = pow2f(*shift);
     // rows outside [0, nrows) or eras outside [0, E) are skipped (only the
@@ -560,13 +587,13 @@ __global__ void __launch_bounds__(SPLIT_WARPS * 32) k_split(
     if (n >= *nn_d) return;
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     const int j = jb * SPLIT_WARPS + warp;
-    const float inv = pow2f(-*shift);
     const int nb = B - 1;
     Key best = key_none();
     if (j < k) {
         const wgb_node &nd = lvl[n];
+        const float inv = pow2f(-shift[node_tree(nd.built)]);
         const long long off = nd.slot * slot_elems + (long long)j * (B + 1);
-        if (nd.built) {
+        if (node_built(nd.built)) {
             for (int b = lane; b < B; b += 32) {
                 sG[warp][b] = __fmul_rn(__ll2float_rn(hg[off + b]), inv);
                 sH[warp][b] = __ll2float_rn(hc[off + b]);
@@ -777,9 +804,9 @@ __global__ void __launch_bounds__(256) k_split_eras(
     const int j0 = jb * FB;
     const int nf = min(FB, k - j0);
     const int B1 = B + 1, nb = B - 1, B1p = B1 | 1;
-    const float inv = pow2f(-*shift);
+    const float inv = pow2f(-shift[node_tree(lvl[n].built)]);
     const long long slot = lvl[n].slot;
-    const bool built = lvl[n].built != 0;
+    const bool built = node_built(lvl[n].built);
     const long long bslot = built ? slot : lvl[n ^ 1].slot;  // built sibling of an unbuilt node
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     float *stg = s_era_split + warp * 2 * FB * B1p;
@@ -887,7 +914,7 @@ __global__ void __launch_bounds__(256) k_split_eras(
 // level's records were written by other blocks of the same launch: they are
 // read through L2 (ld.global.cg).
 __device__ void plan_next_level(wgb_node *__restrict__ lvl, wgb_node *__restrict__ nxt, int *nn, int d,
-                                float inv, int *s_scan) {
+                                const int *shift, int ntree, int *s_scan) {
     const int nnd = __ldcg(nn + d);
     int base = 0;
     for (int b0 = 0; b0 < nnd; b0 += blockDim.x) {
@@ -903,13 +930,15 @@ __device__ void plan_next_level(wgb_node *__restrict__ lvl, wgb_node *__restrict
             const long long sl = __ldcg(&p.lsumq), sm = __ldcg(&p.sumq);
             const long long cr = cnt - cl, sr = sm - sl;
             const int pslot = __ldcg(&p.slot);
+            const int tree = node_tree(__ldcg(&p.built));
+            const float inv = pow2f(-shift[tree]);
             const int builtL = cl <= cr;
-            const int fresh = (1 << d) + r;
+            const int fresh = (ntree << d) + r;  // level d+1's built slots: [ntree 2^d, ntree 2^(d+1))
             wgb_node L, R;
             L.sumq = sl; L.count = cl; R.sumq = sr; R.count = cr;
             L.lsumq = R.lsumq = 0; L.lcount = R.lcount = 0;
             L.lstart = R.lstart = 0; L.lcnt = R.lcnt = 0;
-            L.built = builtL; R.built = !builtL;
+            L.built = node_flags(builtL, tree); R.built = node_flags(!builtL, tree);
             L.slot = builtL ? fresh : pslot;
             R.slot = builtL ? pslot : fresh;
             L.fpos = R.fpos = -1; L.bin = R.bin = 0; L.child = R.child = -1;
@@ -931,16 +960,16 @@ __device__ void plan_next_level(wgb_node *__restrict__ lvl, wgb_node *__restrict
 // to finish then plans the next level (plan_next_level); `done` is a
 // zero-initialised counter that this block returns to zero.
 __global__ void __launch_bounds__(256) k_split_final(
-    wgb_node *__restrict__ lvl, wgb_node *__restrict__ nxt, int *nn, int d, const long long *__restrict__ hg,
-    const long long *__restrict__ hc, long long slot_elems, int k, int E, int B, const int *shift,
-    float mcw, float eps, const int4 *__restrict__ cand, int nblk, float *era_gain, int *done) {
+    wgb_node *__restrict__ lvl, wgb_node *__restrict__ nxt, int *nn, int d, int ntree,
+    const long long *__restrict__ hg, const long long *__restrict__ hc, long long slot_elems, int k, int E, int B,
+    const int *shift, float mcw, float eps, const int4 *__restrict__ cand, int nblk, float *era_gain, int *done) {
     const int n = blockIdx.x;
     __shared__ Key s_best, s_kw[8];
     __shared__ long long s_c[8], s_g[8];
     __shared__ int s_scan[33];
     __shared__ bool s_last;
-    const float inv = pow2f(-*shift);
     if (n < nn[d]) {
+        const float inv = pow2f(-shift[node_tree(lvl[n].built)]);
         {   // arg-max over the node's candidate blocks, all threads
             Key best = key_none();
             for (int b = threadIdx.x; b < nblk; b += blockDim.x) {
@@ -1020,7 +1049,7 @@ __global__ void __launch_bounds__(256) k_split_final(
     __syncthreads();
     if (!s_last) return;
     __threadfence();
-    plan_next_level(lvl, nxt, nn, d, inv, s_scan);
+    plan_next_level(lvl, nxt, nn, d, shift, ntree, s_scan);
     if (threadIdx.x == 0) *done = 0;
 }
 
@@ -1064,7 +1093,7 @@ __global__ void __launch_bounds__(PART_THREADS) k_flags(
     const wgb_node *__restrict__ lvl, const int *nn_d, const int *nact_d, const int *__restrict__ order,
     const int *__restrict__ posnode, const int8_t *__restrict__ bins, long long S,
     const int8_t *__restrict__ bins_fm, long long NT,
-    const int *__restrict__ feats, uint8_t *flags, int *tile_cnt) {
+    const int *__restrict__ feats, uint8_t *flags, int *tile_cnt, long long nloc) {
     // (split feature or -1, split bin) of the level's nodes, cached once per CTA
     constexpr int CACHE = 1024, IPT = PART_TILE / PART_THREADS;
     __shared__ int2 s_nd[CACHE];
@@ -1083,7 +1112,7 @@ __global__ void __launch_bounds__(PART_THREADS) k_flags(
     for (int u = 0; u < IPT; ++u) {
         const long long p = t0 + threadIdx.x + (long long)u * PART_THREADS;
         const bool ok = p < nact;
-        nd[u] = ok ? (posnode ? posnode[p] : 0) : -1;
+        nd[u] = ok ? (posnode ? posnode[p] : (int)(p / nloc)) : -1;  // level 0: tree t's root owns [tN, (t+1)N)
         row[u] = ok ? order[p] : 0;
     }
     int8_t bv[IPT];
@@ -1210,14 +1239,15 @@ __global__ void __launch_bounds__(1024) k_node_offsets(wgb_node *__restrict__ lv
 struct ScatterNode {
     float leaf;
     int lstart, child, px, py, pz;  // part[n]: lefts before the node, start of its children, left count
+    int tree;                       // the node's tree in the batch (its output column is cls + tree)
 };
 
 __global__ void __launch_bounds__(PART_THREADS) k_scatter(
     const wgb_node *__restrict__ lvl, const int *nn_d, const int *nact_d, const int *__restrict__ order,
     const int *__restrict__ posnode, const uint8_t *__restrict__ flags,
     const int *__restrict__ tile_off, const int4 *__restrict__ part, int *__restrict__ order_next,
-    int *__restrict__ posnode_next, float *__restrict__ pred, int K, int cls, float lr, long long N,
-    const wgb_node *__restrict__ last) {
+    int *__restrict__ posnode_next, float *__restrict__ pred, int K, int cls, float lr, long long npos,
+    long long nloc, const wgb_node *__restrict__ last) {
     constexpr int IPT = PART_TILE / PART_THREADS;  // 8 consecutive positions per thread
     constexpr int CACHE = 512;                     // nodes whose records are cached per CTA
     __shared__ ScatterNode s_nc[CACHE];
@@ -1225,7 +1255,7 @@ __global__ void __launch_bounds__(PART_THREADS) k_scatter(
     for (int i = threadIdx.x; i < min(nnd, CACHE); i += PART_THREADS) {
         const wgb_node &nd = lvl[i];
         const int4 pr = nd.fpos >= 0 ? part[i] : make_int4(0, 0, 0, 0);
-        s_nc[i] = ScatterNode{nd.leaf, nd.lstart, nd.child, pr.x, pr.y, pr.z};
+        s_nc[i] = ScatterNode{nd.leaf, nd.lstart, nd.child, pr.x, pr.y, pr.z, node_tree(nd.built)};
     }
     const int nact = *nact_d;
     const long long p0 = (long long)blockIdx.x * PART_TILE + threadIdx.x * IPT;
@@ -1247,7 +1277,7 @@ __global__ void __launch_bounds__(PART_THREADS) k_scatter(
             nid[4] = d.x; nid[5] = d.y; nid[6] = d.z; nid[7] = d.w;
         } else {
 #pragma unroll
-            for (int u = 0; u < IPT; ++u) nid[u] = 0;
+            for (int u = 0; u < IPT; ++u) nid[u] = (int)((p0 + u) / nloc);
         }
     } else {
 #pragma unroll
@@ -1255,7 +1285,7 @@ __global__ void __launch_bounds__(PART_THREADS) k_scatter(
             const bool ok = p0 + u < nact;
             f[u] = ok ? flags[p0 + u] : 3;
             row[u] = ok ? order[p0 + u] : 0;
-            nid[u] = ok && posnode ? posnode[p0 + u] : 0;
+            nid[u] = !ok ? 0 : (posnode ? posnode[p0 + u] : (int)((p0 + u) / nloc));
         }
     }
     int c = 0;
@@ -1286,10 +1316,10 @@ __global__ void __launch_bounds__(PART_THREADS) k_scatter(
         } else {
             const wgb_node &g = lvl[n];
             const int4 pr = g.fpos >= 0 ? part[n] : make_int4(0, 0, 0, 0);
-            nd = ScatterNode{g.leaf, g.lstart, g.child, pr.x, pr.y, pr.z};
+            nd = ScatterNode{g.leaf, g.lstart, g.child, pr.x, pr.y, pr.z, node_tree(g.built)};
         }
         if (f[u] == 2) {
-            float *pp = pred + (long long)row[u] * K + cls;
+            float *pp = pred + (long long)row[u] * K + cls + nd.tree;
             *pp = __fadd_rn(*pp, __fmul_rn(lr, nd.leaf));
         } else {
             const int lb = lp - nd.px;  // lefts before p inside the node
@@ -1302,9 +1332,9 @@ __global__ void __launch_bounds__(PART_THREADS) k_scatter(
                 child = nd.child + 1;
             }
             if (last) {  // the children are the tree's last level: their leaf updates
-                float *pp = pred + (long long)row[u] * K + cls;
+                float *pp = pred + (long long)row[u] * K + cls + nd.tree;
                 *pp = __fadd_rn(*pp, __fmul_rn(lr, last[child].leaf));
-            } else if (np >= 0 && np < N) {  // always true for consistent offsets; guards memory
+            } else if (np >= 0 && np < npos) {  // always true for consistent offsets; guards memory
                 order_next[np] = row[u];
                 posnode_next[np] = child;
             }
@@ -1318,7 +1348,12 @@ __global__ void __launch_bounds__(PART_THREADS) k_scatter(
 // ====================================================================== //
 
 static inline long long *LL(int64_t *p) { return reinterpret_cast<long long *>(p); }
-static inline wgb_node *level_nodes(const wgb_ws *ws, int d) { return ws->nodes + ((1 << d) - 1); }
+// trees grown together (a multiclass round: one per class); levels hold
+// ntree << d node records
+static inline int ws_ntree(const wgb_ws *ws) { return ws->ntree > 1 ? ws->ntree : 1; }
+static inline wgb_node *level_nodes(const wgb_ws *ws, int d) {
+    return ws->nodes + (long long)ws_ntree(ws) * ((1 << d) - 1);
+}
 static inline const int *level_order(const wgb_ws *ws, int d) {
     return d == 0 ? ws->root_order : ws->order[(d - 1) & 1];
 }
@@ -1326,8 +1361,8 @@ static inline const int *level_posnode(const wgb_ws *ws, int d) {
     return d == 0 ? nullptr : ws->posnode[(d - 1) & 1];
 }
 // Histogram pool: one int64 region per slot, [sums E*k*(B+1)][counts E*k*(B+1)][2 spare];
-// slot 0's first spare cell carries the root's sum of q through the level-0
-// reduction, so one collective per level covers sums, counts and the root.
+// root slot t's first spare cell carries tree t's root sum of q through the
+// level-0 reduction, so one collective per level covers sums, counts and roots.
 static inline long long hist_cells(const wgb_ws *ws) { return (long long)ws->E * ws->k * (ws->B + 1); }
 static inline long long slot_elems(const wgb_ws *ws) { return 2 * hist_cells(ws) + 2; }
 
@@ -1358,6 +1393,13 @@ void wgb_built_slots(int32_t d, int32_t *first, int32_t *count) {
         *first = 1 << (d - 1);
         *count = 1 << (d - 1);
     }
+}
+
+void wgb_level_slots(const wgb_ws *ws, int32_t d, int32_t *first, int32_t *count) {
+    wgb_built_slots(d, first, count);
+    const int nt = ws ? ws_ntree(ws) : 1;
+    *first *= nt;
+    *count *= nt;
 }
 
 int64_t wgb_era_mean_plan(int32_t E, int64_t M, int32_t num_sms, int32_t max_threads_per_sm,
@@ -1400,13 +1442,16 @@ static int check_ws(const wgb_ws *ws) {
     WGB_CHECK_ARG(ws->N >= 0 && ws->N < (1ll << 31), "rows per rank must be < 2^31");
     WGB_CHECK_ARG(ws->S >= ws->F && ws->S % 4 == 0, "bins row stride must be >= F and a multiple of 4");
     WGB_CHECK_ARG(ws->hist_ew >= 0, "hist_ew must be >= 0");
+    WGB_CHECK_ARG(ws->ntree >= 0 && ws->cls >= 0 && ws->cls + ws_ntree(ws) <= ws->K,
+                  "trees cls .. cls + ntree - 1 must be output columns (< K)");
+    WGB_CHECK_ARG((long long)ws_ntree(ws) * ws->N < (1ll << 31), "ntree * rows per rank must be < 2^31");
     return WGB_OK;
 }
 
 int wgb_tree_reset(const wgb_ws *ws, void *stream) {
     int rc = check_ws(ws);
     if (rc) return rc;
-    k_reset<<<1, 1, 0, as_stream(stream)>>>(ws->maxabs, LL(ws->rootsum));
+    k_reset<<<1, 32, 0, as_stream(stream)>>>(ws->maxabs, LL(ws->rootsum), ws_ntree(ws));
     WGB_LAUNCHED("k_reset");
     return WGB_OK;
 }
@@ -1415,8 +1460,8 @@ int wgb_tree_residual(const wgb_ws *ws, void *stream) {
     int rc = check_ws(ws);
     if (rc) return rc;
     if (ws->N == 0) return WGB_OK;
-    k_residual<<<grid_for(ws->N, 256), 256, 0, as_stream(stream)>>>(ws->y, ws->pred, ws->K, ws->cls,
-                                                                     ws->g, ws->N, ws->maxabs);
+    const dim3 grid((unsigned)grid_for(ws->N, 256, 148 * 16 / ws_ntree(ws) + 1), (unsigned)ws_ntree(ws));
+    k_residual<<<grid, 256, 0, as_stream(stream)>>>(ws->y, ws->pred, ws->K, ws->cls, ws->g, ws->N, ws->maxabs);
     WGB_LAUNCHED("k_residual");
     return WGB_OK;
 }
@@ -1424,8 +1469,8 @@ int wgb_tree_residual(const wgb_ws *ws, void *stream) {
 int wgb_tree_quantize(const wgb_ws *ws, void *stream) {
     int rc = check_ws(ws);
     if (rc) return rc;
-    k_quantize<<<grid_for(ws->N, 256), 256, 0, as_stream(stream)>>>(ws->g, ws->qg, ws->N, ws->maxabs,
-                                                                     ws->shift, LL(ws->rootsum));
+    const dim3 grid((unsigned)grid_for(ws->N, 256, 148 * 16 / ws_ntree(ws) + 1), (unsigned)ws_ntree(ws));
+    k_quantize<<<grid, 256, 0, as_stream(stream)>>>(ws->g, ws->qg, ws->N, ws->maxabs, ws->shift, LL(ws->rootsum));
     WGB_LAUNCHED("k_quantize");
     return WGB_OK;
 }
@@ -1433,7 +1478,7 @@ int wgb_tree_quantize(const wgb_ws *ws, void *stream) {
 int wgb_tree_root(const wgb_ws *ws, void *stream) {
     int rc = check_ws(ws);
     if (rc) return rc;
-    k_root<<<1, 1, 0, as_stream(stream)>>>(ws->nodes, ws->nn, ws->nact, ws->D, ws->N, ws->N_global);
+    k_root<<<1, 32, 0, as_stream(stream)>>>(ws->nodes, ws->nn, ws->nact, ws->D, ws->N, ws->N_global, ws_ntree(ws));
     WGB_LAUNCHED("k_root");
     return WGB_OK;
 }
@@ -1451,11 +1496,13 @@ int wgb_level_hist(const wgb_ws *ws, int32_t d, void *stream) {
     WGB_CHECK_ARG(d >= 0 && d < ws->D, "level %d out of range", d);
     cudaStream_t st = as_stream(stream);
     int first, count;
-    wgb_built_slots(d, &first, &count);
+    wgb_level_slots(ws, d, &first, &count);
     const long long se = slot_elems(ws), nc = hist_cells(ws);
     WGB_CUDA(cudaMemsetAsync(ws->hg + (long long)first * se, 0, sizeof(int64_t) * se * count, st));
-    if (d == 0)  // this rank's root sum rides along with the level-0 reduction
-        WGB_CUDA(cudaMemcpyAsync(ws->hg + 2 * nc, ws->rootsum, sizeof(int64_t), cudaMemcpyDeviceToDevice, st));
+    if (d == 0) {  // this rank's root sums ride along with the level-0 reduction
+        k_root_cells<<<1, 32, 0, st>>>(LL(ws->hg), LL(ws->rootsum), se, nc, ws_ntree(ws));
+        WGB_LAUNCHED("k_root_cells");
+    }
     wgb_node *lvl = level_nodes(ws, d);
     if (d == 0) {  // later levels' chunk lists are planned by the previous level's partition
         k_chunk_plan<<<1, 1024, 0, st>>>(lvl, ws->nn + d, reinterpret_cast<int4 *>(ws->chunks),
@@ -1463,7 +1510,7 @@ int wgb_level_hist(const wgb_ws *ws, int32_t d, void *stream) {
         WGB_LAUNCHED("k_chunk_plan");
     }
     if (ws->N == 0) return WGB_OK;
-    long long max_chunks = (ws->N + HIST_R - 1) / HIST_R + count;
+    long long max_chunks = ((long long)ws_ntree(ws) * ws->N + HIST_R - 1) / HIST_R + count;
     if (max_chunks > ws->chunk_cap) max_chunks = ws->chunk_cap;
     const int *ord = level_order(ws, d);
     cudaError_t e = launch_hist((int)max_chunks, ws->bins, ws->S, ws->F, ord, ws->qg, nullptr, nullptr,
@@ -1490,9 +1537,9 @@ int wgb_level_split(const wgb_ws *ws, int32_t d, void *stream) {
     const long long se = slot_elems(ws), nc = hist_cells(ws);
     long long *hg = LL(ws->hg), *hc = hg + nc;
     wgb_node *lvl = level_nodes(ws, d);
-    const int cap = 1 << d;
+    const int cap = ws_ntree(ws) << d;
     if (d == 0) {
-        k_root_total<<<1, 1, 0, st>>>(ws->nodes, hg + 2 * nc, ws->shift);
+        k_root_total<<<1, 32, 0, st>>>(ws->nodes, hg, se, nc, ws->shift, ws_ntree(ws));
         WGB_LAUNCHED("k_root_total");
     }
     // (from level 1 on, the split kernels first turn each unbuilt node's
@@ -1534,10 +1581,10 @@ int wgb_level_split(const wgb_ws *ws, int32_t d, void *stream) {
 #undef WGB_SPLIT_ERAS
         WGB_LAUNCHED("k_split_eras");
     }
-    float *eg = ws->era_gain + (long long)((1 << d) - 1) * ws->E;
+    float *eg = ws->era_gain + (long long)ws_ntree(ws) * ((1 << d) - 1) * ws->E;
     WGB_CHECK_ARG(ws->sync != nullptr, "workspace needs its sync counters");
-    k_split_final<<<cap, 256, 0, st>>>(lvl, level_nodes(ws, d + 1), ws->nn, d, hg, hc, se, ws->k, ws->E, ws->B,
-                                       ws->shift, ws->mcw, ws->eps, cand, nblk, eg, ws->sync);
+    k_split_final<<<cap, 256, 0, st>>>(lvl, level_nodes(ws, d + 1), ws->nn, d, ws_ntree(ws), hg, hc, se, ws->k,
+                                       ws->E, ws->B, ws->shift, ws->mcw, ws->eps, cand, nblk, eg, ws->sync);
     WGB_LAUNCHED("k_split_final");
     return WGB_OK;
 }
@@ -1563,12 +1610,13 @@ int wgb_level_partition(const wgb_ws *ws, int32_t d, void *stream) {
     if (ws->N == 0) return WGB_OK;
     cudaStream_t st = as_stream(stream);
     wgb_node *lvl = level_nodes(ws, d);
-    const int ntiles = (int)((ws->N + PART_TILE - 1) / PART_TILE);
+    const long long npos = (long long)ws_ntree(ws) * ws->N;  // positions: tree t's rows at level 0 are [tN, (t+1)N)
+    const int ntiles = (int)((npos + PART_TILE - 1) / PART_TILE);
     WGB_CHECK_ARG(ntiles <= ws->ntiles, "tile buffer too small");
     const int *ord = level_order(ws, d);
     const int *pn = level_posnode(ws, d);
     k_flags<<<ntiles, PART_THREADS, 0, st>>>(lvl, ws->nn + d, ws->nact + d, ord, pn, ws->bins, ws->S, ws->bins_fm,
-                                              (ws->N + 15) & ~15ll, ws->feats, ws->flags, ws->tile_cnt);
+                                              (ws->N + 15) & ~15ll, ws->feats, ws->flags, ws->tile_cnt, ws->N);
     WGB_LAUNCHED("k_flags");
     int4 *part = reinterpret_cast<int4 *>(ws->part);
     const bool last = d == ws->D - 1;
@@ -1579,7 +1627,7 @@ int wgb_level_partition(const wgb_ws *ws, int32_t d, void *stream) {
     WGB_LAUNCHED("k_node_offsets");
     k_scatter<<<ntiles, PART_THREADS, 0, st>>>(lvl, ws->nn + d, ws->nact + d, ord, pn, ws->flags, ws->tile_off, part,
                                                 ws->order[d & 1], ws->posnode[d & 1], ws->pred, ws->K,
-                                                ws->cls, ws->lr, ws->N, last ? level_nodes(ws, d + 1) : nullptr);
+                                                ws->cls, ws->lr, npos, ws->N, last ? level_nodes(ws, d + 1) : nullptr);
     WGB_LAUNCHED("k_scatter");
     return WGB_OK;
 }
