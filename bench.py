@@ -597,8 +597,12 @@ def run_config(args):
         with contextlib.redirect_stdout(io.StringIO()):
             mr = WarpGBM(**params)
             mr._hist_events = []
+            mr._split_events = []
             mr.fit(Xd, yd, era_id=erad)
         hist_ms = sum(a.elapsed_time(b) for a, b in mr._hist_events)
+        line["breakdown_ms"] = {"histogram_kernels": round(hist_ms, 1),
+                                "split_kernels": round(sum(a.elapsed_time(b) for a, b, _ in mr._split_events), 1),
+                                "partition_kernels": round(sum(b.elapsed_time(c) for _, b, c in mr._split_events), 1)}
         k = max(1, int(params["colsample_bytree"] * X.shape[1]))
         hb = hist_algorithmic_bytes(mr, X.shape[0], k, mr.num_eras, params["num_bins"])
         peak, peak_kind = peaks()
