@@ -314,6 +314,28 @@ int wgb_level_partition(const wgb_ws *ws, int32_t d, void *stream);
  * wgb_level_partition(D - 1)); validates the workspace. */
 int wgb_tree_finish(const wgb_ws *ws, void *stream);
 
+/* The whole per-tree sequence as stream work issued from C++: reset,
+ * residual (+ max |g| over ranks), quantise, root, and per level d < D the
+ * histogram build, its int64 SUM over ranks (when comm != NULL), the split
+ * search and the partition; then wgb_tree_finish.  Replaces the reference's
+ * per-node Python recursion (warpgbm/core.py:597-658, 692-744) and the
+ * per-level Python loop of a host driving the entry points above.  comm ==
+ * NULL: one rank. */
+typedef struct wgb_comm wgb_comm;
+int wgb_grow_tree(const wgb_ws *ws, wgb_comm *comm, void *stream);
+
+/* NCCL communicator of a row-sharded fit, owned by this library (NCCL's
+ * entry points are resolved from the libnccl.so.2 already loaded in the
+ * process).  Rank 0 makes the 128-byte id, the host distributes it, every
+ * rank calls wgb_comm_init (collective).  wgb_comm_allreduce sums int64
+ * (kind 0) or takes the max of float32 (kind 1) in place on `stream`. */
+int wgb_comm_unique_id(uint8_t *id128);
+int wgb_comm_init(int32_t rank, int32_t world, const uint8_t *id128,
+                  wgb_comm **out);
+int wgb_comm_destroy(wgb_comm *comm);
+int wgb_comm_allreduce(wgb_comm *comm, void *buf, int64_t count, int32_t kind,
+                       void *stream);
+
 /* Host -> device copy of `bytes` from pageable host memory, pipelined
  * through pinned staging buffers (parallel host copies overlapped with the
  * DMA, one cudaMemcpyAsync per 64 MiB chunk).  Returns once the source has

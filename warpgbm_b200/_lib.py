@@ -86,6 +86,11 @@ _SIGS = {
     "wgb_predict_packed": ([_p, _i64, _i64, _p, _p, _i32, _i32, _f32, _p, _p], _i32),
     "wgb_predict_heap": ([_p, _i64, _i64, _p, _i32, _i32, _i32, _f32, _p, _p], _i32),
     "wgb_h2d": ([_p, _p, _i64, _p], _i32),
+    "wgb_grow_tree": ([_p, _p, _p], _i32),
+    "wgb_comm_unique_id": ([_p], _i32),
+    "wgb_comm_init": ([_i32, _i32, _p, ctypes.POINTER(_p)], _i32),
+    "wgb_comm_destroy": ([_p], _i32),
+    "wgb_comm_allreduce": ([_p, _p, _i64, _i32, _p], _i32),
     "wgb_quantile_edges": ([_p, _i64, _i32, _i64, _p, _i32, _p, _p, _p], _i32),
 }
 
@@ -128,7 +133,8 @@ def check(rc: int, what: str = "") -> None:
 # kernels each entry point launches (bench.py reports the count it saw)
 _KERNELS = {
     "wgb_tree_reset": 1, "wgb_tree_residual": 1, "wgb_tree_quantize": 1, "wgb_tree_root": 1,
-    "wgb_level_hist": 2, "wgb_level_split": 2, "wgb_level_partition": 3, "wgb_tree_finish": 0, "wgb_bins_feature_major": 1, "wgb_prebinned_ingest": 1,
+    "wgb_level_hist": 2, "wgb_level_split": 2, "wgb_level_partition": 3, "wgb_tree_finish": 0,
+    "wgb_grow_tree": 0, "wgb_bins_feature_major": 1, "wgb_prebinned_ingest": 1,
     "wgb_bin_matrix": 1, "wgb_predict_packed": 1, "wgb_predict_heap": 1, "wgb_quantile_edges": 2, "wgb_compute_histogram3": 6, "wgb_compute_histogram3_noalloc": 6,
     "wgb_compute_split": 1, "wgb_custom_cuda_binner": 1, "wgb_predict_forest": 1,
 }

@@ -137,6 +137,45 @@ class _Comm:
         return [o[:c] for o, c in zip(outs, ns)]
 
 
+_NATIVE_COMMS = {}
+
+
+def native_comm(comm: _Comm, dev):
+    """The library's own NCCL communicator over the ranks of `comm` (cached
+    per process group), which wgb_grow_tree uses to sum each level's
+    histograms on the engine's stream; None for one rank or a gloo group."""
+    if not comm.on or comm.host_staging:
+        return None
+    import atexit
+    import ctypes
+    pg = comm.dist.group.WORLD
+    key = (id(pg), comm.rank, comm.world, str(dev))
+    h = _NATIVE_COMMS.get(key)
+    if h is None:
+        uid = torch.zeros(128, dtype=torch.uint8, device=dev)
+        if comm.rank == 0:
+            host = np.zeros(128, np.uint8)
+            _lib.call("wgb_comm_unique_id", host.ctypes.data)
+            uid.copy_(torch.from_numpy(host))
+        comm.bcast_(uid)
+        ids = np.ascontiguousarray(uid.cpu().numpy())
+        h = ctypes.c_void_p()
+        _lib.call("wgb_comm_init", comm.rank, comm.world, ids.ctypes.data, ctypes.byref(h))
+        _NATIVE_COMMS[key] = h
+        atexit.register(lambda hh=h: _lib.lib().wgb_comm_destroy(hh))
+    return h
+
+
+def level_launches(D: int, E: int) -> int:
+    """Kernels one tree (or one batch of trees) launches in wgb_grow_tree."""
+    n = 4                                            # reset, residual, quantize, root
+    for d in range(D):
+        n += (4 if d == 0 else 2) if E == 1 else (3 if d == 0 else 1)   # histogram (+ chunk plan, root cells)
+        n += 3 if d == 0 else 2                      # split (+ root totals), final
+        n += 3                                       # flags, offsets, scatter
+    return n
+
+
 def global_unique_eras(era: torch.Tensor, comm: _Comm):
     """torch.unique(era, return_inverse=True) over the union of all ranks'
     eras (core.py:540): sorted unique ids and the dense id of each local row."""
@@ -854,6 +893,7 @@ class WarpGBM(BaseEstimator, RegressorMixin):
             if ntree > 1:
                 root_order = root_order.repeat(ntree)
             ws = self._alloc_ws(N, F, k, E, K, ntree)
+            self._ncomm = native_comm(comm, dev)
             ws.bins, ws.root_order = bins.data_ptr(), root_order.data_ptr()
             ws.era = era_dense.data_ptr() if E > 1 else None
             ws.N_global = self._n_global
@@ -980,6 +1020,16 @@ class WarpGBM(BaseEstimator, RegressorMixin):
         comm = self._comm
         ws.cls = cls
         p = ctypes_ptr(ws)
+        instrumented = any(getattr(self, a, None) is not None
+                           for a in ("_hist_events", "_comm_events", "_split_events"))
+        if not instrumented and (not comm.on or self._ncomm is not None):
+            # the whole tree from C++ (levels, and the per-level NCCL sums)
+            _lib.call("wgb_grow_tree", p, self._ncomm, st())
+            _lib.LAUNCHES[0] += level_launches(self.max_depth, ws.E)
+            self._after_tree(ws, i, c)
+            return
+        # the same sequence level by level from Python (a gloo group, or the
+        # bench's per-level device timers)
         _lib.call("wgb_tree_reset", p, st())
         _lib.call("wgb_tree_residual", p, st())
         ctimer = getattr(self, "_comm_events", None)   # bench hook: device time of collectives
@@ -1026,6 +1076,9 @@ class WarpGBM(BaseEstimator, RegressorMixin):
                 s2.record()
                 stimer.append((s0, s1, s2))
         _lib.call("wgb_tree_finish", p, st())
+        self._after_tree(ws, i, c)
+
+    def _after_tree(self, ws, i, c):
         if getattr(self, "_record_residuals", False):  # test hook: residual of every tree
             g = self._t["g"][: ws.ntree * ws.N].view(ws.ntree, ws.N).cpu().numpy()
             self._residuals.extend(g[t].copy() for t in range(ws.ntree))

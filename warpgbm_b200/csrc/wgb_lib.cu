@@ -5,3 +5,4 @@
 #include "wgb_io.cu"
 #include "wgb_quantile.cu"
 #include "wgb_noalloc.cu"
+#include "wgb_comm.cu"
