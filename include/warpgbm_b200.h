@@ -324,6 +324,23 @@ int wgb_tree_finish(const wgb_ws *ws, void *stream);
 typedef struct wgb_comm wgb_comm;
 int wgb_grow_tree(const wgb_ws *ws, wgb_comm *comm, void *stream);
 
+/* Host-side decode of tree `root` of a batch of `ntree` trees in the
+ * engine's level-packed node records (a copy of ws->nodes, depth D) into
+ * pre-order arrays: packed[2i], packed[2i+1] = {feature, bin | right << 8}
+ * for a split, {-1, float bits of the leaf} for a leaf (the
+ * wgb_predict_packed format), leaf[i], samples[i] (row count of a leaf);
+ * feats maps feature positions to features.  When imp != NULL the tree's
+ * per-era split gains (era_gain, [ntree(2^D - 1)][E]) are added to imp
+ * [E][F] in pre-order, the order of the reference's depth-first growth
+ * (warpgbm/core.py:624-627); the nested-dict trees of core.py:597-658 are
+ * built from these arrays.  Returns the node count (<= cap) or a negative
+ * status.  Runs on the host; no device memory. */
+int64_t wgb_decode_tree(const wgb_node *nodes, int32_t D, int32_t ntree,
+                        int32_t root, const int32_t *feats,
+                        const float *era_gain, int32_t E, float *imp,
+                        int32_t F, int32_t *packed, float *leaf,
+                        int64_t *samples, int64_t cap);
+
 /* NCCL communicator of a row-sharded fit, owned by this library (NCCL's
  * entry points are resolved from the libnccl.so.2 already loaded in the
  * process).  Rank 0 makes the 128-byte id, the host distributes it, every

@@ -67,6 +67,52 @@ def test_vectorised_decode_matches_depth_first_walk(D, E, p):
         assert np.array_equal(imp, imp_ref)
 
 
+@pytest.mark.parametrize("D,E,p,ntree", [(1, 1, 1.0, 1), (5, 1, 0.8, 1), (10, 1, 0.97, 1), (8, 3, 0.7, 1),
+                                         (4, 1, 0.0, 1), (6, 1, 0.9, 5), (3, 2, 0.8, 3)])
+def test_library_decode_matches_numpy_decode(D, E, p, ntree):
+    """wgb_decode_tree (the library's host decode the fit uses) gives the
+    same pre-order arrays and the same fp32 importance sums as compact_tree
+    and the depth-first walk, for every tree of a batch grown together."""
+    import ctypes
+    rng = np.random.default_rng(D * 10 + ntree)
+    F = 40
+    feats = rng.permutation(F).astype(np.int32)
+    # a batch of ntree trees: level d of the batch = the trees' level-d records in tree order
+    recs = [_records(rng, D, E, F, p) for _ in range(ntree)]
+    levels, gl = [], []
+    for d in range(D + 1):
+        for t, (nodes, gains) in enumerate(recs):
+            lv = nodes[(1 << d) - 1:(1 << (d + 1)) - 1].copy()
+            lv["child"] = np.where(lv["fpos"] >= 0, lv["child"] + t * (1 << (d + 1)), lv["child"])
+            levels.append(lv)
+            if d < D:
+                gl.append(gains.reshape(-1, E)[(1 << d) - 1:(1 << (d + 1)) - 1])
+    batch = np.ascontiguousarray(np.concatenate(levels))
+    bgain = np.ascontiguousarray(np.concatenate(gl).reshape(-1).astype(np.float32))
+    cap = (1 << (D + 1)) - 1
+    L = _lib.lib()
+    for t, (nodes, gains) in enumerate(recs):
+        imp_ref = np.zeros((E, F), np.float32)
+        want = _walk(nodes, gains, feats, D, E, imp_ref)
+        packed = np.empty((cap, 2), np.int32)
+        leaf = np.empty(cap, np.float32)
+        samples = np.empty(cap, np.int64)
+        imp = np.zeros((E, F), np.float32)
+        n = L.wgb_decode_tree(batch.ctypes.data, D, ntree, t, feats.ctypes.data, bgain.ctypes.data, E,
+                              imp.ctypes.data, F, packed.ctypes.data, leaf.ctypes.data, samples.ctypes.data, cap)
+        assert n > 0
+        assert tree_dict(packed[:n], leaf[:n], samples[:n]) == want
+        assert np.array_equal(imp, imp_ref)
+        pk, lf, sm, *_ = compact_tree(batch, bgain, feats, D, E, ntree, t)
+        assert np.array_equal(pk, packed[:n]) and np.array_equal(sm, samples[:n])
+    # malformed records are rejected, not followed
+    bad = batch.copy()
+    bad["child"][0] = 1 << 20
+    bad["fpos"][0] = 0
+    assert L.wgb_decode_tree(bad.ctypes.data, D, ntree, 0, feats.ctypes.data, None, E, None, F,
+                             packed.ctypes.data, leaf.ctypes.data, samples.ctypes.data, cap) < 0
+
+
 def test_forest_dicts_built_on_first_access_and_packing_without_them():
     """fit() keeps compact pre-order arrays and a lazy marker; the nested-dict
     forest (the reference's format) is built only when `forest` is read, and

@@ -15,7 +15,7 @@ import sys
 HERE = os.path.dirname(os.path.abspath(__file__))
 CSRC = os.path.join(HERE, "csrc")
 LIB = os.path.join(HERE, "libwgb_b200.so")
-SOURCES = ["wgb_lib.cu", "wgb_engine.cu", "wgb_ops.cu", "wgb_io.cu", "wgb_quantile.cu", "wgb_noalloc.cu", "wgb_comm.cu", "wgb_common.cuh"]
+SOURCES = ["wgb_lib.cu", "wgb_engine.cu", "wgb_ops.cu", "wgb_io.cu", "wgb_quantile.cu", "wgb_noalloc.cu", "wgb_comm.cu", "wgb_decode.cu", "wgb_common.cuh"]
 
 NVCC_FLAGS = [
     "-gencode", "arch=compute_100a,code=sm_100a",

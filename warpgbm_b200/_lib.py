@@ -87,6 +87,7 @@ _SIGS = {
     "wgb_predict_heap": ([_p, _i64, _i64, _p, _i32, _i32, _i32, _f32, _p, _p], _i32),
     "wgb_h2d": ([_p, _p, _i64, _p], _i32),
     "wgb_grow_tree": ([_p, _p, _p], _i32),
+    "wgb_decode_tree": ([_p, _i32, _i32, _i32, _p, _p, _i32, _p, _i32, _p, _p, _p, _i64], _i64),
     "wgb_comm_unique_id": ([_p], _i32),
     "wgb_comm_init": ([_i32, _i32, _p, ctypes.POINTER(_p)], _i32),
     "wgb_comm_destroy": ([_p], _i32),

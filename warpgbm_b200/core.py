@@ -1004,6 +1004,7 @@ class WarpGBM(BaseEstimator, RegressorMixin):
                 if self.stop:
                     break
             self._finalize_records(classification)
+            self._flush_train_loss()
             self.feature_importance_ = self.per_era_feature_importance_.sum(axis=0)
             self._is_fitted = True
             if classification:
@@ -1102,15 +1103,23 @@ class WarpGBM(BaseEstimator, RegressorMixin):
     def _decode_tree(self, j, t=0, ntree=1):
         """Tree t of record j -> compact pre-order arrays; per-era importance
         of its splits accumulated in pre-order (core.py:624-627 adds them
-        while growing depth first, left before right)."""
+        while growing depth first, left before right).  Decoded on the host
+        by the library (wgb_decode_tree; compact_tree is the same in numpy)."""
         D, E = self.max_depth, self.num_eras
-        nodes = self._rec_nodes[j].numpy().view(_lib.NODE_DTYPE)
-        gains = self._rec_gain[j].numpy()[: ntree * ((1 << D) - 1) * E]
-        feats = self._rec_feats[j].numpy()
-        packed, leaf, samples, sp_pre, sp_feat, sp_gain = compact_tree(nodes, gains, feats, D, E, ntree, t)
-        if len(sp_feat):
-            np.add.at(self.per_era_feature_importance_, (slice(None), sp_feat), sp_gain.T)
-        return packed, leaf, samples
+        cap = (1 << (D + 1)) - 1
+        packed = np.empty((cap, 2), np.int32)
+        leaf = np.empty(cap, np.float32)
+        samples = np.empty(cap, np.int64)
+        imp = self.per_era_feature_importance_
+        if imp.dtype != np.float32 or not imp.flags.c_contiguous:
+            imp = self.per_era_feature_importance_ = np.ascontiguousarray(imp, np.float32)
+        n = _lib.lib().wgb_decode_tree(self._rec_nodes[j].data_ptr(), D, ntree, t,
+                                       self._rec_feats[j].data_ptr(), self._rec_gain[j].data_ptr(), E,
+                                       imp.ctypes.data, imp.shape[1], packed.ctypes.data, leaf.ctypes.data,
+                                       samples.ctypes.data, cap)
+        if n < 0:
+            _lib.check(-n, "wgb_decode_tree")
+        return packed[:n].copy(), leaf[:n].copy(), samples[:n].copy()
 
     def _drain_records(self, classification):
         """Decode the records whose device->host copies have landed, without
@@ -1184,11 +1193,15 @@ class WarpGBM(BaseEstimator, RegressorMixin):
         if self.eval_every_n_trees is None:
             return
         r = (self.Y_gpu - self._pred[:, 0])
-        s = torch.stack([(r * r).sum().double(), torch.tensor(float(r.numel()), dtype=torch.float64, device=r.device)])
-        self._comm.sum_(s)
-        train_loss = float((s[0] / s[1]).item()) if self._comm.on else ((r) ** 2).mean().item()
-        self.training_loss.append(train_loss)
+        if self._comm.on:
+            s = torch.stack([(r * r).sum().double(),
+                             torch.tensor(float(r.numel()), dtype=torch.float64, device=r.device)])
+            self._comm.sum_(s)
+            self._defer_train_loss(s[0] / s[1])
+        else:
+            self._defer_train_loss((r ** 2).mean())
         if i % self.eval_every_n_trees == 0:
+            train_loss = self._flush_train_loss()
             self._sync_records(False)
             self._advance_eval(i + 1)
             yt = self._gather_cat(self._Y_eval)
@@ -1211,11 +1224,11 @@ class WarpGBM(BaseEstimator, RegressorMixin):
             s = torch.stack([-torch.log(p).sum().double(),
                              torch.tensor(float(p.numel()), dtype=torch.float64, device=p.device)])
             self._comm.sum_(s)
-            train_loss = float((s[0] / s[1]).item())
+            self._defer_train_loss(s[0] / s[1])
         else:
-            train_loss = log_loss_torch(self.Y_gpu, probs).item()
-        self.training_loss.append(train_loss)
+            self._defer_train_loss(log_loss_torch(self.Y_gpu, probs))
         if i % self.eval_every_n_trees == 0:
+            train_loss = self._flush_train_loss()
             self._sync_records(True)
             self._advance_eval(i + 1)
             eval_probs = softmax(self._eval_pred, dim=1)
@@ -1232,6 +1245,18 @@ class WarpGBM(BaseEstimator, RegressorMixin):
                     self.stop = True
             print(f"🌲 Round {i+1}/{self.n_estimators} ({self.num_classes} trees) | "
                   f"Train LogLoss: {train_loss:.6f} | Eval {self.eval_metric}: {eval_loss:.6f}")
+
+    def _defer_train_loss(self, t):
+        """The training loss of a tree / round stays on the device until the
+        next eval point (or the end of the fit): no host sync per tree."""
+        self.__dict__.setdefault("_tl_pending", []).append(t.reshape(1).double())
+
+    def _flush_train_loss(self):
+        pend = self.__dict__.get("_tl_pending") or []
+        if pend:
+            self.training_loss.extend(torch.cat(pend).tolist())
+            pend.clear()
+        return self.training_loss[-1] if self.training_loss else float("nan")
 
     def _advance_eval(self, upto):
         """Add the trees [_eval_upto, upto) to the running eval prediction

@@ -6,3 +6,4 @@
 #include "wgb_quantile.cu"
 #include "wgb_noalloc.cu"
 #include "wgb_comm.cu"
+#include "wgb_decode.cu"
