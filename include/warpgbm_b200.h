@@ -199,6 +199,11 @@ typedef struct wgb_ws {
     /* per tree */
     const int32_t *feats;    /* [k] physical feature of each position         */
     int32_t *kpos;           /* [F] position of each physical feature or -1   */
+    int8_t *bins_sub;        /* [N][S_sub] the tree's k features in position  */
+                             /*   order (wgb_tree_subset), or NULL: the       */
+                             /*   histograms then read `bins` through kpos    */
+    int32_t *kpos_sub;       /* [S_sub] j for j < k, -1 past k                 */
+    int64_t S_sub;           /* row stride of bins_sub (k rounded up to 32)   */
     /* row order per level (ping-pong) */
     int32_t *order[2];       /* [T*N]                                         */
     int32_t *posnode[2];     /* [T*N] node index (within level) per position  */
@@ -256,6 +261,11 @@ typedef struct wgb_ws {
 int wgb_tree_residual(const wgb_ws *ws, void *stream);
 /* Zero the per-tree scalars (maxabs, rootsum). */
 int wgb_tree_reset(const wgb_ws *ws, void *stream);
+/* Per tree, when ws->bins_sub != NULL: bins_sub[r][j] = bins[r][feats[j]]
+ * for the tree's k feature positions (padding 0) and kpos_sub, so that the
+ * level histograms read k bytes per row and update k features instead of
+ * all F (colsample_bytree < 1, warpgbm/core.py:721-722). */
+int wgb_tree_subset(const wgb_ws *ws, void *stream);
 /* Quantise g (shift from *maxabs, which must already be the global max),
  * sum q over local rows into *rootsum. */
 int wgb_tree_quantize(const wgb_ws *ws, void *stream);

@@ -38,7 +38,7 @@ class WgbWs(ctypes.Structure):
     _fields_ = [
         ("bins", _p), ("bins_fm", _p), ("era", _p), ("root_order", _p), ("y", _p), ("pred", _p),
         ("g", _p), ("qg", _p),
-        ("feats", _p), ("kpos", _p),
+        ("feats", _p), ("kpos", _p), ("bins_sub", _p), ("kpos_sub", _p), ("S_sub", _i64),
         ("order", _p * 2), ("posnode", _p * 2), ("flags", _p),
         ("tile_cnt", _p), ("tile_off", _p), ("part", _p),
         ("hg", _p),
@@ -72,6 +72,7 @@ _SIGS = {
     "wgb_tree_residual": ([_p, _p], _i32),
     "wgb_tree_reset": ([_p, _p], _i32),
     "wgb_tree_quantize": ([_p, _p], _i32),
+    "wgb_tree_subset": ([_p, _p], _i32),
     "wgb_tree_root": ([_p, _p], _i32),
     "wgb_level_hist": ([_p, _i32, _p], _i32),
     "wgb_built_slots": ([_i32, ctypes.POINTER(_i32), ctypes.POINTER(_i32)], None),
@@ -133,7 +134,7 @@ def check(rc: int, what: str = "") -> None:
 
 # kernels each entry point launches (bench.py reports the count it saw)
 _KERNELS = {
-    "wgb_tree_reset": 1, "wgb_tree_residual": 1, "wgb_tree_quantize": 1, "wgb_tree_root": 1,
+    "wgb_tree_reset": 1, "wgb_tree_residual": 1, "wgb_tree_subset": 1, "wgb_tree_quantize": 1, "wgb_tree_root": 1,
     "wgb_level_hist": 2, "wgb_level_split": 2, "wgb_level_partition": 3, "wgb_tree_finish": 0,
     "wgb_grow_tree": 0, "wgb_bins_feature_major": 1, "wgb_prebinned_ingest": 1,
     "wgb_bin_matrix": 1, "wgb_predict_packed": 1, "wgb_predict_heap": 1, "wgb_quantile_edges": 2, "wgb_compute_histogram3": 6, "wgb_compute_histogram3_noalloc": 6,

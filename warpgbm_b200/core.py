@@ -898,6 +898,15 @@ class WarpGBM(BaseEstimator, RegressorMixin):
             ws.era = era_dense.data_ptr() if E > 1 else None
             ws.N_global = self._n_global
             keep = [bins, root_order, era_dense]
+            # with colsample_bytree < 1 each tree gets its k features as their own
+            # matrix (wgb_tree_subset): the histograms then read and update k
+            # features per row instead of all F
+            S_sub = _round_up(k, 32)
+            if k < F and N and N * S_sub < 0.25 * torch.cuda.mem_get_info(dev)[0]:
+                bins_sub = torch.empty(N * S_sub, dtype=torch.int8, device=dev)
+                kpos_sub = torch.empty(S_sub, dtype=torch.int32, device=dev)
+                ws.bins_sub, ws.kpos_sub, ws.S_sub = bins_sub.data_ptr(), kpos_sub.data_ptr(), S_sub
+                keep += [bins_sub, kpos_sub]
             # feature-major copy for the partition's bin reads, when it fits
             NT = (N + 15) // 16 * 16
             if N and F * NT < 0.25 * torch.cuda.mem_get_info(dev)[0]:
@@ -1043,6 +1052,7 @@ class WarpGBM(BaseEstimator, RegressorMixin):
                 c1.record()
                 ctimer.append((c0, c1))
         _lib.call("wgb_tree_quantize", p, st())
+        _lib.call("wgb_tree_subset", p, st())
         _lib.call("wgb_tree_root", p, st())
         P = 2 * ws.E * ws.k * (ws.B + 1) + 2
         wsp = ctypes_ptr(ws)

@@ -130,6 +130,7 @@ int wgb_grow_tree(const wgb_ws *ws, wgb_comm *comm, void *stream) {
     const int nt = ws->ntree > 1 ? ws->ntree : 1;
     if (comm) WGB_STEP(wgb_comm_allreduce(comm, ws->maxabs, nt, 1, stream));
     WGB_STEP(wgb_tree_quantize(ws, stream));
+    WGB_STEP(wgb_tree_subset(ws, stream));
     WGB_STEP(wgb_tree_root(ws, stream));
     const long long P = 2ll * ws->E * ws->k * (ws->B + 1) + 2;
     for (int d = 0; d < ws->D; ++d) {

@@ -1343,6 +1343,35 @@ __global__ void __launch_bounds__(PART_THREADS) k_scatter(
     }
 }
 
+// The tree's feature subset as its own bin matrix: out[r][j] = bins[r][feats[j]]
+// (j < k; padding bytes 0) and kpos_out[j] = j (-1 past k).  A block takes 16
+// rows; the row bytes it gathers sit in L1, the writes are whole rows.
+__global__ void __launch_bounds__(256) k_bins_subset(const int8_t *__restrict__ bins, long long N, long long S,
+                                                     const int *__restrict__ feats, int k, int8_t *__restrict__ out,
+                                                     long long So, int *__restrict__ kpos_out) {
+    extern __shared__ int s_feat[];
+    for (int j = threadIdx.x; j < So; j += blockDim.x) {
+        s_feat[j] = j < k ? feats[j] : -1;
+        if (blockIdx.x == 0) kpos_out[j] = j < k ? j : -1;
+    }
+    __syncthreads();
+    const long long r0 = (long long)blockIdx.x * 16;
+    const int words = (int)(So / 4);
+    for (int t = threadIdx.x; t < 16 * words; t += blockDim.x) {
+        const long long r = r0 + t / words;
+        if (r >= N) break;
+        const int j0 = (t % words) * 4;
+        const int8_t *src = bins + r * S;
+        uint32_t w = 0;
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+            const int f = s_feat[j0 + u];
+            if (f >= 0) w |= (uint32_t)(uint8_t)__ldg(src + f) << (8 * u);
+        }
+        *reinterpret_cast<uint32_t *>(out + r * So + j0) = w;
+    }
+}
+
 // ====================================================================== //
 // host side                                                              //
 // ====================================================================== //
@@ -1475,6 +1504,22 @@ int wgb_tree_quantize(const wgb_ws *ws, void *stream) {
     return WGB_OK;
 }
 
+int wgb_tree_subset(const wgb_ws *ws, void *stream) {
+    int rc = check_ws(ws);
+    if (rc) return rc;
+    if (!ws->bins_sub) return WGB_OK;
+    WGB_CHECK_ARG(ws->kpos_sub && ws->S_sub >= ws->k && ws->S_sub % 32 == 0, "bins_sub needs kpos_sub and a stride "
+                  "S_sub >= k, a multiple of 32");
+    if (ws->N == 0) return WGB_OK;
+    const size_t sm = (size_t)ws->S_sub * sizeof(int);
+    WGB_CUDA(cudaFuncSetAttribute(k_bins_subset, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm));
+    k_bins_subset<<<(unsigned)((ws->N + 15) / 16), 256, sm, as_stream(stream)>>>(ws->bins, ws->N, ws->S, ws->feats,
+                                                                                ws->k, ws->bins_sub, ws->S_sub,
+                                                                                ws->kpos_sub);
+    WGB_LAUNCHED("k_bins_subset");
+    return WGB_OK;
+}
+
 int wgb_tree_root(const wgb_ws *ws, void *stream) {
     int rc = check_ws(ws);
     if (rc) return rc;
@@ -1513,12 +1558,18 @@ int wgb_level_hist(const wgb_ws *ws, int32_t d, void *stream) {
     long long max_chunks = ((long long)ws_ntree(ws) * ws->N + HIST_R - 1) / HIST_R + count;
     if (max_chunks > ws->chunk_cap) max_chunks = ws->chunk_cap;
     const int *ord = level_order(ws, d);
-    cudaError_t e = launch_hist((int)max_chunks, ws->bins, ws->S, ws->F, ord, ws->qg, nullptr, nullptr,
-                                ws->E > 1 ? ws->era : nullptr, ws->kpos, ws->k, ws->E, ws->B, ws->hist_ew,
+    // the tree's own feature matrix when there is one (k columns in position order)
+    const bool sub = ws->bins_sub != nullptr;
+    const int8_t *hb = sub ? ws->bins_sub : ws->bins;
+    const long long hS = sub ? ws->S_sub : ws->S;
+    const int hF = sub ? ws->k : ws->F;
+    const int *hkpos = sub ? ws->kpos_sub : ws->kpos;
+    cudaError_t e = launch_hist((int)max_chunks, hb, hS, hF, ord, ws->qg, nullptr, nullptr,
+                                ws->E > 1 ? ws->era : nullptr, hkpos, ws->k, ws->E, ws->B, ws->hist_ew,
                                 ws->regular != 0, reinterpret_cast<const int4 *>(ws->chunks), ws->nchunks,
                                 lvl, LL(ws->hg), LL(ws->hg) + nc, se, ws->N, st,
                                 ws->E == 1 && ws->part_hist &&
-                                        ws->part_hist_elems >= wgb_hist_part_elems(ws->S, ws->F, ws->B, max_chunks)
+                                        ws->part_hist_elems >= wgb_hist_part_elems(hS, hF, ws->B, max_chunks)
                                     ? reinterpret_cast<uint2 *>(ws->part_hist)
                                     : nullptr);
     if (e != cudaSuccess) {
