@@ -835,69 +835,23 @@ __global__ void __launch_bounds__(256) k_split_eras(
             for (int t = 0; t < IPT; ++t) acc[t] = __fadd_rn(stk[(sp * IPT + t) * 256 + threadIdx.x], acc[t]);
         }
     };
-    // For up to 8 split points the rows of a warp's next era are loaded into
-    // registers before the current batch's program runs, so their latency
-    // overlaps it (CPL cells per lane: 32 features x at most 10 bins / 32).
-    constexpr bool PIPE = NB <= 8;
-    constexpr int CPL = PIPE ? (FB * (NB + 2) + 31) / 32 : 1;
-    long long rg[CPL], rcn[CPL], rbg[CPL], rbc[CPL];
-    long long rbase = 0;
-    auto load = [&](int e) {
-        rbase = slot * slot_elems + ((long long)e * k + j0) * B1;
-        const long long bbase = bslot * slot_elems + ((long long)e * k + j0) * B1;
-#pragma unroll
-        for (int i = 0; i < CPL; ++i) {
-            const int t = lane + 32 * i;
-            if (t < nf * B1) {
-                rg[i] = hg[rbase + t];
-                rcn[i] = hc[rbase + t];
-                if (!built) {
-                    rbg[i] = hg[bbase + t];
-                    rbc[i] = hc[bbase + t];
-                }
-            }
-        }
-    };
-    auto store = [&]() {
-#pragma unroll
-        for (int i = 0; i < CPL; ++i) {
-            const int t = lane + 32 * i;
-            if (t < nf * B1) {
-                const int f = t / B1, b = t - f * B1;
-                long long gv = rg[i], cv = rcn[i];
-                if (!built) {  // sibling = parent - built sibling, written back in place
-                    gv -= rbg[i];
-                    cv -= rbc[i];
-                    hg[rbase + t] = gv;
-                    hc[rbase + t] = cv;
-                }
-                stg[f * B1p + b] = __fmul_rn(__ll2float_rn(gv), inv);
-                stg[(FB + f) * B1p + b] = __ll2float_rn(cv);
-            }
-        }
-    };
-    if (PIPE && warp < min(EB, E)) load(sched[warp]);
     for (int e0 = 0; e0 < E; e0 += EB) {
         const int ne = min(EB, E - e0);
         if (warp < ne) {
-            if (PIPE) {
-                store();
-            } else {
-                const int e = sched[e0 + warp];
-                const long long base = slot * slot_elems + ((long long)e * k + j0) * B1;
-                const long long bbase = bslot * slot_elems + ((long long)e * k + j0) * B1;
-                for (int t = lane; t < nf * B1; t += 32) {
-                    const int f = t / B1, b = t - f * B1;
-                    long long gv = hg[base + t], cv = hc[base + t];
-                    if (!built) {  // sibling = parent - built sibling, written back in place
-                        gv -= hg[bbase + t];
-                        cv -= hc[bbase + t];
-                        hg[base + t] = gv;
-                        hc[base + t] = cv;
-                    }
-                    stg[f * B1p + b] = __fmul_rn(__ll2float_rn(gv), inv);
-                    stg[(FB + f) * B1p + b] = __ll2float_rn(cv);
+            const int e = sched[e0 + warp];
+            const long long base = slot * slot_elems + ((long long)e * k + j0) * B1;
+            const long long bbase = bslot * slot_elems + ((long long)e * k + j0) * B1;
+            for (int t = lane; t < nf * B1; t += 32) {
+                const int f = t / B1, b = t - f * B1;
+                long long gv = hg[base + t], cv = hc[base + t];
+                if (!built) {  // sibling = parent - built sibling, written back in place
+                    gv -= hg[bbase + t];
+                    cv -= hc[bbase + t];
+                    hg[base + t] = gv;
+                    hc[base + t] = cv;
                 }
+                stg[f * B1p + b] = __fmul_rn(__ll2float_rn(gv), inv);
+                stg[(FB + f) * B1p + b] = __ll2float_rn(cv);
             }
             __syncwarp();
             if (lane < nf) {
@@ -918,7 +872,6 @@ __global__ void __launch_bounds__(256) k_split_eras(
             }
         }
         __syncthreads();
-        if (PIPE && e0 + EB + warp < E && warp < EB) load(sched[e0 + EB + warp]);  // the next batch
         for (int w = 0; w < ne; ++w) {
             uint8_t op;
             while (pc < nops && (op = __ldg(ops + pc++)) != ERA_ADD) step(op);
