@@ -574,13 +574,14 @@ static cudaError_t launch_hist(int grid_x, const int8_t *bins, long long S, int 
 // b = lane, lane + 32, ...  (one gain per lane instead of B-1 per thread:
 // a level with one node still fills the GPU).  A node whose histogram was
 // not built (the larger child, core.py:636-643) first becomes parent -
-// built sibling, written back in place of the parent.  Block arg-max ->
-// cand[node][blk].
+// built sibling, written back in place of the parent unless this is the
+// tree's last split level (its children are leaves; nothing reads it).
+// Block arg-max -> cand[node][blk].
 template <int NBW>  // split points per lane: ceil((B-1) / 32)
 __global__ void __launch_bounds__(SPLIT_WARPS * 32) k_split(
     const wgb_node *__restrict__ lvl, const int *nn_d, long long *hg, long long *hc, long long slot_elems,
     int k, int B, const int *shift,
-    float mcw, float eps, float msg, int4 *cand, int nblk, float *crit_out) {
+    float mcw, float eps, float msg, int4 *cand, int nblk, float *crit_out, bool writeback) {
     __shared__ float sG[SPLIT_WARPS][32 * NBW + 1], sH[SPLIT_WARPS][32 * NBW + 1];
     __shared__ Key s_k[SPLIT_WARPS];
     const int n = blockIdx.x / nblk, jb = blockIdx.x - n * nblk;  // node, feature block
@@ -605,8 +606,10 @@ __global__ void __launch_bounds__(SPLIT_WARPS * 32) k_split(
             for (int b = lane; b <= B; b += 32) {
                 const long long gv = hg[off + b] - hg[boff + b];
                 const long long cv = hc[off + b] - hc[boff + b];
-                hg[off + b] = gv;
-                hc[off + b] = cv;
+                if (writeback) {
+                    hg[off + b] = gv;
+                    hc[off + b] = cv;
+                }
                 if (b < B) {
                     sG[warp][b] = __fmul_rn(__ll2float_rn(gv), inv);
                     sH[warp][b] = __ll2float_rn(cv);
@@ -796,7 +799,8 @@ __global__ void __launch_bounds__(256) k_split_eras(
     const wgb_node *__restrict__ lvl, const int *nn_d, long long *hg, long long *hc, long long slot_elems,
     int k, int E, int B, const int *shift,
     float mcw, float eps, float msg, float factor, const int *__restrict__ sched,
-    const uint8_t *__restrict__ ops, int nops, int depth, int4 *cand, int nblk, float *crit_out) {
+    const uint8_t *__restrict__ ops, int nops, int depth, int4 *cand, int nblk, float *crit_out,
+    bool writeback) {
     constexpr int FB = EraSplitShape<NB>::FB, IPT = EraSplitShape<NB>::IPT, EB = SPLIT_ERA_EB;
     extern __shared__ float s_era_split[];
     const int n = blockIdx.x / nblk, jb = blockIdx.x - n * nblk;  // node, feature block
@@ -847,8 +851,10 @@ __global__ void __launch_bounds__(256) k_split_eras(
                 if (!built) {  // sibling = parent - built sibling, written back in place
                     gv -= hg[bbase + t];
                     cv -= hc[bbase + t];
-                    hg[base + t] = gv;
-                    hc[base + t] = cv;
+                    if (writeback) {  // (not at the last split level: its children are leaves)
+                        hg[base + t] = gv;
+                        hc[base + t] = cv;
+                    }
                 }
                 stg[f * B1p + b] = __fmul_rn(__ll2float_rn(gv), inv);
                 stg[(FB + f) * B1p + b] = __ll2float_rn(cv);
@@ -962,7 +968,8 @@ __device__ void plan_next_level(wgb_node *__restrict__ lvl, wgb_node *__restrict
 __global__ void __launch_bounds__(256) k_split_final(
     wgb_node *__restrict__ lvl, wgb_node *__restrict__ nxt, int *nn, int d, int ntree,
     const long long *__restrict__ hg, const long long *__restrict__ hc, long long slot_elems, int k, int E, int B,
-    const int *shift, float mcw, float eps, const int4 *__restrict__ cand, int nblk, float *era_gain, int *done) {
+    const int *shift, float mcw, float eps, const int4 *__restrict__ cand, int nblk, float *era_gain, int *done,
+    bool writeback) {
     const int n = blockIdx.x;
     __shared__ Key s_best, s_kw[8];
     __shared__ long long s_c[8], s_g[8];
@@ -999,26 +1006,32 @@ __global__ void __launch_bounds__(256) k_split_final(
             const int nb = B - 1, B1 = B + 1;
             const int fpos = best.idx / nb, bin = best.idx - fpos * nb;
             const long long slot = nd.slot;
+            // an unbuilt node's histogram is parent - built sibling; the split
+            // search wrote it back except at the last split level
+            const bool sub = !node_built(nd.built) && !writeback;
+            const long long bslot = sub ? lvl[n ^ 1].slot : 0;
             long long lc = 0, ls = 0;
             for (int e = threadIdx.x; e < E; e += blockDim.x) {
                 const long long off = slot * slot_elems + ((long long)e * k + fpos) * B1;
-                const long long *gp = hg + off;
-                const long long *cp = hc + off;
+                const long long boff = bslot * slot_elems + ((long long)e * k + fpos) * B1;
+                auto gq = [&](int b) { return hg[off + b] - (sub ? hg[boff + b] : 0ll); };
+                auto cq = [&](int b) { return hc[off + b] - (sub ? hc[boff + b] : 0ll); };
                 float GT = 0.0f, HT = 0.0f, GL = 0.0f, HL = 0.0f;
                 for (int b = 0; b < B; ++b) {
-                    float gv = __fmul_rn(__ll2float_rn(gp[b]), inv);
-                    float hv = __ll2float_rn(cp[b]);
+                    const long long gb = gq(b), cb = cq(b);
+                    float gv = __fmul_rn(__ll2float_rn(gb), inv);
+                    float hv = __ll2float_rn(cb);
                     GT = __fadd_rn(GT, gv);
                     HT = __fadd_rn(HT, hv);
                     if (b <= bin) {
                         GL = __fadd_rn(GL, gv);
                         HL = __fadd_rn(HL, hv);
-                        lc += cp[b];
-                        ls += gp[b];
+                        lc += cb;
+                        ls += gb;
                     }
                 }
-                lc += cp[B];
-                ls += gp[B];
+                lc += cq(B);
+                ls += gq(B);
                 era_gain[(long long)n * E + e] = eval_split(GL, HL, GT, HT, mcw, eps).gain;
             }
             lc = warp_sum(lc);
@@ -1604,7 +1617,8 @@ int wgb_level_split(const wgb_ws *ws, int32_t d, void *stream) {
         const unsigned g = (unsigned)nblk * (unsigned)cap;  // node-major blocks
 #define WGB_SPLIT_W(NBW_)                                                                                  \
     k_split<NBW_><<<g, SPLIT_WARPS * 32, 0, st>>>(lvl, ws->nn + d, hg, hc, se, ws->k, ws->B, ws->shift,   \
-                                                ws->mcw, ws->eps, ws->msg, cand, nblk, ws->crit_out)
+                                                ws->mcw, ws->eps, ws->msg, cand, nblk, ws->crit_out,      \
+                                                d < ws->D - 1)
         if (nb <= 32) WGB_SPLIT_W(1); else if (nb <= 64) WGB_SPLIT_W(2); else WGB_SPLIT_W(4);
 #undef WGB_SPLIT_W
         WGB_LAUNCHED("k_split");
@@ -1626,7 +1640,7 @@ int wgb_level_split(const wgb_ws *ws, int32_t d, void *stream) {
         k_split_eras<NB_><<<g, 256, sm, st>>>(lvl, ws->nn + d, hg, hc, se, ws->k, ws->E, ws->B, ws->shift,       \
                                               ws->mcw, ws->eps, ws->msg, ws->mean_factor, ws->era_sched,        \
                                               ws->era_ops, ws->era_nops, ws->era_depth, cand, nblk,             \
-                                              ws->crit_out);                                                    \
+                                              ws->crit_out, d < ws->D - 1);                                     \
     }
         if (nb <= 8) WGB_SPLIT_ERAS(8) else if (nb <= 32) WGB_SPLIT_ERAS(32) else WGB_SPLIT_ERAS(128)
 #undef WGB_SPLIT_ERAS
@@ -1635,7 +1649,8 @@ int wgb_level_split(const wgb_ws *ws, int32_t d, void *stream) {
     float *eg = ws->era_gain + (long long)ws_ntree(ws) * ((1 << d) - 1) * ws->E;
     WGB_CHECK_ARG(ws->sync != nullptr, "workspace needs its sync counters");
     k_split_final<<<cap, 256, 0, st>>>(lvl, level_nodes(ws, d + 1), ws->nn, d, ws_ntree(ws), hg, hc, se, ws->k,
-                                       ws->E, ws->B, ws->shift, ws->mcw, ws->eps, cand, nblk, eg, ws->sync);
+                                       ws->E, ws->B, ws->shift, ws->mcw, ws->eps, cand, nblk, eg, ws->sync,
+                                       d < ws->D - 1);
     WGB_LAUNCHED("k_split_final");
     return WGB_OK;
 }
