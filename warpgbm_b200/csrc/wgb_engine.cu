@@ -247,6 +247,37 @@ __device__ __forceinline__ void hist_row(const uint32_t (&w)[FPL / 4], uint32_t 
     }
 }
 
+// Fast-path row update (one era, every bin in [0, B)): one byte-permute
+// puts the bin into byte 1 of the lane's word offset (4*lane < 256), so the
+// cell address is a single instruction and an update is three: permute and
+// the two reductions.
+template <int FPL, int NSC, int J = 0>
+__device__ __forceinline__ void hist_row_fast(const uint32_t (&w)[FPL / 4], uint32_t sh0, uint32_t lane4,
+                                              uint32_t pa, uint32_t pb) {
+    if constexpr (J < FPL) {
+        constexpr int OFF = (J >> 1) * NSC * 256 + (J & 1) * 128;
+        constexpr int BOFF = (FPL / 2) * NSC * 256;
+        const uint32_t a = sh0 + __byte_perm(w[J >> 2], lane4, 0x7604u | ((J & 3) << 4));
+        red_shared<OFF>(a, pa);
+        red_shared<BOFF + OFF>(a, pb);
+        hist_row_fast<FPL, NSC, J + 1>(w, sh0, lane4, pa, pb);
+    }
+}
+
+// FPL bytes of one row at src (FPL-aligned)
+template <int FPL>
+__device__ __forceinline__ void load_row(const int8_t *src, uint32_t (&w)[FPL / 4]) {
+    if constexpr (FPL == 16) {
+        const uint4 v = __ldg(reinterpret_cast<const uint4 *>(src));
+        w[0] = v.x; w[1] = v.y; w[2] = v.z; w[3] = v.w;
+    } else if constexpr (FPL == 8) {
+        const uint2 v = __ldg(reinterpret_cast<const uint2 *>(src));
+        w[0] = v.x; w[1] = v.y;
+    } else {
+        w[0] = __ldg(reinterpret_cast<const uint32_t *>(src));
+    }
+}
+
 template <int FPL, int NT, int MINB, int NSC, int EWC, bool HAS_ERA, bool REGULAR>
 __global__ void __launch_bounds__(NT, MINB) k_hist(
     const int8_t *__restrict__ bins, long long S, int F, const int *__restrict__ order,
@@ -260,9 +291,14 @@ __global__ void __launch_bounds__(NT, MINB) k_hist(
     constexpr int NW = NT / 32;
     constexpr int WPR = FPL / 4;             // 32-bit words per lane per row
     constexpr int ESLOT = 2 * NSC * FT;      // words per era slot (A and B arrays)
+    constexpr int UF = 8;                    // rows per fast-path step per warp
+    constexpr int PADR = NW * UF;            // padding rows read past the chunk's end
     extern __shared__ uint32_t sh32[];       // [EWC][A|B][j/2][NSC][j%2][32]
     __shared__ int s_kp[FT];                 // lane-major: [j][lane]
-    __shared__ int2 s_rec[HIST_R];           // {row or -1, q}
+    // per chunk row: the row (0 when skipped or padding) and its two word
+    // increments; pa == 0 marks a skipped or padding row (pa >= 2^20 otherwise)
+    __shared__ int s_row[HIST_R + PADR];
+    __shared__ uint2 s_pq[HIST_R + PADR];
     __shared__ int s_era[HIST_ERA_R(HAS_ERA)];
     __shared__ int s_red[33];
 
@@ -286,17 +322,22 @@ __global__ void __launch_bounds__(NT, MINB) k_hist(
     if (!q) sc = pow2f(*shift);
     // rows outside [0, nrows) or eras outside [0, E) are skipped (only the
     // drop-in entry point can receive them; the engine never produces them)
-    for (int i = threadIdx.x; i < cnt; i += NT) {
-        int r = order[ch.y + i];
-        bool ok = r >= 0 && r < nrows;
-        int e = 0;
-        if (HAS_ERA && ok) {
-            e = era[r];
-            ok = e >= 0 && e < E;
+    for (int i = threadIdx.x; i < cnt + PADR; i += NT) {
+        int r = -1, e = 0;
+        bool ok = false;
+        if (i < cnt) {
+            r = order[ch.y + i];
+            ok = r >= 0 && r < nrows;
+            if (HAS_ERA && ok) {
+                e = era[r];
+                ok = e >= 0 && e < E;
+            }
         }
         const int qv = ok ? (q ? q[r] : __float2int_rn(__fmul_rn(g[r], sc))) : 0;
-        s_rec[i] = make_int2(ok ? r : -1, qv);
-        if (HAS_ERA) s_era[i] = ok ? e : INT_MAX;
+        s_row[i] = ok ? r : 0;
+        s_pq[i] = ok ? make_uint2((1u << HIST_CNT_SHIFT) | ((uint32_t)qv & HIST_LO_MASK), (uint32_t)(qv >> HIST_LO_BITS))
+                     : make_uint2(0u, 0u);
+        if (HAS_ERA && i < cnt) s_era[i] = ok ? e : INT_MAX;
     }
     __syncthreads();
     const bool aligned = (S % FPL) == 0;
@@ -337,21 +378,55 @@ __global__ void __launch_bounds__(NT, MINB) k_hist(
             for (int t = threadIdx.x; t < (nsl * ESLOT) / 4; t += NT) z[t] = zero;
         }
         __syncthreads();
-        if (lane_live) {
+        bool fast = false;
+        if constexpr (!HAS_ERA && REGULAR) fast = aligned;
+        if constexpr (!HAS_ERA && REGULAR) {
+            if (lane_live && fast) {
+                // rows of step k+1 load into one register set while step k's
+                // cells are updated from the other (no copies between steps);
+                // rows past the chunk's end are row 0 with zero increments
+                uint32_t wa[UF][WPR], wb[UF][WPR];
+                const uint32_t sh0 = (uint32_t)__cvta_generic_to_shared(sh32), lane4 = 4u * lane;
+                const unsigned S32 = (unsigned)S;
+                auto load = [&](int i0, uint32_t (&ww)[UF][WPR]) {
+#pragma unroll
+                    for (int u = 0; u < UF; ++u)
+                        load_row<FPL>(tile + (unsigned long long)(unsigned)s_row[i0 + NW * u] * S32, ww[u]);
+                };
+                auto update = [&](int i0, const uint32_t (&ww)[UF][WPR]) {
+#pragma unroll
+                    for (int u = 0; u < UF; ++u) {
+                        const uint2 pq = s_pq[i0 + NW * u];
+                        hist_row_fast<FPL, NSC>(ww[u], sh0, lane4, pq.x, pq.y);
+                    }
+                };
+                int i0 = warp;
+                if (i0 < cnt) load(i0, wa);
+                while (i0 < cnt) {
+                    const int i1 = i0 + NW * UF;
+                    if (i1 < cnt) load(i1, wb);
+                    update(i0, wa);
+                    if (i1 >= cnt) break;
+                    i0 = i1 + NW * UF;
+                    if (i0 < cnt) load(i0, wa);
+                    update(i1, wb);
+                }
+            }
+        }
+        if (lane_live && !fast) {
             // software pipeline: rows of step k+1 are loaded while step k's
             // cells are updated
             uint32_t w[U][WPR], wn[U][WPR];
-            int4 rec[U], recn[U];                // {row or -1, q, era slot, -}
-            auto fetch = [&](int i0, int4 (&rr)[U], uint32_t (&ww)[U][WPR]) {
+            int2 rec[U], recn[U];                // {row or -1, era slot}
+            auto fetch = [&](int i0, int2 (&rr)[U], uint32_t (&ww)[U][WPR]) {
 #pragma unroll
                 for (int u = 0; u < U; ++u) {
                     const int i = i0 + NW * u;
-                    const int2 rq = i < i_hi ? s_rec[i] : make_int2(-1, 0);
-                    int4 r4 = make_int4(rq.x, rq.y, 0, 0);
+                    int2 r4 = make_int2(i < i_hi && s_pq[i].x ? s_row[i] : -1, 0);
                     if (HAS_ERA && r4.x >= 0) {
                         const int e = s_era[i] - e_lo;
                         if (e < 0 || e >= ew_n) r4.x = -1;
-                        r4.z = e;
+                        r4.y = e;
                     }
                     rr[u] = r4;
 #pragma unroll
@@ -384,10 +459,9 @@ __global__ void __launch_bounds__(NT, MINB) k_hist(
 #pragma unroll
                 for (int u = 0; u < U; ++u) {
                     if (rec[u].x < 0) continue;
-                    const uint32_t ra = sbase + (HAS_ERA ? (uint32_t)rec[u].z * (ESLOT * 4) : 0u);
-                    const int qv = rec[u].y;
-                    hist_row<FPL, NSC, REGULAR>(w[u], ra, (1u << HIST_CNT_SHIFT) + ((uint32_t)qv & HIST_LO_MASK),
-                                                (uint32_t)(qv >> HIST_LO_BITS), B);
+                    const uint32_t ra = sbase + (HAS_ERA ? (uint32_t)rec[u].y * (ESLOT * 4) : 0u);
+                    const uint2 pq = s_pq[i0 + NW * u];
+                    hist_row<FPL, NSC, REGULAR>(w[u], ra, pq.x, pq.y, B);
                 }
 #pragma unroll
                 for (int u = 0; u < U; ++u) {
