@@ -242,6 +242,16 @@ typedef struct wgb_ws {
     const uint8_t *era_ops;  /* [era_nops] accumulator program                */
     float *crit_out;         /* optional [k][B-1]: criterion of node 0 of each */
                              /*   level (inspection), or NULL                  */
+    /* feature-sliced multi-rank fits (nslice > 1): rank `slice` keeps the
+     * histograms of positions [slice*ks, slice*ks + ks) only -- hg is then a
+     * pool of slots laid out as above with ks in place of k -- and searches
+     * splits among them; see wgb_level_hist / wgb_level_split / wgb_level_pick */
+    int64_t *hstage;         /* [nslice][built slots of a level][slot_elems]: */
+                             /*   the level's local histograms, slice-major,  */
+                             /*   reduce-scattered over the ranks into hg     */
+    int64_t hstage_elems;    /* capacity of hstage                            */
+    int32_t *win;            /* [nslice][T 2^(D-1)][win_words]: every rank's  */
+                             /*   best split per node of the level (all-gathered) */
     /* sizes */
     int64_t N, S;
     int64_t N_global;
@@ -252,6 +262,10 @@ typedef struct wgb_ws {
     int32_t regular;         /* 1 if every bin is known to lie in [0, B)      */
     int32_t era_nops, era_depth; /* program length and stack depth of the plan */
     int32_t ntree;           /* T, trees grown together (0 is taken as 1)     */
+    int32_t nslice, slice;   /* ranks sharing the features (0 or 1: none), this rank */
+    int32_t ks;              /* positions per slice (ceil(k / nslice))         */
+    int32_t win_words;       /* 32-bit words per node record in win: 8 + E    */
+                             /*   rounded up to even (int64 fields aligned)   */
     /* hyper-parameters (fp32 as the reference passes them) */
     float mcw, eps, msg, lr, mean_factor;
 } wgb_ws;
@@ -293,6 +307,13 @@ int64_t wgb_hist_part_elems(int64_t S, int32_t F, int32_t B, int64_t chunks);
  * torch's CUDA per_era_gain.mean(dim=0) (warpgbm/core.py:581-582) bit for
  * bit: the eras are added in the order of ws->era_sched / ws->era_ops. */
 int wgb_level_split(const wgb_ws *ws, int32_t d, void *stream);
+/* Level d of a feature-sliced fit (ws->nslice > 1), after wgb_level_split
+ * wrote this rank's best split per node into its region of ws->win and the
+ * regions were all-gathered: the best record per node by the split key
+ * (directional agreement, criterion, position index -- the choice one rank
+ * searching every position makes), its child totals and per-era gains into
+ * the node, and the next level's node records.  No-op otherwise. */
+int wgb_level_pick(const wgb_ws *ws, int32_t d, void *stream);
 
 /* Plan of the order in which torch's CUDA mean(dim=0) of a contiguous fp32
  * [E][M] tensor adds its E rows (ATen's reduce kernel: rows spread over the
@@ -327,7 +348,10 @@ int wgb_tree_finish(const wgb_ws *ws, void *stream);
 /* The whole per-tree sequence as stream work issued from C++: reset,
  * residual (+ max |g| over ranks), quantise, root, and per level d < D the
  * histogram build, its int64 SUM over ranks (when comm != NULL), the split
- * search and the partition; then wgb_tree_finish.  Replaces the reference's
+ * search and the partition; then wgb_tree_finish.  A feature-sliced fit
+ * (ws->nslice > 1, comm of those ranks) reduce-scatters the level's
+ * histograms from ws->hstage instead of summing them everywhere, and
+ * all-gathers ws->win before wgb_level_pick.  Replaces the reference's
  * per-node Python recursion (warpgbm/core.py:597-658, 692-744) and the
  * per-level Python loop of a host driving the entry points above.  comm ==
  * NULL: one rank. */
@@ -362,6 +386,14 @@ int wgb_comm_init(int32_t rank, int32_t world, const uint8_t *id128,
 int wgb_comm_destroy(wgb_comm *comm);
 int wgb_comm_allreduce(wgb_comm *comm, void *buf, int64_t count, int32_t kind,
                        void *stream);
+/* int64 SUM of every rank's send[world][recvcount]; rank r receives the sum
+ * of block r (ncclReduceScatter) on `stream`. */
+int wgb_comm_reduce_scatter(wgb_comm *comm, const int64_t *send, int64_t *recv,
+                            int64_t recvcount, void *stream);
+/* In place: every rank's buf[rank*count .. +count) to all ranks
+ * (ncclAllGather of int32) on `stream`. */
+int wgb_comm_allgather_i32(wgb_comm *comm, int32_t *buf, int64_t count,
+                           void *stream);
 
 /* Host -> device copy of `bytes` from pageable host memory, pipelined
  * through pinned staging buffers (parallel host copies overlapped with the

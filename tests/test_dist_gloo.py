@@ -1,7 +1,9 @@
 """Row-sharded host logic on world_size-2 gloo process groups (CPU only):
 era union, base prediction, column exchange for the quantile edges, exact
-histogram all-reduce, and detection of a rank that dies before a
-collective."""
+histogram all-reduce, the feature-sliced exchange (reduce-scatter of a
+level's slice-major staging buffer, all-gather of the per-node best-split
+records; also with three ranks and uneven slices), and detection of a rank
+that dies before a collective."""
 import os
 import socket
 import tempfile
@@ -99,6 +101,40 @@ def w_hist_allreduce(rank, world):
     return {"ok": bool(np.array_equal(Gt.numpy(), Gall) and np.array_equal(Ct.numpy(), Call))}
 
 
+def w_slices(rank, world):
+    """One level of a feature-sliced fit: each rank's local histograms of
+    all 7 positions in the staging layout [slice][sums ks*(B+1)][counts
+    ks*(B+1)][root sum, spare], reduce-scattered; then the ranks' node
+    records all-gathered in place."""
+    import oracle as O
+    from warpgbm_b200.core import _Comm
+    X, y, era, cut = _data()
+    B, F = 8, X.shape[1]
+    bins = O.bin_matrix(X, np.tile(np.linspace(-1.5, 1.5, B - 1, dtype=np.float32), (F, 1)))
+    q = O.quantize(y, O.quant_shift(float(np.abs(y).max())))
+    rows = np.arange(len(y), dtype=np.int32)
+    cuts = np.linspace(0, len(y), world + 1).astype(int)
+    mine = rows[cuts[rank]:cuts[rank + 1]]
+    feats = np.arange(F, dtype=np.int32)
+    G, C = O.hist_q(bins, q, mine, feats, np.zeros(len(y), np.int32), 1, B)
+    ks = (F + world - 1) // world
+    SE = 2 * ks * (B + 1) + 2
+    stage = np.zeros((world, SE), np.int64)
+    for r in range(world):
+        js = feats[r * ks:(r + 1) * ks]
+        stage[r, :len(js) * (B + 1)] = G[0, js].reshape(-1)
+        stage[r, ks * (B + 1):ks * (B + 1) + len(js) * (B + 1)] = C[0, js].reshape(-1)
+        stage[r, 2 * ks * (B + 1)] = int(q[mine].astype(np.int64).sum())
+    comm = _Comm(True)
+    out = torch.zeros(SE, dtype=torch.int64)
+    comm.reduce_scatter_(out, torch.from_numpy(stage.reshape(-1)))
+    cnt = 5
+    win = torch.zeros(world * cnt, dtype=torch.int32)
+    win[rank * cnt:(rank + 1) * cnt] = torch.arange(cnt, dtype=torch.int32) + 100 * rank
+    comm.all_gather_inplace_(win, cnt)
+    return {"out": out.numpy(), "win": win.numpy(), "ks": ks}
+
+
 def w_dead_rank(rank, world):
     if rank == 1:
         raise RuntimeError("rank 1 failed before the collective")
@@ -134,6 +170,29 @@ def test_column_exchange_gives_full_columns():
 def test_histogram_allreduce_is_exact():
     res = _run("w_hist_allreduce")
     assert all(r["ok"] for r in res)
+
+
+@pytest.mark.parametrize("world", [2, 3])
+def test_feature_sliced_exchange_is_exact(world):
+    import oracle as O
+    X, y, era, cut = _data()
+    B, F = 8, X.shape[1]
+    bins = O.bin_matrix(X, np.tile(np.linspace(-1.5, 1.5, B - 1, dtype=np.float32), (F, 1)))
+    q = O.quantize(y, O.quant_shift(float(np.abs(y).max())))
+    G, C = O.hist_q(bins, q, np.arange(len(y), dtype=np.int32), np.arange(F, dtype=np.int32),
+                    np.zeros(len(y), np.int32), 1, B)
+    res = _run("w_slices", world=world)
+    for r, got in enumerate(res):
+        assert "error" not in got, got
+        ks = got["ks"]
+        js = np.arange(F)[r * ks:(r + 1) * ks]
+        out = got["out"]
+        assert np.array_equal(out[:len(js) * (B + 1)], G[0, js].reshape(-1))
+        assert np.array_equal(out[ks * (B + 1):ks * (B + 1) + len(js) * (B + 1)], C[0, js].reshape(-1))
+        assert not out[len(js) * (B + 1):ks * (B + 1)].any()          # an uneven slice's padding
+        assert out[2 * ks * (B + 1)] == int(q.astype(np.int64).sum())  # the root sum
+        want = np.concatenate([np.arange(5) + 100 * w for w in range(world)])
+        assert np.array_equal(got["win"], want)
 
 
 def test_dead_rank_is_detected_by_peer():

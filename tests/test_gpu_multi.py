@@ -1,9 +1,13 @@
 """Row-sharded fit (WarpGBM(distributed=True)) against a single-process fit
 on the same rows: identical trees, importance and predictions.
 
-Two ranks always run on one GPU over a gloo group (host-staged collectives),
-which exercises every exchange step of the sharded engine; with two or more
-GPUs the same check also runs over NCCL, one GPU per rank."""
+Two and three ranks always run on one GPU over a gloo group (host-staged
+collectives), which exercises every exchange step of the sharded engine --
+the feature-sliced one (each rank keeps and searches a slice of the
+positions: reduce-scatter of the level histograms, all-gather of the best
+split per node; three ranks give uneven slices) and the one that sums
+every histogram on every rank; with two or more GPUs the sliced check also
+runs over NCCL, one GPU per rank."""
 import os
 import socket
 import tempfile
@@ -53,7 +57,7 @@ def _fit_summary(m, X):
     return {"flat": flat, "imp": m.per_era_feature_importance_, "pred": pred}
 
 
-def _worker(rank, world, port, backend, outdir):
+def _worker(rank, world, port, backend, outdir, slices):
     import contextlib
     import datetime
     import io
@@ -73,6 +77,7 @@ def _worker(rank, world, port, backend, outdir):
         cut = np.linspace(0, len(y), world + 1).astype(int)
         sl = slice(cut[rank], cut[rank + 1])
         m = WarpGBM(distributed=True, **params)
+        m._feature_slices = slices
         with contextlib.redirect_stdout(io.StringIO()):
             m.fit(X[sl], y[sl], era_id=None if era is None else era[sl])
             out[name] = _fit_summary(m, X)
@@ -93,10 +98,10 @@ def _single():
     return res
 
 
-def _check(backend, world):
+def _check(backend, world, slices=True):
     single = _single()
     with tempfile.TemporaryDirectory() as d:
-        mp.spawn(_worker, args=(world, _port(), backend, d), nprocs=world, join=True)
+        mp.spawn(_worker, args=(world, _port(), backend, d, slices), nprocs=world, join=True)
         outs = [torch.load(os.path.join(d, f"r{r}.pt"), weights_only=False) for r in range(world)]
     for name, ref in single.items():
         for r, o in enumerate(outs):
@@ -112,8 +117,13 @@ def _check(backend, world):
                 assert np.array_equal(got["pred"], ref["pred"]), (backend, name, r)
 
 
-def test_two_ranks_gloo_one_gpu_match_single_process(cuda):
-    _check("gloo", 2)
+@pytest.mark.parametrize("slices", [True, False])
+def test_two_ranks_gloo_one_gpu_match_single_process(cuda, slices):
+    _check("gloo", 2, slices)
+
+
+def test_three_ranks_gloo_one_gpu_uneven_slices_match_single_process(cuda):
+    _check("gloo", 3)
 
 
 @pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs two GPUs for one NCCL rank per GPU")

@@ -47,11 +47,13 @@ class WgbWs(ctypes.Structure):
         ("nodes", _p), ("nn", _p), ("nact", _p),
         ("maxabs", _p), ("shift", _p), ("rootsum", _p), ("sync", _p), ("part_hist", _p), ("part_hist_elems", _i64),
         ("era_sched", _p), ("era_ops", _p), ("crit_out", _p),
+        ("hstage", _p), ("hstage_elems", _i64), ("win", _p),
         ("N", _i64), ("S", _i64), ("N_global", _i64),
         ("F", _i32), ("k", _i32), ("E", _i32), ("B", _i32), ("D", _i32), ("K", _i32),
         ("cls", _i32),
         ("chunk_cap", _i32), ("ntiles", _i32), ("ncand_blk", _i32),
         ("hist_ew", _i32), ("regular", _i32), ("era_nops", _i32), ("era_depth", _i32), ("ntree", _i32),
+        ("nslice", _i32), ("slice", _i32), ("ks", _i32), ("win_words", _i32),
         ("mcw", _f32), ("eps", _f32), ("msg", _f32), ("lr", _f32), ("mean_factor", _f32),
     ]
 
@@ -78,6 +80,7 @@ _SIGS = {
     "wgb_built_slots": ([_i32, ctypes.POINTER(_i32), ctypes.POINTER(_i32)], None),
     "wgb_level_slots": ([_p, _i32, ctypes.POINTER(_i32), ctypes.POINTER(_i32)], None),
     "wgb_level_split": ([_p, _i32, _p], _i32),
+    "wgb_level_pick": ([_p, _i32, _p], _i32),
     "wgb_era_mean_plan": ([_i32, _i64, _i32, _i32, _p, _p, _i64, ctypes.POINTER(_i32)], _i64),
     "wgb_level_partition": ([_p, _i32, _p], _i32),
     "wgb_bins_feature_major": ([_p, _p, _p], _i32),
@@ -93,6 +96,8 @@ _SIGS = {
     "wgb_comm_init": ([_i32, _i32, _p, ctypes.POINTER(_p)], _i32),
     "wgb_comm_destroy": ([_p], _i32),
     "wgb_comm_allreduce": ([_p, _p, _i64, _i32, _p], _i32),
+    "wgb_comm_reduce_scatter": ([_p, _p, _p, _i64, _p], _i32),
+    "wgb_comm_allgather_i32": ([_p, _p, _i64, _p], _i32),
     "wgb_quantile_edges": ([_p, _i64, _i32, _i64, _p, _i32, _p, _p, _p], _i32),
 }
 
@@ -135,7 +140,8 @@ def check(rc: int, what: str = "") -> None:
 # kernels each entry point launches (bench.py reports the count it saw)
 _KERNELS = {
     "wgb_tree_reset": 1, "wgb_tree_residual": 1, "wgb_tree_subset": 1, "wgb_tree_quantize": 1, "wgb_tree_root": 1,
-    "wgb_level_hist": 2, "wgb_level_split": 2, "wgb_level_partition": 3, "wgb_tree_finish": 0,
+    "wgb_level_hist": 2, "wgb_level_split": 2, "wgb_level_pick": 1, "wgb_level_partition": 3,
+    "wgb_tree_finish": 0,
     "wgb_grow_tree": 0, "wgb_bins_feature_major": 1, "wgb_prebinned_ingest": 1,
     "wgb_bin_matrix": 1, "wgb_predict_packed": 1, "wgb_predict_heap": 1, "wgb_quantile_edges": 2, "wgb_compute_histogram3": 6, "wgb_compute_histogram3_noalloc": 6,
     "wgb_compute_split": 1, "wgb_custom_cuda_binner": 1, "wgb_predict_forest": 1,

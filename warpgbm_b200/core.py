@@ -97,6 +97,32 @@ class _Comm:
             self._inplace(t, lambda x: self.dist.all_reduce(x, op=self.dist.ReduceOp.SUM))
         return t
 
+    def reduce_scatter_(self, out, inp):
+        """out = this rank's block of the element-wise sum over ranks of inp
+        ([world * out.numel()], block r to rank r).  gloo: an all-reduce of
+        the whole buffer, then the block (the same integer sums)."""
+        if not self.on:
+            out.copy_(inp[: out.numel()])
+        elif self.host_staging:
+            h = inp.cpu()
+            self.dist.all_reduce(h, op=self.dist.ReduceOp.SUM)
+            m = out.numel()
+            out.copy_(h[self.rank * m:(self.rank + 1) * m])
+        else:
+            self.dist.reduce_scatter_tensor(out, inp)
+        return out
+
+    def all_gather_inplace_(self, buf, count):
+        """buf[r*count:(r+1)*count] of every rank r to all ranks."""
+        if self.on:
+            mine = buf[self.rank * count:(self.rank + 1) * count].clone()
+            if self.host_staging:
+                outs = list(buf[: self.world * count].view(self.world, count).unbind(0))
+                self.all_gather(outs, mine)
+            else:
+                self.dist.all_gather_into_tensor(buf[: self.world * count], mine)
+        return buf
+
     def bcast_(self, t, src=0):
         if self.on:
             self._inplace(t, lambda x: self.dist.broadcast(x, src))
@@ -166,13 +192,20 @@ def native_comm(comm: _Comm, dev):
     return h
 
 
-def level_launches(D: int, E: int) -> int:
+def fused_partition(ws) -> bool:
+    """The engine's choice for a workspace (wgb_engine.cu fused_partition):
+    single-rank one-era fits partition each level in one launch (k_partition)."""
+    return ws.N_global == ws.N and ws.E == 1 and ws.nslice <= 1
+
+
+def level_launches(D: int, E: int, fused: bool = True, sliced: bool = False) -> int:
     """Kernels one tree (or one batch of trees) launches in wgb_grow_tree."""
     n = 4                                            # reset, residual, quantize, root
     for d in range(D):
         n += (4 if d == 0 else 2) if E == 1 else (3 if d == 0 else 1)   # histogram (+ chunk plan, root cells)
         n += 3 if d == 0 else 2                      # split (+ root totals), final
-        n += 3                                       # flags, offsets, scatter
+        n += 1 if sliced else 0                      # pick
+        n += 1 if fused else 3                       # partition, or flags, offsets, scatter
     return n
 
 
@@ -777,18 +810,25 @@ class WarpGBM(BaseEstimator, RegressorMixin):
                   bins.data_ptr(), S, torch.cuda.current_stream().cuda_stream)
         return bins, False
 
-    def _alloc_ws(self, N, F, k, E, K, ntree=1):
+    def _alloc_ws(self, N, F, k, E, K, ntree=1, nslice=1, slice_=0):
         """Device workspace for growing `ntree` trees together (one per class
-        in a multiclass round: a level's node set spans the batch)."""
+        in a multiclass round: a level's node set spans the batch).  With
+        nslice > 1 ranks the fit is feature-sliced: this rank keeps the
+        histograms of ks = ceil(k / nslice) positions and a staging buffer
+        for one level's local histograms of all positions."""
         dev = self._dev
         B, D = self.num_bins, self.max_depth
         S = bins_stride(F)
         T = ntree
         NP = T * N                      # level-0 positions: tree t's rows at [tN, (t+1)N)
         nslots = T << (D - 1)
-        se = E * k * (B + 1)
+        ks = (k + nslice - 1) // nslice if nslice > 1 else k
+        se = E * ks * (B + 1)
         P = 2 * se + 2                  # int64 per slot: sums, counts, root sum, spare
-        hist_bytes = nslots * P * 8
+        stage_slots = T * max(1, 1 << max(D - 2, 0))  # most built slots of one level
+        stage_elems = stage_slots * nslice * P if nslice > 1 else 0
+        win_words = (8 + E + 1) & ~1    # even: every record's int64 totals stay 8-byte aligned
+        hist_bytes = (nslots * P + stage_elems) * 8
         free, _ = torch.cuda.mem_get_info(dev)
         if hist_bytes > 0.6 * free:
             raise MemoryError(
@@ -819,7 +859,7 @@ class WarpGBM(BaseEstimator, RegressorMixin):
         # per-node partial arg-max: blocks of 8 features with one era, of
         # 32 (or 8 for num_bins > 33) with eras
         fb = SPLIT_WARPS if E == 1 else split_era_features(B)
-        ncand = (k + fb - 1) // fb
+        ncand = (ks + fb - 1) // fb
         t["cand"] = torch.empty((nslots, ncand, 4), **i32)
         if E > 1:
             # order in which the reference's per_era_gain.mean(dim=0) adds the
@@ -842,6 +882,9 @@ class WarpGBM(BaseEstimator, RegressorMixin):
         t["qg"] = torch.empty(max(NP, 1), **i32)
         t["feats"] = torch.empty(k, **i32)
         t["kpos"] = torch.empty(F, **i32)
+        if nslice > 1:
+            t["hstage"] = torch.empty(max(stage_elems, 1), dtype=torch.int64, device=dev)
+            t["win"] = torch.zeros(nslice * nslots * win_words, **i32)
         self._t = t
         ws = _lib.WgbWs()
         ws.order[0], ws.order[1] = t["order0"].data_ptr(), t["order1"].data_ptr()
@@ -856,6 +899,10 @@ class WarpGBM(BaseEstimator, RegressorMixin):
         ws.part_hist_elems = part_elems
         ws.hist_ew = 0  # automatic
         ws.ntree = T
+        if nslice > 1:
+            ws.nslice, ws.slice, ws.ks, ws.win_words = nslice, slice_, ks, win_words
+            ws.hstage, ws.hstage_elems = t["hstage"].data_ptr(), stage_elems
+            ws.win = t["win"].data_ptr()
         ws.regular = 1 if self._bins_regular else 0
         ws.mcw = float(np.float32(self.min_child_weight))
         ws.eps = float(np.float32(self.L2_reg))
@@ -892,7 +939,12 @@ class WarpGBM(BaseEstimator, RegressorMixin):
             ntree = K if classification else 1
             if ntree > 1:
                 root_order = root_order.repeat(ntree)
-            ws = self._alloc_ws(N, F, k, E, K, ntree)
+            # several ranks: each keeps and searches a slice of the positions
+            # (reduce-scatter of the level histograms, all-gather of the best
+            # split per node); _feature_slices = False sums every histogram on
+            # every rank instead
+            nslice = comm.world if comm.on and getattr(self, "_feature_slices", True) else 1
+            ws = self._alloc_ws(N, F, k, E, K, ntree, nslice, comm.rank)
             self._ncomm = native_comm(comm, dev)
             ws.bins, ws.root_order = bins.data_ptr(), root_order.data_ptr()
             ws.era = era_dense.data_ptr() if E > 1 else None
@@ -1035,7 +1087,7 @@ class WarpGBM(BaseEstimator, RegressorMixin):
         if not instrumented and (not comm.on or self._ncomm is not None):
             # the whole tree from C++ (levels, and the per-level NCCL sums)
             _lib.call("wgb_grow_tree", p, self._ncomm, st())
-            _lib.LAUNCHES[0] += level_launches(self.max_depth, ws.E)
+            _lib.LAUNCHES[0] += level_launches(self.max_depth, ws.E, fused_partition(ws), ws.nslice > 1)
             self._after_tree(ws, i, c)
             return
         # the same sequence level by level from Python (a gloo group, or the
@@ -1054,7 +1106,8 @@ class WarpGBM(BaseEstimator, RegressorMixin):
         _lib.call("wgb_tree_quantize", p, st())
         _lib.call("wgb_tree_subset", p, st())
         _lib.call("wgb_tree_root", p, st())
-        P = 2 * ws.E * ws.k * (ws.B + 1) + 2
+        sliced = ws.nslice > 1
+        P = 2 * ws.E * (ws.ks if sliced else ws.k) * (ws.B + 1) + 2  # pool slot size
         wsp = ctypes_ptr(ws)
         timer = getattr(self, "_hist_events", None)
         for d in range(self.max_depth):
@@ -1071,7 +1124,11 @@ class WarpGBM(BaseEstimator, RegressorMixin):
                 if ctimer is not None:
                     c0, c1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
                     c0.record()
-                comm.sum_(self._t["hg"][first * P:(first + count) * P])
+                if sliced:  # this rank's slice of the level's slots, summed over ranks
+                    comm.reduce_scatter_(self._t["hg"][first * P:(first + count) * P],
+                                         self._t["hstage"][: ws.nslice * count * P])
+                else:
+                    comm.sum_(self._t["hg"][first * P:(first + count) * P])
                 if ctimer is not None:
                     c1.record()
                     ctimer.append((c0, c1))
@@ -1080,9 +1137,15 @@ class WarpGBM(BaseEstimator, RegressorMixin):
                 s0, s1, s2 = (torch.cuda.Event(enable_timing=True) for _ in range(3))
                 s0.record()
             _lib.call("wgb_level_split", p, d, st())
+            if sliced:  # every rank's best split per node, the same choice everywhere
+                cnt = (max(ws.ntree, 1) << d) * ws.win_words
+                comm.all_gather_inplace_(self._t["win"], cnt)
+                _lib.call("wgb_level_pick", p, d, st())
             if stimer is not None:
                 s1.record()
             _lib.call("wgb_level_partition", p, d, st())
+            if fused_partition(ws):
+                _lib.LAUNCHES[0] -= 2  # one launch instead of three
             if stimer is not None:
                 s2.record()
                 stimer.append((s0, s1, s2))

@@ -28,15 +28,19 @@ struct NcclUid {
 using nccl_get_uid_t = int (*)(NcclUid *);
 using nccl_init_rank_t = int (*)(void **, int, NcclUid, int);
 using nccl_all_reduce_t = int (*)(const void *, void *, size_t, int, int, void *, cudaStream_t);
+using nccl_reduce_scatter_t = int (*)(const void *, void *, size_t, int, int, void *, cudaStream_t);
+using nccl_all_gather_t = int (*)(const void *, void *, size_t, int, void *, cudaStream_t);
 using nccl_destroy_t = int (*)(void *);
 using nccl_err_t = const char *(*)(int);
-constexpr int NCCL_INT64 = 4, NCCL_FLOAT32 = 7, NCCL_SUM = 0, NCCL_MAX = 2;
+constexpr int NCCL_INT32 = 2, NCCL_INT64 = 4, NCCL_FLOAT32 = 7, NCCL_SUM = 0, NCCL_MAX = 2;
 
 struct NcclApi {
     bool ok = false;
     nccl_get_uid_t get_uid = nullptr;
     nccl_init_rank_t init_rank = nullptr;
     nccl_all_reduce_t all_reduce = nullptr;
+    nccl_reduce_scatter_t reduce_scatter = nullptr;
+    nccl_all_gather_t all_gather = nullptr;
     nccl_destroy_t destroy = nullptr;
     nccl_err_t err = nullptr;
 };
@@ -51,9 +55,11 @@ static NcclApi &nccl() {
         a.get_uid = reinterpret_cast<nccl_get_uid_t>(dlsym(h, "ncclGetUniqueId"));
         a.init_rank = reinterpret_cast<nccl_init_rank_t>(dlsym(h, "ncclCommInitRank"));
         a.all_reduce = reinterpret_cast<nccl_all_reduce_t>(dlsym(h, "ncclAllReduce"));
+        a.reduce_scatter = reinterpret_cast<nccl_reduce_scatter_t>(dlsym(h, "ncclReduceScatter"));
+        a.all_gather = reinterpret_cast<nccl_all_gather_t>(dlsym(h, "ncclAllGather"));
         a.destroy = reinterpret_cast<nccl_destroy_t>(dlsym(h, "ncclCommDestroy"));
         a.err = reinterpret_cast<nccl_err_t>(dlsym(h, "ncclGetErrorString"));
-        a.ok = a.get_uid && a.init_rank && a.all_reduce && a.destroy && a.err;
+        a.ok = a.get_uid && a.init_rank && a.all_reduce && a.reduce_scatter && a.all_gather && a.destroy && a.err;
         return a;
     }();
     return api;
@@ -120,6 +126,28 @@ int wgb_comm_allreduce(wgb_comm *comm, void *buf, int64_t count, int32_t kind, v
     return WGB_OK;
 }
 
+int wgb_comm_reduce_scatter(wgb_comm *comm, const int64_t *send, int64_t *recv, int64_t recvcount, void *stream) {
+    WGB_CHECK_ARG(comm != nullptr && send != nullptr && recv != nullptr && recvcount >= 0,
+                  "bad reduce-scatter arguments");
+    if (recvcount == 0) return WGB_OK;
+    if (comm->world == 1) {
+        WGB_CUDA(cudaMemcpyAsync(recv, send, sizeof(int64_t) * recvcount, cudaMemcpyDeviceToDevice,
+                                 as_stream(stream)));
+        return WGB_OK;
+    }
+    WGB_NCCL(nccl().reduce_scatter(send, recv, (size_t)recvcount, NCCL_INT64, NCCL_SUM, comm->nccl_comm,
+                                   as_stream(stream)));
+    return WGB_OK;
+}
+
+int wgb_comm_allgather_i32(wgb_comm *comm, int32_t *buf, int64_t count, void *stream) {
+    WGB_CHECK_ARG(comm != nullptr && (buf != nullptr || count == 0) && count >= 0, "bad all-gather arguments");
+    if (count == 0 || comm->world == 1) return WGB_OK;
+    WGB_NCCL(nccl().all_gather(buf + (long long)comm->rank * count, buf, (size_t)count, NCCL_INT32,
+                               comm->nccl_comm, as_stream(stream)));
+    return WGB_OK;
+}
+
 int wgb_grow_tree(const wgb_ws *ws, wgb_comm *comm, void *stream) {
     int rc;
 #define WGB_STEP(expr)      \
@@ -132,15 +160,28 @@ int wgb_grow_tree(const wgb_ws *ws, wgb_comm *comm, void *stream) {
     WGB_STEP(wgb_tree_quantize(ws, stream));
     WGB_STEP(wgb_tree_subset(ws, stream));
     WGB_STEP(wgb_tree_root(ws, stream));
-    const long long P = 2ll * ws->E * ws->k * (ws->B + 1) + 2;
+    const bool sliced = ws->nslice > 1;
+    WGB_CHECK_ARG(!sliced || (comm && comm->world == ws->nslice && comm->rank == ws->slice),
+                  "a feature-sliced fit needs the communicator of its nslice ranks");
+    // slot size of the pool (ks positions per slot when sliced)
+    const long long P = 2ll * ws->E * (sliced ? ws->ks : ws->k) * (ws->B + 1) + 2;
     for (int d = 0; d < ws->D; ++d) {
         WGB_STEP(wgb_level_hist(ws, d, stream));
-        if (comm) {
-            int first, count;
-            wgb_level_slots(ws, d, &first, &count);
+        int first, count;
+        wgb_level_slots(ws, d, &first, &count);
+        if (sliced) {
+            // every rank gets the global sums of its slice of the level's slots
+            WGB_STEP(wgb_comm_reduce_scatter(comm, ws->hstage, ws->hg + (long long)first * P, (long long)count * P,
+                                             stream));
+        } else if (comm) {
             WGB_STEP(wgb_comm_allreduce(comm, ws->hg + (long long)first * P, (long long)count * P, 0, stream));
         }
         WGB_STEP(wgb_level_split(ws, d, stream));
+        if (sliced) {
+            // every rank's best split per node, then the same choice on all ranks
+            WGB_STEP(wgb_comm_allgather_i32(comm, ws->win, (long long)(nt << d) * ws->win_words, stream));
+            WGB_STEP(wgb_level_pick(ws, d, stream));
+        }
         WGB_STEP(wgb_level_partition(ws, d, stream));
     }
     WGB_STEP(wgb_tree_finish(ws, stream));

@@ -56,6 +56,18 @@ constexpr uint32_t HIST_LO_MASK = (1u << HIST_LO_BITS) - 1u;
 constexpr uint32_t HIST_A_SUM_MASK = (1u << HIST_CNT_SHIFT) - 1u;
 #define HIST_ERA_R(has_era) ((has_era) ? HIST_R : 1)
 constexpr int HIST_THREADS = 256;
+
+// Where a histogram build adds its cells: cell (slot, era e, position kp,
+// bin b) of the sums is g[(kp / ks) * slice_stride + (slot - slot0) *
+// slot_elems + (e * ks + kp % ks) * (B + 1) + b], the count the same offset
+// from c.  The histogram pool is the case ks = k, slice_stride = 0, slot0 =
+// 0; a sliced fit's staging buffer holds one region of the level's slots per
+// slice of ks positions.
+struct HistOut {
+    long long *g, *c;
+    long long slot_elems, slice_stride;
+    int ks, slot0;
+};
 constexpr int SPLIT_WARPS = 8;     // features per single-era split block (one warp each)
 constexpr int PART_TILE = 2048;     // positions per partition tile
 constexpr int PART_THREADS = 256;

@@ -132,11 +132,15 @@ __global__ void k_root(wgb_node *nodes, int *nn, int *nact, int D, long long n_l
     }
 }
 
-// Copies each tree's local root sum into its root slot's first spare cell,
-// so that the level-0 reduction carries it.
+// Copies each tree's local root sum into its root slot's first spare cell
+// (of every slice region of a sliced fit's staging buffer), so that the
+// level-0 reduction carries it.
 __global__ void k_root_cells(long long *hg, const long long *rootsum, long long slot_elems, long long nc,
-                             int ntree) {
-    for (int t = threadIdx.x; t < ntree; t += blockDim.x) hg[t * slot_elems + 2 * nc] = rootsum[t];
+                             int ntree, int nregion, long long region_stride) {
+    for (int i = threadIdx.x; i < ntree * nregion; i += blockDim.x) {
+        const int t = i % ntree, r = i / ntree;
+        hg[r * region_stride + t * slot_elems + 2 * nc] = rootsum[t];
+    }
 }
 
 __global__ void k_root_total(wgb_node *nodes, const long long *hg, long long slot_elems, long long nc,
@@ -153,14 +157,15 @@ __global__ void k_root_total(wgb_node *nodes, const long long *hg, long long slo
 // ====================================================================== //
 
 // Chunk list of a level: every built node's local rows cut into HIST_R-row
-// pieces, by one block of 1024 threads.  The level's records come from
-// earlier launches or from this block (visible after its barrier).
-__device__ void plan_chunks(const wgb_node *__restrict__ lvl, int nnd, int4 *chunks, int *nchunks, int cap) {
+// pieces, by one block (any size up to 1024 threads).  The level's records
+// come from earlier launches or from this block (visible after its barrier).
+__device__ __forceinline__ void plan_chunks(const wgb_node *__restrict__ lvl, int nnd, int4 *chunks, int *nchunks, int cap) {
     __shared__ int s_cnt[1024];
     __shared__ int s_off[1025];
     __shared__ int s_scan[33];
+    const int nt = blockDim.x;
     int base = 0;
-    for (int b0 = 0; b0 < nnd; b0 += 1024) {
+    for (int b0 = 0; b0 < nnd; b0 += nt) {
         int i = b0 + threadIdx.x;
         int c = 0;
         if (i < nnd && node_built(lvl[i].built)) c = (lvl[i].lcnt + HIST_R - 1) / HIST_R;
@@ -168,12 +173,12 @@ __device__ void plan_chunks(const wgb_node *__restrict__ lvl, int nnd, int4 *chu
         int tot;
         const int ex = block_scan_excl(c, s_scan, tot);
         s_off[threadIdx.x] = base + ex;
-        if (threadIdx.x == 0) s_off[1024] = base + tot;
+        if (threadIdx.x == 0) s_off[nt] = base + tot;
         __syncthreads();
-        int lo = s_off[0], hi = s_off[1024];
-        for (int c2 = lo + threadIdx.x; c2 < hi; c2 += 1024) {
+        int lo = s_off[0], hi = s_off[nt];
+        for (int c2 = lo + threadIdx.x; c2 < hi; c2 += nt) {
             // node of chunk c2: last t with s_off[t] <= c2 and s_cnt[t] > 0
-            int a = 0, z = 1023;
+            int a = 0, z = nt - 1;
             while (a < z) {
                 int m = (a + z + 1) >> 1;
                 if (s_off[m] <= c2) a = m; else z = m - 1;
@@ -284,8 +289,7 @@ __global__ void __launch_bounds__(NT, MINB) k_hist(
     const int *__restrict__ q, const float *__restrict__ g, const int *shift,
     const int *__restrict__ era, const int *__restrict__ kpos, int k, int E, int B, int EW,
     const int4 *__restrict__ chunks, const int *nchunks, const wgb_node *__restrict__ lvl,
-    long long *__restrict__ hg, long long *__restrict__ hc, long long slot_elems, long long nrows,
-    uint2 *__restrict__ part) {
+    const HistOut out, long long nrows, uint2 *__restrict__ part) {
     constexpr int FT = 32 * FPL;             // features per tile
     constexpr int U = (FPL >= 16 || MINB > 1) ? 4 : 8;  // rows per pipeline step per warp
     constexpr int NW = NT / 32;
@@ -297,8 +301,8 @@ __global__ void __launch_bounds__(NT, MINB) k_hist(
     __shared__ int s_kp[FT];                 // lane-major: [j][lane]
     // per chunk row: the row (0 when skipped or padding) and its two word
     // increments; pa == 0 marks a skipped or padding row (pa >= 2^20 otherwise)
-    __shared__ int s_row[HIST_R + PADR];
-    __shared__ uint2 s_pq[HIST_R + PADR];
+    __shared__ __align__(16) int s_row[HIST_R + PADR];
+    __shared__ __align__(16) uint2 s_pq[HIST_R + PADR];
     __shared__ int s_era[HIST_ERA_R(HAS_ERA)];
     __shared__ int s_red[33];
 
@@ -384,23 +388,31 @@ __global__ void __launch_bounds__(NT, MINB) k_hist(
             if (lane_live && fast) {
                 // rows of step k+1 load into one register set while step k's
                 // cells are updated from the other (no copies between steps);
-                // rows past the chunk's end are row 0 with zero increments
+                // a warp takes UF consecutive rows of a step, so their row
+                // ids and increments arrive in 16-byte shared loads; rows past
+                // the chunk's end are row 0 with zero increments
                 uint32_t wa[UF][WPR], wb[UF][WPR];
                 const uint32_t sh0 = (uint32_t)__cvta_generic_to_shared(sh32), lane4 = 4u * lane;
                 const unsigned S32 = (unsigned)S;
                 auto load = [&](int i0, uint32_t (&ww)[UF][WPR]) {
 #pragma unroll
-                    for (int u = 0; u < UF; ++u)
-                        load_row<FPL>(tile + (unsigned long long)(unsigned)s_row[i0 + NW * u] * S32, ww[u]);
+                    for (int u = 0; u < UF; u += 4) {
+                        const int4 r4 = *reinterpret_cast<const int4 *>(&s_row[i0 + u]);
+                        load_row<FPL>(tile + (unsigned long long)(unsigned)r4.x * S32, ww[u]);
+                        load_row<FPL>(tile + (unsigned long long)(unsigned)r4.y * S32, ww[u + 1]);
+                        load_row<FPL>(tile + (unsigned long long)(unsigned)r4.z * S32, ww[u + 2]);
+                        load_row<FPL>(tile + (unsigned long long)(unsigned)r4.w * S32, ww[u + 3]);
+                    }
                 };
                 auto update = [&](int i0, const uint32_t (&ww)[UF][WPR]) {
 #pragma unroll
-                    for (int u = 0; u < UF; ++u) {
-                        const uint2 pq = s_pq[i0 + NW * u];
+                    for (int u = 0; u < UF; u += 2) {
+                        const uint4 pq = *reinterpret_cast<const uint4 *>(&s_pq[i0 + u]);
                         hist_row_fast<FPL, NSC>(ww[u], sh0, lane4, pq.x, pq.y);
+                        hist_row_fast<FPL, NSC>(ww[u + 1], sh0, lane4, pq.z, pq.w);
                     }
                 };
-                int i0 = warp;
+                int i0 = warp * UF;
                 if (i0 < cnt) load(i0, wa);
                 while (i0 < cnt) {
                     const int i1 = i0 + NW * UF;
@@ -483,8 +495,8 @@ __global__ void __launch_bounds__(NT, MINB) k_hist(
         // walking the words in layout order (conflict-free reads); a word's
         // cell index is decoded once for all era slots of the window
         {
-            const long long estride = (long long)k * B1;
-            const long long wbase = slot * slot_elems + (long long)e_lo * estride;
+            const long long estride = (long long)out.ks * B1;
+            const long long wbase = (slot - out.slot0) * out.slot_elems + (long long)e_lo * estride;
             for (int wi = threadIdx.x; wi < NSC * FT; wi += NT) {
                 const int jb = wi / (NSC * 64), rem = wi % (NSC * 64);
                 const int sl = rem >> 6, r2 = rem & 63;
@@ -492,7 +504,8 @@ __global__ void __launch_bounds__(NT, MINB) k_hist(
                 const int jj = 2 * jb + (r2 >> 5), lj = r2 & 31;
                 const int kp = s_kp[jj * 32 + lj];
                 if (kp < 0) continue;
-                const long long cidx = wbase + (long long)kp * B1 + sl;
+                const long long cidx = wbase + (long long)(kp / out.ks) * out.slice_stride +
+                                       (long long)(kp % out.ks) * B1 + sl;
                 for (int ew = 0; ew < nsl; ++ew) {
                     const uint32_t a = sh32[ew * ESLOT + wi];
                     if (a == 0u) continue;
@@ -500,8 +513,8 @@ __global__ void __launch_bounds__(NT, MINB) k_hist(
                     const int cntv = (int)(a >> HIST_CNT_SHIFT);
                     const long long gs = (long long)(int)bw * (1ll << HIST_LO_BITS) + (long long)(a & HIST_A_SUM_MASK);
                     const long long idx = cidx + (long long)ew * estride;
-                    atomicAdd(reinterpret_cast<unsigned long long *>(hg + idx), (unsigned long long)gs);
-                    atomicAdd(reinterpret_cast<unsigned long long *>(hc + idx), (unsigned long long)cntv);
+                    atomicAdd(reinterpret_cast<unsigned long long *>(out.g + idx), (unsigned long long)gs);
+                    atomicAdd(reinterpret_cast<unsigned long long *>(out.c + idx), (unsigned long long)cntv);
                 }
             }
         }
@@ -524,8 +537,7 @@ template <int FPL, int NSC>
 __global__ void __launch_bounds__(256) k_hist_reduce(const uint2 *__restrict__ part, const int4 *__restrict__ chunks,
                                                      const int *nchunks, const wgb_node *__restrict__ lvl,
                                                      const int *__restrict__ kpos, int F, int B, int seg,
-                                                     long long *__restrict__ hg, long long *__restrict__ hc,
-                                                     long long slot_elems) {
+                                                     const HistOut out) {
     constexpr int FT = 32 * FPL, CELLS = NSC * FT;
     const int nch = *nchunks;
     const int c0 = blockIdx.z * seg;
@@ -543,11 +555,12 @@ __global__ void __launch_bounds__(256) k_hist_reduce(const uint2 *__restrict__ p
     const int ntile = gridDim.y;
     long long gs = 0, cn = 0;
     int node = chunks[c0].x;
+    const long long kofs = (long long)(kp / out.ks) * out.slice_stride + (long long)(kp % out.ks) * B1 + sl;
     auto add = [&]() {
         if (cn == 0) return;
-        const long long idx = (long long)lvl[node].slot * slot_elems + (long long)kp * B1 + sl;
-        atomicAdd(reinterpret_cast<unsigned long long *>(hg + idx), (unsigned long long)gs);
-        atomicAdd(reinterpret_cast<unsigned long long *>(hc + idx), (unsigned long long)cn);
+        const long long idx = (long long)(lvl[node].slot - out.slot0) * out.slot_elems + kofs;
+        atomicAdd(reinterpret_cast<unsigned long long *>(out.g + idx), (unsigned long long)gs);
+        atomicAdd(reinterpret_cast<unsigned long long *>(out.c + idx), (unsigned long long)cn);
     };
     constexpr int UR = 8;  // chunk words in flight per thread
     const uint2 *src = part + (long long)blockIdx.y * CELLS + wi;
@@ -591,8 +604,7 @@ static cudaError_t launch_hist(int grid_x, const int8_t *bins, long long S, int 
                                const int *q, const float *g, const int *shift, const int *era,
                                const int *kpos, int k, int E, int B, int EW, bool regular,
                                const int4 *chunks, const int *nchunks, const wgb_node *lvl,
-                               long long *hg, long long *hc, long long slot_elems, long long nrows,
-                               cudaStream_t st, uint2 *part = nullptr) {
+                               const HistOut &out, long long nrows, cudaStream_t st, uint2 *part = nullptr) {
     const bool has_era = E > 1;
     int fpl, nsc;
     hist_shape(S, F, B, fpl, nsc);
@@ -605,13 +617,12 @@ static cudaError_t launch_hist(int grid_x, const int8_t *bins, long long S, int 
         if (e != cudaSuccess) return e;                                                                \
         dim3 grid((unsigned)grid_x, (unsigned)((F + 32 * FPL_ - 1) / (32 * FPL_)));                    \
         fn<<<grid, NT_, smem, st>>>(bins, S, F, order, q, g, shift, era, kpos, k, E, B, ew, chunks,   \
-                                    nchunks, lvl, hg, hc, slot_elems, nrows, part);                    \
+                                    nchunks, lvl, out, nrows, part);                                   \
         e = cudaGetLastError();                                                                        \
         if (e != cudaSuccess || !part || ERA_) return e;                                              \
         const int seg = 16;                                                                            \
         dim3 rg((unsigned)((NSC_ * 32 * FPL_ + 255) / 256), grid.y, (unsigned)((grid_x + seg - 1) / seg)); \
-        k_hist_reduce<FPL_, NSC_><<<rg, 256, 0, st>>>(part, chunks, nchunks, lvl, kpos, F, B, seg, hg, hc, \
-                                                      slot_elems);                                      \
+        k_hist_reduce<FPL_, NSC_><<<rg, 256, 0, st>>>(part, chunks, nchunks, lvl, kpos, F, B, seg, out);  \
         return cudaGetLastError();                                                                     \
     }
 #define WGB_HIST_REG(FPL_, NT_, MINB_, NSC_, EWC_, ERA_) \
@@ -654,7 +665,7 @@ static cudaError_t launch_hist(int grid_x, const int8_t *bins, long long S, int 
 template <int NBW>  // split points per lane: ceil((B-1) / 32)
 __global__ void __launch_bounds__(SPLIT_WARPS * 32) k_split(
     const wgb_node *__restrict__ lvl, const int *nn_d, long long *hg, long long *hc, long long slot_elems,
-    int k, int B, const int *shift,
+    int k, int jofs, int B, const int *shift,
     float mcw, float eps, float msg, int4 *cand, int nblk, float *crit_out, bool writeback) {
     __shared__ float sG[SPLIT_WARPS][32 * NBW + 1], sH[SPLIT_WARPS][32 * NBW + 1];
     __shared__ Key s_k[SPLIT_WARPS];
@@ -708,8 +719,8 @@ __global__ void __launch_bounds__(SPLIT_WARPS * 32) k_split(
                 HL = __fadd_rn(HL, h[b]);
             }
             const SplitEval r = eval_split(GL, HL, GT, HT, mcw, eps);
-            if (crit_out && n == 0) crit_out[j * nb + bi] = r.gain;
-            const Key kk{0, r.gain > msg ? r.gain : -INFINITY, j * nb + bi};
+            if (crit_out && n == 0) crit_out[(jofs + j) * nb + bi] = r.gain;
+            const Key kk{0, r.gain > msg ? r.gain : -INFINITY, (jofs + j) * nb + bi};
             if (key_better(kk, best)) best = kk;
         }
     }
@@ -871,7 +882,7 @@ static inline size_t split_eras_smem(int B, int NB, int FB, int depth) {
 template <int NB>
 __global__ void __launch_bounds__(256) k_split_eras(
     const wgb_node *__restrict__ lvl, const int *nn_d, long long *hg, long long *hc, long long slot_elems,
-    int k, int E, int B, const int *shift,
+    int k, int kl, int jofs, int E, int B, const int *shift,
     float mcw, float eps, float msg, float factor, const int *__restrict__ sched,
     const uint8_t *__restrict__ ops, int nops, int depth, int4 *cand, int nblk, float *crit_out,
     bool writeback) {
@@ -917,8 +928,8 @@ __global__ void __launch_bounds__(256) k_split_eras(
         const int ne = min(EB, E - e0);
         if (warp < ne) {
             const int e = sched[e0 + warp];
-            const long long base = slot * slot_elems + ((long long)e * k + j0) * B1;
-            const long long bbase = bslot * slot_elems + ((long long)e * k + j0) * B1;
+            const long long base = slot * slot_elems + ((long long)e * kl + j0) * B1;
+            const long long bbase = bslot * slot_elems + ((long long)e * kl + j0) * B1;
             for (int t = lane; t < nf * B1; t += 32) {
                 const int f = t / B1, b = t - f * B1;
                 long long gv = hg[base + t], cv = hc[base + t];
@@ -972,8 +983,8 @@ __global__ void __launch_bounds__(256) k_split_eras(
         const int b = it / FB, f = it - b * FB;
         if (b < nb && f < nf) {
             const float cr = __fmul_rn(acc[t], factor);
-            if (crit_out && n == 0) crit_out[(j0 + f) * nb + b] = cr;
-            const Key kk{abs(ds[t]), cr > msg ? cr : -INFINITY, (j0 + f) * nb + b};
+            if (crit_out && n == 0) crit_out[(jofs + j0 + f) * nb + b] = cr;
+            const Key kk{abs(ds[t]), cr > msg ? cr : -INFINITY, (jofs + j0 + f) * nb + b};
             if (key_better(kk, best)) best = kk;
         }
     }
@@ -1034,21 +1045,65 @@ __device__ void plan_next_level(wgb_node *__restrict__ lvl, wgb_node *__restrict
     if (threadIdx.x == 0) nn[d + 1] = 2 * base;
 }
 
+// Single-rank fits: a node's exact left count (lcount, from its histogram)
+// is also its local one, so the next level's row layout is known before the
+// partition.  Per splitting node n (node order): part[n] = {left cursor 0,
+// start of n's children in the next order, left count, right cursor 0};
+// the children's segments [ns, ns+L) and [ns+L, ns+lcnt); the next level's
+// active rows; then (chunks != NULL) the next level's histogram chunk list.
+// Runs after plan_next_level in the same block.
+__device__ void plan_children(const wgb_node *__restrict__ lvl, wgb_node *__restrict__ nxt, const int *nn,
+                              int *nact, int d, int4 *part, int4 *chunks, int *nchunks, int chunk_cap,
+                              int *s_scan) {
+    __syncthreads();  // nxt records and nn[d + 1] of plan_next_level
+    const int nnd = __ldcg(nn + d);
+    int base = 0;
+    for (int b0 = 0; b0 < nnd; b0 += blockDim.x) {
+        const int i = b0 + threadIdx.x;
+        const bool spl = i < nnd && __ldcg(&lvl[i].fpos) >= 0;
+        const int v = spl ? __ldcg(&lvl[i].lcnt) : 0;
+        int tot;
+        const int ns = base + block_scan_excl(v, s_scan, tot);
+        if (spl) {
+            const int L = (int)__ldcg(&lvl[i].lcount);
+            part[i] = make_int4(0, ns, L, 0);
+            const int c = __ldcg(&lvl[i].child);
+            nxt[c].lstart = ns;
+            nxt[c].lcnt = L;
+            nxt[c + 1].lstart = ns + L;
+            nxt[c + 1].lcnt = v - L;
+        }
+        base += tot;
+    }
+    if (threadIdx.x == 0) nact[d + 1] = base;
+    if (chunks) {
+        __syncthreads();
+        plan_chunks(nxt, nn[d + 1], chunks, nchunks, chunk_cap);
+    }
+}
+
 // Per node: final arg-max, per-era gain of the chosen split (importance,
 // core.py:624-627) and the exact left-child totals (bins <= bin plus the
 // negative-bin slot, which always goes left).  The last block of the launch
 // to finish then plans the next level (plan_next_level); `done` is a
 // zero-initialised counter that this block returns to zero.
+// Feature-sliced fits (win != NULL): the arg-max, totals and gains are this
+// rank's best among its own positions [jofs, jofs + k) (pool layout width
+// kl), written as the node's record in this rank's region of win --
+// {key A, key c, key idx, -, lcount (int64), lsumq (int64), gain[E]} -- for
+// k_split_pick to choose from after the all-gather; nothing is planned.
 __global__ void __launch_bounds__(256) k_split_final(
     wgb_node *__restrict__ lvl, wgb_node *__restrict__ nxt, int *nn, int d, int ntree,
-    const long long *__restrict__ hg, const long long *__restrict__ hc, long long slot_elems, int k, int E, int B,
-    const int *shift, float mcw, float eps, const int4 *__restrict__ cand, int nblk, float *era_gain, int *done,
-    bool writeback) {
+    const long long *__restrict__ hg, const long long *__restrict__ hc, long long slot_elems, int kl, int jofs,
+    int E, int B, const int *shift, float mcw, float eps, const int4 *__restrict__ cand, int nblk, float *era_gain,
+    int *done, bool writeback, int4 *part, int *nact, int4 *chunks, int *nchunks, int chunk_cap, int *win,
+    int win_words, int wslice) {
     const int n = blockIdx.x;
     __shared__ Key s_best, s_kw[8];
     __shared__ long long s_c[8], s_g[8];
     __shared__ int s_scan[33];
     __shared__ bool s_last;
+    int *rec = win ? win + ((long long)wslice * (ntree << d) + n) * win_words : nullptr;
     if (n < nn[d]) {
         const float inv = pow2f(-shift[node_tree(lvl[n].built)]);
         {   // arg-max over the node's candidate blocks, all threads
@@ -1072,22 +1127,33 @@ __global__ void __launch_bounds__(256) k_split_final(
         wgb_node &nd = lvl[n];
         if (!(best.c > -INFINITY)) {
             if (threadIdx.x == 0) {
-                nd.fpos = -1;
-                nd.lsumq = 0;
-                nd.lcount = 0;
+                if (rec) {
+                    rec[0] = best.A;
+                    rec[1] = __float_as_int(best.c);
+                    rec[2] = best.idx;
+                    rec[3] = 0;
+                    *reinterpret_cast<long long *>(rec + 4) = 0;
+                    *reinterpret_cast<long long *>(rec + 6) = 0;
+                } else {
+                    nd.fpos = -1;
+                    nd.lsumq = 0;
+                    nd.lcount = 0;
+                }
             }
         } else {
             const int nb = B - 1, B1 = B + 1;
             const int fpos = best.idx / nb, bin = best.idx - fpos * nb;
+            const int fl = fpos - jofs;  // position in the pool's layout
             const long long slot = nd.slot;
             // an unbuilt node's histogram is parent - built sibling; the split
             // search wrote it back except at the last split level
             const bool sub = !node_built(nd.built) && !writeback;
             const long long bslot = sub ? lvl[n ^ 1].slot : 0;
+            float *gain_out = rec ? reinterpret_cast<float *>(rec + 8) : era_gain + (long long)n * E;
             long long lc = 0, ls = 0;
             for (int e = threadIdx.x; e < E; e += blockDim.x) {
-                const long long off = slot * slot_elems + ((long long)e * k + fpos) * B1;
-                const long long boff = bslot * slot_elems + ((long long)e * k + fpos) * B1;
+                const long long off = slot * slot_elems + ((long long)e * kl + fl) * B1;
+                const long long boff = bslot * slot_elems + ((long long)e * kl + fl) * B1;
                 auto gq = [&](int b) { return hg[off + b] - (sub ? hg[boff + b] : 0ll); };
                 auto cq = [&](int b) { return hc[off + b] - (sub ? hc[boff + b] : 0ll); };
                 float GT = 0.0f, HT = 0.0f, GL = 0.0f, HL = 0.0f;
@@ -1106,7 +1172,7 @@ __global__ void __launch_bounds__(256) k_split_final(
                 }
                 lc += cq(B);
                 ls += gq(B);
-                era_gain[(long long)n * E + e] = eval_split(GL, HL, GT, HT, mcw, eps).gain;
+                gain_out[e] = eval_split(GL, HL, GT, HT, mcw, eps).gain;
             }
             lc = warp_sum(lc);
             ls = warp_sum(ls);
@@ -1120,14 +1186,84 @@ __global__ void __launch_bounds__(256) k_split_final(
                     lc += s_c[w];
                     ls += s_g[w];
                 }
-                nd.fpos = fpos;
-                nd.bin = bin;
-                nd.lcount = lc;
-                nd.lsumq = ls;
+                if (rec) {
+                    rec[0] = best.A;
+                    rec[1] = __float_as_int(best.c);
+                    rec[2] = best.idx;
+                    rec[3] = 0;
+                    *reinterpret_cast<long long *>(rec + 4) = lc;
+                    *reinterpret_cast<long long *>(rec + 6) = ls;
+                } else {
+                    nd.fpos = fpos;
+                    nd.bin = bin;
+                    nd.lcount = lc;
+                    nd.lsumq = ls;
+                }
             }
         }
     }
+    if (rec) return;  // k_split_pick decides and plans
     // the last block to get here plans the next level
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        __threadfence();
+        s_last = atomicAdd(done, 1) == (int)gridDim.x - 1;
+    }
+    __syncthreads();
+    if (!s_last) return;
+    __threadfence();
+    plan_next_level(lvl, nxt, nn, d, shift, ntree, s_scan);
+    if (part) plan_children(lvl, nxt, nn, nact, d, part, chunks, nchunks, chunk_cap, s_scan);
+    if (threadIdx.x == 0) *done = 0;
+}
+
+// Feature-sliced fits, after the all-gather of win: per node the best of the
+// ranks' records by the same key order (so the choice is the one a single
+// rank searching every position makes), its totals and per-era gains into
+// the node; the last block plans the next level.
+__global__ void __launch_bounds__(256) k_split_pick(wgb_node *__restrict__ lvl, wgb_node *__restrict__ nxt, int *nn,
+                                                    int d, int ntree, int B, int E, const int *shift,
+                                                    const int *__restrict__ win, int win_words, int nslice,
+                                                    float *era_gain, int *done) {
+    const int n = blockIdx.x;
+    __shared__ int s_w;
+    __shared__ int s_scan[33];
+    __shared__ bool s_last;
+    const long long region = (long long)(ntree << d) * win_words;
+    if (n < nn[d]) {
+        if (threadIdx.x == 0) {
+            Key best = key_none();
+            int w = -1;
+            for (int r = 0; r < nslice; ++r) {
+                const int *rc = win + r * region + (long long)n * win_words;
+                const Key kk{rc[0], __int_as_float(rc[1]), rc[2]};
+                if (key_better(kk, best)) {
+                    best = kk;
+                    w = r;
+                }
+            }
+            wgb_node &nd = lvl[n];
+            if (w < 0 || !(best.c > -INFINITY)) {
+                nd.fpos = -1;
+                nd.lsumq = 0;
+                nd.lcount = 0;
+                w = -1;
+            } else {
+                const int *rc = win + w * region + (long long)n * win_words;
+                const int nb = B - 1;
+                nd.fpos = best.idx / nb;
+                nd.bin = best.idx % nb;
+                nd.lcount = *reinterpret_cast<const long long *>(rc + 4);
+                nd.lsumq = *reinterpret_cast<const long long *>(rc + 6);
+            }
+            s_w = w;
+        }
+        __syncthreads();
+        if (s_w >= 0) {
+            const float *g = reinterpret_cast<const float *>(win + s_w * region + (long long)n * win_words + 8);
+            for (int e = threadIdx.x; e < E; e += blockDim.x) era_gain[(long long)n * E + e] = g[e];
+        }
+    }
     __syncthreads();
     if (threadIdx.x == 0) {
         __threadfence();
@@ -1392,6 +1528,34 @@ __global__ void __launch_bounds__(PART_THREADS) k_scatter(
     int wbase = 0;
     for (int w = 0; w < warp; ++w) wbase += sw[w];
     int lp = tile_off[blockIdx.x] + wbase + incl - c;
+    if (last) {
+        // every row's leaf update (the children are the tree's last level);
+        // the rows are distinct, so all prediction loads go before any store
+        float lv[IPT], pv[IPT];
+        long long at[IPT];
+#pragma unroll
+        for (int u = 0; u < IPT; ++u) {
+            at[u] = -1;
+            lv[u] = 0.0f;
+            if (f[u] == 3) continue;
+            const int n = nid[u];
+            ScatterNode nd;
+            if (n < CACHE) {
+                nd = s_nc[n];
+            } else {
+                const wgb_node &g = lvl[n];
+                nd = ScatterNode{g.leaf, g.lstart, g.child, 0, 0, 0, node_tree(g.built)};
+            }
+            lv[u] = f[u] == 2 ? nd.leaf : last[nd.child + (f[u] == 1 ? 0 : 1)].leaf;
+            at[u] = (long long)row[u] * K + cls + nd.tree;
+        }
+#pragma unroll
+        for (int u = 0; u < IPT; ++u) pv[u] = at[u] >= 0 ? pred[at[u]] : 0.0f;
+#pragma unroll
+        for (int u = 0; u < IPT; ++u)
+            if (at[u] >= 0) pred[at[u]] = __fadd_rn(pv[u], __fmul_rn(lr, lv[u]));
+        return;
+    }
 #pragma unroll
     for (int u = 0; u < IPT; ++u) {
         if (f[u] == 3) break;
@@ -1418,15 +1582,184 @@ __global__ void __launch_bounds__(PART_THREADS) k_scatter(
                 np = nd.py + nd.pz + (int)(p - nd.lstart) - lb;
                 child = nd.child + 1;
             }
-            if (last) {  // the children are the tree's last level: their leaf updates
-                float *pp = pred + (long long)row[u] * K + cls + nd.tree;
-                *pp = __fadd_rn(*pp, __fmul_rn(lr, last[child].leaf));
-            } else if (np >= 0 && np < npos) {  // always true for consistent offsets; guards memory
+            if (np >= 0 && np < npos) {  // always true for consistent offsets; guards memory
                 order_next[np] = row[u];
                 posnode_next[np] = child;
             }
             if (f[u] == 1) ++lp;
         }
+    }
+}
+
+// Single-rank one-era level partition in one launch.  plan_children has
+// laid out the next level (part[n] = {left cursor 0, start of n's children,
+// left count, right cursor 0}).  Each CTA takes PART_TILE consecutive
+// positions, computes their flags (k_flags' rule), ranks its rows per
+// (node, side) with shared atomics, reserves each (node, side) range with
+// one global atomic on the node's cursor, and writes the rows to their
+// child's segment.  Within a child the rows are not in their previous
+// relative order: nothing depends on it with one era (the histograms are
+// exact integer sums; era windows, which need era-sorted rows, take the
+// stable three-kernel partition).  At the tree's last level (`last`) every
+// row only gets its leaf update.
+__global__ void __launch_bounds__(PART_THREADS) k_partition(
+    const wgb_node *__restrict__ lvl, const int *nn_d, const int *nact_d, const int *__restrict__ order,
+    const int *__restrict__ posnode, const int8_t *__restrict__ bins, long long S,
+    const int8_t *__restrict__ bins_fm, long long NT, const int *__restrict__ feats, int4 *part,
+    int *__restrict__ order_next, int *__restrict__ posnode_next, float *__restrict__ pred, int K, int cls,
+    float lr, long long npos, long long nloc, const wgb_node *__restrict__ last) {
+    constexpr int IPT = PART_TILE / PART_THREADS;  // 8 consecutive positions per thread
+    constexpr int CACHE = 512;                     // nodes whose records are cached per CTA
+    struct PNode {
+        float leaf;
+        int child, ns, L;
+        int tree, feat, bin;  // feat: split feature, -1 leaf
+    };
+    __shared__ PNode s_nc[CACHE];
+    __shared__ int s_key[2 * PART_TILE];  // per (node - first node, side): local count, then range start
+    __shared__ int s_first, s_lastn;
+    const int nnd = *nn_d;
+    auto node_rec = [&](int i) {
+        const wgb_node &nd = lvl[i];
+        const int fp = nd.fpos;
+        const int4 pr = fp >= 0 ? part[i] : make_int4(0, 0, 0, 0);
+        return PNode{nd.leaf, nd.child, pr.y, pr.z, node_tree(nd.built), fp >= 0 ? feats[fp] : -1, nd.bin};
+    };
+    auto rec = [&](int n) { return n < CACHE ? s_nc[n] : node_rec(n); };
+    for (int i = threadIdx.x; i < min(nnd, CACHE); i += PART_THREADS) s_nc[i] = node_rec(i);
+    if (!last)
+        for (int i = threadIdx.x; i < 2 * PART_TILE; i += PART_THREADS) s_key[i] = 0;
+    if (threadIdx.x == 0) {
+        s_first = INT_MAX;
+        s_lastn = -1;
+    }
+    const int nact = *nact_d;
+    const long long p0 = (long long)blockIdx.x * PART_TILE + threadIdx.x * IPT;
+    int nid[IPT], row[IPT];
+    if (p0 + IPT <= nact) {  // p0 is a multiple of 8: 32-byte index loads
+        const int4 *o4 = reinterpret_cast<const int4 *>(order + p0);
+        const int4 a = o4[0], b = o4[1];
+        row[0] = a.x; row[1] = a.y; row[2] = a.z; row[3] = a.w;
+        row[4] = b.x; row[5] = b.y; row[6] = b.z; row[7] = b.w;
+        if (posnode) {
+            const int4 *n4 = reinterpret_cast<const int4 *>(posnode + p0);
+            const int4 c4 = n4[0], d4 = n4[1];
+            nid[0] = c4.x; nid[1] = c4.y; nid[2] = c4.z; nid[3] = c4.w;
+            nid[4] = d4.x; nid[5] = d4.y; nid[6] = d4.z; nid[7] = d4.w;
+        } else {
+#pragma unroll
+            for (int u = 0; u < IPT; ++u) nid[u] = (int)((p0 + u) / nloc);  // level 0: tree t owns [tN, (t+1)N)
+        }
+    } else {
+#pragma unroll
+        for (int u = 0; u < IPT; ++u) {
+            const bool ok = p0 + u < nact;
+            row[u] = ok ? order[p0 + u] : 0;
+            nid[u] = !ok ? -1 : (posnode ? posnode[p0 + u] : (int)((p0 + u) / nloc));
+        }
+    }
+    __syncthreads();  // node cache, zeroed counters
+    // flags: 1 left, 0 right, 2 the node is a leaf, 3 no position
+    uint32_t fb = 0;  // 2 bits per position
+    int nmin = INT_MAX, nmax = -1;
+#pragma unroll
+    for (int u = 0; u < IPT; ++u) {
+        if ((unsigned)nid[u] >= (unsigned)nnd || (unsigned long long)(unsigned)row[u] >= (unsigned long long)nloc)
+            nid[u] = -1;  // out of range: treated as no position (guards memory)
+        uint32_t fu = 3u;
+        if (nid[u] >= 0) {
+            int feat, bin;
+            if (nid[u] < CACHE) {
+                feat = s_nc[nid[u]].feat;
+                bin = s_nc[nid[u]].bin;
+            } else {
+                const PNode r = node_rec(nid[u]);
+                feat = r.feat;
+                bin = r.bin;
+            }
+            fu = 2u;
+            if (feat >= 0) {
+                const int8_t bv = bins_fm ? bins_fm[(long long)feat * NT + row[u]] : bins[(long long)row[u] * S + feat];
+                fu = bv <= bin ? 1u : 0u;
+                nmin = min(nmin, nid[u]);
+                nmax = max(nmax, nid[u]);
+            }
+        }
+        fb |= fu << (2 * u);
+    }
+    if (!last) {
+        // the splitting nodes of the tile (positions are in node order)
+        if (nmax >= 0) {
+            atomicMin(&s_first, nmin);
+            atomicMax(&s_lastn, nmax);
+        }
+        __syncthreads();
+        const int first = s_first;
+        const bool local = s_lastn - first < PART_TILE;  // else per-row global atomics (sparse node ids)
+        int rank[IPT];
+#pragma unroll
+        for (int u = 0; u < IPT; ++u) {
+            const uint32_t fu = (fb >> (2 * u)) & 3u;
+            rank[u] = 0;
+            if (local && fu <= 1u) rank[u] = atomicAdd(&s_key[2 * (nid[u] - first) + (fu == 1u ? 0 : 1)], 1);
+        }
+        __syncthreads();
+        if (local) {
+            const int nk = s_lastn >= first ? 2 * (s_lastn - first + 1) : 0;
+            for (int key = threadIdx.x; key < nk; key += PART_THREADS) {
+                const int cnt = s_key[key];
+                if (cnt > 0) {
+                    int4 *pr = part + first + (key >> 1);
+                    s_key[key] = atomicAdd((key & 1) ? &pr->w : &pr->x, cnt);
+                }
+            }
+        }
+        __syncthreads();
+#pragma unroll
+        for (int u = 0; u < IPT; ++u) {
+            const uint32_t fu = (fb >> (2 * u)) & 3u;
+            if (fu == 3u) continue;
+            const PNode nd = rec(nid[u]);
+            if (fu == 2u) {
+                float *pp = pred + (long long)row[u] * K + cls + nd.tree;
+                *pp = __fadd_rn(*pp, __fmul_rn(lr, nd.leaf));
+                continue;
+            }
+            const int side = fu == 1u ? 0 : 1;
+            int r;
+            if (local) {
+                r = s_key[2 * (nid[u] - first) + side] + rank[u];
+            } else {
+                int4 *pr = part + nid[u];
+                r = atomicAdd(side ? &pr->w : &pr->x, 1);
+            }
+            const long long np = (long long)nd.ns + (side ? nd.L : 0) + r;
+            if (np >= 0 && np < npos) {  // always true for consistent counts; guards memory
+                order_next[np] = row[u];
+                posnode_next[np] = nd.child + side;
+            }
+        }
+    } else {
+        // every row's leaf update; the rows are distinct, so all eight
+        // prediction loads are issued before any store
+        float lv[IPT], pv[IPT];
+        long long at[IPT];
+#pragma unroll
+        for (int u = 0; u < IPT; ++u) {
+            const uint32_t fu = (fb >> (2 * u)) & 3u;
+            at[u] = -1;
+            lv[u] = 0.0f;
+            if (fu != 3u) {
+                const PNode nd = rec(nid[u]);
+                lv[u] = fu == 2u ? nd.leaf : last[nd.child + (fu == 1u ? 0 : 1)].leaf;
+                at[u] = (long long)row[u] * K + cls + nd.tree;
+            }
+        }
+#pragma unroll
+        for (int u = 0; u < IPT; ++u) pv[u] = at[u] >= 0 ? pred[at[u]] : 0.0f;
+#pragma unroll
+        for (int u = 0; u < IPT; ++u)
+            if (at[u] >= 0) pred[at[u]] = __fadd_rn(pv[u], __fmul_rn(lr, lv[u]));
     }
 }
 
@@ -1467,6 +1800,12 @@ static inline long long *LL(int64_t *p) { return reinterpret_cast<long long *>(p
 // trees grown together (a multiclass round: one per class); levels hold
 // ntree << d node records
 static inline int ws_ntree(const wgb_ws *ws) { return ws->ntree > 1 ? ws->ntree : 1; }
+// Single-rank one-era fit (the local rows are all rows): the split's exact
+// left counts are the local ones, so the split plans the next level's row
+// layout and the partition is one launch (k_partition).
+static inline bool fused_partition(const wgb_ws *ws) {
+    return ws->N_global == ws->N && ws->E == 1 && ws->sync != nullptr && ws->nslice <= 1;
+}
 static inline wgb_node *level_nodes(const wgb_ws *ws, int d) {
     return ws->nodes + (long long)ws_ntree(ws) * ((1 << d) - 1);
 }
@@ -1476,10 +1815,22 @@ static inline const int *level_order(const wgb_ws *ws, int d) {
 static inline const int *level_posnode(const wgb_ws *ws, int d) {
     return d == 0 ? nullptr : ws->posnode[(d - 1) & 1];
 }
-// Histogram pool: one int64 region per slot, [sums E*k*(B+1)][counts E*k*(B+1)][2 spare];
-// root slot t's first spare cell carries tree t's root sum of q through the
-// level-0 reduction, so one collective per level covers sums, counts and roots.
-static inline long long hist_cells(const wgb_ws *ws) { return (long long)ws->E * ws->k * (ws->B + 1); }
+// Feature-sliced multi-rank fit: rank `slice` keeps and searches positions
+// [slice*ks, slice*ks + ks) of the tree's k (the last slices may be short
+// or empty).
+static inline bool sliced(const wgb_ws *ws) { return ws->nslice > 1; }
+static inline int hist_k(const wgb_ws *ws) { return sliced(ws) ? ws->ks : ws->k; }  // the pool's k
+static inline int slice_j0(const wgb_ws *ws) { return sliced(ws) ? ws->slice * ws->ks : 0; }
+static inline int slice_kr(const wgb_ws *ws) {
+    if (!sliced(ws)) return ws->k;
+    const int r = ws->k - slice_j0(ws);
+    return r < 0 ? 0 : (r < ws->ks ? r : ws->ks);
+}
+// Histogram pool: one int64 region per slot, [sums E*k*(B+1)][counts E*k*(B+1)][2 spare]
+// (ks in place of k when sliced); root slot t's first spare cell carries
+// tree t's root sum of q through the level-0 reduction, so one collective
+// per level covers sums, counts and roots.
+static inline long long hist_cells(const wgb_ws *ws) { return (long long)ws->E * hist_k(ws) * (ws->B + 1); }
 static inline long long slot_elems(const wgb_ws *ws) { return 2 * hist_cells(ws) + 2; }
 
 static int grid_for(long long n, int threads, int cap = 148 * 16) {
@@ -1561,6 +1912,13 @@ static int check_ws(const wgb_ws *ws) {
     WGB_CHECK_ARG(ws->ntree >= 0 && ws->cls >= 0 && ws->cls + ws_ntree(ws) <= ws->K,
                   "trees cls .. cls + ntree - 1 must be output columns (< K)");
     WGB_CHECK_ARG((long long)ws_ntree(ws) * ws->N < (1ll << 31), "ntree * rows per rank must be < 2^31");
+    if (sliced(ws)) {
+        WGB_CHECK_ARG(ws->slice >= 0 && ws->slice < ws->nslice, "slice %d of %d", ws->slice, ws->nslice);
+        WGB_CHECK_ARG(ws->ks >= 1 && (long long)ws->ks * ws->nslice >= ws->k, "ks * nslice must cover k");
+        WGB_CHECK_ARG(ws->hstage != nullptr && ws->win != nullptr && ws->win_words >= 8 + ws->E &&
+                          ws->win_words % 2 == 0 && (reinterpret_cast<uintptr_t>(ws->win) & 7) == 0,
+                      "a sliced fit needs hstage and an 8-byte aligned win of even win_words >= 8 + E");
+    }
     return WGB_OK;
 }
 
@@ -1630,10 +1988,28 @@ int wgb_level_hist(const wgb_ws *ws, int32_t d, void *stream) {
     int first, count;
     wgb_level_slots(ws, d, &first, &count);
     const long long se = slot_elems(ws), nc = hist_cells(ws);
-    WGB_CUDA(cudaMemsetAsync(ws->hg + (long long)first * se, 0, sizeof(int64_t) * se * count, st));
-    if (d == 0) {  // this rank's root sums ride along with the level-0 reduction
-        k_root_cells<<<1, 32, 0, st>>>(LL(ws->hg), LL(ws->rootsum), se, nc, ws_ntree(ws));
-        WGB_LAUNCHED("k_root_cells");
+    // where the build adds its cells: the built slots of the pool, or (a
+    // sliced fit) the staging buffer, one region of `count` slots per slice,
+    // which the reduce-scatter over the ranks turns into those slots of each
+    // rank's pool
+    HistOut out;
+    if (sliced(ws)) {
+        const long long region = (long long)count * se;
+        WGB_CHECK_ARG(region * ws->nslice <= ws->hstage_elems, "hstage holds %lld elements, level %d needs %lld",
+                      (long long)ws->hstage_elems, d, region * ws->nslice);
+        WGB_CUDA(cudaMemsetAsync(ws->hstage, 0, sizeof(int64_t) * region * ws->nslice, st));
+        if (d == 0) {  // this rank's root sums ride along with the level-0 reduction
+            k_root_cells<<<1, 32, 0, st>>>(LL(ws->hstage), LL(ws->rootsum), se, nc, ws_ntree(ws), ws->nslice, region);
+            WGB_LAUNCHED("k_root_cells");
+        }
+        out = HistOut{LL(ws->hstage), LL(ws->hstage) + nc, se, region, ws->ks, first};
+    } else {
+        WGB_CUDA(cudaMemsetAsync(ws->hg + (long long)first * se, 0, sizeof(int64_t) * se * count, st));
+        if (d == 0) {
+            k_root_cells<<<1, 32, 0, st>>>(LL(ws->hg), LL(ws->rootsum), se, nc, ws_ntree(ws), 1, 0);
+            WGB_LAUNCHED("k_root_cells");
+        }
+        out = HistOut{LL(ws->hg), LL(ws->hg) + nc, se, 0, ws->k, 0};
     }
     wgb_node *lvl = level_nodes(ws, d);
     if (d == 0) {  // later levels' chunk lists are planned by the previous level's partition
@@ -1654,7 +2030,7 @@ int wgb_level_hist(const wgb_ws *ws, int32_t d, void *stream) {
     cudaError_t e = launch_hist((int)max_chunks, hb, hS, hF, ord, ws->qg, nullptr, nullptr,
                                 ws->E > 1 ? ws->era : nullptr, hkpos, ws->k, ws->E, ws->B, ws->hist_ew,
                                 ws->regular != 0, reinterpret_cast<const int4 *>(ws->chunks), ws->nchunks,
-                                lvl, LL(ws->hg), LL(ws->hg) + nc, se, ws->N, st,
+                                lvl, out, ws->N, st,
                                 ws->E == 1 && ws->part_hist &&
                                         ws->part_hist_elems >= wgb_hist_part_elems(hS, hF, ws->B, max_chunks)
                                     ? reinterpret_cast<uint2 *>(ws->part_hist)
@@ -1683,24 +2059,28 @@ int wgb_level_split(const wgb_ws *ws, int32_t d, void *stream) {
     // (from level 1 on, the split kernels first turn each unbuilt node's
     // parent histogram into parent - built sibling)
     const int nb = ws->B - 1;
+    // this rank's positions (all k unless the fit is feature-sliced)
+    const int j0 = slice_j0(ws), kr = slice_kr(ws), kl = hist_k(ws);
     int4 *cand = reinterpret_cast<int4 *>(ws->cand);
     int nblk;
     if (ws->E == 1) {
-        nblk = (ws->k + SPLIT_WARPS - 1) / SPLIT_WARPS;
+        nblk = (kr + SPLIT_WARPS - 1) / SPLIT_WARPS;
         WGB_CHECK_ARG(nblk <= ws->ncand_blk, "candidate buffer too small: %d blocks per node needed", nblk);
         const unsigned g = (unsigned)nblk * (unsigned)cap;  // node-major blocks
 #define WGB_SPLIT_W(NBW_)                                                                                  \
-    k_split<NBW_><<<g, SPLIT_WARPS * 32, 0, st>>>(lvl, ws->nn + d, hg, hc, se, ws->k, ws->B, ws->shift,   \
+    k_split<NBW_><<<g, SPLIT_WARPS * 32, 0, st>>>(lvl, ws->nn + d, hg, hc, se, kr, j0, ws->B, ws->shift,  \
                                                 ws->mcw, ws->eps, ws->msg, cand, nblk, ws->crit_out,      \
                                                 d < ws->D - 1)
-        if (nb <= 32) WGB_SPLIT_W(1); else if (nb <= 64) WGB_SPLIT_W(2); else WGB_SPLIT_W(4);
+        if (g > 0) {
+            if (nb <= 32) WGB_SPLIT_W(1); else if (nb <= 64) WGB_SPLIT_W(2); else WGB_SPLIT_W(4);
+            WGB_LAUNCHED("k_split");
+        }
 #undef WGB_SPLIT_W
-        WGB_LAUNCHED("k_split");
     } else {
         WGB_CHECK_ARG(ws->era_sched && ws->era_ops && ws->era_nops >= ws->E && ws->era_depth >= 1,
                       "levels with eras need the criterion plan of wgb_era_mean_plan in the workspace");
         const int fb = split_era_fb(ws->B);
-        nblk = (ws->k + fb - 1) / fb;
+        nblk = (kr + fb - 1) / fb;
         WGB_CHECK_ARG(nblk <= ws->ncand_blk, "candidate buffer too small: %d blocks per node needed", nblk);
         const unsigned g = (unsigned)nblk * (unsigned)cap;
         int dev = 0, smem_max = 0;
@@ -1711,21 +2091,41 @@ int wgb_level_split(const wgb_ws *ws, int32_t d, void *stream) {
         const size_t sm = split_eras_smem(ws->B, NB_, EraSplitShape<NB_>::FB, ws->era_depth);                  \
         WGB_CHECK_ARG(sm <= (size_t)smem_max, "era criterion plan too deep (%d) for shared memory", ws->era_depth); \
         WGB_CUDA(cudaFuncSetAttribute(k_split_eras<NB_>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm)); \
-        k_split_eras<NB_><<<g, 256, sm, st>>>(lvl, ws->nn + d, hg, hc, se, ws->k, ws->E, ws->B, ws->shift,       \
+        k_split_eras<NB_><<<g, 256, sm, st>>>(lvl, ws->nn + d, hg, hc, se, kr, kl, j0, ws->E, ws->B, ws->shift, \
                                               ws->mcw, ws->eps, ws->msg, ws->mean_factor, ws->era_sched,        \
                                               ws->era_ops, ws->era_nops, ws->era_depth, cand, nblk,             \
                                               ws->crit_out, d < ws->D - 1);                                     \
     }
-        if (nb <= 8) WGB_SPLIT_ERAS(8) else if (nb <= 32) WGB_SPLIT_ERAS(32) else WGB_SPLIT_ERAS(128)
+        if (g > 0) {
+            if (nb <= 8) WGB_SPLIT_ERAS(8) else if (nb <= 32) WGB_SPLIT_ERAS(32) else WGB_SPLIT_ERAS(128)
+            WGB_LAUNCHED("k_split_eras");
+        }
 #undef WGB_SPLIT_ERAS
-        WGB_LAUNCHED("k_split_eras");
     }
     float *eg = ws->era_gain + (long long)ws_ntree(ws) * ((1 << d) - 1) * ws->E;
     WGB_CHECK_ARG(ws->sync != nullptr, "workspace needs its sync counters");
-    k_split_final<<<cap, 256, 0, st>>>(lvl, level_nodes(ws, d + 1), ws->nn, d, ws_ntree(ws), hg, hc, se, ws->k,
+    const bool fp = fused_partition(ws);
+    k_split_final<<<cap, 256, 0, st>>>(lvl, level_nodes(ws, d + 1), ws->nn, d, ws_ntree(ws), hg, hc, se, kl, j0,
                                        ws->E, ws->B, ws->shift, ws->mcw, ws->eps, cand, nblk, eg, ws->sync,
-                                       d < ws->D - 1);
+                                       d < ws->D - 1, fp ? reinterpret_cast<int4 *>(ws->part) : nullptr, ws->nact,
+                                       fp && d < ws->D - 1 ? reinterpret_cast<int4 *>(ws->chunks) : nullptr,
+                                       ws->nchunks, ws->chunk_cap, sliced(ws) ? ws->win : nullptr, ws->win_words,
+                                       ws->slice);
     WGB_LAUNCHED("k_split_final");
+    return WGB_OK;
+}
+
+int wgb_level_pick(const wgb_ws *ws, int32_t d, void *stream) {
+    int rc = check_ws(ws);
+    if (rc) return rc;
+    WGB_CHECK_ARG(d >= 0 && d < ws->D, "level %d out of range", d);
+    if (!sliced(ws)) return WGB_OK;  // wgb_level_split already decided
+    const int cap = ws_ntree(ws) << d;
+    float *eg = ws->era_gain + (long long)ws_ntree(ws) * ((1 << d) - 1) * ws->E;
+    k_split_pick<<<cap, 256, 0, as_stream(stream)>>>(level_nodes(ws, d), level_nodes(ws, d + 1), ws->nn, d,
+                                                     ws_ntree(ws), ws->B, ws->E, ws->shift, ws->win,
+                                                     ws->win_words, ws->nslice, eg, ws->sync);
+    WGB_LAUNCHED("k_split_pick");
     return WGB_OK;
 }
 
@@ -1755,11 +2155,19 @@ int wgb_level_partition(const wgb_ws *ws, int32_t d, void *stream) {
     WGB_CHECK_ARG(ntiles <= ws->ntiles, "tile buffer too small");
     const int *ord = level_order(ws, d);
     const int *pn = level_posnode(ws, d);
+    const bool last = d == ws->D - 1;
+    int4 *part = reinterpret_cast<int4 *>(ws->part);
+    if (fused_partition(ws)) {
+        k_partition<<<ntiles, PART_THREADS, 0, st>>>(
+            lvl, ws->nn + d, ws->nact + d, ord, pn, ws->bins, ws->S, ws->bins_fm, (ws->N + 15) & ~15ll, ws->feats,
+            part, ws->order[d & 1], ws->posnode[d & 1], ws->pred, ws->K, ws->cls, ws->lr, npos, ws->N,
+            last ? level_nodes(ws, d + 1) : nullptr);
+        WGB_LAUNCHED("k_partition");
+        return WGB_OK;
+    }
     k_flags<<<ntiles, PART_THREADS, 0, st>>>(lvl, ws->nn + d, ws->nact + d, ord, pn, ws->bins, ws->S, ws->bins_fm,
                                               (ws->N + 15) & ~15ll, ws->feats, ws->flags, ws->tile_cnt, ws->N);
     WGB_LAUNCHED("k_flags");
-    int4 *part = reinterpret_cast<int4 *>(ws->part);
-    const bool last = d == ws->D - 1;
     k_node_offsets<<<1, 1024, 0, st>>>(lvl, level_nodes(ws, d + 1), ws->nn, ws->nact, d, ws->flags,
                                        ws->tile_cnt, ws->tile_off, ntiles, part,
                                        last ? nullptr : reinterpret_cast<int4 *>(ws->chunks), ws->nchunks,

@@ -105,7 +105,7 @@ extern "C" int wgb_compute_histogram3_noalloc(const int8_t *bin_indices, int64_t
     WGB_LAUNCHED("wgb_compute_histogram3_noalloc setup");
     cudaError_t le = launch_hist(nchunk, bin_indices, F_master, (int)F_master, sample_indices, nullptr, residuals,
                                  shift, num_eras > 1 ? era_indices : nullptr, kpos, k, num_eras, num_bins, 0, false,
-                                 chunks, nchunks, nd, hg, hc, se, num_rows, st);
+                                 chunks, nchunks, nd, HistOut{hg, hc, se, 0, k, 0}, num_rows, st);
     if (le != cudaSuccess) {
         set_error("k_hist launch failed: %s", cudaGetErrorString(le));
         return WGB_ERR_CUDA;

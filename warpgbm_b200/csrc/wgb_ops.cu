@@ -668,8 +668,8 @@ int wgb_compute_histogram3(const int8_t *bin_indices, int64_t num_rows, int64_t 
         k_chunk_plan<<<1, 1024, 0, st>>>(nd, nn, chunks, nchunks, nchunk);
         cudaError_t le = launch_hist(nchunk, bin_indices, F_master, (int)F_master, sample_indices, nullptr,
                                      residuals, shift, num_eras > 1 ? era_indices : nullptr, kpos, k,
-                                     num_eras, num_bins, 0, false, chunks, nchunks, nd, hg, hc, se, num_rows,
-                                     st);
+                                     num_eras, num_bins, 0, false, chunks, nchunks, nd,
+                                     HistOut{hg, hc, se, 0, k, 0}, num_rows, st);
         if (le != cudaSuccess) {
             set_error("k_hist launch failed: %s", cudaGetErrorString(le));
             rc = WGB_ERR_CUDA;
