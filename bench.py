@@ -57,6 +57,8 @@ def parse():
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-c5", action="store_true", help="skip the config-5 strong-scaling sub-record")
     ap.add_argument("--no-cpu", action="store_true", help="skip the cpu_baseline sample")
+    ap.add_argument("--no-slices", action="store_true",
+                    help="multi-rank fits: all-reduce whole level histograms (no feature slices)")
     ap.add_argument("--clock-ms", type=int, default=200,
                     help="nvidia-smi sampling period during the timed region (0: no sampling)")
     ap.add_argument("--config", default="c2", choices=["c1", "c2", "c3", "c4", "c5"],
@@ -64,6 +66,18 @@ def parse():
                          "depth 10, 50 trees, then batch predict; c1 / c3 / c4: the other "
                          "BASELINE configs on one GPU (one line each, not the headline)")
     return ap.parse_args()
+
+
+FEATURE_SLICES = True  # --no-slices: multi-rank fits sum every histogram on every rank
+
+
+def new_model(params):
+    """WarpGBM(**params); with --no-slices a multi-rank fit all-reduces whole
+    histograms instead of reduce-scattering feature slices."""
+    from warpgbm_b200 import WarpGBM
+    m = WarpGBM(**params)
+    m._feature_slices = FEATURE_SLICES
+    return m
 
 
 def peaks():
@@ -375,7 +389,7 @@ def c5_measure(args, world, rank, local, dev, steps, warmup, clock_ms, rows=None
     import io
     with contextlib.redirect_stdout(io.StringIO()):
         for _ in range(warmup):
-            WarpGBM(**params).fit(X, y)
+            new_model(params).fit(X, y)
     barrier()
     launches0 = _lib.LAUNCHES[0]
     fit_ms, pred_ms = [], []
@@ -386,7 +400,7 @@ def c5_measure(args, world, rank, local, dev, steps, warmup, clock_ms, rows=None
             e0, e1, e2 = (torch.cuda.Event(enable_timing=True) for _ in range(3))
             e0.record()
             with contextlib.redirect_stdout(io.StringIO()):
-                model = WarpGBM(**params)
+                model = new_model(params)
                 model.fit(X, y)
             e1.record()
             pred = model.predict(X)
@@ -396,7 +410,7 @@ def c5_measure(args, world, rank, local, dev, steps, warmup, clock_ms, rows=None
             pred_ms.append(max_over_ranks(e1.elapsed_time(e2)))
     launches = _lib.LAUNCHES[0] - launches0
     with contextlib.redirect_stdout(io.StringIO()):  # roofline fit, per-level events
-        model = WarpGBM(**params)
+        model = new_model(params)
         model._hist_events = []
         model._comm_events = []
         model._split_events = []
@@ -544,7 +558,7 @@ def run_config(args):
 
     def fit(Xa, ya, ea):
         with contextlib.redirect_stdout(io.StringIO()):
-            m = WarpGBM(**params)
+            m = new_model(params)
             m.fit(Xa, ya, era_id=ea, **d["fit_kw"])
         return m
 
@@ -595,7 +609,7 @@ def run_config(args):
                         "eval_points": len(m.eval_loss)}
     if args.config == "c4":
         with contextlib.redirect_stdout(io.StringIO()):
-            mr = WarpGBM(**params)
+            mr = new_model(params)
             mr._hist_events = []
             mr._split_events = []
             mr.fit(Xd, yd, era_id=erad)
@@ -655,7 +669,9 @@ def run_reference_cuda_config(args):
 
 
 def main():
+    global FEATURE_SLICES
     args = parse()
+    FEATURE_SLICES = not args.no_slices
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
     local = int(os.environ.get("LOCAL_RANK", "0"))
@@ -699,7 +715,7 @@ def main():
     quiet = contextlib.redirect_stdout(io.StringIO())
     with quiet:
         for _ in range(args.warmup):
-            WarpGBM(**params).fit(X, y)
+            new_model(params).fit(X, y)
     barrier()
     model = None
     launches0 = _lib.LAUNCHES[0]
@@ -711,7 +727,7 @@ def main():
         w0 = time.perf_counter()
         with contextlib.redirect_stdout(io.StringIO()):
             for _ in range(args.steps):
-                model = WarpGBM(**params)
+                model = new_model(params)
                 model.fit(X, y)
         w1 = time.perf_counter()
         e1.record()
@@ -725,7 +741,7 @@ def main():
     barrier()
     r0.record()
     with contextlib.redirect_stdout(io.StringIO()):
-        model = WarpGBM(**params)
+        model = new_model(params)
         model._hist_events = []
         model._comm_events = []
         model._split_events = []
@@ -752,14 +768,14 @@ def main():
     e2e = None
     if not args.no_e2e:
         with contextlib.redirect_stdout(io.StringIO()):
-            WarpGBM(**{**params, "n_estimators": 1}).fit(Xh, yh)  # untimed: pinned staging setup
+            new_model({**params, "n_estimators": 1}).fit(Xh, yh)  # untimed: pinned staging setup
         barrier()
         f0 = torch.cuda.Event(enable_timing=True)
         f1 = torch.cuda.Event(enable_timing=True)
         f0.record()
         with contextlib.redirect_stdout(io.StringIO()):
             for _ in range(args.steps):
-                WarpGBM(**params).fit(Xh, yh)
+                new_model(params).fit(Xh, yh)
         f1.record()
         barrier()
         te = f0.elapsed_time(f1) / args.steps
