@@ -1150,12 +1150,25 @@ __global__ void __launch_bounds__(256) k_split_final(
             const bool sub = !node_built(nd.built) && !writeback;
             const long long bslot = sub ? lvl[n ^ 1].slot : 0;
             float *gain_out = rec ? reinterpret_cast<float *>(rec + 8) : era_gain + (long long)n * E;
+            // one era: the block loads the feature's cells in parallel first
+            // (the sums below stay sequential in bin order)
+            __shared__ long long s_cg[128], s_cc[128];
+            const bool staged = E == 1;
+            if (staged) {
+                const long long off = slot * slot_elems + (long long)fl * B1;
+                const long long boff = bslot * slot_elems + (long long)fl * B1;
+                for (int b = threadIdx.x; b < B1; b += blockDim.x) {
+                    s_cg[b] = hg[off + b] - (sub ? hg[boff + b] : 0ll);
+                    s_cc[b] = hc[off + b] - (sub ? hc[boff + b] : 0ll);
+                }
+                __syncthreads();
+            }
             long long lc = 0, ls = 0;
             for (int e = threadIdx.x; e < E; e += blockDim.x) {
                 const long long off = slot * slot_elems + ((long long)e * kl + fl) * B1;
                 const long long boff = bslot * slot_elems + ((long long)e * kl + fl) * B1;
-                auto gq = [&](int b) { return hg[off + b] - (sub ? hg[boff + b] : 0ll); };
-                auto cq = [&](int b) { return hc[off + b] - (sub ? hc[boff + b] : 0ll); };
+                auto gq = [&](int b) { return staged ? s_cg[b] : hg[off + b] - (sub ? hg[boff + b] : 0ll); };
+                auto cq = [&](int b) { return staged ? s_cc[b] : hc[off + b] - (sub ? hc[boff + b] : 0ll); };
                 float GT = 0.0f, HT = 0.0f, GL = 0.0f, HL = 0.0f;
                 for (int b = 0; b < B; ++b) {
                     const long long gb = gq(b), cb = cq(b);
