@@ -930,19 +930,43 @@ __global__ void __launch_bounds__(256) k_split_eras(
             const int e = sched[e0 + warp];
             const long long base = slot * slot_elems + ((long long)e * kl + j0) * B1;
             const long long bbase = bslot * slot_elems + ((long long)e * kl + j0) * B1;
-            for (int t = lane; t < nf * B1; t += 32) {
-                const int f = t / B1, b = t - f * B1;
-                long long gv = hg[base + t], cv = hc[base + t];
-                if (!built) {  // sibling = parent - built sibling, written back in place
-                    gv -= hg[bbase + t];
-                    cv -= hc[bbase + t];
-                    if (writeback) {  // (not at the last split level: its children are leaves)
-                        hg[base + t] = gv;
-                        hc[base + t] = cv;
+            // groups of LU cells per lane: every load of a group is issued
+            // before its write-back stores (which may alias later loads as
+            // far as the compiler knows), so a group costs one round trip
+            constexpr int LU = 4;
+            const int ncell = nf * B1;
+            for (int t0 = lane; t0 < ncell; t0 += 32 * LU) {
+                long long gv[LU], cv[LU], gb[LU], cb[LU];
+#pragma unroll
+                for (int u = 0; u < LU; ++u) {
+                    const int t = t0 + 32 * u;
+                    gv[u] = cv[u] = gb[u] = cb[u] = 0;
+                    if (t < ncell) {
+                        gv[u] = hg[base + t];
+                        cv[u] = hc[base + t];
+                        if (!built) {
+                            gb[u] = hg[bbase + t];
+                            cb[u] = hc[bbase + t];
+                        }
                     }
                 }
-                stg[f * B1p + b] = __fmul_rn(__ll2float_rn(gv), inv);
-                stg[(FB + f) * B1p + b] = __ll2float_rn(cv);
+#pragma unroll
+                for (int u = 0; u < LU; ++u) {
+                    const int t = t0 + 32 * u;
+                    if (t >= ncell) break;
+                    const int f = t / B1, b = t - f * B1;
+                    long long g = gv[u], c = cv[u];
+                    if (!built) {  // sibling = parent - built sibling, written back in place
+                        g -= gb[u];
+                        c -= cb[u];
+                        if (writeback) {  // (not at the last split level: its children are leaves)
+                            hg[base + t] = g;
+                            hc[base + t] = c;
+                        }
+                    }
+                    stg[f * B1p + b] = __fmul_rn(__ll2float_rn(g), inv);
+                    stg[(FB + f) * B1p + b] = __ll2float_rn(c);
+                }
             }
             __syncwarp();
             if (lane < nf) {
