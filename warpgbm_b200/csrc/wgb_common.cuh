@@ -126,6 +126,27 @@ __device__ __forceinline__ SplitEval eval_split(float GL, float HL, float GT, fl
     return r;
 }
 
+// The same with the parent term t3 = (GT*GT) / (HT + eps) computed once per
+// feature (it does not depend on the split point; identical value).
+__device__ __forceinline__ float parent_term(float GT, float HT, float eps) {
+    return __fdiv_rn(__fmul_rn(GT, GT), __fadd_rn(HT, eps));
+}
+__device__ __forceinline__ SplitEval eval_split_pt(float GL, float HL, float GT, float HT, float t3, float mcw,
+                                                   float eps) {
+    SplitEval r{0.0f, 0.0f};
+    float GR = __fsub_rn(GT, GL);
+    float HR = __fsub_rn(HT, HL);
+    if (HL >= mcw && HR >= mcw) {
+        float dl = __fadd_rn(HL, eps), dr = __fadd_rn(HR, eps);
+        float t1 = __fdiv_rn(__fmul_rn(GL, GL), dl);
+        float t2 = __fdiv_rn(__fmul_rn(GR, GR), dr);
+        r.gain = __fsub_rn(__fadd_rn(t1, t2), t3);
+        float lv = __fdiv_rn(GL, dl), rv = __fdiv_rn(GR, dr);
+        r.dir = (lv > rv) ? 1.0f : -1.0f;
+    }
+    return r;
+}
+
 // Arg-max key of the directional era split (core.py:577-594): higher
 // agreement first (max over every candidate), then higher masked criterion
 // (-inf where crit <= min_split_gain), then the lower flat index.

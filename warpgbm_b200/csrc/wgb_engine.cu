@@ -935,6 +935,10 @@ __global__ void __launch_bounds__(256) k_split_eras(
             // far as the compiler knows), so a group costs one round trip
             constexpr int LU = 4;
             const int ncell = nf * B1;
+            // t / B1 without an integer division: t < 2^12, so the fp32
+            // product (t + 0.5) / B1 stays more than 0.5/B1 away from an
+            // integer and truncates to the exact quotient
+            const float rB1 = 1.0f / (float)B1;
             for (int t0 = lane; t0 < ncell; t0 += 32 * LU) {
                 long long gv[LU], cv[LU], gb[LU], cb[LU];
 #pragma unroll
@@ -954,7 +958,7 @@ __global__ void __launch_bounds__(256) k_split_eras(
                 for (int u = 0; u < LU; ++u) {
                     const int t = t0 + 32 * u;
                     if (t >= ncell) break;
-                    const int f = t / B1, b = t - f * B1;
+                    const int f = (int)(((float)t + 0.5f) * rB1), b = t - f * B1;
                     long long g = gv[u], c = cv[u];
                     if (!built) {  // sibling = parent - built sibling, written back in place
                         g -= gb[u];
@@ -965,7 +969,7 @@ __global__ void __launch_bounds__(256) k_split_eras(
                         }
                     }
                     stg[f * B1p + b] = __fmul_rn(__ll2float_rn(g), inv);
-                    stg[(FB + f) * B1p + b] = __ll2float_rn(c);
+                    stg[(FB + f) * B1p + b] = __int2float_rn((int)c);  // counts < 2^31: the same float
                 }
             }
             __syncwarp();
@@ -976,11 +980,12 @@ __global__ void __launch_bounds__(256) k_split_eras(
                     GT = __fadd_rn(GT, g[b]);
                     HT = __fadd_rn(HT, h[b]);
                 }
+                const float t3 = parent_term(GT, HT, eps);
                 float GL = 0.0f, HL = 0.0f;
                 for (int b = 0; b < nb; ++b) {
                     GL = __fadd_rn(GL, g[b]);
                     HL = __fadd_rn(HL, h[b]);
-                    const SplitEval r = eval_split(GL, HL, GT, HT, mcw, eps);
+                    const SplitEval r = eval_split_pt(GL, HL, GT, HT, t3, mcw, eps);
                     sg[(warp * NB + b) * FB + lane] = r.gain;
                     sd[(warp * NB + b) * FB + lane] = (signed char)r.dir;
                 }
