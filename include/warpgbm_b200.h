@@ -336,10 +336,14 @@ int64_t wgb_era_mean_plan(int32_t E, int64_t M, int32_t num_sms,
  * multiple of 16, 16-byte aligned): the partition reads one feature of many
  * rows, which this layout makes contiguous.  Set ws->bins_fm = out after. */
 int wgb_bins_feature_major(const wgb_ws *ws, int8_t *out, void *stream);
-/* Level d: stable partition of local rows into the next level's order; rows
- * of nodes that became leaves get pred[:, cls] += lr * leaf; then the next
+/* Level d: partition of local rows into the next level's order; rows of
+ * nodes that became leaves get pred[:, cls] += lr * leaf; then the next
  * level's histogram chunk list.  At d = D - 1 every row gets its leaf
- * update (the children are the last level). */
+ * update (the children are the last level).  Stable (three launches) for
+ * era fits and multi-rank fits; a single-rank one-era fit uses the layout
+ * wgb_level_split planned and one launch, without keeping the rows'
+ * relative order inside a child (nothing reads it: the histogram sums are
+ * exact integers). */
 int wgb_level_partition(const wgb_ws *ws, int32_t d, void *stream);
 /* Tree end: nothing left to launch (the last level's leaf updates happen in
  * wgb_level_partition(D - 1)); validates the workspace. */
