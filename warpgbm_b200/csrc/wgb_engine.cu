@@ -425,6 +425,45 @@ __global__ void __launch_bounds__(NT, MINB) k_hist(
                 }
             }
         }
+        if constexpr (HAS_ERA && REGULAR) {
+            // era windows of an era-sorted chunk: rows [i_lo, i_hi), each
+            // added into its era's slot (the slot's base joins the cell
+            // address); the same branchless ping-pong steps as above, rows
+            // past the window with zero increments
+            fast = aligned && era_sorted;
+            if (lane_live && fast) {
+                constexpr int UE = 4;  // rows per step per warp
+                uint32_t wa[UE][WPR], wb[UE][WPR];
+                const uint32_t sh0 = (uint32_t)__cvta_generic_to_shared(sh32), lane4 = 4u * lane;
+                const unsigned S32 = (unsigned)S;
+                auto load = [&](int i0, uint32_t (&ww)[UE][WPR]) {
+#pragma unroll
+                    for (int u = 0; u < UE; ++u)
+                        load_row<FPL>(tile + (unsigned long long)(unsigned)s_row[i0 + u] * S32, ww[u]);
+                };
+                auto update = [&](int i0, const uint32_t (&ww)[UE][WPR]) {
+#pragma unroll
+                    for (int u = 0; u < UE; ++u) {
+                        const int i = i0 + u;
+                        const bool in = i < i_hi;
+                        const uint2 pq = in ? s_pq[i] : make_uint2(0u, 0u);
+                        const uint32_t rb = sh0 + (in ? (uint32_t)(s_era[i] - e_lo) * (uint32_t)(ESLOT * 4) : 0u);
+                        hist_row_fast<FPL, NSC>(ww[u], rb, lane4, pq.x, pq.y);
+                    }
+                };
+                int i0 = i_lo + warp * UE;
+                if (i0 < i_hi) load(i0, wa);
+                while (i0 < i_hi) {
+                    const int i1 = i0 + NW * UE;
+                    if (i1 < i_hi) load(i1, wb);
+                    update(i0, wa);
+                    if (i1 >= i_hi) break;
+                    i0 = i1 + NW * UE;
+                    if (i0 < i_hi) load(i0, wa);
+                    update(i1, wb);
+                }
+            }
+        }
         if (lane_live && !fast) {
             // software pipeline: rows of step k+1 are loaded while step k's
             // cells are updated
