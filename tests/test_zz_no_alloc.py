@@ -1,4 +1,5 @@
-"""The no-allocation histogram entry point against the regular one.
+"""The no-allocation histogram entry point against the regular one and
+against the oracle (canonical exact sums on the grid of max |g|).
 
 wgb_compute_histogram3_noalloc is for hosts that may not allocate device
 memory while building a histogram (a fixed memory budget handed to the
@@ -13,6 +14,7 @@ import numpy as np
 import pytest
 import torch
 
+import oracle as O
 from warpgbm_b200 import _lib
 
 pytestmark = pytest.mark.gpu
@@ -44,10 +46,15 @@ def test_noalloc_matches_regular_entry_point_twice(n, F, k, E, B):
     samples = rng.permutation(n + 3)[:n].astype(np.int32)
     feats = rng.permutation(F)[:k].astype(np.int32)
     want = _hist("wgb_compute_histogram3", bins, g, samples, feats, era, E, B, dev)
+    s = O.quant_shift(float(np.abs(g[samples]).max()))
+    Gq, Cq = O.hist_q(bins, O.quantize(g, s), samples, feats, era, E, B)
+    Gf, Hf = O.dequant(Gq, Cq, s)
     for _ in range(2):  # the block keeps the last call's contents: both calls must agree
         got = _hist("wgb_compute_histogram3_noalloc", bins, g, samples, feats, era, E, B, dev)
         assert np.array_equal(got[0], want[0])   # exact: same integer sums
         assert np.array_equal(got[1], want[1])
+        assert np.array_equal(got[0], Gf)        # and the oracle's, on their own
+        assert np.array_equal(got[1], Hf)
 
 
 def test_noalloc_rejects_work_beyond_its_block():
