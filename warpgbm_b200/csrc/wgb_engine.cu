@@ -924,14 +924,9 @@ __global__ void __launch_bounds__(256) k_split_eras(
     int k, int kl, int jofs, int E, int B, const int *shift,
     float mcw, float eps, float msg, float factor, const int *__restrict__ sched,
     const uint8_t *__restrict__ ops, int nops, int depth, int4 *cand, int nblk, float *crit_out,
-    bool writeback, uint4 *zero, long long zero_n) {
+    bool writeback) {
     constexpr int FB = EraSplitShape<NB>::FB, IPT = EraSplitShape<NB>::IPT, EB = SPLIT_ERA_EB;
     extern __shared__ float s_era_split[];
-    // the next level's built slots (untouched by this level) are zeroed here
-    // instead of by a memset before the next histogram build
-    for (long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x; i < zero_n;
-         i += (long long)gridDim.x * blockDim.x)
-        zero[i] = make_uint4(0u, 0u, 0u, 0u);
     const int n = blockIdx.x / nblk, jb = blockIdx.x - n * nblk;  // node, feature block
     if (n >= *nn_d) return;
     const int j0 = jb * FB;
@@ -1918,12 +1913,6 @@ static inline int slice_kr(const wgb_ws *ws) {
 // per level covers sums, counts and roots.
 static inline long long hist_cells(const wgb_ws *ws) { return (long long)ws->E * hist_k(ws) * (ws->B + 1); }
 static inline long long slot_elems(const wgb_ws *ws) { return 2 * hist_cells(ws) + 2; }
-// Level d >= 1 of an unsliced era fit finds its built slots zeroed by the
-// previous level's era split (k_split_eras); every other level zeroes them
-// before its histogram build.
-static inline bool era_zeroes_next(const wgb_ws *ws, int d) {
-    return d >= 1 && d < ws->D && ws->E > 1 && !sliced(ws) && slot_elems(ws) % 2 == 0;
-}
 
 static int grid_for(long long n, int threads, int cap = 148 * 16) {
     long long b = (n + threads - 1) / threads;
@@ -2096,8 +2085,7 @@ int wgb_level_hist(const wgb_ws *ws, int32_t d, void *stream) {
         }
         out = HistOut{LL(ws->hstage), LL(ws->hstage) + nc, se, region, ws->ks, first};
     } else {
-        if (!era_zeroes_next(ws, d))
-            WGB_CUDA(cudaMemsetAsync(ws->hg + (long long)first * se, 0, sizeof(int64_t) * se * count, st));
+        WGB_CUDA(cudaMemsetAsync(ws->hg + (long long)first * se, 0, sizeof(int64_t) * se * count, st));
         if (d == 0) {
             k_root_cells<<<1, 32, 0, st>>>(LL(ws->hg), LL(ws->rootsum), se, nc, ws_ntree(ws), 1, 0);
             WGB_LAUNCHED("k_root_cells");
@@ -2176,16 +2164,6 @@ int wgb_level_split(const wgb_ws *ws, int32_t d, void *stream) {
         nblk = (kr + fb - 1) / fb;
         WGB_CHECK_ARG(nblk <= ws->ncand_blk, "candidate buffer too small: %d blocks per node needed", nblk);
         const unsigned g = (unsigned)nblk * (unsigned)cap;
-        // the next level's built slots of the pool (the sliced staging buffer
-        // is zeroed by wgb_level_hist itself)
-        uint4 *zero = nullptr;
-        long long zero_n = 0;
-        if (era_zeroes_next(ws, d + 1)) {
-            int nf, ncount;
-            wgb_level_slots(ws, d + 1, &nf, &ncount);
-            zero = reinterpret_cast<uint4 *>(hg + (long long)nf * se);
-            zero_n = (long long)ncount * se / 2;
-        }
         int dev = 0, smem_max = 0;
         WGB_CUDA(cudaGetDevice(&dev));
         WGB_CUDA(cudaDeviceGetAttribute(&smem_max, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev));
@@ -2197,7 +2175,7 @@ int wgb_level_split(const wgb_ws *ws, int32_t d, void *stream) {
         k_split_eras<NB_><<<g, 256, sm, st>>>(lvl, ws->nn + d, hg, hc, se, kr, kl, j0, ws->E, ws->B, ws->shift, \
                                               ws->mcw, ws->eps, ws->msg, ws->mean_factor, ws->era_sched,        \
                                               ws->era_ops, ws->era_nops, ws->era_depth, cand, nblk,             \
-                                              ws->crit_out, d < ws->D - 1, zero, zero_n);                      \
+                                              ws->crit_out, d < ws->D - 1);                                     \
     }
         if (g > 0) {
             if (nb <= 8) WGB_SPLIT_ERAS(8) else if (nb <= 32) WGB_SPLIT_ERAS(32) else WGB_SPLIT_ERAS(128)
