@@ -568,10 +568,12 @@ __global__ void __launch_bounds__(NT, MINB) k_hist(
 }
 
 // Sums the per-chunk words k_hist stored for each node (one era): thread =
-// one cell of one feature tile over a segment of `seg` consecutive chunks;
-// chunks of one node are consecutive, so a thread adds its running total to
-// the node's int64 cell whenever the node changes -- one atomic per node and
-// segment instead of one per chunk.
+// two neighbouring cells of one feature tile (one 16-byte load per chunk)
+// over a segment of `seg` consecutive chunks; chunks of one node are
+// consecutive, so a thread adds its running totals to the node's int64
+// cells whenever the node changes -- one atomic per cell, node and segment
+// instead of one per chunk.  Both cells of a pair share their bin slot and
+// feature pair index (cell indices 2i, 2i+1 differ in the lane only).
 template <int FPL, int NSC>
 __global__ void __launch_bounds__(256) k_hist_reduce(const uint2 *__restrict__ part, const int4 *__restrict__ chunks,
                                                      const int *nchunks, const wgb_node *__restrict__ lvl,
@@ -580,37 +582,45 @@ __global__ void __launch_bounds__(256) k_hist_reduce(const uint2 *__restrict__ p
     constexpr int FT = 32 * FPL, CELLS = NSC * FT;
     const int nch = *nchunks;
     const int c0 = blockIdx.z * seg;
-    const int wi = blockIdx.x * 256 + threadIdx.x;
+    const int wi = 2 * (blockIdx.x * 256 + threadIdx.x);
     if (c0 >= nch || wi >= CELLS) return;
     const int jb = wi / (NSC * 64), rem = wi % (NSC * 64);
     const int sl = rem >> 6, r2 = rem & 63;
     if (sl > B) return;  // trash slot
     const int jj = 2 * jb + (r2 >> 5), lj = r2 & 31;
     const int f = blockIdx.y * FT + lj * FPL + jj;
-    const int kp = f < F ? kpos[f] : -1;
-    if (kp < 0) return;
+    const int kp0 = f < F ? kpos[f] : -1, kp1 = f + FPL < F ? kpos[f + FPL] : -1;
+    if (kp0 < 0 && kp1 < 0) return;
     const int B1 = B + 1;
     const int c1 = min(nch, c0 + seg);
     const int ntile = gridDim.y;
-    long long gs = 0, cn = 0;
+    long long gs0 = 0, cn0 = 0, gs1 = 0, cn1 = 0;
     int node = chunks[c0].x;
-    const long long kofs = (long long)(kp / out.ks) * out.slice_stride + (long long)(kp % out.ks) * B1 + sl;
-    auto add = [&]() {
-        if (cn == 0) return;
-        const long long idx = (long long)(lvl[node].slot - out.slot0) * out.slot_elems + kofs;
-        atomicAdd(reinterpret_cast<unsigned long long *>(out.g + idx), (unsigned long long)gs);
-        atomicAdd(reinterpret_cast<unsigned long long *>(out.c + idx), (unsigned long long)cn);
+    auto kofs = [&](int kp) {
+        return (long long)(kp / out.ks) * out.slice_stride + (long long)(kp % out.ks) * B1 + sl;
     };
-    constexpr int UR = 8;  // chunk words in flight per thread
-    const uint2 *src = part + (long long)blockIdx.y * CELLS + wi;
-    const long long cstride = (long long)ntile * CELLS;
+    const long long k0 = kp0 >= 0 ? kofs(kp0) : 0, k1 = kp1 >= 0 ? kofs(kp1) : 0;
+    auto add = [&]() {
+        const long long base = (long long)(lvl[node].slot - out.slot0) * out.slot_elems;
+        if (kp0 >= 0 && cn0 != 0) {
+            atomicAdd(reinterpret_cast<unsigned long long *>(out.g + base + k0), (unsigned long long)gs0);
+            atomicAdd(reinterpret_cast<unsigned long long *>(out.c + base + k0), (unsigned long long)cn0);
+        }
+        if (kp1 >= 0 && cn1 != 0) {
+            atomicAdd(reinterpret_cast<unsigned long long *>(out.g + base + k1), (unsigned long long)gs1);
+            atomicAdd(reinterpret_cast<unsigned long long *>(out.c + base + k1), (unsigned long long)cn1);
+        }
+    };
+    constexpr int UR = 8;  // chunk word pairs in flight per thread
+    const uint4 *src = reinterpret_cast<const uint4 *>(part + (long long)blockIdx.y * CELLS + wi);
+    const long long cstride = (long long)ntile * CELLS / 2;  // in uint4
     for (int cb = c0; cb < c1; cb += UR) {
-        uint2 v[UR];
+        uint4 v[UR];
         int nd[UR];
 #pragma unroll
         for (int u = 0; u < UR; ++u) {
             const int c = cb + u;
-            v[u] = c < c1 ? src[c * cstride] : make_uint2(0u, 0u);
+            v[u] = c < c1 ? __ldcs(src + c * cstride) : make_uint4(0u, 0u, 0u, 0u);
             nd[u] = c < c1 ? chunks[c].x : node;
         }
 #pragma unroll
@@ -618,11 +628,12 @@ __global__ void __launch_bounds__(256) k_hist_reduce(const uint2 *__restrict__ p
             if (nd[u] != node) {
                 add();
                 node = nd[u];
-                gs = 0;
-                cn = 0;
+                gs0 = cn0 = gs1 = cn1 = 0;
             }
-            cn += v[u].x >> HIST_CNT_SHIFT;
-            gs += (long long)(int)v[u].y * (1ll << HIST_LO_BITS) + (long long)(v[u].x & HIST_A_SUM_MASK);
+            cn0 += v[u].x >> HIST_CNT_SHIFT;
+            gs0 += (long long)(int)v[u].y * (1ll << HIST_LO_BITS) + (long long)(v[u].x & HIST_A_SUM_MASK);
+            cn1 += v[u].z >> HIST_CNT_SHIFT;
+            gs1 += (long long)(int)v[u].w * (1ll << HIST_LO_BITS) + (long long)(v[u].z & HIST_A_SUM_MASK);
         }
     }
     add();
@@ -660,7 +671,7 @@ static cudaError_t launch_hist(int grid_x, const int8_t *bins, long long S, int 
         e = cudaGetLastError();                                                                        \
         if (e != cudaSuccess || !part || ERA_) return e;                                              \
         const int seg = 16;                                                                            \
-        dim3 rg((unsigned)((NSC_ * 32 * FPL_ + 255) / 256), grid.y, (unsigned)((grid_x + seg - 1) / seg)); \
+        dim3 rg((unsigned)((NSC_ * 16 * FPL_ + 255) / 256), grid.y, (unsigned)((grid_x + seg - 1) / seg)); \
         k_hist_reduce<FPL_, NSC_><<<rg, 256, 0, st>>>(part, chunks, nchunks, lvl, kpos, F, B, seg, out);  \
         return cudaGetLastError();                                                                     \
     }
