@@ -56,3 +56,38 @@ def test_multiclass_batch_bit_exact(cuda):
     o = _oracle_for(m, params, X, y, None)
     assert _same(_flat(m, 4, classification=True), o.flat_forest())
     assert np.abs(m.predict_proba(X) - o.predict_proba(X)).max() < 1e-6
+
+
+def _node_fields(raw):
+    """lstart, lcnt, built of 64-byte wgb_node records (include/warpgbm_b200.h)."""
+    i32 = raw.view(np.int32)
+    return i32[:, 8], i32[:, 9], i32[:, 11]
+
+
+@pytest.mark.parametrize("n,F", [(300_000, 300), (70_000, 1000), (5_000, 40)])
+def test_level_chunks_cover_built_rows_once(cuda, n, F):
+    """The histogram chunk list of every level (sized so that the chunks fill
+    whole waves of the histogram kernel's CTA slots): each built node's local
+    rows [lstart, lstart + lcnt) are cut into consecutive pieces of equal size
+    (within one row), none above 2048 rows, and into no more pieces than a
+    1024-row target gives; nothing else is listed.  The trees stay bit-exact."""
+    X, y = _data(n, F, 3)
+    params = dict(num_bins=32, max_depth=5, n_estimators=2, learning_rate=0.3)
+    m = WarpGBM(**params)
+    m._chunk_log = []
+    m.fit(X, y)
+    assert m._chunk_log
+    for d, ch, raw, nn in m._chunk_log:
+        lstart, lcnt, built = _node_fields(raw[:nn])
+        want = {i for i in range(nn) if built[i] & 1 and lcnt[i] > 0}
+        assert set(ch[:, 0].tolist()) == want, d
+        for i in want:
+            pieces = ch[ch[:, 0] == i]
+            lo, hi = pieces[:, 1], pieces[:, 2]
+            assert lo[0] == lstart[i] and hi[-1] == lstart[i] + lcnt[i], (d, i)
+            assert np.array_equal(lo[1:], hi[:-1]), (d, i)  # consecutive, no gap or overlap
+            size = hi - lo
+            assert size.max() <= 2048 and size.max() - size.min() <= 1, (d, i, size)
+            assert len(size) <= -(-int(lcnt[i]) // 1024), (d, i, size)  # pieces of >= 1024 rows' target
+    o = _oracle_for(m, params, X, y, None)
+    assert _same(_flat(m, 5), o.flat_forest())

@@ -1083,7 +1083,7 @@ class WarpGBM(BaseEstimator, RegressorMixin):
         ws.cls = cls
         p = ctypes_ptr(ws)
         instrumented = any(getattr(self, a, None) is not None
-                           for a in ("_hist_events", "_comm_events", "_split_events"))
+                           for a in ("_hist_events", "_comm_events", "_split_events", "_chunk_log"))
         if not instrumented and (not comm.on or self._ncomm is not None):
             # the whole tree from C++ (levels, and the per-level NCCL sums)
             _lib.call("wgb_grow_tree", p, self._ncomm, st())
@@ -1119,6 +1119,13 @@ class WarpGBM(BaseEstimator, RegressorMixin):
             if timer is not None:
                 ev1.record()
                 timer.append((ev0, ev1))
+            clog = getattr(self, "_chunk_log", None)  # test hook: each level's chunk list
+            if clog is not None:
+                T = max(ws.ntree, 1)
+                nodes = self._t["nodes"].view(-1, 64)[T * ((1 << d) - 1): T * ((1 << (d + 1)) - 1)]
+                nch = int(self._t["nchunks"][0])
+                clog.append((d, self._t["chunks"][:nch].cpu().numpy().copy(),
+                             nodes.cpu().numpy().copy(), int(self._t["nn"][d])))
             if comm.on:
                 first, count = _lib.built_slots(d, wsp)
                 if ctimer is not None:

@@ -156,19 +156,49 @@ __global__ void k_root_total(wgb_node *nodes, const long long *hg, long long slo
 // histogram build                                                        //
 // ====================================================================== //
 
-// Chunk list of a level: every built node's local rows cut into HIST_R-row
-// pieces, by one block (any size up to 1024 threads).  The level's records
-// come from earlier launches or from this block (visible after its barrier).
-__device__ __forceinline__ void plan_chunks(const wgb_node *__restrict__ lvl, int nnd, int4 *chunks, int *nchunks, int cap) {
+// Chunk list of a level, by one block (any size up to 1024 threads): every
+// built node's local rows cut into m = ceil(rows / R) pieces of equal size
+// (at most R <= HIST_R rows each).  With wave = 0, R = HIST_R.  With wave > 0
+// (the chunks that one wave of the histogram kernel's resident CTAs builds at
+// once, all feature tiles included), R is chosen so that the chunk count fills the
+// waves that HIST_R-row chunks would start: one full wave plus a few chunks
+// would otherwise take two wave times.  R never goes below HIST_R / 2 nor
+// below what keeps the list within `cap` entries.  The level's records come
+// from earlier launches or from this block (visible after its barrier).
+__device__ __forceinline__ void plan_chunks(const wgb_node *__restrict__ lvl, int nnd, int4 *chunks, int *nchunks,
+                                            int cap, int wave) {
     __shared__ int s_cnt[1024];
     __shared__ int s_off[1025];
     __shared__ int s_scan[33];
     const int nt = blockDim.x;
+    int R = HIST_R;
+    if (wave > 0) {
+        int T = 0, nb = 0, u0 = 0;  // rows, nodes and HIST_R-row chunks of the built nodes
+        for (int b0 = 0; b0 < nnd; b0 += nt) {
+            const int i = b0 + threadIdx.x;
+            const int n = i < nnd && node_built(lvl[i].built) ? lvl[i].lcnt : 0;
+            int t;
+            block_scan_excl(n, s_scan, t);
+            T += t;
+            block_scan_excl(n > 0 ? 1 : 0, s_scan, t);
+            nb += t;
+            block_scan_excl((n + HIST_R - 1) / HIST_R, s_scan, t);
+            u0 += t;
+        }
+        if (nb > 0) {
+            const long long K = (long long)((u0 + wave - 1) / wave) * wave;  // chunks of those whole waves
+            long long r = K > nb ? ((long long)T + K - nb - 1) / (K - nb) : HIST_R;
+            if (cap > nb) r = max(r, ((long long)T + cap - nb - 1) / (cap - nb));
+            else r = HIST_R;
+            if (r < HIST_R / 2) r = HIST_R / 2;
+            R = r < HIST_R ? (int)r : HIST_R;
+        }
+    }
     int base = 0;
     for (int b0 = 0; b0 < nnd; b0 += nt) {
         int i = b0 + threadIdx.x;
         int c = 0;
-        if (i < nnd && node_built(lvl[i].built)) c = (lvl[i].lcnt + HIST_R - 1) / HIST_R;
+        if (i < nnd && node_built(lvl[i].built)) c = (lvl[i].lcnt + R - 1) / R;
         s_cnt[threadIdx.x] = c;
         int tot;
         const int ex = block_scan_excl(c, s_scan, tot);
@@ -184,10 +214,10 @@ __device__ __forceinline__ void plan_chunks(const wgb_node *__restrict__ lvl, in
                 if (s_off[m] <= c2) a = m; else z = m - 1;
             }
             while (s_cnt[a] == 0) --a;
-            int node = b0 + a;
-            int piece = c2 - s_off[a];
-            int p0 = lvl[node].lstart + piece * HIST_R;
-            int p1 = min(p0 + HIST_R, lvl[node].lstart + lvl[node].lcnt);
+            const int node = b0 + a;
+            const long long piece = c2 - s_off[a], m = s_cnt[a], n = lvl[node].lcnt;
+            const int p0 = lvl[node].lstart + (int)(piece * n / m);
+            const int p1 = lvl[node].lstart + (int)((piece + 1) * n / m);
             if (c2 < cap) chunks[c2] = make_int4(node, p0, p1, 0);
         }
         __syncthreads();
@@ -198,8 +228,8 @@ __device__ __forceinline__ void plan_chunks(const wgb_node *__restrict__ lvl, in
 
 // Chunk list of level 0 (later levels are planned by k_node_offsets).
 __global__ void __launch_bounds__(1024) k_chunk_plan(const wgb_node *__restrict__ lvl, const int *nn_d,
-                                                     int4 *chunks, int *nchunks, int cap) {
-    plan_chunks(lvl, *nn_d, chunks, nchunks, cap);
+                                                     int4 *chunks, int *nchunks, int cap, int wave) {
+    plan_chunks(lvl, *nn_d, chunks, nchunks, cap, wave);
 }
 
 // One CTA = one chunk (<= HIST_R rows of one node) x one tile of 32*FPL
@@ -284,12 +314,12 @@ __device__ __forceinline__ void load_row(const int8_t *src, uint32_t (&w)[FPL / 
 }
 
 template <int FPL, int NT, int MINB, int NSC, int EWC, bool HAS_ERA, bool REGULAR>
-__global__ void __launch_bounds__(NT, MINB) k_hist(
-    const int8_t *__restrict__ bins, long long S, int F, const int *__restrict__ order,
+__device__ __forceinline__ void hist_item(
+    int c, int ft, int ntile, const int8_t *__restrict__ bins, long long S, int F, const int *__restrict__ order,
     const int *__restrict__ q, const float *__restrict__ g, const int *shift,
     const int *__restrict__ era, const int *__restrict__ kpos, int k, int E, int B, int EW,
-    const int4 *__restrict__ chunks, const int *nchunks, const wgb_node *__restrict__ lvl,
-    const HistOut out, long long nrows, uint2 *__restrict__ part) {
+    const int4 *__restrict__ chunks, const wgb_node *__restrict__ lvl,
+    const HistOut &out, long long nrows, uint2 *__restrict__ part) {
     constexpr int FT = 32 * FPL;             // features per tile
     constexpr int U = (FPL >= 16 || MINB > 1) ? 4 : 8;  // rows per pipeline step per warp
     constexpr int NW = NT / 32;
@@ -306,9 +336,7 @@ __global__ void __launch_bounds__(NT, MINB) k_hist(
     __shared__ int s_era[HIST_ERA_R(HAS_ERA)];
     __shared__ int s_red[33];
 
-    const int c = blockIdx.x;
-    if (c >= *nchunks) return;
-    const int f0 = blockIdx.y * FT;
+    const int f0 = ft * FT;
     int any = 0;
     for (int t = threadIdx.x; t < FT; t += NT) {
         int f = f0 + t;
@@ -526,7 +554,7 @@ __global__ void __launch_bounds__(NT, MINB) k_hist(
         // one era and a partial buffer: store the chunk's raw words (coalesced,
         // no atomics); k_hist_reduce sums the chunks of each node afterwards
         if (!HAS_ERA && part) {
-            uint2 *dst = part + ((long long)c * gridDim.y + blockIdx.y) * (NSC * FT);
+            uint2 *dst = part + ((long long)c * ntile + ft) * (NSC * FT);
             for (int wi = threadIdx.x; wi < NSC * FT; wi += NT) dst[wi] = make_uint2(sh32[wi], sh32[NSC * FT + wi]);
             break;
         }
@@ -567,6 +595,24 @@ __global__ void __launch_bounds__(NT, MINB) k_hist(
     }
 }
 
+// The histogram kernel: CTA x builds item x -- chunk x / ntile of the
+// level's list, feature tile x % ntile -- when the chunk exists (the grid is
+// sized for the most chunks the level can have; the tiles of a chunk are
+// neighbours, so they share its row records through L2, and CTAs past the
+// list come last).
+template <int FPL, int NT, int MINB, int NSC, int EWC, bool HAS_ERA, bool REGULAR>
+__global__ void __launch_bounds__(NT, MINB) k_hist(
+    const int8_t *__restrict__ bins, long long S, int F, const int *__restrict__ order,
+    const int *__restrict__ q, const float *__restrict__ g, const int *shift,
+    const int *__restrict__ era, const int *__restrict__ kpos, int k, int E, int B, int EW,
+    const int4 *__restrict__ chunks, const int *nchunks, const wgb_node *__restrict__ lvl,
+    const HistOut out, long long nrows, uint2 *__restrict__ part, int ntile) {
+    const int c = blockIdx.x / ntile;
+    if (c >= *nchunks) return;
+    hist_item<FPL, NT, MINB, NSC, EWC, HAS_ERA, REGULAR>(c, blockIdx.x - c * ntile, ntile, bins, S, F, order, q, g,
+                                                         shift, era, kpos, k, E, B, EW, chunks, lvl, out, nrows, part);
+}
+
 // Sums the per-chunk words k_hist stored for each node (one era): thread =
 // two neighbouring cells of one feature tile (one 16-byte load per chunk)
 // over a segment of `seg` consecutive chunks; chunks of one node are
@@ -581,9 +627,8 @@ __global__ void __launch_bounds__(256) k_hist_reduce(const uint2 *__restrict__ p
                                                      const HistOut out) {
     constexpr int FT = 32 * FPL, CELLS = NSC * FT;
     const int nch = *nchunks;
-    const int c0 = blockIdx.z * seg;
     const int wi = 2 * (blockIdx.x * 256 + threadIdx.x);
-    if (c0 >= nch || wi >= CELLS) return;
+    if ((int)blockIdx.z * seg >= nch || wi >= CELLS) return;
     const int jb = wi / (NSC * 64), rem = wi % (NSC * 64);
     const int sl = rem >> 6, r2 = rem & 63;
     if (sl > B) return;  // trash slot
@@ -592,51 +637,54 @@ __global__ void __launch_bounds__(256) k_hist_reduce(const uint2 *__restrict__ p
     const int kp0 = f < F ? kpos[f] : -1, kp1 = f + FPL < F ? kpos[f + FPL] : -1;
     if (kp0 < 0 && kp1 < 0) return;
     const int B1 = B + 1;
-    const int c1 = min(nch, c0 + seg);
     const int ntile = gridDim.y;
-    long long gs0 = 0, cn0 = 0, gs1 = 0, cn1 = 0;
-    int node = chunks[c0].x;
     auto kofs = [&](int kp) {
         return (long long)(kp / out.ks) * out.slice_stride + (long long)(kp % out.ks) * B1 + sl;
     };
     const long long k0 = kp0 >= 0 ? kofs(kp0) : 0, k1 = kp1 >= 0 ? kofs(kp1) : 0;
-    auto add = [&]() {
-        const long long base = (long long)(lvl[node].slot - out.slot0) * out.slot_elems;
-        if (kp0 >= 0 && cn0 != 0) {
-            atomicAdd(reinterpret_cast<unsigned long long *>(out.g + base + k0), (unsigned long long)gs0);
-            atomicAdd(reinterpret_cast<unsigned long long *>(out.c + base + k0), (unsigned long long)cn0);
-        }
-        if (kp1 >= 0 && cn1 != 0) {
-            atomicAdd(reinterpret_cast<unsigned long long *>(out.g + base + k1), (unsigned long long)gs1);
-            atomicAdd(reinterpret_cast<unsigned long long *>(out.c + base + k1), (unsigned long long)cn1);
-        }
-    };
     constexpr int UR = 8;  // chunk word pairs in flight per thread
     const uint4 *src = reinterpret_cast<const uint4 *>(part + (long long)blockIdx.y * CELLS + wi);
     const long long cstride = (long long)ntile * CELLS / 2;  // in uint4
-    for (int cb = c0; cb < c1; cb += UR) {
-        uint4 v[UR];
-        int nd[UR];
-#pragma unroll
-        for (int u = 0; u < UR; ++u) {
-            const int c = cb + u;
-            v[u] = c < c1 ? __ldcs(src + c * cstride) : make_uint4(0u, 0u, 0u, 0u);
-            nd[u] = c < c1 ? chunks[c].x : node;
-        }
-#pragma unroll
-        for (int u = 0; u < UR; ++u) {
-            if (nd[u] != node) {
-                add();
-                node = nd[u];
-                gs0 = cn0 = gs1 = cn1 = 0;
+    // segments z, z + gridDim.z, ... (the grid may hold fewer segments than the list)
+    for (int c0 = blockIdx.z * seg; c0 < nch; c0 += gridDim.z * seg) {
+        const int c1 = min(nch, c0 + seg);
+        long long gs0 = 0, cn0 = 0, gs1 = 0, cn1 = 0;
+        int node = chunks[c0].x;
+        auto add = [&]() {
+            const long long base = (long long)(lvl[node].slot - out.slot0) * out.slot_elems;
+            if (kp0 >= 0 && cn0 != 0) {
+                atomicAdd(reinterpret_cast<unsigned long long *>(out.g + base + k0), (unsigned long long)gs0);
+                atomicAdd(reinterpret_cast<unsigned long long *>(out.c + base + k0), (unsigned long long)cn0);
             }
-            cn0 += v[u].x >> HIST_CNT_SHIFT;
-            gs0 += (long long)(int)v[u].y * (1ll << HIST_LO_BITS) + (long long)(v[u].x & HIST_A_SUM_MASK);
-            cn1 += v[u].z >> HIST_CNT_SHIFT;
-            gs1 += (long long)(int)v[u].w * (1ll << HIST_LO_BITS) + (long long)(v[u].z & HIST_A_SUM_MASK);
+            if (kp1 >= 0 && cn1 != 0) {
+                atomicAdd(reinterpret_cast<unsigned long long *>(out.g + base + k1), (unsigned long long)gs1);
+                atomicAdd(reinterpret_cast<unsigned long long *>(out.c + base + k1), (unsigned long long)cn1);
+            }
+        };
+        for (int cb = c0; cb < c1; cb += UR) {
+            uint4 v[UR];
+            int nd[UR];
+#pragma unroll
+            for (int u = 0; u < UR; ++u) {
+                const int c = cb + u;
+                v[u] = c < c1 ? __ldcs(src + c * cstride) : make_uint4(0u, 0u, 0u, 0u);
+                nd[u] = c < c1 ? chunks[c].x : node;
+            }
+#pragma unroll
+            for (int u = 0; u < UR; ++u) {
+                if (nd[u] != node) {
+                    add();
+                    node = nd[u];
+                    gs0 = cn0 = gs1 = cn1 = 0;
+                }
+                cn0 += v[u].x >> HIST_CNT_SHIFT;
+                gs0 += (long long)(int)v[u].y * (1ll << HIST_LO_BITS) + (long long)(v[u].x & HIST_A_SUM_MASK);
+                cn1 += v[u].z >> HIST_CNT_SHIFT;
+                gs1 += (long long)(int)v[u].w * (1ll << HIST_LO_BITS) + (long long)(v[u].z & HIST_A_SUM_MASK);
+            }
         }
+        add();
     }
-    add();
 }
 
 // Feature width per lane and bin-slot capacity of the histogram kernel
@@ -645,6 +693,19 @@ __global__ void __launch_bounds__(256) k_hist_reduce(const uint2 *__restrict__ p
 static inline void hist_shape(long long S, int F, int B, int &fpl, int &nsc) {
     fpl = (S % 8 == 0 && F > 128 && B <= 32) ? 8 : 4;
     nsc = (B + 2 <= 8) ? 8 : (B + 2 <= 34 ? 34 : 130);
+}
+
+// Multiprocessors of the current device (cached per device).
+static int num_sms() {
+    static int cache[64];
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return 148;
+    if (!cache[dev]) {
+        int n = 0;
+        if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || n <= 0) n = 148;
+        cache[dev] = n;
+    }
+    return cache[dev];
 }
 
 // Launch of the histogram kernel for one level: picks the feature width per
@@ -665,13 +726,13 @@ static cudaError_t launch_hist(int grid_x, const int8_t *bins, long long S, int 
         size_t smem = (size_t)EWC_ * 2 * NSC_ * 32 * FPL_ * 4;                                         \
         cudaError_t e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem); \
         if (e != cudaSuccess) return e;                                                                \
-        dim3 grid((unsigned)grid_x, (unsigned)((F + 32 * FPL_ - 1) / (32 * FPL_)));                    \
-        fn<<<grid, NT_, smem, st>>>(bins, S, F, order, q, g, shift, era, kpos, k, E, B, ew, chunks,   \
-                                    nchunks, lvl, out, nrows, part);                                   \
+        const int ntile = (F + 32 * FPL_ - 1) / (32 * FPL_);                                          \
+        fn<<<(unsigned)grid_x * ntile, NT_, smem, st>>>(bins, S, F, order, q, g, shift, era, kpos, k, E, B, \
+                                                        ew, chunks, nchunks, lvl, out, nrows, part, ntile); \
         e = cudaGetLastError();                                                                        \
         if (e != cudaSuccess || !part || ERA_) return e;                                              \
         const int seg = 16;                                                                            \
-        dim3 rg((unsigned)((NSC_ * 16 * FPL_ + 255) / 256), grid.y, (unsigned)((grid_x + seg - 1) / seg)); \
+        dim3 rg((unsigned)((NSC_ * 16 * FPL_ + 255) / 256), (unsigned)ntile, (unsigned)((grid_x + seg - 1) / seg)); \
         k_hist_reduce<FPL_, NSC_><<<rg, 256, 0, st>>>(part, chunks, nchunks, lvl, kpos, F, B, seg, out);  \
         return cudaGetLastError();                                                                     \
     }
@@ -1132,7 +1193,7 @@ __device__ void plan_next_level(wgb_node *__restrict__ lvl, wgb_node *__restrict
 // active rows; then (chunks != NULL) the next level's histogram chunk list.
 // Runs after plan_next_level in the same block.
 __device__ void plan_children(const wgb_node *__restrict__ lvl, wgb_node *__restrict__ nxt, const int *nn,
-                              int *nact, int d, int4 *part, int4 *chunks, int *nchunks, int chunk_cap,
+                              int *nact, int d, int4 *part, int4 *chunks, int *nchunks, int chunk_cap, int wave,
                               int *s_scan) {
     __syncthreads();  // nxt records and nn[d + 1] of plan_next_level
     const int nnd = __ldcg(nn + d);
@@ -1157,7 +1218,7 @@ __device__ void plan_children(const wgb_node *__restrict__ lvl, wgb_node *__rest
     if (threadIdx.x == 0) nact[d + 1] = base;
     if (chunks) {
         __syncthreads();
-        plan_chunks(nxt, nn[d + 1], chunks, nchunks, chunk_cap);
+        plan_chunks(nxt, nn[d + 1], chunks, nchunks, chunk_cap, wave);
     }
 }
 
@@ -1176,7 +1237,7 @@ __global__ void __launch_bounds__(256) k_split_final(
     const long long *__restrict__ hg, const long long *__restrict__ hc, long long slot_elems, int kl, int jofs,
     int E, int B, const int *shift, float mcw, float eps, const int4 *__restrict__ cand, int nblk, float *era_gain,
     int *done, bool writeback, int4 *part, int *nact, int4 *chunks, int *nchunks, int chunk_cap, int *win,
-    int win_words, int wslice) {
+    int win_words, int wslice, int wave) {
     const int n = blockIdx.x;
     __shared__ Key s_best, s_kw[8];
     __shared__ long long s_c[8], s_g[8];
@@ -1305,7 +1366,7 @@ __global__ void __launch_bounds__(256) k_split_final(
     if (!s_last) return;
     __threadfence();
     plan_next_level(lvl, nxt, nn, d, shift, ntree, s_scan);
-    if (part) plan_children(lvl, nxt, nn, nact, d, part, chunks, nchunks, chunk_cap, s_scan);
+    if (part) plan_children(lvl, nxt, nn, nact, d, part, chunks, nchunks, chunk_cap, wave, s_scan);
     if (threadIdx.x == 0) *done = 0;
 }
 
@@ -1495,7 +1556,7 @@ __global__ void __launch_bounds__(1024) k_node_offsets(wgb_node *__restrict__ lv
                                                        const int *nn, int *nact, int d,
                                                        const uint8_t *flags, const int *tile_cnt,
                                                        int *tile_off, int ntiles, int4 *part, int4 *chunks,
-                                                       int *nchunks, int chunk_cap) {
+                                                       int *nchunks, int chunk_cap, int wave) {
     __shared__ int s_scan[33];
     {   // exclusive scan of the tiles' left counts (tile_off[ntiles] = total)
         int base = 0;
@@ -1543,7 +1604,7 @@ __global__ void __launch_bounds__(1024) k_node_offsets(wgb_node *__restrict__ lv
     // the next level's histogram chunk list (chunks == NULL at the last level)
     if (chunks) {
         __syncthreads();
-        plan_chunks(nxt, nn[d + 1], chunks, nchunks, chunk_cap);
+        plan_chunks(nxt, nn[d + 1], chunks, nchunks, chunk_cap, wave);
     }
 }
 
@@ -1911,6 +1972,23 @@ static inline const int *level_posnode(const wgb_ws *ws, int d) {
 // [slice*ks, slice*ks + ks) of the tree's k (the last slices may be short
 // or empty).
 static inline bool sliced(const wgb_ws *ws) { return ws->nslice > 1; }
+// The histogram's matrix: the tree's own feature matrix when there is one
+// (k columns in position order), else the full bin matrix.
+static inline long long hist_S(const wgb_ws *ws) { return ws->bins_sub ? ws->S_sub : ws->S; }
+static inline int hist_F(const wgb_ws *ws) { return ws->bins_sub ? ws->k : ws->F; }
+// One-era levels: the chunks that one wave of the histogram kernel's
+// resident CTAs builds at once over all feature tiles -- the chunk planner
+// sizes the level's chunks to fill whole waves -- or 0 (era levels: chunks
+// of HIST_R rows).
+static int hist_wave(const wgb_ws *ws) {
+    if (ws->E != 1) return 0;
+    int fpl, nsc;
+    hist_shape(hist_S(ws), hist_F(ws), ws->B, fpl, nsc);
+    const int minb = (fpl == 8 && nsc <= 34) ? 2 : 1;  // CTAs per SM of the one-era instantiations
+    const int ntile = (hist_F(ws) + 32 * fpl - 1) / (32 * fpl);
+    const int w = minb * num_sms() / (ntile > 0 ? ntile : 1);
+    return w > 0 ? w : 1;
+}
 static inline int hist_k(const wgb_ws *ws) { return sliced(ws) ? ws->ks : ws->k; }  // the pool's k
 static inline int slice_j0(const wgb_ws *ws) { return sliced(ws) ? ws->slice * ws->ks : 0; }
 static inline int slice_kr(const wgb_ws *ws) {
@@ -2106,18 +2184,20 @@ int wgb_level_hist(const wgb_ws *ws, int32_t d, void *stream) {
     wgb_node *lvl = level_nodes(ws, d);
     if (d == 0) {  // later levels' chunk lists are planned by the previous level's partition
         k_chunk_plan<<<1, 1024, 0, st>>>(lvl, ws->nn + d, reinterpret_cast<int4 *>(ws->chunks),
-                                         ws->nchunks, ws->chunk_cap);
+                                         ws->nchunks, ws->chunk_cap, hist_wave(ws));
         WGB_LAUNCHED("k_chunk_plan");
     }
     if (ws->N == 0) return WGB_OK;
-    long long max_chunks = ((long long)ws_ntree(ws) * ws->N + HIST_R - 1) / HIST_R + count;
+    // most chunks the level can have: pieces of at least HIST_R rows, or of
+    // HIST_R / 2 where the planner balances the chunk size
+    const int rmin = hist_wave(ws) > 0 ? HIST_R / 2 : HIST_R;
+    long long max_chunks = ((long long)ws_ntree(ws) * ws->N + rmin - 1) / rmin + count;
     if (max_chunks > ws->chunk_cap) max_chunks = ws->chunk_cap;
     const int *ord = level_order(ws, d);
-    // the tree's own feature matrix when there is one (k columns in position order)
     const bool sub = ws->bins_sub != nullptr;
     const int8_t *hb = sub ? ws->bins_sub : ws->bins;
-    const long long hS = sub ? ws->S_sub : ws->S;
-    const int hF = sub ? ws->k : ws->F;
+    const long long hS = hist_S(ws);
+    const int hF = hist_F(ws);
     const int *hkpos = sub ? ws->kpos_sub : ws->kpos;
     cudaError_t e = launch_hist((int)max_chunks, hb, hS, hF, ord, ws->qg, nullptr, nullptr,
                                 ws->E > 1 ? ws->era : nullptr, hkpos, ws->k, ws->E, ws->B, ws->hist_ew,
@@ -2202,7 +2282,7 @@ int wgb_level_split(const wgb_ws *ws, int32_t d, void *stream) {
                                        d < ws->D - 1, fp ? reinterpret_cast<int4 *>(ws->part) : nullptr, ws->nact,
                                        fp && d < ws->D - 1 ? reinterpret_cast<int4 *>(ws->chunks) : nullptr,
                                        ws->nchunks, ws->chunk_cap, sliced(ws) ? ws->win : nullptr, ws->win_words,
-                                       ws->slice);
+                                       ws->slice, hist_wave(ws));
     WGB_LAUNCHED("k_split_final");
     return WGB_OK;
 }
@@ -2263,7 +2343,7 @@ int wgb_level_partition(const wgb_ws *ws, int32_t d, void *stream) {
     k_node_offsets<<<1, 1024, 0, st>>>(lvl, level_nodes(ws, d + 1), ws->nn, ws->nact, d, ws->flags,
                                        ws->tile_cnt, ws->tile_off, ntiles, part,
                                        last ? nullptr : reinterpret_cast<int4 *>(ws->chunks), ws->nchunks,
-                                       ws->chunk_cap);
+                                       ws->chunk_cap, hist_wave(ws));
     WGB_LAUNCHED("k_node_offsets");
     k_scatter<<<ntiles, PART_THREADS, 0, st>>>(lvl, ws->nn + d, ws->nact + d, ord, pn, ws->flags, ws->tile_off, part,
                                                 ws->order[d & 1], ws->posnode[d & 1], ws->pred, ws->K,

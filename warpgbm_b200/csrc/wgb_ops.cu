@@ -665,7 +665,7 @@ int wgb_compute_histogram3(const int8_t *bin_indices, int64_t num_rows, int64_t 
         k_kpos<<<(k + 255) / 256, 256, 0, st>>>(feature_indices, k, (int)F_master, kpos);
         k_max_abs_rows<<<grid_cap(n, 256), 256, 0, st>>>(residuals, sample_indices, n, num_rows, maxabs);
         k_single_node<<<1, 1, 0, st>>>(maxabs, shift, nd, (int)n, nn);
-        k_chunk_plan<<<1, 1024, 0, st>>>(nd, nn, chunks, nchunks, nchunk);
+        k_chunk_plan<<<1, 1024, 0, st>>>(nd, nn, chunks, nchunks, nchunk, 0);
         cudaError_t le = launch_hist(nchunk, bin_indices, F_master, (int)F_master, sample_indices, nullptr,
                                      residuals, shift, num_eras > 1 ? era_indices : nullptr, kpos, k,
                                      num_eras, num_bins, 0, false, chunks, nchunks, nd,
