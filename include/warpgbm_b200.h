@@ -16,7 +16,7 @@
  *
  * 2. The level-wise tree engine that warpgbm_b200.core.WarpGBM drives: one
  *    fused histogram build per tree level over all of that level's nodes,
- *    one split search per level, an on-device stable partition, and no host
+ *    one split search per level, an on-device partition, and no host
  *    synchronisation inside a tree.  It replaces the depth-first recursion
  *    of warpgbm/core.py:543-658 and 692-744.
  */
@@ -340,10 +340,10 @@ int wgb_bins_feature_major(const wgb_ws *ws, int8_t *out, void *stream);
  * nodes that became leaves get pred[:, cls] += lr * leaf; then the next
  * level's histogram chunk list.  At d = D - 1 every row gets its leaf
  * update (the children are the last level).  Stable (three launches) for
- * era fits and multi-rank fits; a single-rank one-era fit uses the layout
- * wgb_level_split planned and one launch, without keeping the rows'
+ * era fits; a one-era fit takes one launch that does not keep the rows'
  * relative order inside a child (nothing reads it: the histogram sums are
- * exact integers). */
+ * exact integers), with the layout wgb_level_split planned on one rank and
+ * finished by the launch's last CTA on several. */
 int wgb_level_partition(const wgb_ws *ws, int32_t d, void *stream);
 /* Tree end: nothing left to launch (the last level's leaf updates happen in
  * wgb_level_partition(D - 1)); validates the workspace. */

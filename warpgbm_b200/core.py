@@ -194,8 +194,8 @@ def native_comm(comm: _Comm, dev):
 
 def fused_partition(ws) -> bool:
     """The engine's choice for a workspace (wgb_engine.cu fused_partition):
-    single-rank one-era fits partition each level in one launch (k_partition)."""
-    return ws.N_global == ws.N and ws.E == 1 and ws.nslice <= 1
+    one-era fits partition each level in one launch (k_partition)."""
+    return ws.E == 1
 
 
 def level_launches(D: int, E: int, fused: bool = True, sliced: bool = False) -> int:

@@ -1185,16 +1185,20 @@ __device__ void plan_next_level(wgb_node *__restrict__ lvl, wgb_node *__restrict
     if (threadIdx.x == 0) nn[d + 1] = 2 * base;
 }
 
-// Single-rank fits: a node's exact left count (lcount, from its histogram)
-// is also its local one, so the next level's row layout is known before the
-// partition.  Per splitting node n (node order): part[n] = {left cursor 0,
-// start of n's children in the next order, left count, right cursor 0};
-// the children's segments [ns, ns+L) and [ns+L, ns+lcnt); the next level's
-// active rows; then (chunks != NULL) the next level's histogram chunk list.
-// Runs after plan_next_level in the same block.
+// Row layout of the next level for the one-launch partition.  Per
+// splitting node n (node order): part[n] = {left cursor 0, start ns of n's
+// children in the next order, left count, right cursor 0}; the partition
+// puts n's left rows at ns, ns+1, ... and its right rows at ns+lcnt-1,
+// ns+lcnt-2, ...  Single-rank fits (local_known): a node's exact left count
+// (lcount, from its histogram) is also its local one, so the children's
+// segments [ns, ns+L) and [ns+L, ns+lcnt), the next level's active rows and
+// (chunks != NULL) its histogram chunk list are planned here.  Multi-rank
+// fits know only global counts: the partition's last CTA finishes the
+// layout from its left cursors (finish_children).  Runs after
+// plan_next_level in the same block.
 __device__ void plan_children(const wgb_node *__restrict__ lvl, wgb_node *__restrict__ nxt, const int *nn,
                               int *nact, int d, int4 *part, int4 *chunks, int *nchunks, int chunk_cap, int wave,
-                              int *s_scan) {
+                              bool local_known, int *s_scan) {
     __syncthreads();  // nxt records and nn[d + 1] of plan_next_level
     const int nnd = __ldcg(nn + d);
     int base = 0;
@@ -1205,8 +1209,42 @@ __device__ void plan_children(const wgb_node *__restrict__ lvl, wgb_node *__rest
         int tot;
         const int ns = base + block_scan_excl(v, s_scan, tot);
         if (spl) {
-            const int L = (int)__ldcg(&lvl[i].lcount);
+            const int L = local_known ? (int)__ldcg(&lvl[i].lcount) : 0;
             part[i] = make_int4(0, ns, L, 0);
+            if (local_known) {
+                const int c = __ldcg(&lvl[i].child);
+                nxt[c].lstart = ns;
+                nxt[c].lcnt = L;
+                nxt[c + 1].lstart = ns + L;
+                nxt[c + 1].lcnt = v - L;
+            }
+        }
+        base += tot;
+    }
+    if (!local_known) return;
+    if (threadIdx.x == 0) nact[d + 1] = base;
+    if (chunks) {
+        __syncthreads();
+        plan_chunks(nxt, nn[d + 1], chunks, nchunks, chunk_cap, wave);
+    }
+}
+
+// Multi-rank fits, by the partition's last CTA: each splitting node's local
+// left count is its final left cursor part[n].x; the children's segments,
+// the next level's active rows and (chunks != NULL) its chunk list follow.
+__device__ void finish_children(const wgb_node *__restrict__ lvl, wgb_node *__restrict__ nxt, const int *nn,
+                                int *nact, int d, const int4 *part, int4 *chunks, int *nchunks, int chunk_cap,
+                                int wave, int *s_scan) {
+    const int nnd = __ldcg(nn + d);
+    int base = 0;
+    for (int b0 = 0; b0 < nnd; b0 += blockDim.x) {
+        const int i = b0 + threadIdx.x;
+        const bool spl = i < nnd && __ldcg(&lvl[i].fpos) >= 0;
+        const int v = spl ? __ldcg(&lvl[i].lcnt) : 0;
+        int tot;
+        block_scan_excl(v, s_scan, tot);
+        if (spl) {
+            const int L = __ldcg(&part[i].x), ns = __ldcg(&part[i].y);
             const int c = __ldcg(&lvl[i].child);
             nxt[c].lstart = ns;
             nxt[c].lcnt = L;
@@ -1218,7 +1256,7 @@ __device__ void plan_children(const wgb_node *__restrict__ lvl, wgb_node *__rest
     if (threadIdx.x == 0) nact[d + 1] = base;
     if (chunks) {
         __syncthreads();
-        plan_chunks(nxt, nn[d + 1], chunks, nchunks, chunk_cap, wave);
+        plan_chunks(nxt, __ldcg(nn + d + 1), chunks, nchunks, chunk_cap, wave);
     }
 }
 
@@ -1237,7 +1275,7 @@ __global__ void __launch_bounds__(256) k_split_final(
     const long long *__restrict__ hg, const long long *__restrict__ hc, long long slot_elems, int kl, int jofs,
     int E, int B, const int *shift, float mcw, float eps, const int4 *__restrict__ cand, int nblk, float *era_gain,
     int *done, bool writeback, int4 *part, int *nact, int4 *chunks, int *nchunks, int chunk_cap, int *win,
-    int win_words, int wslice, int wave) {
+    int win_words, int wslice, int wave, bool local_known) {
     const int n = blockIdx.x;
     __shared__ Key s_best, s_kw[8];
     __shared__ long long s_c[8], s_g[8];
@@ -1366,18 +1404,19 @@ __global__ void __launch_bounds__(256) k_split_final(
     if (!s_last) return;
     __threadfence();
     plan_next_level(lvl, nxt, nn, d, shift, ntree, s_scan);
-    if (part) plan_children(lvl, nxt, nn, nact, d, part, chunks, nchunks, chunk_cap, wave, s_scan);
+    if (part) plan_children(lvl, nxt, nn, nact, d, part, chunks, nchunks, chunk_cap, wave, local_known, s_scan);
     if (threadIdx.x == 0) *done = 0;
 }
 
 // Feature-sliced fits, after the all-gather of win: per node the best of the
 // ranks' records by the same key order (so the choice is the one a single
 // rank searching every position makes), its totals and per-era gains into
-// the node; the last block plans the next level.
+// the node; the last block plans the next level and (part != NULL: the
+// one-launch partition) each splitting node's children range.
 __global__ void __launch_bounds__(256) k_split_pick(wgb_node *__restrict__ lvl, wgb_node *__restrict__ nxt, int *nn,
                                                     int d, int ntree, int B, int E, const int *shift,
                                                     const int *__restrict__ win, int win_words, int nslice,
-                                                    float *era_gain, int *done) {
+                                                    float *era_gain, int *done, int4 *part) {
     const int n = blockIdx.x;
     __shared__ int s_w;
     __shared__ int s_scan[33];
@@ -1426,6 +1465,7 @@ __global__ void __launch_bounds__(256) k_split_pick(wgb_node *__restrict__ lvl, 
     if (!s_last) return;
     __threadfence();
     plan_next_level(lvl, nxt, nn, d, shift, ntree, s_scan);
+    if (part) plan_children(lvl, nxt, nn, nullptr, d, part, nullptr, nullptr, 0, 0, false, s_scan);
     if (threadIdx.x == 0) *done = 0;
 }
 
@@ -1744,28 +1784,33 @@ __global__ void __launch_bounds__(PART_THREADS) k_scatter(
     }
 }
 
-// Single-rank one-era level partition in one launch.  plan_children has
-// laid out the next level (part[n] = {left cursor 0, start of n's children,
-// left count, right cursor 0}).  Each CTA takes PART_TILE consecutive
-// positions, computes their flags (k_flags' rule), ranks its rows per
-// (node, side) with shared atomics, reserves each (node, side) range with
-// one global atomic on the node's cursor, and writes the rows to their
-// child's segment.  Within a child the rows are not in their previous
-// relative order: nothing depends on it with one era (the histograms are
-// exact integer sums; era windows, which need era-sorted rows, take the
-// stable three-kernel partition).  At the tree's last level (`last`) every
-// row only gets its leaf update.
+// One-era level partition in one launch.  plan_children has given each
+// splitting node n its children's range [ns, ns + lcnt) of the next order
+// (part[n] = {left cursor 0, ns, -, right cursor 0}).  Each CTA takes
+// PART_TILE consecutive positions, computes their flags (k_flags' rule),
+// ranks its rows per (node, side) with shared atomics, reserves each (node,
+// side) range with one global atomic on the node's cursor, and writes left
+// rows upward from ns and right rows downward from ns + lcnt - 1, so the
+// left count need not be known in advance.  Within a child the rows are not
+// in their previous relative order: nothing depends on it with one era (the
+// histograms are exact integer sums; era windows, which need era-sorted
+// rows, take the stable three-kernel partition).  Multi-rank fits (finish):
+// the last CTA to finish, counted in `done` (zero-initialised, returned to
+// zero), lays out the next level from the final left cursors
+// (finish_children).  At the tree's last level (`last`) every row only gets
+// its leaf update.
 __global__ void __launch_bounds__(PART_THREADS) k_partition(
     const wgb_node *__restrict__ lvl, const int *nn_d, const int *nact_d, const int *__restrict__ order,
     const int *__restrict__ posnode, const int8_t *__restrict__ bins, long long S,
     const int8_t *__restrict__ bins_fm, long long NT, const int *__restrict__ feats, int4 *part,
     int *__restrict__ order_next, int *__restrict__ posnode_next, float *__restrict__ pred, int K, int cls,
-    float lr, long long npos, long long nloc, const wgb_node *__restrict__ last) {
+    float lr, long long npos, long long nloc, const wgb_node *__restrict__ last, bool finish, wgb_node *nxt,
+    int *nn, int *nact_all, int d, int *done, int4 *chunks, int *nchunks, int chunk_cap, int wave) {
     constexpr int IPT = PART_TILE / PART_THREADS;  // 8 consecutive positions per thread
     constexpr int CACHE = 512;                     // nodes whose records are cached per CTA
     struct PNode {
         float leaf;
-        int child, ns, L;
+        int child, ns, cnt;   // children's range [ns, ns + cnt) of the next order
         int tree, feat, bin;  // feat: split feature, -1 leaf
     };
     __shared__ PNode s_nc[CACHE];
@@ -1776,7 +1821,7 @@ __global__ void __launch_bounds__(PART_THREADS) k_partition(
         const wgb_node &nd = lvl[i];
         const int fp = nd.fpos;
         const int4 pr = fp >= 0 ? part[i] : make_int4(0, 0, 0, 0);
-        return PNode{nd.leaf, nd.child, pr.y, pr.z, node_tree(nd.built), fp >= 0 ? feats[fp] : -1, nd.bin};
+        return PNode{nd.leaf, nd.child, pr.y, nd.lcnt, node_tree(nd.built), fp >= 0 ? feats[fp] : -1, nd.bin};
     };
     auto rec = [&](int n) { return n < CACHE ? s_nc[n] : node_rec(n); };
     for (int i = threadIdx.x; i < min(nnd, CACHE); i += PART_THREADS) s_nc[i] = node_rec(i);
@@ -1886,11 +1931,25 @@ __global__ void __launch_bounds__(PART_THREADS) k_partition(
                 int4 *pr = part + nid[u];
                 r = atomicAdd(side ? &pr->w : &pr->x, 1);
             }
-            const long long np = (long long)nd.ns + (side ? nd.L : 0) + r;
+            const long long np = side ? (long long)nd.ns + nd.cnt - 1 - r : (long long)nd.ns + r;
             if (np >= 0 && np < npos) {  // always true for consistent counts; guards memory
                 order_next[np] = row[u];
                 posnode_next[np] = nd.child + side;
             }
+        }
+        if (finish) {
+            __shared__ int s_scan[33];
+            __shared__ bool s_last;
+            __syncthreads();
+            if (threadIdx.x == 0) {
+                __threadfence();  // this CTA's cursor reservations precede its count
+                s_last = atomicAdd(done, 1) == (int)gridDim.x - 1;
+            }
+            __syncthreads();
+            if (!s_last) return;
+            __threadfence();
+            finish_children(lvl, nxt, nn, nact_all, d, part, chunks, nchunks, chunk_cap, wave, s_scan);
+            if (threadIdx.x == 0) *done = 0;
         }
     } else {
         // every row's leaf update; the rows are distinct, so all eight
@@ -1953,12 +2012,12 @@ static inline long long *LL(int64_t *p) { return reinterpret_cast<long long *>(p
 // trees grown together (a multiclass round: one per class); levels hold
 // ntree << d node records
 static inline int ws_ntree(const wgb_ws *ws) { return ws->ntree > 1 ? ws->ntree : 1; }
-// Single-rank one-era fit (the local rows are all rows): the split's exact
-// left counts are the local ones, so the split plans the next level's row
-// layout and the partition is one launch (k_partition).
-static inline bool fused_partition(const wgb_ws *ws) {
-    return ws->N_global == ws->N && ws->E == 1 && ws->sync != nullptr && ws->nslice <= 1;
-}
+// One-era fits partition each level in one launch (k_partition).  On a
+// single rank (the local rows are all rows) the split's exact left counts
+// are the local ones, so the split plans the next level's row layout; on
+// several ranks the partition's last CTA finishes it from the rows it moved.
+static inline bool fused_partition(const wgb_ws *ws) { return ws->E == 1 && ws->sync != nullptr; }
+static inline bool single_rank(const wgb_ws *ws) { return ws->N_global == ws->N && ws->nslice <= 1; }
 static inline wgb_node *level_nodes(const wgb_ws *ws, int d) {
     return ws->nodes + (long long)ws_ntree(ws) * ((1 << d) - 1);
 }
@@ -2276,13 +2335,13 @@ int wgb_level_split(const wgb_ws *ws, int32_t d, void *stream) {
     }
     float *eg = ws->era_gain + (long long)ws_ntree(ws) * ((1 << d) - 1) * ws->E;
     WGB_CHECK_ARG(ws->sync != nullptr, "workspace needs its sync counters");
-    const bool fp = fused_partition(ws);
+    const bool fp = fused_partition(ws), one = single_rank(ws);
     k_split_final<<<cap, 256, 0, st>>>(lvl, level_nodes(ws, d + 1), ws->nn, d, ws_ntree(ws), hg, hc, se, kl, j0,
                                        ws->E, ws->B, ws->shift, ws->mcw, ws->eps, cand, nblk, eg, ws->sync,
                                        d < ws->D - 1, fp ? reinterpret_cast<int4 *>(ws->part) : nullptr, ws->nact,
-                                       fp && d < ws->D - 1 ? reinterpret_cast<int4 *>(ws->chunks) : nullptr,
+                                       fp && one && d < ws->D - 1 ? reinterpret_cast<int4 *>(ws->chunks) : nullptr,
                                        ws->nchunks, ws->chunk_cap, sliced(ws) ? ws->win : nullptr, ws->win_words,
-                                       ws->slice, hist_wave(ws));
+                                       ws->slice, hist_wave(ws), one);
     WGB_LAUNCHED("k_split_final");
     return WGB_OK;
 }
@@ -2296,7 +2355,9 @@ int wgb_level_pick(const wgb_ws *ws, int32_t d, void *stream) {
     float *eg = ws->era_gain + (long long)ws_ntree(ws) * ((1 << d) - 1) * ws->E;
     k_split_pick<<<cap, 256, 0, as_stream(stream)>>>(level_nodes(ws, d), level_nodes(ws, d + 1), ws->nn, d,
                                                      ws_ntree(ws), ws->B, ws->E, ws->shift, ws->win,
-                                                     ws->win_words, ws->nslice, eg, ws->sync);
+                                                     ws->win_words, ws->nslice, eg, ws->sync,
+                                                     fused_partition(ws) ? reinterpret_cast<int4 *>(ws->part)
+                                                                         : nullptr);
     WGB_LAUNCHED("k_split_pick");
     return WGB_OK;
 }
@@ -2330,10 +2391,13 @@ int wgb_level_partition(const wgb_ws *ws, int32_t d, void *stream) {
     const bool last = d == ws->D - 1;
     int4 *part = reinterpret_cast<int4 *>(ws->part);
     if (fused_partition(ws)) {
+        // several ranks: the last CTA lays out the next level (sync[1] counts the CTAs)
+        const bool finish = !single_rank(ws) && !last;
         k_partition<<<ntiles, PART_THREADS, 0, st>>>(
             lvl, ws->nn + d, ws->nact + d, ord, pn, ws->bins, ws->S, ws->bins_fm, (ws->N + 15) & ~15ll, ws->feats,
             part, ws->order[d & 1], ws->posnode[d & 1], ws->pred, ws->K, ws->cls, ws->lr, npos, ws->N,
-            last ? level_nodes(ws, d + 1) : nullptr);
+            last ? level_nodes(ws, d + 1) : nullptr, finish, level_nodes(ws, d + 1), ws->nn, ws->nact, d,
+            ws->sync + 1, reinterpret_cast<int4 *>(ws->chunks), ws->nchunks, ws->chunk_cap, hist_wave(ws));
         WGB_LAUNCHED("k_partition");
         return WGB_OK;
     }
