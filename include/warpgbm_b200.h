@@ -157,6 +157,29 @@ int wgb_quantile_edges(const float *X, int64_t n, int32_t F, int64_t x_stride,
                        const float *q, int32_t nq, float *XT, float *edges,
                        void *stream);
 
+/* The same edges for a column whose rows are spread over several ranks
+ * (row-sharded fits; replaces the per-column torch.quantile of
+ * warpgbm/core.py:529-534 over the full column): the radix selection one
+ * digit pass at a time, pass = 0..3, nq <= 32.  wgb_quantile_pass
+ * histograms the digit of this rank's n rows of the F columns of X (pass 0
+ * first copies them column-major into XT, which later passes read: keep it)
+ * into hist -- pass 0: [F][4096] words and nan_flags[F]; passes 1-3:
+ * [F][16384] words -- from the digits resolved so far in state
+ * ([F][129] words).  The caller sums hist (and, pass 0, nan_flags) over
+ * the ranks as int32, then wgb_quantile_pick resolves the digit of every
+ * target from the sums with the ranks' total row count n_total (<= 2^24,
+ * torch's limit) into state; after pass 3 it writes edges[F][nq], bit for
+ * bit torch.quantile over the concatenated column (NaN edges for a column
+ * with any NaN, written at pass 0).  No row moves between ranks. */
+int wgb_quantile_pass(int32_t pass, const float *X, int64_t n, int32_t F,
+                      int64_t x_stride, int32_t nq, float *XT,
+                      const uint32_t *state, uint32_t *hist, int32_t *nan_flags,
+                      void *stream);
+int wgb_quantile_pick(int32_t pass, const uint32_t *hist,
+                      const int32_t *nan_flags, int64_t n_total, const float *q,
+                      int32_t nq, int32_t F, uint32_t *state, float *edges,
+                      void *stream);
+
 /* One node of one tree level (64 bytes).  Global quantities (summed over all
  * ranks of a row-sharded job) and local ones (this rank's rows). */
 typedef struct wgb_node {

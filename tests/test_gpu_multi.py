@@ -129,3 +129,66 @@ def test_three_ranks_gloo_one_gpu_uneven_slices_match_single_process(cuda):
 @pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs two GPUs for one NCCL rank per GPU")
 def test_two_ranks_nccl_match_single_process(cuda):
     _check("nccl", 2)
+
+
+def _edge_columns():
+    rng = np.random.default_rng(9)
+    n = 5000
+    X = rng.standard_normal((n, 9)).astype(np.float32)
+    X[:, 1] = np.round(X[:, 1] * 2) / 2                 # many ties
+    X[::7, 2] = 0.0
+    X[1::7, 2] = -0.0                                    # signed zeros
+    X[5, 3] = np.nan                                     # one NaN: every edge NaN
+    X[:, 4] = 3.0                                        # constant
+    X[::11, 5] = np.inf
+    X[3::11, 5] = -np.inf
+    X[:, 6] = rng.exponential(1e-30, n).astype(np.float32)  # tiny magnitudes
+    X[:, 7] = (rng.standard_normal(n) * 1e30).astype(np.float32)
+    return X
+
+
+def _edge_worker(rank, world, port, outdir, nq):
+    import datetime
+    import sys
+    sys.path.insert(0, os.path.dirname(os.path.dirname(os.path.abspath(__file__))))
+    import torch.distributed as dist
+    from warpgbm_b200.core import _Comm, sharded_quantile_edges
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    torch.cuda.set_device(0)
+    dist.init_process_group("gloo", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=120))
+    X = _edge_columns()
+    cut = [0, 0, 1700, len(X)][: world + 1] if world == 3 else np.linspace(0, len(X), world + 1).astype(int)
+    Xd = torch.from_numpy(X[cut[rank]:cut[rank + 1]]).cuda()
+    q = torch.linspace(0, 1, nq + 2, device="cuda", dtype=torch.float32)[1:-1]
+    e = sharded_quantile_edges(Xd, q, _Comm(True))
+    torch.save(e.cpu(), os.path.join(outdir, f"e{rank}.pt"))
+    dist.barrier()
+    dist.destroy_process_group()
+
+
+@pytest.mark.parametrize("nq", [31, 7])
+def test_sharded_quantile_edges_equal_torch_quantile(cuda, nq):
+    """Quantile edges of row-sharded columns (3 gloo ranks on one GPU, one of
+    them holding no rows): the digit histograms summed over the ranks select
+    the same order statistics as the one-launch select over the concatenated
+    column (bit for bit), and the edges equal torch.quantile's -- ties,
+    signed zeros, infinities, a NaN column, a constant column, tiny and huge
+    magnitudes.  (Against torch the comparison is by value, as for the
+    one-launch select: a zero edge's sign bins nothing differently.)"""
+    from warpgbm_b200.core import _quantile_columns
+    X = _edge_columns()
+    q = torch.linspace(0, 1, nq + 2, device="cuda", dtype=torch.float32)[1:-1]
+    Xd = torch.from_numpy(X).cuda()
+    want = torch.stack([torch.quantile(Xd[:, f], q) for f in range(X.shape[1])]).cpu().numpy()
+    one = _quantile_columns(Xd, q).cpu().numpy()
+    nan = np.isnan(want)
+    assert nan[3].all() and np.array_equal(np.isnan(one), nan)
+    with tempfile.TemporaryDirectory() as d:
+        mp.spawn(_edge_worker, args=(3, _port(), d, nq), nprocs=3, join=True)
+        for r in range(3):
+            got = torch.load(os.path.join(d, f"e{r}.pt")).numpy()
+            assert np.array_equal(np.isnan(got), nan), r
+            assert np.array_equal(got[~nan].view(np.int32), one[~nan].view(np.int32)), \
+                (r, np.argwhere((got.view(np.int32) != one.view(np.int32)) & ~nan)[:5])
+            assert np.array_equal(got, want, equal_nan=True), (r, np.argwhere((got != want) & ~nan)[:5])

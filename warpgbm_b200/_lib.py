@@ -99,6 +99,8 @@ _SIGS = {
     "wgb_comm_reduce_scatter": ([_p, _p, _p, _i64, _p], _i32),
     "wgb_comm_allgather_i32": ([_p, _p, _i64, _p], _i32),
     "wgb_quantile_edges": ([_p, _i64, _i32, _i64, _p, _i32, _p, _p, _p], _i32),
+    "wgb_quantile_pass": ([_i32, _p, _i64, _i32, _i64, _i32, _p, _p, _p, _p, _p], _i32),
+    "wgb_quantile_pick": ([_i32, _p, _p, _i64, _p, _i32, _i32, _p, _p, _p], _i32),
 }
 
 EXPORTED = tuple(_SIGS)
@@ -143,7 +145,8 @@ _KERNELS = {
     "wgb_level_hist": 2, "wgb_level_split": 2, "wgb_level_pick": 1, "wgb_level_partition": 3,
     "wgb_tree_finish": 0,
     "wgb_grow_tree": 0, "wgb_bins_feature_major": 1, "wgb_prebinned_ingest": 1,
-    "wgb_bin_matrix": 1, "wgb_predict_packed": 1, "wgb_predict_heap": 1, "wgb_quantile_edges": 2, "wgb_compute_histogram3": 6, "wgb_compute_histogram3_noalloc": 6,
+    "wgb_bin_matrix": 1, "wgb_predict_packed": 1, "wgb_predict_heap": 1, "wgb_quantile_edges": 2, "wgb_quantile_pass": 1, "wgb_quantile_pick": 1,
+    "wgb_compute_histogram3": 6, "wgb_compute_histogram3_noalloc": 6,
     "wgb_compute_split": 1, "wgb_custom_cuda_binner": 1, "wgb_predict_forest": 1,
 }
 LAUNCHES = [0]

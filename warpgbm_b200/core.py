@@ -264,16 +264,59 @@ def exchange_columns(Xd: torch.Tensor, comm: _Comm):
 def sharded_quantile_edges(Xd: torch.Tensor, q: torch.Tensor, comm: _Comm) -> torch.Tensor:
     """Quantile edges [F, B-1] of every column of the row-sharded float
     matrix, bit-identical to torch.quantile over the full column
-    (core.py:529-534): columns are exchanged so each rank holds complete
-    columns of a feature slice, then the edges are all-gathered."""
+    (core.py:529-534): up to 32 quantiles by a radix select over the ranks'
+    summed digit histograms (_sharded_select); more by exchanging columns so
+    each rank holds complete columns of a feature slice, then all-gathering
+    the edges."""
     F = Xd.shape[1]
     if not comm.on:
         return _quantile_columns(Xd, q)
+    if q.numel() <= QS_MAXQ:
+        return _sharded_select(Xd, q, comm)
     cols, per = exchange_columns(Xd, comm)
     mine = _quantile_columns(cols, q)                      # [per, B-1]
     outs = [torch.empty_like(mine) for _ in range(comm.world)]
     comm.all_gather(outs, mine)
     return torch.cat(outs, 0)[:F].contiguous()
+
+
+QS_MAXQ, QS_H0, QS_HCOL, QS_STATE = 32, 4096, 64 * 256, 2 * 64 + 1  # wgb_quantile_pass / _pick sizes
+
+
+def _sharded_select(Xd: torch.Tensor, q: torch.Tensor, comm: _Comm, chunk_elems: int = 1 << 28):
+    """Quantile edges [F, B-1] of the row-sharded float matrix without moving
+    rows: the radix select of wgb_quantile_edges one digit pass at a time --
+    every rank histograms the digit of its own rows (wgb_quantile_pass), one
+    int32 sum over the ranks per pass, and every rank resolves the same
+    digits from the sums (wgb_quantile_pick).  Bit-identical to
+    torch.quantile over the concatenated column (core.py:529-534)."""
+    n, F = Xd.shape
+    dev = Xd.device
+    ng = int(comm.sum_(torch.tensor([n], dtype=torch.int64, device=dev)).item())
+    if ng > (1 << 24):
+        raise ValueError("quantile() input tensor is too large")  # torch's own limit
+    nq = q.numel()
+    Xd = Xd.contiguous()
+    qd = q.contiguous()
+    out = torch.empty((F, nq), dtype=torch.float32, device=dev)
+    step = max(1, min(F, chunk_elems // max(n + 3, 1)))
+    ld = (n + 3) // 4 * 4
+    XT = torch.empty(max(ld * step, 4), dtype=torch.float32, device=dev)
+    hist = torch.empty(step * QS_HCOL, dtype=torch.int32, device=dev)
+    state = torch.empty(step * QS_STATE, dtype=torch.int32, device=dev)
+    nanf = torch.empty(step, dtype=torch.int32, device=dev)
+    st = torch.cuda.current_stream().cuda_stream
+    for c0 in range(0, F, step):
+        m = min(F, c0 + step) - c0
+        for p in range(4):
+            _lib.call("wgb_quantile_pass", p, Xd.data_ptr() + 4 * c0, n, m, F, nq, XT.data_ptr(),
+                      state.data_ptr(), hist.data_ptr(), nanf.data_ptr(), st)
+            comm.sum_(hist[: m * (QS_H0 if p == 0 else QS_HCOL)])
+            if p == 0:
+                comm.sum_(nanf[:m])
+            _lib.call("wgb_quantile_pick", p, hist.data_ptr(), nanf.data_ptr(), ng, qd.data_ptr(), nq, m,
+                      state.data_ptr(), out[c0:c0 + m].data_ptr(), st)
+    return out
 
 
 def _quantile_columns(Xd: torch.Tensor, q: torch.Tensor, chunk_elems: int = 1 << 28):

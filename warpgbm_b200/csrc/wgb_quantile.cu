@@ -259,6 +259,165 @@ __global__ void __launch_bounds__(QS_NT, 2) k_qselect(const float *__restrict__ 
     }
 }
 
+// ---------------------------------------------------------------------------
+// Row-sharded columns (several ranks): the same radix select, one digit pass
+// per launch.  Each rank histograms the digit of its own rows
+// (k_qs_local<P>), the histograms are summed over the ranks between passes
+// (an int32 all-reduce), and every rank resolves the same digits from the
+// sums (k_qs_pick<P>) -- the order statistics of the concatenated column, so
+// torch.quantile's edges over it bit for bit, without moving any row.  At
+// most QS_MAXQ quantiles.  Per-column state (uint32): the resolved keys of
+// the 2*nq targets, their residual ranks, and a NaN flag.
+constexpr int QS_STATE = 2 * QS_MAXT + 1;
+constexpr int QS_HCOL = QS_MAXT * 256;  // histogram words per column, passes 1-3 (pass 0: QS_H0)
+
+// Slots of digit pass p (1..3): the distinct resolved prefixes (key >> sh,
+// sh = the low bit of pass p-1's digit) in target order.  One thread.
+__device__ __forceinline__ int qs_slots(const uint32_t *key, int nt, int sh, int *slot, uint32_t *pre) {
+    int ns = 0;
+    for (int t = 0; t < nt; ++t) {
+        const uint32_t pr = key[t] >> sh;
+        int sl = -1;
+        for (int u = 0; u < ns; ++u)
+            if (pre[u] == pr) { sl = u; break; }
+        if (sl < 0) { sl = ns; pre[ns++] = pr; }
+        slot[t] = sl;
+    }
+    return ns;
+}
+
+template <int P>
+__global__ void __launch_bounds__(QS_NT, 2) k_qs_local(const float *__restrict__ XT, long long n, long long ld,
+                                                       int nq, const uint32_t *__restrict__ state,
+                                                       uint32_t *__restrict__ hist_out, int *__restrict__ nan_out) {
+    extern __shared__ __align__(16) uint32_t qs_dyn[];
+    uint32_t *hist = qs_dyn;
+    uint8_t *tbl12 = reinterpret_cast<uint8_t *>(qs_dyn + QS_MAXT * 256);
+    uint8_t *tbl8a = tbl12 + QS_H0;
+    uint8_t *tbl8b = tbl8a + QS_MAXT * 256;
+    __shared__ uint32_t t_key[QS_MAXT], s_pre[QS_MAXT];
+    __shared__ int t_slot[QS_MAXT], s_nslot;
+    constexpr int SHIFT[4] = {20, 12, 4, 0};
+    const int f = blockIdx.x, tid = threadIdx.x;
+    const uint4 *colv = reinterpret_cast<const uint4 *>(XT + (long long)f * ld);
+    if (P == 0) {
+        for (int t = tid; t < QS_H0; t += QS_NT) hist[t] = 0;
+        __syncthreads();
+        const int nan_seen = n > 0 ? qs_sweep<0>(colv, n, hist, tbl12, tbl8a, tbl8b) : 0;
+        const int any = __syncthreads_or(nan_seen);
+        for (int t = tid; t < QS_H0; t += QS_NT) hist_out[(long long)f * QS_H0 + t] = hist[t];
+        if (tid == 0) nan_out[f] = any;
+        return;
+    }
+    const uint32_t *st = state + (long long)f * QS_STATE;
+    if (st[2 * QS_MAXT]) return;  // NaN column: its edges are decided
+    const int nt = 2 * nq;
+    if (tid < nt) t_key[tid] = st[tid];
+    __syncthreads();
+    // the slot tables of passes 1..P, as the one-launch select builds them
+    for (int p = 1; p <= P; ++p) {
+        if (tid == 0) s_nslot = qs_slots(t_key, nt, SHIFT[p - 1], t_slot, s_pre);
+        if (p == 1) {
+            for (int t = tid; t < QS_H0; t += QS_NT) tbl12[t] = QS_NONE;
+        } else {
+            uint8_t *tb = p == 2 ? tbl8a : tbl8b;
+            for (int t = tid; t < QS_MAXT * 256; t += QS_NT) tb[t] = QS_NONE;
+        }
+        __syncthreads();
+        if (tid < s_nslot) {
+            const uint32_t pre = s_pre[tid];
+            if (p == 1) {
+                tbl12[pre] = (uint8_t)tid;
+            } else if (p == 2) {
+                tbl8a[tbl12[pre >> 8] * 256 + (pre & 0xFF)] = (uint8_t)tid;
+            } else {
+                const int s1 = tbl12[pre >> 16];
+                const int s2 = tbl8a[s1 * 256 + ((pre >> 8) & 0xFF)];
+                tbl8b[s2 * 256 + (pre & 0xFF)] = (uint8_t)tid;
+            }
+        }
+        __syncthreads();
+    }
+    const int ns = s_nslot;
+    for (int t = tid; t < ns * 256; t += QS_NT) hist[t] = 0;
+    __syncthreads();
+    if (n > 0) qs_sweep<P>(colv, n, hist, tbl12, tbl8a, tbl8b);
+    __syncthreads();
+    for (int t = tid; t < ns * 256; t += QS_NT) hist_out[(long long)f * QS_HCOL + t] = hist[t];
+}
+
+template <int P>
+__global__ void __launch_bounds__(256) k_qs_pick(const uint32_t *__restrict__ hist_in, const int *__restrict__ nan_in,
+                                                 long long n, const float *__restrict__ q, int nq,
+                                                 uint32_t *__restrict__ state, float *__restrict__ edges) {
+    extern __shared__ __align__(16) uint32_t qs_row[];  // the column's summed histogram
+    __shared__ uint32_t t_key[QS_MAXT], t_resid[QS_MAXT], s_pre[QS_MAXT];
+    __shared__ int t_slot[QS_MAXT], s_nslot;
+    constexpr int SHIFT[4] = {20, 12, 4, 0};
+    const int f = blockIdx.x, tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    constexpr int NW = 256 / 32;
+    const int nt = 2 * nq;
+    uint32_t *st = state + (long long)f * QS_STATE;
+    if (P == 0) {
+        if (nan_in[f]) {  // torch: every rank -> n-1 (the NaN)
+            if (tid == 0) st[2 * QS_MAXT] = 1u;
+            for (int j = tid; j < nq; j += 256) edges[(long long)f * nq + j] = __int_as_float(0x7fc00000);
+            return;
+        }
+        for (int t = tid; t < QS_H0; t += 256) qs_row[t] = hist_in[(long long)f * QS_H0 + t];
+        if (tid < nq) {
+            const float rank = __fmul_rn(q[tid], (float)(n - 1));
+            t_resid[2 * tid] = (uint32_t)(long long)rank;
+            t_resid[2 * tid + 1] = (uint32_t)(long long)ceilf(rank);
+        }
+        __syncthreads();
+        for (int t = warp; t < nt; t += NW) {
+            int d;
+            uint32_t before;
+            qs_find<QS_H0>(qs_row, t_resid[t], d, before);
+            if (lane == 0) {
+                st[t] = (uint32_t)d << 20;
+                st[QS_MAXT + t] = t_resid[t] - before;
+            }
+        }
+        if (tid == 0) st[2 * QS_MAXT] = 0u;
+        return;
+    }
+    if (st[2 * QS_MAXT]) return;
+    if (tid < nt) {
+        t_key[tid] = st[tid];
+        t_resid[tid] = st[QS_MAXT + tid];
+    }
+    __syncthreads();
+    if (tid == 0) s_nslot = qs_slots(t_key, nt, SHIFT[P - 1], t_slot, s_pre);
+    __syncthreads();
+    for (int t = tid; t < s_nslot * 256; t += 256) qs_row[t] = hist_in[(long long)f * QS_HCOL + t];
+    __syncthreads();
+    for (int t = warp; t < nt; t += NW) {
+        int d;
+        uint32_t before;
+        qs_find<256>(qs_row + t_slot[t] * 256, t_resid[t], d, before);
+        if (lane == 0) {
+            t_key[t] |= (uint32_t)d << SHIFT[P];
+            t_resid[t] -= before;
+        }
+    }
+    __syncthreads();
+    if (tid < nt) {
+        st[tid] = t_key[tid];
+        st[QS_MAXT + tid] = t_resid[tid];
+    }
+    if (P == 3 && tid < nq) {  // edges: torch's lerp with one FMA per branch
+        const float rank = __fmul_rn(q[tid], (float)(n - 1));
+        const float w = __fsub_rn(rank, (float)(long long)rank);
+        const float a = __int_as_float((int)key2f(t_key[2 * tid]));
+        const float b = __int_as_float((int)key2f(t_key[2 * tid + 1]));
+        const float dd = __fsub_rn(b, a);
+        edges[(long long)f * nq + tid] =
+            (fabsf(w) < 0.5f) ? __fmaf_rn(w, dd, a) : __fmaf_rn(-dd, __fsub_rn(1.0f, w), b);
+    }
+}
+
 }  // namespace wgb
 
 using namespace wgb;
@@ -278,5 +437,48 @@ extern "C" int wgb_quantile_edges(const float *X, int64_t n, int32_t F, int64_t 
     WGB_CUDA(cudaFuncSetAttribute(k_qselect, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)QS_SMEM));
     k_qselect<<<(unsigned)F, QS_NT, QS_SMEM, st>>>(XT, n, ld, q, nq, edges);
     WGB_LAUNCHED("k_qselect");
+    return WGB_OK;
+}
+
+extern "C" int wgb_quantile_pass(int32_t pass, const float *X, int64_t n, int32_t F, int64_t x_stride, int32_t nq,
+                                 float *XT, const uint32_t *state, uint32_t *hist, int32_t *nan_flags, void *stream) {
+    WGB_CHECK_ARG(pass >= 0 && pass <= 3, "pass %d out of range", pass);
+    WGB_CHECK_ARG(n >= 0 && F >= 1 && nq >= 1 && nq <= QS_MAXQ, "bad sizes n=%lld F=%d nq=%d (nq <= %d)",
+                  (long long)n, F, nq, QS_MAXQ);
+    WGB_CHECK_ARG(n <= (1ll << 24), "quantile() input tensor is too large");
+    WGB_CHECK_ARG(x_stride >= F, "x_stride < F");
+    WGB_CHECK_ARG(XT && state && hist && nan_flags && (pass > 0 || X || n == 0), "NULL pointer");
+    WGB_CHECK_ARG((reinterpret_cast<uintptr_t>(XT) & 15) == 0, "XT must be 16-byte aligned");
+    cudaStream_t st = as_stream(stream);
+    const long long ld = (n + 3) & ~3ll;
+    if (pass == 0 && n > 0) {
+        dim3 tg((unsigned)((n + 31) / 32), (unsigned)((F + 31) / 32));
+        k_transpose<<<tg, 256, 0, st>>>(X, n, F, x_stride, ld, XT);
+        WGB_LAUNCHED("k_transpose");
+    }
+#define WGB_QS_LOCAL(P_)                                                                                      \
+    WGB_CUDA(cudaFuncSetAttribute(k_qs_local<P_>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)QS_SMEM)); \
+    k_qs_local<P_><<<(unsigned)F, QS_NT, QS_SMEM, st>>>(XT, n, ld, nq, state, hist, nan_flags);
+    if (pass == 0) { WGB_QS_LOCAL(0) } else if (pass == 1) { WGB_QS_LOCAL(1) } else if (pass == 2) { WGB_QS_LOCAL(2) } else { WGB_QS_LOCAL(3) }
+#undef WGB_QS_LOCAL
+    WGB_LAUNCHED("k_qs_local");
+    return WGB_OK;
+}
+
+extern "C" int wgb_quantile_pick(int32_t pass, const uint32_t *hist, const int32_t *nan_flags, int64_t n_total,
+                                 const float *q, int32_t nq, int32_t F, uint32_t *state, float *edges,
+                                 void *stream) {
+    WGB_CHECK_ARG(pass >= 0 && pass <= 3, "pass %d out of range", pass);
+    WGB_CHECK_ARG(n_total >= 1 && n_total <= (1ll << 24), "n_total=%lld outside [1, 2^24]", (long long)n_total);
+    WGB_CHECK_ARG(F >= 1 && nq >= 1 && nq <= QS_MAXQ, "bad sizes F=%d nq=%d (nq <= %d)", F, nq, QS_MAXQ);
+    WGB_CHECK_ARG(hist && nan_flags && q && state && edges, "NULL pointer");
+    cudaStream_t st = as_stream(stream);
+    const size_t sm = (size_t)(pass == 0 ? QS_H0 : QS_HCOL) * sizeof(uint32_t);
+#define WGB_QS_PICK(P_)                                                                                   \
+    WGB_CUDA(cudaFuncSetAttribute(k_qs_pick<P_>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm));  \
+    k_qs_pick<P_><<<(unsigned)F, 256, sm, st>>>(hist, nan_flags, n_total, q, nq, state, edges);
+    if (pass == 0) { WGB_QS_PICK(0) } else if (pass == 1) { WGB_QS_PICK(1) } else if (pass == 2) { WGB_QS_PICK(2) } else { WGB_QS_PICK(3) }
+#undef WGB_QS_PICK
+    WGB_LAUNCHED("k_qs_pick");
     return WGB_OK;
 }
