@@ -39,9 +39,9 @@ CONFIG = dict(n=1_000_000, F=1000, num_bins=32, max_depth=5, n_estimators=100,
               learning_rate=0.01)
 # DRAM bytes (read + write) per algorithmic byte of one level's histogram
 # build (k_hist + k_hist_reduce), from an ncu capture of a 300k-row x
-# 1000-feature root launch (339.6 MB k_hist + 40.3 MB k_hist_reduce measured
+# 1000-feature root launch (335.5 MB k_hist + 40.3 MB k_hist_reduce measured
 # for 302.8 MB algorithmic); the traffic grows with the rows processed.
-HIST_TRAFFIC_PER_ALG_BYTE = 1.255
+HIST_TRAFFIC_PER_ALG_BYTE = 1.241
 
 
 def parse():
@@ -802,7 +802,7 @@ def main():
                          "peak_kind": peak_kind,
                          "traffic": round(HIST_TRAFFIC_PER_ALG_BYTE * hist_bytes / max(nlaunch, 1))
                          if hist_bytes else None,
-                         "traffic_unit": "bytes per launch (ncu ratio 1.255 x algorithmic)",
+                         "traffic_unit": f"bytes per launch (ncu ratio {HIST_TRAFFIC_PER_ALG_BYTE} x algorithmic)",
                          "launches_timed": nlaunch,
                          "avg_launch_ms": round(hist_ms / max(nlaunch, 1), 4),
                          "timed_on": "one extra fit with CUDA events around every histogram level"},
