@@ -30,24 +30,59 @@ __device__ __forceinline__ uint32_t f2key(uint32_t b) { return b ^ ((b >> 31) ? 
 __device__ __forceinline__ uint32_t key2f(uint32_t k) { return k ^ ((k >> 31) ? 0x80000000u : 0xFFFFFFFFu); }
 
 // XT[f * ld + r] = X[r][f], ld = n rounded up to a multiple of 4 (every
-// column starts 16-byte aligned): 32 x 32 tiles through shared memory.
+// column starts 16-byte aligned): 64 x 64 tiles through shared memory, a
+// thread moving four consecutive floats per access -- a row's four columns
+// in one 16-byte load when X allows it (vec: 16-byte aligned, row stride a
+// multiple of 4), a column's four rows in one 16-byte store.  Rows in
+// [n, ld) of XT get zeros (nothing reads them).
 __global__ void __launch_bounds__(256) k_transpose(const float *__restrict__ X, long long n, int F, long long xs,
-                                                   long long ld, float *__restrict__ XT) {
-    __shared__ float t[32][33];
-    const long long r0 = (long long)blockIdx.x * 32;
-    const int f0 = blockIdx.y * 32;
-    const int tx = threadIdx.x & 31, ty = threadIdx.x >> 5;  // 8 rows of threads
-    for (int y = ty; y < 32; y += 8) {
-        long long r = r0 + y;
-        int f = f0 + tx;
-        t[y][tx] = (r < n && f < F) ? __ldg(X + r * xs + f) : 0.0f;
+                                                   long long ld, float *__restrict__ XT, bool vec) {
+    __shared__ float t[64][65];
+    const long long r0 = (long long)blockIdx.x * 64;
+    const int f0 = blockIdx.y * 64;
+    const int lo = threadIdx.x & 15, hi = threadIdx.x >> 4;  // 16 groups of four x 16 lines
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+        const int rr = hi + 16 * i;
+        const long long r = r0 + rr;
+        const int f = f0 + 4 * lo;
+        float4 v = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+        if (r < n) {
+            const float *src = X + r * xs + f;
+            if (vec && f + 3 < F) {
+                v = __ldg(reinterpret_cast<const float4 *>(src));
+            } else {
+                if (f < F) v.x = __ldg(src);
+                if (f + 1 < F) v.y = __ldg(src + 1);
+                if (f + 2 < F) v.z = __ldg(src + 2);
+                if (f + 3 < F) v.w = __ldg(src + 3);
+            }
+        }
+        t[rr][4 * lo] = v.x;
+        t[rr][4 * lo + 1] = v.y;
+        t[rr][4 * lo + 2] = v.z;
+        t[rr][4 * lo + 3] = v.w;
     }
     __syncthreads();
-    for (int y = ty; y < 32; y += 8) {
-        int f = f0 + y;
-        long long r = r0 + tx;
-        if (f < F && r < n) XT[(long long)f * ld + r] = t[tx][y];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+        const int fl = hi + 16 * i;
+        const int f = f0 + fl;
+        const long long r = r0 + 4 * lo;
+        if (f < F && r < n)  // r + 3 < ld: r is a multiple of 4 below n
+            *reinterpret_cast<float4 *>(XT + (long long)f * ld + r) =
+                make_float4(t[4 * lo][fl], t[4 * lo + 1][fl], t[4 * lo + 2][fl], t[4 * lo + 3][fl]);
     }
+}
+
+// Launch of k_transpose for X [n][F] (row stride xs) into XT (ld = n rounded
+// up to 4).
+static cudaError_t launch_transpose(const float *X, long long n, int F, long long xs, long long ld, float *XT,
+                                   cudaStream_t st) {
+    const bool vec = (reinterpret_cast<uintptr_t>(X) & 15) == 0 && xs % 4 == 0;
+    dim3 tg((unsigned)((n + 63) / 64), (unsigned)((F + 63) / 64));
+    k_transpose<<<tg, 256, 0, st>>>(X, n, F, xs, ld, XT, vec);
+    return cudaGetLastError();
 }
 
 // Cumulative search of one L-bucket row by one warp: bucket holding the
@@ -87,56 +122,97 @@ __device__ __forceinline__ void qs_find(const uint32_t *row, uint32_t resid, int
     before = __shfl_sync(0xffffffffu, b, src);
 }
 
-// One sweep over the column for digit pass P (0..3): counts the digit of
-// every element whose higher digits match a target prefix (slot tables of
-// the previous passes).  Pass 0 also reports NaNs.
+// Digits of QS_V vectors (4 elements each) loaded by one sweep step, for
+// digit pass P (0..3): elements whose higher digits match a target prefix
+// (slot tables of the previous passes) are counted; pass 0 counts runs of
+// one bucket with one atomic per run and reports NaNs.
 template <int P>
-__device__ __forceinline__ int qs_sweep(const uint4 *__restrict__ colv, long long n, uint32_t *hist,
+__device__ __forceinline__ int qs_count(const uint4 (&x)[QS_V], long long v0, long long n, uint32_t *hist,
                                         const uint8_t *tbl12, const uint8_t *tbl8a, const uint8_t *tbl8b) {
+    int nan_seen = 0;
+    uint32_t last = 0xFFFFFFFFu, run = 0;  // pass 0: runs of one bucket, one atomic per run
+#pragma unroll
+    for (int u = 0; u < QS_V; ++u) {
+        const long long e0 = (v0 + (long long)u * QS_NT) * 4;
+#pragma unroll
+        for (int c = 0; c < 4; ++c) {
+            if (e0 + c >= n) continue;
+            const uint32_t b = c == 0 ? x[u].x : c == 1 ? x[u].y : c == 2 ? x[u].z : x[u].w;
+            const uint32_t k = f2key(b);
+            if (P == 0) {
+                nan_seen |= (b & 0x7FFFFFFFu) > 0x7F800000u;
+                const uint32_t d = k >> 20;
+                if (d != last) {
+                    if (run) atomicAdd(hist + last, run);
+                    last = d;
+                    run = 0;
+                }
+                ++run;
+                continue;
+            }
+            uint32_t sl = tbl12[k >> 20];
+            if (sl == QS_NONE) continue;
+            if (P >= 2) {
+                sl = tbl8a[sl * 256 + ((k >> 12) & 0xFF)];
+                if (sl == QS_NONE) continue;
+            }
+            if (P >= 3) {
+                sl = tbl8b[sl * 256 + ((k >> 4) & 0xFF)];
+                if (sl == QS_NONE) continue;
+            }
+            const uint32_t d = P == 1 ? (k >> 12) & 0xFF : P == 2 ? (k >> 4) & 0xFF : k & 0xF;
+            atomicAdd(hist + sl * 256 + d, 1u);
+        }
+    }
+    if (P == 0 && run) atomicAdd(hist + last, run);
+    return nan_seen;
+}
+
+__device__ __forceinline__ void qs_load(const uint4 *__restrict__ colv, long long v0, long long nvec,
+                                        uint4 (&x)[QS_V]) {
+#pragma unroll
+    for (int u = 0; u < QS_V; ++u) {
+        const long long v = v0 + (long long)u * QS_NT;
+        x[u] = v < nvec ? __ldg(colv + v) : make_uint4(0u, 0u, 0u, 0u);
+    }
+}
+
+// One sweep over the column for digit pass P, one register set (the
+// one-launch select: its four passes in one kernel leave no registers for a
+// second set).
+template <int P>
+__device__ __forceinline__ int qs_sweep1(const uint4 *__restrict__ colv, long long n, uint32_t *hist,
+                                         const uint8_t *tbl12, const uint8_t *tbl8a, const uint8_t *tbl8b) {
     const long long nvec = (n + 3) >> 2;
     int nan_seen = 0;
     for (long long v0 = threadIdx.x; v0 < nvec; v0 += (long long)QS_NT * QS_V) {
         uint4 x[QS_V];
-#pragma unroll
-        for (int u = 0; u < QS_V; ++u) {
-            const long long v = v0 + (long long)u * QS_NT;
-            x[u] = v < nvec ? __ldg(colv + v) : make_uint4(0u, 0u, 0u, 0u);
-        }
-        uint32_t last = 0xFFFFFFFFu, run = 0;  // pass 0: runs of one bucket, one atomic per run
-#pragma unroll
-        for (int u = 0; u < QS_V; ++u) {
-            const long long e0 = (v0 + (long long)u * QS_NT) * 4;
-#pragma unroll
-            for (int c = 0; c < 4; ++c) {
-                if (e0 + c >= n) continue;
-                const uint32_t b = c == 0 ? x[u].x : c == 1 ? x[u].y : c == 2 ? x[u].z : x[u].w;
-                const uint32_t k = f2key(b);
-                if (P == 0) {
-                    nan_seen |= (b & 0x7FFFFFFFu) > 0x7F800000u;
-                    const uint32_t d = k >> 20;
-                    if (d != last) {
-                        if (run) atomicAdd(hist + last, run);
-                        last = d;
-                        run = 0;
-                    }
-                    ++run;
-                    continue;
-                }
-                uint32_t sl = tbl12[k >> 20];
-                if (sl == QS_NONE) continue;
-                if (P >= 2) {
-                    sl = tbl8a[sl * 256 + ((k >> 12) & 0xFF)];
-                    if (sl == QS_NONE) continue;
-                }
-                if (P >= 3) {
-                    sl = tbl8b[sl * 256 + ((k >> 4) & 0xFF)];
-                    if (sl == QS_NONE) continue;
-                }
-                const uint32_t d = P == 1 ? (k >> 12) & 0xFF : P == 2 ? (k >> 4) & 0xFF : k & 0xF;
-                atomicAdd(hist + sl * 256 + d, 1u);
-            }
-        }
-        if (P == 0 && run) atomicAdd(hist + last, run);
+        qs_load(colv, v0, nvec, x);
+        nan_seen |= qs_count<P>(x, v0, n, hist, tbl12, tbl8a, tbl8b);
+    }
+    return nan_seen;
+}
+
+// One sweep over the column for digit pass P: two register sets alternate,
+// so the next step's loads are in flight while this step's digits are
+// counted.
+template <int P>
+__device__ __forceinline__ int qs_sweep(const uint4 *__restrict__ colv, long long n, uint32_t *hist,
+                                        const uint8_t *tbl12, const uint8_t *tbl8a, const uint8_t *tbl8b) {
+    const long long nvec = (n + 3) >> 2;
+    constexpr long long STEP = (long long)QS_NT * QS_V;
+    int nan_seen = 0;
+    uint4 xa[QS_V], xb[QS_V];
+    long long v0 = threadIdx.x;
+    if (v0 < nvec) qs_load(colv, v0, nvec, xa);
+    while (v0 < nvec) {
+        if (v0 + STEP < nvec) qs_load(colv, v0 + STEP, nvec, xb);
+        nan_seen |= qs_count<P>(xa, v0, n, hist, tbl12, tbl8a, tbl8b);
+        v0 += STEP;
+        if (v0 >= nvec) break;
+        if (v0 + STEP < nvec) qs_load(colv, v0 + STEP, nvec, xa);
+        nan_seen |= qs_count<P>(xb, v0, n, hist, tbl12, tbl8a, tbl8b);
+        v0 += STEP;
     }
     return nan_seen;
 }
@@ -177,7 +253,7 @@ __global__ void __launch_bounds__(QS_NT, 2) k_qselect(const float *__restrict__ 
         // ---- pass 0: first digit, NaN detection
         for (int t = tid; t < QS_H0; t += QS_NT) hist[t] = 0;
         __syncthreads();
-        const int nan_seen = qs_sweep<0>(colv, n, hist, tbl12, tbl8a, tbl8b);
+        const int nan_seen = qs_sweep1<0>(colv, n, hist, tbl12, tbl8a, tbl8b);
         if (__syncthreads_or(nan_seen)) {  // torch: every rank -> n-1 (the NaN)
             for (int j = tid; j < nq; j += QS_NT) edges[(long long)f * nq + j] = __int_as_float(0x7fc00000);
             return;
@@ -231,9 +307,9 @@ __global__ void __launch_bounds__(QS_NT, 2) k_qselect(const float *__restrict__ 
                 }
             }
             __syncthreads();
-            if (p == 1) qs_sweep<1>(colv, n, hist, tbl12, tbl8a, tbl8b);
-            else if (p == 2) qs_sweep<2>(colv, n, hist, tbl12, tbl8a, tbl8b);
-            else qs_sweep<3>(colv, n, hist, tbl12, tbl8a, tbl8b);
+            if (p == 1) qs_sweep1<1>(colv, n, hist, tbl12, tbl8a, tbl8b);
+            else if (p == 2) qs_sweep1<2>(colv, n, hist, tbl12, tbl8a, tbl8b);
+            else qs_sweep1<3>(colv, n, hist, tbl12, tbl8a, tbl8b);
             __syncthreads();
             for (int t = warp; t < nt; t += NW) {
                 int d;
@@ -431,9 +507,7 @@ extern "C" int wgb_quantile_edges(const float *X, int64_t n, int32_t F, int64_t 
     WGB_CHECK_ARG((reinterpret_cast<uintptr_t>(XT) & 15) == 0, "XT must be 16-byte aligned");
     cudaStream_t st = as_stream(stream);
     const long long ld = (n + 3) & ~3ll;
-    dim3 tg((unsigned)((n + 31) / 32), (unsigned)((F + 31) / 32));
-    k_transpose<<<tg, 256, 0, st>>>(X, n, F, x_stride, ld, XT);
-    WGB_LAUNCHED("k_transpose");
+    WGB_CUDA(launch_transpose(X, n, F, x_stride, ld, XT, st));
     WGB_CUDA(cudaFuncSetAttribute(k_qselect, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)QS_SMEM));
     k_qselect<<<(unsigned)F, QS_NT, QS_SMEM, st>>>(XT, n, ld, q, nq, edges);
     WGB_LAUNCHED("k_qselect");
@@ -451,11 +525,7 @@ extern "C" int wgb_quantile_pass(int32_t pass, const float *X, int64_t n, int32_
     WGB_CHECK_ARG((reinterpret_cast<uintptr_t>(XT) & 15) == 0, "XT must be 16-byte aligned");
     cudaStream_t st = as_stream(stream);
     const long long ld = (n + 3) & ~3ll;
-    if (pass == 0 && n > 0) {
-        dim3 tg((unsigned)((n + 31) / 32), (unsigned)((F + 31) / 32));
-        k_transpose<<<tg, 256, 0, st>>>(X, n, F, x_stride, ld, XT);
-        WGB_LAUNCHED("k_transpose");
-    }
+    if (pass == 0 && n > 0) WGB_CUDA(launch_transpose(X, n, F, x_stride, ld, XT, st));
 #define WGB_QS_LOCAL(P_)                                                                                      \
     WGB_CUDA(cudaFuncSetAttribute(k_qs_local<P_>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)QS_SMEM)); \
     k_qs_local<P_><<<(unsigned)F, QS_NT, QS_SMEM, st>>>(XT, n, ld, nq, state, hist, nan_flags);
