@@ -44,6 +44,39 @@ void set_error(const char *fmt, ...);
 
 inline cudaStream_t as_stream(void *s) { return reinterpret_cast<cudaStream_t>(s); }
 
+// Programmatic dependent launch: the kernels of a tree level are launched
+// with programmatic stream serialisation, so each one's launch is prepared
+// while its predecessor on the stream finishes; every such kernel first
+// waits (griddepcontrol.wait) until that predecessor has completed and its
+// writes are visible.  Launched without the attribute, the wait returns at
+// once.
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+
+template <typename... KArgs, typename... Args>
+inline cudaError_t launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t st,
+                              Args &&...args) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = grid;
+    cfg.blockDim = block;
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = st;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, kernel, static_cast<KArgs>(args)...);
+}
+
+#define WGB_PDL(name, ...)                                                                 \
+    do {                                                                                   \
+        cudaError_t e_ = ::wgb::launch_pdl(__VA_ARGS__);                                   \
+        if (e_ != cudaSuccess) {                                                           \
+            ::wgb::set_error("launch of %s failed: %s", name, cudaGetErrorString(e_));     \
+            return WGB_ERR_CUDA;                                                           \
+        }                                                                                  \
+    } while (0)
+
 // ------------------------------------------------------------ constants --
 constexpr int HIST_R = 2048;        // rows per histogram chunk (cell packing needs <= 2048)
 // Packing of a histogram cell into two 32-bit shared words for <= HIST_R rows:

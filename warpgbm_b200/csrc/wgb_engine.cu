@@ -145,6 +145,7 @@ __global__ void k_root_cells(long long *hg, const long long *rootsum, long long 
 
 __global__ void k_root_total(wgb_node *nodes, const long long *hg, long long slot_elems, long long nc,
                              const int *shift, int ntree) {
+    pdl_wait();  // the previous kernel on the stream has completed
     for (int t = threadIdx.x; t < ntree; t += blockDim.x) {
         wgb_node &r = nodes[t];
         r.sumq = hg[t * slot_elems + 2 * nc];
@@ -229,6 +230,7 @@ __device__ __forceinline__ void plan_chunks(const wgb_node *__restrict__ lvl, in
 // Chunk list of level 0 (later levels are planned by k_node_offsets).
 __global__ void __launch_bounds__(1024) k_chunk_plan(const wgb_node *__restrict__ lvl, const int *nn_d,
                                                      int4 *chunks, int *nchunks, int cap, int wave) {
+    pdl_wait();  // the previous kernel on the stream has completed
     plan_chunks(lvl, *nn_d, chunks, nchunks, cap, wave);
 }
 
@@ -607,6 +609,7 @@ __global__ void __launch_bounds__(NT, MINB) k_hist(
     const int *__restrict__ era, const int *__restrict__ kpos, int k, int E, int B, int EW,
     const int4 *__restrict__ chunks, const int *nchunks, const wgb_node *__restrict__ lvl,
     const HistOut out, long long nrows, uint2 *__restrict__ part, int ntile) {
+    pdl_wait();  // the previous kernel on the stream has completed
     const int c = blockIdx.x / ntile;
     if (c >= *nchunks) return;
     hist_item<FPL, NT, MINB, NSC, EWC, HAS_ERA, REGULAR>(c, blockIdx.x - c * ntile, ntile, bins, S, F, order, q, g,
@@ -625,6 +628,7 @@ __global__ void __launch_bounds__(256) k_hist_reduce(const uint2 *__restrict__ p
                                                      const int *nchunks, const wgb_node *__restrict__ lvl,
                                                      const int *__restrict__ kpos, int F, int B, int seg,
                                                      const HistOut out) {
+    pdl_wait();  // the previous kernel on the stream has completed
     constexpr int FT = 32 * FPL, CELLS = NSC * FT;
     const int nch = *nchunks;
     const int wi = 2 * (blockIdx.x * 256 + threadIdx.x);
@@ -727,14 +731,13 @@ static cudaError_t launch_hist(int grid_x, const int8_t *bins, long long S, int 
         cudaError_t e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem); \
         if (e != cudaSuccess) return e;                                                                \
         const int ntile = (F + 32 * FPL_ - 1) / (32 * FPL_);                                          \
-        fn<<<(unsigned)grid_x * ntile, NT_, smem, st>>>(bins, S, F, order, q, g, shift, era, kpos, k, E, B, \
-                                                        ew, chunks, nchunks, lvl, out, nrows, part, ntile); \
-        e = cudaGetLastError();                                                                        \
+        e = launch_pdl(fn, dim3((unsigned)grid_x * ntile), dim3(NT_), smem, st, bins, S, F, order, q, g, \
+                       shift, era, kpos, k, E, B, ew, chunks, nchunks, lvl, out, nrows, part, ntile);     \
         if (e != cudaSuccess || !part || ERA_) return e;                                              \
         const int seg = 16;                                                                            \
         dim3 rg((unsigned)((NSC_ * 16 * FPL_ + 255) / 256), (unsigned)ntile, (unsigned)((grid_x + seg - 1) / seg)); \
-        k_hist_reduce<FPL_, NSC_><<<rg, 256, 0, st>>>(part, chunks, nchunks, lvl, kpos, F, B, seg, out);  \
-        return cudaGetLastError();                                                                     \
+        return launch_pdl(k_hist_reduce<FPL_, NSC_>, rg, dim3(256), 0, st, part, chunks, nchunks, lvl, kpos, \
+                          F, B, seg, out);                                                             \
     }
 #define WGB_HIST_REG(FPL_, NT_, MINB_, NSC_, EWC_, ERA_) \
     WGB_HIST_CASE(FPL_, NT_, MINB_, NSC_, EWC_, ERA_, true) WGB_HIST_CASE(FPL_, NT_, MINB_, NSC_, EWC_, ERA_, false)
@@ -778,6 +781,7 @@ __global__ void __launch_bounds__(SPLIT_WARPS * 32) k_split(
     const wgb_node *__restrict__ lvl, const int *nn_d, long long *hg, long long *hc, long long slot_elems,
     int k, int jofs, int B, const int *shift,
     float mcw, float eps, float msg, int4 *cand, int nblk, float *crit_out, bool writeback) {
+    pdl_wait();  // the previous kernel on the stream has completed
     __shared__ float sG[SPLIT_WARPS][32 * NBW + 1], sH[SPLIT_WARPS][32 * NBW + 1];
     __shared__ Key s_k[SPLIT_WARPS];
     const int n = blockIdx.x / nblk, jb = blockIdx.x - n * nblk;  // node, feature block
@@ -997,6 +1001,7 @@ __global__ void __launch_bounds__(256) k_split_eras(
     float mcw, float eps, float msg, float factor, const int *__restrict__ sched,
     const uint8_t *__restrict__ ops, int nops, int depth, int4 *cand, int nblk, float *crit_out,
     bool writeback) {
+    pdl_wait();  // the previous kernel on the stream has completed
     constexpr int FB = EraSplitShape<NB>::FB, IPT = EraSplitShape<NB>::IPT, EB = SPLIT_ERA_EB;
     extern __shared__ float s_era_split[];
     const int n = blockIdx.x / nblk, jb = blockIdx.x - n * nblk;  // node, feature block
@@ -1276,6 +1281,7 @@ __global__ void __launch_bounds__(256) k_split_final(
     int E, int B, const int *shift, float mcw, float eps, const int4 *__restrict__ cand, int nblk, float *era_gain,
     int *done, bool writeback, int4 *part, int *nact, int4 *chunks, int *nchunks, int chunk_cap, int *win,
     int win_words, int wslice, int wave, bool local_known) {
+    pdl_wait();  // the previous kernel on the stream has completed
     const int n = blockIdx.x;
     __shared__ Key s_best, s_kw[8];
     __shared__ long long s_c[8], s_g[8];
@@ -1417,6 +1423,7 @@ __global__ void __launch_bounds__(256) k_split_pick(wgb_node *__restrict__ lvl, 
                                                     int d, int ntree, int B, int E, const int *shift,
                                                     const int *__restrict__ win, int win_words, int nslice,
                                                     float *era_gain, int *done, int4 *part) {
+    pdl_wait();  // the previous kernel on the stream has completed
     const int n = blockIdx.x;
     __shared__ int s_w;
     __shared__ int s_scan[33];
@@ -1510,6 +1517,7 @@ __global__ void __launch_bounds__(PART_THREADS) k_flags(
     const int *__restrict__ posnode, const int8_t *__restrict__ bins, long long S,
     const int8_t *__restrict__ bins_fm, long long NT,
     const int *__restrict__ feats, uint8_t *flags, int *tile_cnt, long long nloc) {
+    pdl_wait();  // the previous kernel on the stream has completed
     // (split feature or -1, split bin) of the level's nodes, cached once per CTA
     constexpr int CACHE = 1024, IPT = PART_TILE / PART_THREADS;
     __shared__ int2 s_nd[CACHE];
@@ -1597,6 +1605,7 @@ __global__ void __launch_bounds__(1024) k_node_offsets(wgb_node *__restrict__ lv
                                                        const uint8_t *flags, const int *tile_cnt,
                                                        int *tile_off, int ntiles, int4 *part, int4 *chunks,
                                                        int *nchunks, int chunk_cap, int wave) {
+    pdl_wait();  // the previous kernel on the stream has completed
     __shared__ int s_scan[33];
     {   // exclusive scan of the tiles' left counts (tile_off[ntiles] = total)
         int base = 0;
@@ -1664,6 +1673,7 @@ __global__ void __launch_bounds__(PART_THREADS) k_scatter(
     const int *__restrict__ tile_off, const int4 *__restrict__ part, int *__restrict__ order_next,
     int *__restrict__ posnode_next, float *__restrict__ pred, int K, int cls, float lr, long long npos,
     long long nloc, const wgb_node *__restrict__ last) {
+    pdl_wait();  // the previous kernel on the stream has completed
     constexpr int IPT = PART_TILE / PART_THREADS;  // 8 consecutive positions per thread
     constexpr int CACHE = 512;                     // nodes whose records are cached per CTA
     __shared__ ScatterNode s_nc[CACHE];
@@ -1806,6 +1816,7 @@ __global__ void __launch_bounds__(PART_THREADS) k_partition(
     int *__restrict__ order_next, int *__restrict__ posnode_next, float *__restrict__ pred, int K, int cls,
     float lr, long long npos, long long nloc, const wgb_node *__restrict__ last, bool finish, wgb_node *nxt,
     int *nn, int *nact_all, int d, int *done, int4 *chunks, int *nchunks, int chunk_cap, int wave) {
+    pdl_wait();  // the previous kernel on the stream has completed
     constexpr int IPT = PART_TILE / PART_THREADS;  // 8 consecutive positions per thread
     constexpr int CACHE = 512;                     // nodes whose records are cached per CTA
     struct PNode {
@@ -2242,9 +2253,8 @@ int wgb_level_hist(const wgb_ws *ws, int32_t d, void *stream) {
     }
     wgb_node *lvl = level_nodes(ws, d);
     if (d == 0) {  // later levels' chunk lists are planned by the previous level's partition
-        k_chunk_plan<<<1, 1024, 0, st>>>(lvl, ws->nn + d, reinterpret_cast<int4 *>(ws->chunks),
-                                         ws->nchunks, ws->chunk_cap, hist_wave(ws));
-        WGB_LAUNCHED("k_chunk_plan");
+        WGB_PDL("k_chunk_plan", k_chunk_plan, dim3(1), dim3(1024), 0, st, lvl, ws->nn + d,
+                reinterpret_cast<int4 *>(ws->chunks), ws->nchunks, ws->chunk_cap, hist_wave(ws));
     }
     if (ws->N == 0) return WGB_OK;
     // most chunks the level can have: pieces of at least HIST_R rows, or of
@@ -2284,8 +2294,8 @@ int wgb_level_split(const wgb_ws *ws, int32_t d, void *stream) {
     wgb_node *lvl = level_nodes(ws, d);
     const int cap = ws_ntree(ws) << d;
     if (d == 0) {
-        k_root_total<<<1, 32, 0, st>>>(ws->nodes, hg, se, nc, ws->shift, ws_ntree(ws));
-        WGB_LAUNCHED("k_root_total");
+        WGB_PDL("k_root_total", k_root_total, dim3(1), dim3(32), 0, st, ws->nodes, hg, se, nc, ws->shift,
+                ws_ntree(ws));
     }
     // (from level 1 on, the split kernels first turn each unbuilt node's
     // parent histogram into parent - built sibling)
@@ -2299,12 +2309,10 @@ int wgb_level_split(const wgb_ws *ws, int32_t d, void *stream) {
         WGB_CHECK_ARG(nblk <= ws->ncand_blk, "candidate buffer too small: %d blocks per node needed", nblk);
         const unsigned g = (unsigned)nblk * (unsigned)cap;  // node-major blocks
 #define WGB_SPLIT_W(NBW_)                                                                                  \
-    k_split<NBW_><<<g, SPLIT_WARPS * 32, 0, st>>>(lvl, ws->nn + d, hg, hc, se, kr, j0, ws->B, ws->shift,  \
-                                                ws->mcw, ws->eps, ws->msg, cand, nblk, ws->crit_out,      \
-                                                d < ws->D - 1)
+    WGB_PDL("k_split", k_split<NBW_>, dim3(g), dim3(SPLIT_WARPS * 32), 0, st, lvl, ws->nn + d, hg, hc, se, kr, \
+            j0, ws->B, ws->shift, ws->mcw, ws->eps, ws->msg, cand, nblk, ws->crit_out, d < ws->D - 1)
         if (g > 0) {
             if (nb <= 32) WGB_SPLIT_W(1); else if (nb <= 64) WGB_SPLIT_W(2); else WGB_SPLIT_W(4);
-            WGB_LAUNCHED("k_split");
         }
 #undef WGB_SPLIT_W
     } else {
@@ -2322,27 +2330,23 @@ int wgb_level_split(const wgb_ws *ws, int32_t d, void *stream) {
         const size_t sm = split_eras_smem(ws->B, NB_, EraSplitShape<NB_>::FB, ws->era_depth);                  \
         WGB_CHECK_ARG(sm <= (size_t)smem_max, "era criterion plan too deep (%d) for shared memory", ws->era_depth); \
         WGB_CUDA(cudaFuncSetAttribute(k_split_eras<NB_>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm)); \
-        k_split_eras<NB_><<<g, 256, sm, st>>>(lvl, ws->nn + d, hg, hc, se, kr, kl, j0, ws->E, ws->B, ws->shift, \
-                                              ws->mcw, ws->eps, ws->msg, ws->mean_factor, ws->era_sched,        \
-                                              ws->era_ops, ws->era_nops, ws->era_depth, cand, nblk,             \
-                                              ws->crit_out, d < ws->D - 1);                                     \
+        WGB_PDL("k_split_eras", k_split_eras<NB_>, dim3(g), dim3(256), sm, st, lvl, ws->nn + d, hg, hc, se, kr, \
+                kl, j0, ws->E, ws->B, ws->shift, ws->mcw, ws->eps, ws->msg, ws->mean_factor, ws->era_sched,    \
+                ws->era_ops, ws->era_nops, ws->era_depth, cand, nblk, ws->crit_out, d < ws->D - 1);            \
     }
         if (g > 0) {
             if (nb <= 8) WGB_SPLIT_ERAS(8) else if (nb <= 32) WGB_SPLIT_ERAS(32) else WGB_SPLIT_ERAS(128)
-            WGB_LAUNCHED("k_split_eras");
         }
 #undef WGB_SPLIT_ERAS
     }
     float *eg = ws->era_gain + (long long)ws_ntree(ws) * ((1 << d) - 1) * ws->E;
     WGB_CHECK_ARG(ws->sync != nullptr, "workspace needs its sync counters");
     const bool fp = fused_partition(ws), one = single_rank(ws);
-    k_split_final<<<cap, 256, 0, st>>>(lvl, level_nodes(ws, d + 1), ws->nn, d, ws_ntree(ws), hg, hc, se, kl, j0,
-                                       ws->E, ws->B, ws->shift, ws->mcw, ws->eps, cand, nblk, eg, ws->sync,
-                                       d < ws->D - 1, fp ? reinterpret_cast<int4 *>(ws->part) : nullptr, ws->nact,
-                                       fp && one && d < ws->D - 1 ? reinterpret_cast<int4 *>(ws->chunks) : nullptr,
-                                       ws->nchunks, ws->chunk_cap, sliced(ws) ? ws->win : nullptr, ws->win_words,
-                                       ws->slice, hist_wave(ws), one);
-    WGB_LAUNCHED("k_split_final");
+    WGB_PDL("k_split_final", k_split_final, dim3(cap), dim3(256), 0, st, lvl, level_nodes(ws, d + 1), ws->nn, d,
+            ws_ntree(ws), hg, hc, se, kl, j0, ws->E, ws->B, ws->shift, ws->mcw, ws->eps, cand, nblk, eg, ws->sync,
+            d < ws->D - 1, fp ? reinterpret_cast<int4 *>(ws->part) : nullptr, ws->nact,
+            fp && one && d < ws->D - 1 ? reinterpret_cast<int4 *>(ws->chunks) : nullptr, ws->nchunks, ws->chunk_cap,
+            sliced(ws) ? ws->win : nullptr, ws->win_words, ws->slice, hist_wave(ws), one);
     return WGB_OK;
 }
 
@@ -2353,12 +2357,9 @@ int wgb_level_pick(const wgb_ws *ws, int32_t d, void *stream) {
     if (!sliced(ws)) return WGB_OK;  // wgb_level_split already decided
     const int cap = ws_ntree(ws) << d;
     float *eg = ws->era_gain + (long long)ws_ntree(ws) * ((1 << d) - 1) * ws->E;
-    k_split_pick<<<cap, 256, 0, as_stream(stream)>>>(level_nodes(ws, d), level_nodes(ws, d + 1), ws->nn, d,
-                                                     ws_ntree(ws), ws->B, ws->E, ws->shift, ws->win,
-                                                     ws->win_words, ws->nslice, eg, ws->sync,
-                                                     fused_partition(ws) ? reinterpret_cast<int4 *>(ws->part)
-                                                                         : nullptr);
-    WGB_LAUNCHED("k_split_pick");
+    WGB_PDL("k_split_pick", k_split_pick, dim3(cap), dim3(256), 0, as_stream(stream), level_nodes(ws, d),
+            level_nodes(ws, d + 1), ws->nn, d, ws_ntree(ws), ws->B, ws->E, ws->shift, ws->win, ws->win_words,
+            ws->nslice, eg, ws->sync, fused_partition(ws) ? reinterpret_cast<int4 *>(ws->part) : nullptr);
     return WGB_OK;
 }
 
@@ -2393,26 +2394,21 @@ int wgb_level_partition(const wgb_ws *ws, int32_t d, void *stream) {
     if (fused_partition(ws)) {
         // several ranks: the last CTA lays out the next level (sync[1] counts the CTAs)
         const bool finish = !single_rank(ws) && !last;
-        k_partition<<<ntiles, PART_THREADS, 0, st>>>(
-            lvl, ws->nn + d, ws->nact + d, ord, pn, ws->bins, ws->S, ws->bins_fm, (ws->N + 15) & ~15ll, ws->feats,
-            part, ws->order[d & 1], ws->posnode[d & 1], ws->pred, ws->K, ws->cls, ws->lr, npos, ws->N,
-            last ? level_nodes(ws, d + 1) : nullptr, finish, level_nodes(ws, d + 1), ws->nn, ws->nact, d,
-            ws->sync + 1, reinterpret_cast<int4 *>(ws->chunks), ws->nchunks, ws->chunk_cap, hist_wave(ws));
-        WGB_LAUNCHED("k_partition");
+        WGB_PDL("k_partition", k_partition, dim3(ntiles), dim3(PART_THREADS), 0, st, lvl, ws->nn + d,
+                ws->nact + d, ord, pn, ws->bins, ws->S, ws->bins_fm, (ws->N + 15) & ~15ll, ws->feats, part,
+                ws->order[d & 1], ws->posnode[d & 1], ws->pred, ws->K, ws->cls, ws->lr, npos, ws->N,
+                last ? level_nodes(ws, d + 1) : nullptr, finish, level_nodes(ws, d + 1), ws->nn, ws->nact, d,
+                ws->sync + 1, reinterpret_cast<int4 *>(ws->chunks), ws->nchunks, ws->chunk_cap, hist_wave(ws));
         return WGB_OK;
     }
-    k_flags<<<ntiles, PART_THREADS, 0, st>>>(lvl, ws->nn + d, ws->nact + d, ord, pn, ws->bins, ws->S, ws->bins_fm,
-                                              (ws->N + 15) & ~15ll, ws->feats, ws->flags, ws->tile_cnt, ws->N);
-    WGB_LAUNCHED("k_flags");
-    k_node_offsets<<<1, 1024, 0, st>>>(lvl, level_nodes(ws, d + 1), ws->nn, ws->nact, d, ws->flags,
-                                       ws->tile_cnt, ws->tile_off, ntiles, part,
-                                       last ? nullptr : reinterpret_cast<int4 *>(ws->chunks), ws->nchunks,
-                                       ws->chunk_cap, hist_wave(ws));
-    WGB_LAUNCHED("k_node_offsets");
-    k_scatter<<<ntiles, PART_THREADS, 0, st>>>(lvl, ws->nn + d, ws->nact + d, ord, pn, ws->flags, ws->tile_off, part,
-                                                ws->order[d & 1], ws->posnode[d & 1], ws->pred, ws->K,
-                                                ws->cls, ws->lr, npos, ws->N, last ? level_nodes(ws, d + 1) : nullptr);
-    WGB_LAUNCHED("k_scatter");
+    WGB_PDL("k_flags", k_flags, dim3(ntiles), dim3(PART_THREADS), 0, st, lvl, ws->nn + d, ws->nact + d, ord, pn,
+            ws->bins, ws->S, ws->bins_fm, (ws->N + 15) & ~15ll, ws->feats, ws->flags, ws->tile_cnt, ws->N);
+    WGB_PDL("k_node_offsets", k_node_offsets, dim3(1), dim3(1024), 0, st, lvl, level_nodes(ws, d + 1), ws->nn,
+            ws->nact, d, ws->flags, ws->tile_cnt, ws->tile_off, ntiles, part,
+            last ? nullptr : reinterpret_cast<int4 *>(ws->chunks), ws->nchunks, ws->chunk_cap, hist_wave(ws));
+    WGB_PDL("k_scatter", k_scatter, dim3(ntiles), dim3(PART_THREADS), 0, st, lvl, ws->nn + d, ws->nact + d, ord, pn,
+            ws->flags, ws->tile_off, part, ws->order[d & 1], ws->posnode[d & 1], ws->pred, ws->K, ws->cls, ws->lr,
+            npos, ws->N, last ? level_nodes(ws, d + 1) : nullptr);
     return WGB_OK;
 }
 
