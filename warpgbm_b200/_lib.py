@@ -142,7 +142,7 @@ def check(rc: int, what: str = "") -> None:
 # kernels each entry point launches (bench.py reports the count it saw)
 _KERNELS = {
     "wgb_tree_reset": 1, "wgb_tree_residual": 1, "wgb_tree_subset": 1, "wgb_tree_quantize": 1, "wgb_tree_root": 1,
-    "wgb_level_hist": 2, "wgb_level_split": 2, "wgb_level_pick": 1, "wgb_level_partition": 3,
+    "wgb_level_hist": 3, "wgb_level_split": 2, "wgb_level_pick": 1, "wgb_level_partition": 3,
     "wgb_tree_finish": 0,
     "wgb_grow_tree": 0, "wgb_bins_feature_major": 1, "wgb_prebinned_ingest": 1,
     "wgb_bin_matrix": 1, "wgb_predict_packed": 1, "wgb_predict_heap": 1, "wgb_quantile_edges": 2, "wgb_quantile_pass": 1, "wgb_quantile_pick": 1,

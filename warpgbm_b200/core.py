@@ -202,7 +202,7 @@ def level_launches(D: int, E: int, fused: bool = True, sliced: bool = False) -> 
     """Kernels one tree (or one batch of trees) launches in wgb_grow_tree."""
     n = 4                                            # reset, residual, quantize, root
     for d in range(D):
-        n += (4 if d == 0 else 2) if E == 1 else (3 if d == 0 else 1)   # histogram (+ chunk plan, root cells)
+        n += (5 if d == 0 else 3) if E == 1 else (4 if d == 0 else 2)   # zero, histogram (+ chunk plan, root cells)
         n += 3 if d == 0 else 2                      # split (+ root totals), final
         n += 1 if sliced else 0                      # pick
         n += 1 if fused else 3                       # partition, or flags, offsets, scatter

@@ -39,6 +39,7 @@ void set_error(const char *fmt, ...) {
 // ====================================================================== //
 
 __global__ void k_reset(float *maxabs, long long *rootsum, int ntree) {
+    pdl_wait();  // the previous kernel on the stream has completed
     for (int t = threadIdx.x; t < ntree; t += blockDim.x) {
         maxabs[t] = 0.0f;
         rootsum[t] = 0;
@@ -50,6 +51,7 @@ __global__ void k_reset(float *maxabs, long long *rootsum, int ntree) {
 // residuals of a multiclass round, core.py:782) and max |g| of the tree.
 __global__ void k_residual(const float *__restrict__ y, const float *__restrict__ pred, int K,
                            int cls, float *__restrict__ g, long long n, float *maxabs) {
+    pdl_wait();  // the previous kernel on the stream has completed
     const int t = blockIdx.y;
     g += (long long)t * n;
     float m = 0.0f;
@@ -79,6 +81,7 @@ __global__ void k_residual(const float *__restrict__ y, const float *__restrict_
 // Tree t = blockIdx.y: q = rint(g * 2^s) with the tree's own shift, sum of q.
 __global__ void k_quantize(const float *__restrict__ g, int *__restrict__ qg, long long n,
                            const float *maxabs, int *shift_out, long long *rootsum) {
+    pdl_wait();  // the previous kernel on the stream has completed
     const int t = blockIdx.y;
     g += (long long)t * n;
     qg += (long long)t * n;
@@ -108,6 +111,7 @@ __global__ void k_quantize(const float *__restrict__ g, int *__restrict__ qg, lo
 // complete on every rank.
 __global__ void k_root(wgb_node *nodes, int *nn, int *nact, int D, long long n_local,
                        long long n_global, int ntree) {
+    pdl_wait();  // the previous kernel on the stream has completed
     for (int t = threadIdx.x; t < ntree; t += blockDim.x) {
         wgb_node r;
         r.sumq = 0;
@@ -135,8 +139,20 @@ __global__ void k_root(wgb_node *nodes, int *nn, int *nact, int D, long long n_l
 // Copies each tree's local root sum into its root slot's first spare cell
 // (of every slice region of a sliced fit's staging buffer), so that the
 // level-0 reduction carries it.
+// out[0, n) = 0: a level's histogram slots before its build (a kernel, so
+// the level's launches stay one chain of dependent launches).
+__global__ void __launch_bounds__(256) k_zero(long long *out, long long n) {
+    pdl_wait();  // the previous kernel on the stream has completed
+    for (long long i = (long long)blockIdx.x * 256 + threadIdx.x; i < n; i += (long long)gridDim.x * 256) out[i] = 0;
+}
+static inline unsigned zero_grid(long long n) {
+    const long long g = (n + 255) / 256;
+    return (unsigned)(g < 1 ? 1 : (g > 148 * 8 ? 148 * 8 : g));
+}
+
 __global__ void k_root_cells(long long *hg, const long long *rootsum, long long slot_elems, long long nc,
                              int ntree, int nregion, long long region_stride) {
+    pdl_wait();  // the previous kernel on the stream has completed
     for (int i = threadIdx.x; i < ntree * nregion; i += blockDim.x) {
         const int t = i % ntree, r = i / ntree;
         hg[r * region_stride + t * slot_elems + 2 * nc] = rootsum[t];
@@ -1992,6 +2008,7 @@ __global__ void __launch_bounds__(PART_THREADS) k_partition(
 __global__ void __launch_bounds__(256) k_bins_subset(const int8_t *__restrict__ bins, long long N, long long S,
                                                      const int *__restrict__ feats, int k, int8_t *__restrict__ out,
                                                      long long So, int *__restrict__ kpos_out) {
+    pdl_wait();  // the previous kernel on the stream has completed
     extern __shared__ int s_feat[];
     for (int j = threadIdx.x; j < So; j += blockDim.x) {
         s_feat[j] = j < k ? feats[j] : -1;
@@ -2165,8 +2182,8 @@ static int check_ws(const wgb_ws *ws) {
 int wgb_tree_reset(const wgb_ws *ws, void *stream) {
     int rc = check_ws(ws);
     if (rc) return rc;
-    k_reset<<<1, 32, 0, as_stream(stream)>>>(ws->maxabs, LL(ws->rootsum), ws_ntree(ws));
-    WGB_LAUNCHED("k_reset");
+    WGB_PDL("k_reset", k_reset, dim3(1), dim3(32), 0, as_stream(stream), ws->maxabs, LL(ws->rootsum),
+            ws_ntree(ws));
     return WGB_OK;
 }
 
@@ -2175,8 +2192,8 @@ int wgb_tree_residual(const wgb_ws *ws, void *stream) {
     if (rc) return rc;
     if (ws->N == 0) return WGB_OK;
     const dim3 grid((unsigned)grid_for(ws->N, 256, 148 * 16 / ws_ntree(ws) + 1), (unsigned)ws_ntree(ws));
-    k_residual<<<grid, 256, 0, as_stream(stream)>>>(ws->y, ws->pred, ws->K, ws->cls, ws->g, ws->N, ws->maxabs);
-    WGB_LAUNCHED("k_residual");
+    WGB_PDL("k_residual", k_residual, grid, dim3(256), 0, as_stream(stream), ws->y, ws->pred, ws->K, ws->cls, ws->g,
+            ws->N, ws->maxabs);
     return WGB_OK;
 }
 
@@ -2184,8 +2201,8 @@ int wgb_tree_quantize(const wgb_ws *ws, void *stream) {
     int rc = check_ws(ws);
     if (rc) return rc;
     const dim3 grid((unsigned)grid_for(ws->N, 256, 148 * 16 / ws_ntree(ws) + 1), (unsigned)ws_ntree(ws));
-    k_quantize<<<grid, 256, 0, as_stream(stream)>>>(ws->g, ws->qg, ws->N, ws->maxabs, ws->shift, LL(ws->rootsum));
-    WGB_LAUNCHED("k_quantize");
+    WGB_PDL("k_quantize", k_quantize, grid, dim3(256), 0, as_stream(stream), ws->g, ws->qg, ws->N, ws->maxabs,
+            ws->shift, LL(ws->rootsum));
     return WGB_OK;
 }
 
@@ -2198,18 +2215,16 @@ int wgb_tree_subset(const wgb_ws *ws, void *stream) {
     if (ws->N == 0) return WGB_OK;
     const size_t sm = (size_t)ws->S_sub * sizeof(int);
     WGB_CUDA(cudaFuncSetAttribute(k_bins_subset, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm));
-    k_bins_subset<<<(unsigned)((ws->N + 15) / 16), 256, sm, as_stream(stream)>>>(ws->bins, ws->N, ws->S, ws->feats,
-                                                                                ws->k, ws->bins_sub, ws->S_sub,
-                                                                                ws->kpos_sub);
-    WGB_LAUNCHED("k_bins_subset");
+    WGB_PDL("k_bins_subset", k_bins_subset, dim3((unsigned)((ws->N + 15) / 16)), dim3(256), sm, as_stream(stream),
+            ws->bins, ws->N, ws->S, ws->feats, ws->k, ws->bins_sub, ws->S_sub, ws->kpos_sub);
     return WGB_OK;
 }
 
 int wgb_tree_root(const wgb_ws *ws, void *stream) {
     int rc = check_ws(ws);
     if (rc) return rc;
-    k_root<<<1, 32, 0, as_stream(stream)>>>(ws->nodes, ws->nn, ws->nact, ws->D, ws->N, ws->N_global, ws_ntree(ws));
-    WGB_LAUNCHED("k_root");
+    WGB_PDL("k_root", k_root, dim3(1), dim3(32), 0, as_stream(stream), ws->nodes, ws->nn, ws->nact, ws->D, ws->N,
+            ws->N_global, ws_ntree(ws));
     return WGB_OK;
 }
 
@@ -2237,17 +2252,19 @@ int wgb_level_hist(const wgb_ws *ws, int32_t d, void *stream) {
         const long long region = (long long)count * se;
         WGB_CHECK_ARG(region * ws->nslice <= ws->hstage_elems, "hstage holds %lld elements, level %d needs %lld",
                       (long long)ws->hstage_elems, d, region * ws->nslice);
-        WGB_CUDA(cudaMemsetAsync(ws->hstage, 0, sizeof(int64_t) * region * ws->nslice, st));
+        WGB_PDL("k_zero", k_zero, dim3(zero_grid(region * ws->nslice)), dim3(256), 0, st, LL(ws->hstage),
+                region * ws->nslice);
         if (d == 0) {  // this rank's root sums ride along with the level-0 reduction
-            k_root_cells<<<1, 32, 0, st>>>(LL(ws->hstage), LL(ws->rootsum), se, nc, ws_ntree(ws), ws->nslice, region);
-            WGB_LAUNCHED("k_root_cells");
+            WGB_PDL("k_root_cells", k_root_cells, dim3(1), dim3(32), 0, st, LL(ws->hstage), LL(ws->rootsum), se, nc,
+                    ws_ntree(ws), ws->nslice, region);
         }
         out = HistOut{LL(ws->hstage), LL(ws->hstage) + nc, se, region, ws->ks, first};
     } else {
-        WGB_CUDA(cudaMemsetAsync(ws->hg + (long long)first * se, 0, sizeof(int64_t) * se * count, st));
+        WGB_PDL("k_zero", k_zero, dim3(zero_grid(se * count)), dim3(256), 0, st, LL(ws->hg) + (long long)first * se,
+                se * count);
         if (d == 0) {
-            k_root_cells<<<1, 32, 0, st>>>(LL(ws->hg), LL(ws->rootsum), se, nc, ws_ntree(ws), 1, 0);
-            WGB_LAUNCHED("k_root_cells");
+            WGB_PDL("k_root_cells", k_root_cells, dim3(1), dim3(32), 0, st, LL(ws->hg), LL(ws->rootsum), se, nc,
+                    ws_ntree(ws), 1, 0ll);
         }
         out = HistOut{LL(ws->hg), LL(ws->hg) + nc, se, 0, ws->k, 0};
     }
