@@ -167,12 +167,13 @@ def _edge_worker(rank, world, port, outdir, nq):
     dist.destroy_process_group()
 
 
-@pytest.mark.parametrize("nq", [31, 7])
+@pytest.mark.parametrize("nq", [31, 7, 63])
 def test_sharded_quantile_edges_equal_torch_quantile(cuda, nq):
     """Quantile edges of row-sharded columns (3 gloo ranks on one GPU, one of
-    them holding no rows): the digit histograms summed over the ranks select
-    the same order statistics as the one-launch select over the concatenated
-    column (bit for bit), and the edges equal torch.quantile's -- ties,
+    them holding no rows): the digit histograms summed over the ranks (up to
+    32 quantiles; more take the column exchange) select the same order
+    statistics as the one-launch select over the concatenated column (bit
+    for bit), and the edges equal torch.quantile's -- ties,
     signed zeros, infinities, a NaN column, a constant column, tiny and huge
     magnitudes.  (Against torch the comparison is by value, as for the
     one-launch select: a zero edge's sign bins nothing differently.)"""
