@@ -805,7 +805,11 @@ def main():
                          "traffic_unit": f"bytes per launch (ncu ratio {HIST_TRAFFIC_PER_ALG_BYTE} x algorithmic)",
                          "launches_timed": nlaunch,
                          "avg_launch_ms": round(hist_ms / max(nlaunch, 1), 4),
-                         "timed_on": "one extra fit with CUDA events around every histogram level"},
+                         "timed_on": "one extra fit with CUDA events around every histogram level",
+                         "limited_by": "shared-memory reductions, not HBM: two red.shared.add.u32 per "
+                                       "(row, feature) for the exact 30-bit fixed-point sums; at the "
+                                       "microbenchmarked 0.955 per SM-clock the build's ceiling is about "
+                                       "0.65 of the HBM figure (profiles/k_hist_config2.md)"},
             "e2e": e2e,
             "breakdown_rank0_ms_per_step": {"histogram_kernels": round(hist_ms, 1),
                                             "collectives": round(comm_ms, 1),
