@@ -222,9 +222,11 @@ def exact_mean(y: torch.Tensor, comm: _Comm) -> float:
     """Base prediction: mean of y from an exact fixed-point sum, identical at
     every GPU count.  t = 62 - L - e (n < 2^L, max|y| < 2^e);
     mean = float32(float64(sum rint(y * 2^t)) * 2^-t / n)."""
-    n = torch.tensor([y.numel()], dtype=torch.int64, device=y.device)
-    comm.sum_(n)
-    n = int(n.item())
+    n = y.numel()
+    if comm.on:
+        nt = torch.tensor([n], dtype=torch.int64, device=y.device)
+        comm.sum_(nt)
+        n = int(nt.item())
     m = torch.zeros(1, dtype=torch.float32, device=y.device)
     if y.numel():
         m[0] = y.abs().max()
@@ -735,7 +737,9 @@ class WarpGBM(BaseEstimator, RegressorMixin):
                 print(f"Model already has {self._trees_trained} trees (n_estimators={self.n_estimators}). "
                       "No additional training needed.")
                 return self
-        if era_id is None:
+        if era_id is None and self._comm.on:
+            # every rank takes part in the era exchange (a single rank with no
+            # era ids has one era and needs none: _fit)
             era_id = np.ones(X.shape[0], dtype="int32")
         if self.objective in ("multiclass", "binary") and torch.is_tensor(y):
             y = y.cpu().numpy()
@@ -965,14 +969,22 @@ class WarpGBM(BaseEstimator, RegressorMixin):
             self.num_samples, self.num_features = X.shape
             N, F = X.shape
             bins, _ = self._upload_bins(X, fit=True)
-            era_d = _to_dev(era_id, dev)
-            self.unique_eras, era_dense = global_unique_eras(era_d, comm)
+            if era_id is None:
+                # the reference's default, era_id = ones: one era, every row in it;
+                # nothing to upload, no host round trip
+                self.unique_eras, era_dense = torch.ones(1, dtype=torch.int32, device=dev), None
+            else:
+                era_d = _to_dev(era_id, dev)
+                self.unique_eras, era_dense = global_unique_eras(era_d, comm)
             self.num_eras = E = int(self.unique_eras.numel())
             K = self.num_classes if classification else 1
             k = max(1, int(self.colsample_bytree * F)) if self.colsample_bytree < 1.0 else F
-            nglob = torch.tensor([N], dtype=torch.int64, device=dev)
-            comm.sum_(nglob)
-            self._n_global = int(nglob.item())
+            if comm.on:
+                nglob = torch.tensor([N], dtype=torch.int64, device=dev)
+                comm.sum_(nglob)
+                self._n_global = int(nglob.item())
+            else:
+                self._n_global = N
             if E > 1:
                 root_order = torch.sort(era_dense, stable=True).indices.to(torch.int32)
             else:
