@@ -968,6 +968,14 @@ class WarpGBM(BaseEstimator, RegressorMixin):
         with torch.no_grad():
             self.num_samples, self.num_features = X.shape
             N, F = X.shape
+            resume = self.warm_start and self._is_fitted and self._trees_trained > 0
+            if not classification:
+                # the base prediction reads two scalars back from the device:
+                # done first, while the GPU is idle anyway, so that from the
+                # binning to the last tree nothing waits on the host
+                Yf = _to_dev(y, dev, torch.float32)
+                if not resume:
+                    self.base_prediction = exact_mean(Yf, comm)
             bins, _ = self._upload_bins(X, fit=True)
             if era_id is None:
                 # the reference's default, era_id = ones: one era, every row in it;
@@ -1024,7 +1032,6 @@ class WarpGBM(BaseEstimator, RegressorMixin):
             else:
                 ws.bins_fm = None
 
-            resume = self.warm_start and self._is_fitted and self._trees_trained > 0
             if classification:
                 Yl = _to_dev(y, dev, torch.int32)
                 pred = torch.zeros((N, K), dtype=torch.float32, device=dev)
@@ -1040,9 +1047,6 @@ class WarpGBM(BaseEstimator, RegressorMixin):
                 ws.y = None
                 self.Y_gpu = Yl
             else:
-                Yf = _to_dev(y, dev, torch.float32)
-                if not resume:
-                    self.base_prediction = exact_mean(Yf, comm)
                 pred = torch.zeros((N, 1), dtype=torch.float32, device=dev) + np.float32(self.base_prediction)
                 ws.y = Yf.data_ptr()
                 self.Y_gpu = Yf
